@@ -1,0 +1,743 @@
+// api.cu -- the C ABI (include/astro_moe.h): validation, error reporting, the
+// block context and the orchestration of one MoE block.
+//
+// Host-side mirror of the reference operator: astro_moe_block_forward plays the
+// role of Qwen3_5Model::forward_qwen3_5_moe's resident branch
+// (crates/model-serving/src/qwen3_5_moe/model/forward.rs:19-127 and
+// resident_execution.rs:70-143): route once, sort the assignments (always on the
+// device -- the sort only permutes rows, so it never changes a row's value), run
+// the gathered gate/up projection with SwiGLU, the gathered down projection, and
+// the weighted combine with the shared expert.  The reference's sorted/unsorted
+// switch (routing.rs:13, assignment count >= 64) still selects the weighted-sum
+// arithmetic, exactly as in the reference.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/astro_moe.h"
+#include "kernels.h"
+#include "moe_gemm.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int status, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  if (e == cudaErrorMemoryAllocation)
+    return fail(ASTRO_MOE_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
+  return fail(ASTRO_MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(expr, what)                              \
+  do {                                              \
+    cudaError_t _e = (expr);                        \
+    if (_e != cudaSuccess) return cuda_fail(_e, what); \
+  } while (0)
+
+inline cudaStream_t S(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+bool valid_dtype(int d) {
+  return d == ASTRO_MOE_DTYPE_BF16 || d == ASTRO_MOE_DTYPE_F16 || d == ASTRO_MOE_DTYPE_F32;
+}
+bool valid_group(int g) { return g == 32 || g == 64 || g == 128; }
+bool valid_bits(int b) { return b == 2 || b == 3 || b == 4 || b == 5 || b == 6 || b == 8; }
+
+// affine profile check, mlx_quantized_operations.rs:226-330 (in_features here is
+// the unpacked width; rows of 32 elements are the unit of the kernels)
+int check_affine(const char* op, int64_t in_features, int group, int bits) {
+  if (!valid_group(group)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: affine group size must be 32, 64, or 128", op);
+  if (!valid_bits(bits)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: affine bit width must be 2, 3, 4, 5, 6, or 8", op);
+  if (in_features <= 0 || in_features % group != 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: input width %lld is not a multiple of the group size", op, (long long)in_features);
+  if (in_features % 32 != 0)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: input width must be a multiple of 32", op);
+  return ASTRO_MOE_OK;
+}
+
+// per-device status word and scratch
+struct DeviceState {
+  uint32_t* status = nullptr;
+};
+std::mutex g_dev_mu;
+std::map<int, DeviceState> g_dev;
+
+int device_status_ptr(uint32_t** out) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceState& ds = g_dev[dev];
+  if (!ds.status) {
+    CK(cudaMalloc(&ds.status, sizeof(uint32_t)), "cudaMalloc(status)");
+    CK(cudaMemset(ds.status, 0, sizeof(uint32_t)), "cudaMemset(status)");
+  }
+  *out = ds.status;
+  return ASTRO_MOE_OK;
+}
+
+}  // namespace
+
+// ===========================================================================
+// context
+// ===========================================================================
+struct LayerState {
+  astro_moe_layer_weights w{};
+  bool registered = false;
+  astro::MoeGemmPlan gemm{};  // tensor-core plan (TMA descriptors), when eligible
+};
+
+struct astro_moe_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  astro_moe_options opt{};
+  std::map<int, LayerState> layers;
+  uint32_t* status = nullptr;
+  // workspace
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  void* io = nullptr;  // device staging for the host-buffer entry point
+  size_t io_bytes = 0;
+  // stage attribution
+  bool attribution = false;
+  std::vector<cudaEvent_t> event_pool;
+  std::vector<std::vector<cudaEvent_t>> pending;  // 6 events per measured call
+  astro_moe_attribution acc{};
+  int64_t launches = 0;
+};
+
+namespace {
+
+struct BlockWorkspace {
+  uint16_t* logits;
+  uint32_t* ids;
+  uint16_t* scores;
+  uint16_t* gate_logit;
+  uint32_t* order;
+  uint32_t* inverse;
+  uint32_t* sids;
+  uint32_t* stok;
+  uint32_t* offsets;
+  uint16_t* states;  // gathered activation rows [rows, H] (tensor-core path)
+  uint16_t* act;     // [rows, I]
+  uint16_t* yrows;   // [rows, H]
+  void* gemm_scratch;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+size_t plan_workspace(const astro_moe_layer_weights& w, int64_t T, BlockWorkspace* out,
+                      char* base) {
+  const int64_t H = w.hidden, E = w.experts, K = w.top_k;
+  const int64_t Imax = w.intermediate;
+  const int64_t N = T * K;
+  const int64_t rows = N + (w.shared_intermediate > 0 ? T : 0);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off = align_up(off + bytes, 256);
+    return p;
+  };
+  BlockWorkspace b{};
+  b.logits = (uint16_t*)take(sizeof(uint16_t) * T * E);
+  b.ids = (uint32_t*)take(sizeof(uint32_t) * N);
+  b.scores = (uint16_t*)take(sizeof(uint16_t) * N);
+  b.gate_logit = (uint16_t*)take(sizeof(uint16_t) * T);
+  b.order = (uint32_t*)take(sizeof(uint32_t) * N);
+  b.inverse = (uint32_t*)take(sizeof(uint32_t) * N);
+  b.sids = (uint32_t*)take(sizeof(uint32_t) * rows);
+  b.stok = (uint32_t*)take(sizeof(uint32_t) * rows);
+  b.offsets = (uint32_t*)take(sizeof(uint32_t) * (E + 2));
+  b.states = (uint16_t*)take(sizeof(uint16_t) * rows * H);
+  b.act = (uint16_t*)take(sizeof(uint16_t) * rows * Imax);
+  b.yrows = (uint16_t*)take(sizeof(uint16_t) * rows * H);
+  b.gemm_scratch = take(astro::moe_gemm_scratch_bytes());
+  if (out) *out = b;
+  return off;
+}
+
+int ensure_ws(astro_moe_ctx* ctx, size_t bytes) {
+  if (ctx->ws_bytes >= bytes) return ASTRO_MOE_OK;
+  if (ctx->ws) {
+    CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    cudaFree(ctx->ws);
+    ctx->ws = nullptr;
+    ctx->ws_bytes = 0;
+  }
+  CK(cudaMalloc(&ctx->ws, bytes), "cudaMalloc(workspace)");
+  ctx->ws_bytes = bytes;
+  return ASTRO_MOE_OK;
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) == cudaSuccess && prev != dev) cudaSetDevice(dev);
+    else prev = -1;
+  }
+  ~DeviceGuard() {
+    if (prev >= 0) cudaSetDevice(prev);
+  }
+};
+
+int validate_affine_tensor(const char* name, const astro_moe_affine& a) {
+  if (!a.packed || !a.scales || !a.biases)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "register layer: %s has a null pointer", name);
+  if ((reinterpret_cast<uintptr_t>(a.packed) & 15u) != 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "register layer: %s packed weights must be 16-byte aligned", name);
+  return ASTRO_MOE_OK;
+}
+
+cudaEvent_t take_event(astro_moe_ctx* ctx) {
+  if (!ctx->event_pool.empty()) {
+    cudaEvent_t e = ctx->event_pool.back();
+    ctx->event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+struct StageMarks {
+  astro_moe_ctx* ctx;
+  std::vector<cudaEvent_t> ev;
+  explicit StageMarks(astro_moe_ctx* c) : ctx(c) {}
+  void mark() {
+    if (!ctx->attribution) return;
+    cudaEvent_t e = take_event(ctx);
+    cudaEventRecord(e, ctx->stream);
+    ev.push_back(e);
+  }
+  void commit() {
+    if (ctx->attribution && ev.size() == 6) ctx->pending.push_back(ev);
+    else for (auto e : ev) ctx->event_pool.push_back(e);
+    ev.clear();
+  }
+};
+
+int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void* out,
+              const astro_moe_block_taps* taps) {
+  const astro_moe_layer_weights& w = L.w;
+  const int H = w.hidden, E = w.experts, K = w.top_k, I = w.intermediate;
+  const int Is = w.shared_intermediate;
+  const bool has_shared = Is > 0;
+  cudaStream_t st = ctx->stream;
+  if (T == 0) return ASTRO_MOE_OK;
+  const size_t need = plan_workspace(w, T, nullptr, nullptr);
+  if (int rc = ensure_ws(ctx, need)) return rc;
+  BlockWorkspace b{};
+  plan_workspace(w, T, &b, (char*)ctx->ws);
+  const int64_t N = T * K;
+  const int64_t rows = N + (has_shared ? T : 0);
+  const int threshold = ctx->opt.sorted_threshold > 0 ? ctx->opt.sorted_threshold : 64;
+  const bool sorted_semantics = N >= threshold;
+
+  StageMarks marks(ctx);
+  marks.mark();
+  // a1: router projection
+  const bool use_tc = astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores);
+  ctx->launches += use_tc ? 7 : 6;
+  if (use_tc) {
+    CK(astro::moe_gemm_router(L.gemm, x, T, b.logits, b.gemm_scratch, st), "router projection");
+  } else {
+    CK(astro::launch_dense_nt_simt(x, w.router_weight, T, E, H, b.logits, E, st), "router projection");
+  }
+  marks.mark();
+  // a2: route (+ shared-expert gate logit)
+  CK(astro::launch_route_experts(b.logits, ASTRO_MOE_DTYPE_BF16, T, E, K, w.normalize_top_k,
+                                 b.ids, b.scores, x, has_shared ? w.shared_expert_gate : nullptr, H,
+                                 has_shared ? b.gate_logit : nullptr, st),
+     "route experts");
+  // a3: sort (+ shared segment E)
+  CK(astro::launch_sort_assignments(b.ids, T, K, E, has_shared ? T : 0, b.order, b.inverse,
+                                    b.sids, b.stok, b.offsets, ctx->status, st),
+     "sort expert assignments");
+
+  if (use_tc) {
+    // a4-a6 on tcgen05: gather rows, gate/up + SwiGLU, down
+    CK(astro::launch_take_rows(x, T, b.stok, rows, H, b.states, ctx->status, st), "take rows");
+    marks.mark();
+    CK(astro::moe_gemm_gate_up(L.gemm, b.states, rows, b.offsets, b.act, b.gemm_scratch, st),
+       "gate/up projection");
+    marks.mark();
+    CK(astro::moe_gemm_down(L.gemm, b.act, rows, b.offsets, b.yrows, b.gemm_scratch, st),
+       "down projection");
+  } else {
+    marks.mark();
+    // a4-a6 on CUDA cores (grouped GEMV tiles); the shared expert is segment E
+    astro::GroupedGemvDesc d;
+    d.x = x;
+    d.x_rows = b.stok;
+    d.x_limit = T;
+    d.in_features = H;
+    d.seg_offsets = b.offsets;
+    d.nseg = E + (has_shared ? 1 : 0);
+    d.shared_seg = has_shared ? E : -1;
+    d.rows_total = rows;
+    if (w.gate_up_fused) {
+      d.wa[0] = astro::AffineRef{w.gate.packed, w.gate.scales, w.gate.biases, 2LL * I, 0};
+      d.wb[0] = astro::AffineRef{w.gate.packed, w.gate.scales, w.gate.biases, 2LL * I, I};
+    } else {
+      d.wa[0] = astro::AffineRef{w.gate.packed, w.gate.scales, w.gate.biases, I, 0};
+      d.wb[0] = astro::AffineRef{w.up.packed, w.up.scales, w.up.biases, I, 0};
+    }
+    if (has_shared) {
+      d.wa[1] = astro::AffineRef{w.shared_gate.packed, w.shared_gate.scales, w.shared_gate.biases, Is, 0};
+      d.wb[1] = astro::AffineRef{w.shared_up.packed, w.shared_up.scales, w.shared_up.biases, Is, 0};
+    }
+    d.out_features = I;
+    d.group = w.group_size;
+    d.bits = w.bits;
+    d.swiglu = true;
+    d.y = b.act;
+    d.y_limit = rows;
+    d.ldy = I;
+    d.status = ctx->status;
+    CK(astro::launch_grouped_gemv(d, st), "gate/up projection");
+    marks.mark();
+    astro::GroupedGemvDesc dd = d;
+    dd.x = b.act;
+    dd.x_rows = nullptr;
+    dd.x_limit = rows;
+    dd.in_features = I;
+    dd.wa[0] = astro::AffineRef{w.down.packed, w.down.scales, w.down.biases, H, 0};
+    if (has_shared)
+      dd.wa[1] = astro::AffineRef{w.shared_down.packed, w.shared_down.scales, w.shared_down.biases, H, 0};
+    dd.wb[0] = dd.wb[1] = astro::AffineRef{};
+    dd.out_features = H;
+    dd.swiglu = false;
+    dd.y = b.yrows;
+    dd.ldy = H;
+    CK(astro::launch_grouped_gemv(dd, st), "down projection");
+  }
+  marks.mark();
+  // a7 + a8: weighted sum fused with the shared expert and its gate
+  CK(astro::launch_block_combine(b.yrows, b.inverse, b.scores, has_shared ? b.gate_logit : nullptr,
+                                 N, T, K, H, sorted_semantics ? 1 : 0, out, st),
+     "weighted combine");
+  marks.mark();
+  marks.commit();
+  if (ctx->attribution) ctx->acc.calls += 1;
+  if (taps) {
+    if (taps->router_logits)
+      CK(cudaMemcpyAsync(taps->router_logits, b.logits, sizeof(uint16_t) * T * E,
+                         cudaMemcpyDeviceToDevice, st), "taps");
+    if (taps->selected_indices)
+      CK(cudaMemcpyAsync(taps->selected_indices, b.ids, sizeof(uint32_t) * N,
+                         cudaMemcpyDeviceToDevice, st), "taps");
+    if (taps->selected_scores)
+      CK(cudaMemcpyAsync(taps->selected_scores, b.scores, sizeof(uint16_t) * N,
+                         cudaMemcpyDeviceToDevice, st), "taps");
+    if (taps->expert_offsets)
+      CK(cudaMemcpyAsync(taps->expert_offsets, b.offsets,
+                         sizeof(uint32_t) * (E + (has_shared ? 2 : 1)), cudaMemcpyDeviceToDevice, st),
+         "taps");
+  }
+  return ASTRO_MOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* astro_moe_last_error(void) { return g_last_error.c_str(); }
+int astro_moe_abi_version(void) { return ASTRO_MOE_ABI_VERSION; }
+
+int astro_moe_device_status(int32_t device, uint32_t* status, int32_t reset) {
+  if (!status) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "device status: null output");
+  DeviceGuard g(device);
+  uint32_t* p = nullptr;
+  if (int rc = device_status_ptr(&p)) return rc;
+  CK(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+  CK(cudaMemcpy(status, p, sizeof(uint32_t), cudaMemcpyDeviceToHost), "read device status");
+  if (reset) CK(cudaMemset(p, 0, sizeof(uint32_t)), "reset device status");
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_route_experts(const void* logits, int32_t dtype, int64_t tokens, int32_t experts,
+                            int32_t top_k, int32_t normalize, uint32_t* ids, void* scores,
+                            void* stream) {
+  const char* op = "route Qwen3.5-MoE sparse experts";
+  if (!valid_dtype(dtype))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: router logits must use float16, bfloat16, or float32", op);
+  if (tokens < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: negative token count", op);
+  if (experts <= 0 || top_k <= 0 || top_k > experts)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "%s: selected expert count must be positive and no larger than the router dimension", op);
+  if (top_k > 32 || experts > 1024)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: top_k <= 32 and experts <= 1024 are supported", op);
+  if (tokens > 0 && (!logits || !ids || !scores))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  CK(astro::launch_route_experts(logits, dtype, tokens, experts, top_k, normalize, ids, scores,
+                                 nullptr, nullptr, 0, nullptr, S(stream)),
+     op);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_sort_expert_assignments(const uint32_t* ids, int64_t tokens, int32_t top_k,
+                                      int32_t experts, uint32_t* sorted_order,
+                                      uint32_t* inverse_order, uint32_t* sorted_ids,
+                                      uint32_t* sorted_tokens, uint32_t* expert_offsets,
+                                      void* stream) {
+  const char* op = "sort stacked expert assignments";
+  if (tokens < 0 || top_k < 0 || experts <= 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: expert assignments have invalid shapes", op);
+  if (experts > 1024) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: experts <= 1024 are supported", op);
+  if (tokens * (int64_t)top_k > 0xffffffffLL)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: expert assignment count exceeds the integer range", op);
+  if (tokens * top_k > 0 && !ids) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null ids", op);
+  uint32_t* status = nullptr;
+  if (int rc = device_status_ptr(&status)) return rc;
+  uint32_t* offs = expert_offsets;
+  bool tmp = false;
+  if (!offs) {
+    CK(cudaMallocAsync(&offs, sizeof(uint32_t) * (experts + 1), S(stream)), "cudaMallocAsync");
+    tmp = true;
+  }
+  CK(astro::launch_sort_assignments(ids, tokens, top_k, experts, 0, sorted_order, inverse_order,
+                                    sorted_ids, sorted_tokens, offs, status, S(stream)),
+     op);
+  if (tmp) CK(cudaFreeAsync(offs, S(stream)), "cudaFreeAsync");
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_take_rows(const void* states, int64_t state_rows, int32_t hidden,
+                        const uint32_t* rows, int64_t n, void* out, void* stream) {
+  if (hidden <= 0 || hidden % 8 != 0 || n < 0 || state_rows < 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "take rows: hidden must be a positive multiple of 8");
+  uint32_t* status = nullptr;
+  if (int rc = device_status_ptr(&status)) return rc;
+  CK(astro::launch_take_rows(states, state_rows, rows, n, hidden, out, status, S(stream)), "take rows");
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_gather_qmm(const void* x, int64_t x_rows, int32_t in_features,
+                         const uint32_t* lhs, const uint32_t* rhs, int64_t n_rows,
+                         const uint32_t* packed, const void* scales, const void* biases,
+                         int32_t experts, int32_t out_features, int32_t group, int32_t bits,
+                         int32_t sorted_indices, void* out, void* stream) {
+  const char* op = "build affine gather_qmm";
+  if (int rc = check_affine(op, in_features, group, bits)) return rc;
+  if (n_rows < 0 || x_rows < 0 || experts <= 0 || out_features <= 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid shapes", op);
+  if (experts > 1024) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: experts <= 1024 are supported", op);
+  if (n_rows == 0) return ASTRO_MOE_OK;
+  if (!x || !packed || !scales || !biases || !out)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  if (!lhs && x_rows < n_rows)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: activation rows do not cover the assignments", op);
+  uint32_t* status = nullptr;
+  if (int rc = device_status_ptr(&status)) return rc;
+  cudaStream_t st = S(stream);
+  astro::GroupedGemvDesc d;
+  d.x = x;
+  d.x_limit = x_rows;
+  d.in_features = in_features;
+  d.wa[0] = astro::AffineRef{packed, scales, biases, out_features, 0};
+  d.out_features = out_features;
+  d.group = group;
+  d.bits = bits;
+  d.y = out;
+  d.y_limit = n_rows;
+  d.ldy = out_features;
+  d.status = status;
+  d.rows_total = n_rows;
+  uint32_t* buf = nullptr;
+  if (!rhs) {
+    // single expert: one segment [0, n)
+    CK(cudaMallocAsync(&buf, sizeof(uint32_t) * 2, st), "cudaMallocAsync");
+    const uint32_t h[2] = {0u, (uint32_t)n_rows};
+    CK(cudaMemcpyAsync(buf, h, sizeof(h), cudaMemcpyHostToDevice, st), "copy offsets");
+    CK(cudaStreamSynchronize(st), "sync");  // h is a stack array
+    d.seg_offsets = buf;
+    d.nseg = 1;
+    d.x_rows = lhs;
+  } else if (sorted_indices) {
+    CK(cudaMallocAsync(&buf, sizeof(uint32_t) * (experts + 1), st), "cudaMallocAsync");
+    CK(astro::launch_offsets_from_sorted(rhs, n_rows, experts, buf, status, st), op);
+    d.seg_offsets = buf;
+    d.nseg = experts;
+    d.x_rows = lhs;
+  } else {
+    // group rows by expert with the stable sort, gather through the order and
+    // write every result back to its original row
+    const size_t n = (size_t)n_rows;
+    CK(cudaMallocAsync(&buf, sizeof(uint32_t) * (2 * n + experts + 1), st), "cudaMallocAsync");
+    uint32_t* order = buf;
+    uint32_t* xr = buf + n;
+    uint32_t* offs = buf + 2 * n;
+    CK(astro::launch_sort_assignments(rhs, n_rows, 1, experts, 0, order, nullptr, nullptr, nullptr,
+                                      offs, status, st),
+       op);
+    CK(astro::launch_compose_rows(lhs, order, n_rows, xr, st), op);
+    d.seg_offsets = offs;
+    d.nseg = experts;
+    d.x_rows = xr;
+    d.y_rows = order;
+  }
+  CK(astro::launch_grouped_gemv(d, st), op);
+  CK(cudaFreeAsync(buf, st), "cudaFreeAsync");
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_quantized_matmul(const void* x, int64_t rows, int32_t in_features,
+                               const uint32_t* packed, const void* scales, const void* biases,
+                               int32_t out_features, int32_t group, int32_t bits, void* out,
+                               void* stream) {
+  return astro_moe_gather_qmm(x, rows, in_features, nullptr, nullptr, rows, packed, scales, biases,
+                              1, out_features, group, bits, 1, out, stream);
+}
+
+int astro_moe_swiglu(const void* gate, const void* up, int64_t n, void* out, void* stream) {
+  if (n < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "apply a compiled MLX SwiGLU graph: negative size");
+  CK(astro::launch_swiglu(gate, up, n, out, S(stream)), "apply a compiled MLX SwiGLU graph");
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_sorted_expert_weighted_sum(const void* sorted_outputs, int32_t out_dtype,
+                                         const uint32_t* inverse, const void* scores,
+                                         int32_t score_dtype, int64_t tokens, int32_t top_k,
+                                         int64_t dim, void* out, void* stream) {
+  const char* op = "reduce stacked expert outputs";
+  if (!valid_dtype(out_dtype) || !valid_dtype(score_dtype) || tokens < 0 || top_k < 0 || dim < 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "%s: sorted expert outputs, inverse order, and scores have invalid shapes or dtypes", op);
+  CK(astro::launch_sorted_weighted_sum(sorted_outputs, out_dtype, inverse, scores, score_dtype,
+                                       tokens, top_k, dim, out, S(stream)),
+     op);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_unsorted_expert_weighted_sum(const void* outputs, int32_t out_dtype,
+                                           const void* scores, int32_t score_dtype,
+                                           int64_t tokens, int32_t top_k, int64_t dim, void* out,
+                                           void* stream) {
+  const char* op = "reduce stacked expert outputs";
+  if (!valid_dtype(out_dtype) || !valid_dtype(score_dtype) || tokens < 0 || top_k < 0 || dim < 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "%s: unsorted expert outputs and scores must include an assignment axis", op);
+  if (top_k == 0) {
+    // empty reduction: zeros (weighted_sum.rs:172-188, empty_weighted_outputs)
+    const size_t es = out_dtype == ASTRO_MOE_DTYPE_F32 ? 4 : 2;
+    CK(cudaMemsetAsync(out, 0, es * (size_t)(tokens * dim), S(stream)), op);
+    return ASTRO_MOE_OK;
+  }
+  CK(astro::launch_unsorted_weighted_sum(outputs, out_dtype, scores, score_dtype, tokens, top_k,
+                                         dim, out, S(stream)),
+     op);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_combine_sparse_and_shared(const void* sparse, const void* shared,
+                                        const void* gate_logits, int32_t dtype, int64_t tokens,
+                                        int64_t dim, void* out, void* stream) {
+  const char* op = "combine Qwen3.5-MoE sparse and shared experts";
+  if (!valid_dtype(dtype) || tokens < 0 || dim < 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid shapes", op);
+  CK(astro::launch_combine_shared(sparse, shared, gate_logits, dtype, tokens, dim, out, S(stream)), op);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_invert_assignment_order(const uint32_t* order, int64_t n, uint32_t* inverse) {
+  if (n < 0 || n > 0xffffffffLL)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "assignment permutation length exceeds u32");
+  std::vector<unsigned char> seen((size_t)n, 0);
+  for (int64_t s = 0; s < n; ++s) {
+    const uint32_t o = order[s];
+    if ((int64_t)o >= n)
+      return fail(ASTRO_MOE_ERR_OUT_OF_RANGE_SLOT, "assignment permutation contains an out-of-range slot");
+    if (seen[o]) return fail(ASTRO_MOE_ERR_DUPLICATE_SLOT, "assignment permutation contains a duplicate slot");
+    seen[o] = 1;
+    inverse[o] = (uint32_t)s;
+  }
+  return ASTRO_MOE_OK;
+}
+
+// ---------------------------------------------------------------------------
+// context API
+// ---------------------------------------------------------------------------
+int astro_moe_ctx_create(int32_t device, void* stream, const astro_moe_options* options,
+                         astro_moe_ctx** out_ctx) {
+  if (!out_ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "ctx create: null output");
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+  if (device < 0 || device >= ndev)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "ctx create: device %d out of range", device);
+  DeviceGuard g(device);
+  auto* ctx = new astro_moe_ctx();
+  ctx->device = device;
+  ctx->stream = S(stream);
+  if (options) ctx->opt = *options;
+  if (int rc = device_status_ptr(&ctx->status)) {
+    delete ctx;
+    return rc;
+  }
+  *out_ctx = ctx;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ctx_destroy(astro_moe_ctx* ctx) {
+  if (!ctx) return ASTRO_MOE_OK;
+  DeviceGuard g(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  for (auto& kv : ctx->layers) astro::moe_gemm_release(kv.second.gemm);
+  for (auto& ev : ctx->pending)
+    for (auto e : ev) cudaEventDestroy(e);
+  for (auto e : ctx->event_pool) cudaEventDestroy(e);
+  if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->io) cudaFree(ctx->io);
+  delete ctx;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ctx_set_stream(astro_moe_ctx* ctx, void* stream) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "ctx: null");
+  ctx->stream = S(stream);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ctx_synchronize(astro_moe_ctx* ctx) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "ctx: null");
+  DeviceGuard g(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  uint32_t st = 0;
+  CK(cudaMemcpy(&st, ctx->status, sizeof(st), cudaMemcpyDeviceToHost), "read device status");
+  if (st) {
+    cudaMemset(ctx->status, 0, sizeof(uint32_t));
+    return fail(ASTRO_MOE_ERR_DEVICE_STATUS, "device status 0x%x (1: expert id out of range, 2: wait timeout, 4: bad row)", st);
+  }
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_moe_layer_weights* w) {
+  const char* op = "register layer";
+  if (!ctx || !w) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null argument", op);
+  if (layer < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: negative layer index", op);
+  if (w->hidden <= 0 || w->experts <= 0 || w->top_k <= 0 || w->top_k > w->experts ||
+      w->intermediate <= 0 || w->shared_intermediate < 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid geometry", op);
+  if (w->top_k > 32 || w->experts > 1024)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: top_k <= 32 and experts <= 1024 are supported", op);
+  if (w->hidden % 8 != 0) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: hidden must be a multiple of 8", op);
+  if (int rc = check_affine(op, w->hidden, w->group_size, w->bits)) return rc;
+  if (int rc = check_affine(op, w->intermediate, w->group_size, w->bits)) return rc;
+  if (w->shared_intermediate > 0)
+    if (int rc = check_affine(op, w->shared_intermediate, w->group_size, w->bits)) return rc;
+  if (w->shared_intermediate != 0 && w->shared_intermediate != w->intermediate)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED,
+                "%s: the shared expert must have the routed intermediate width (or be absent)", op);
+  if (!w->router_weight) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight", op);
+  if (int rc = validate_affine_tensor("gate", w->gate)) return rc;
+  if (!w->gate_up_fused)
+    if (int rc = validate_affine_tensor("up", w->up)) return rc;
+  if (int rc = validate_affine_tensor("down", w->down)) return rc;
+  if (w->shared_intermediate > 0) {
+    if (int rc = validate_affine_tensor("shared gate", w->shared_gate)) return rc;
+    if (int rc = validate_affine_tensor("shared up", w->shared_up)) return rc;
+    if (int rc = validate_affine_tensor("shared down", w->shared_down)) return rc;
+    if (!w->shared_expert_gate) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate", op);
+  }
+  DeviceGuard g(ctx->device);
+  LayerState& L = ctx->layers[layer];
+  astro::moe_gemm_release(L.gemm);
+  L.w = *w;
+  L.registered = true;
+  if (int st = astro::moe_gemm_plan(*w, &L.gemm)) {
+    L.registered = false;
+    return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);
+  }
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_block_forward_taps(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T,
+                                 void* out, const astro_moe_block_taps* taps) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: null ctx");
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.registered)
+    return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "block forward: layer %d is not registered", layer);
+  if (T < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: negative token count");
+  if (T * (int64_t)it->second.w.top_k + T > 0x7fffffffLL)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: too many tokens");
+  if (T > 0 && (!x || !out)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: null array");
+  DeviceGuard g(ctx->device);
+  return run_block(ctx, it->second, x, T, out, taps);
+}
+
+int astro_moe_block_forward(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T, void* out) {
+  return astro_moe_block_forward_taps(ctx, layer, x, T, out, nullptr);
+}
+
+int astro_moe_ctx_set_attribution(astro_moe_ctx* ctx, int32_t enabled) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "ctx: null");
+  ctx->attribution = enabled != 0;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ctx_read_attribution(astro_moe_ctx* ctx, astro_moe_attribution* out, int32_t reset) {
+  if (!ctx || !out) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "attribution: null argument");
+  DeviceGuard g(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  for (auto& ev : ctx->pending) {
+    float ms[5] = {0, 0, 0, 0, 0};
+    for (int i = 0; i < 5; ++i) cudaEventElapsedTime(&ms[i], ev[i], ev[i + 1]);
+    ctx->acc.router_projection_ms += ms[0];
+    ctx->acc.assignment_preparation_ms += ms[1];
+    ctx->acc.gate_up_ms += ms[2];
+    ctx->acc.down_ms += ms[3];
+    ctx->acc.weighted_reduction_ms += ms[4];
+    for (auto e : ev) ctx->event_pool.push_back(e);
+  }
+  ctx->pending.clear();
+  *out = ctx->acc;
+  out->kernel_launches = ctx->launches;
+  if (reset) {
+    ctx->acc = astro_moe_attribution{};
+    ctx->launches = 0;
+  }
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_block_forward_host(astro_moe_ctx* ctx, int32_t layer, const void* host_x, int64_t T,
+                                 void* host_out) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: null ctx");
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.registered)
+    return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "block forward: layer %d is not registered", layer);
+  if (T <= 0) return T == 0 ? ASTRO_MOE_OK : fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "negative tokens");
+  DeviceGuard g(ctx->device);
+  const size_t bytes = sizeof(uint16_t) * (size_t)T * it->second.w.hidden;
+  if (ctx->io_bytes < 2 * bytes) {
+    if (ctx->io) {
+      CK(cudaStreamSynchronize(ctx->stream), "sync");
+      cudaFree(ctx->io);
+    }
+    ctx->io = nullptr;
+    ctx->io_bytes = 0;
+    CK(cudaMalloc(&ctx->io, 2 * bytes), "cudaMalloc(io)");
+    ctx->io_bytes = 2 * bytes;
+  }
+  char* dx = (char*)ctx->io;
+  char* dy = dx + bytes;
+  CK(cudaMemcpyAsync(dx, host_x, bytes, cudaMemcpyHostToDevice, ctx->stream), "copy hidden states in");
+  if (int rc = run_block(ctx, it->second, dx, T, dy, nullptr)) return rc;
+  CK(cudaMemcpyAsync(host_out, dy, bytes, cudaMemcpyDeviceToHost, ctx->stream), "copy output out");
+  return astro_moe_ctx_synchronize(ctx);
+}
+
+}  // extern "C"

@@ -1,0 +1,106 @@
+// common.cuh -- device numerics and small utilities shared by every kernel of
+// libastro_moe.  The scalar numerics (bf16 rounding, exp, sigmoid, SwiGLU) are
+// evaluated with explicitly rounded intrinsics in the same step order as the
+// CPU restatement, so elementwise results are bit-identical to it.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define ASTRO_DEVINL __device__ __forceinline__
+
+namespace astro {
+
+// dtype codes of the C ABI
+enum DType : int { kBF16 = 1, kF16 = 2, kF32 = 3 };
+
+// Device-side status word bits (written by kernels, read by the host after a
+// synchronising call).  No kernel traps; a failed check records a bit and the
+// kernel skips the offending access.
+enum DeviceStatus : uint32_t {
+  kDevOk = 0,
+  kDevBadExpertId = 1u << 0,
+  kDevWaitTimeout = 1u << 1,
+  kDevBadShape = 1u << 2,
+};
+
+ASTRO_DEVINL float bf16_to_f32(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+ASTRO_DEVINL uint16_t f32_to_bf16(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+ASTRO_DEVINL float round_bf16(float f) { return bf16_to_f32(f32_to_bf16(f)); }
+
+template <typename T> struct Num;
+template <> struct Num<float> {
+  static ASTRO_DEVINL float load(const float* p, int64_t i) { return p[i]; }
+  static ASTRO_DEVINL void store(float* p, int64_t i, float v) { p[i] = v; }
+  static ASTRO_DEVINL float round(float v) { return v; }
+};
+template <> struct Num<__nv_bfloat16> {
+  static ASTRO_DEVINL float load(const __nv_bfloat16* p, int64_t i) {
+    return __bfloat162float(p[i]);
+  }
+  static ASTRO_DEVINL void store(__nv_bfloat16* p, int64_t i, float v) {
+    p[i] = __float2bfloat16_rn(v);
+  }
+  static ASTRO_DEVINL float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+};
+template <> struct Num<__half> {
+  static ASTRO_DEVINL float load(const __half* p, int64_t i) { return __half2float(p[i]); }
+  static ASTRO_DEVINL void store(__half* p, int64_t i, float v) { p[i] = __float2half_rn(v); }
+  static ASTRO_DEVINL float round(float v) { return __half2float(__float2half_rn(v)); }
+};
+
+// e^x: Cody-Waite reduction with a 12-significant-bit head of ln2, degree-7
+// Taylor polynomial by Horner with fused multiply-adds, exact scaling by 2^n.
+// Results below ~1.6e-38 flush to zero.  Same steps as ao_expf in the oracle.
+ASTRO_DEVINL float expf_cw(float x) {
+  if (x != x) return x;
+  if (x > 88.72283172607421875f) return __int_as_float(0x7f800000);
+  if (x < -87.0f) return 0.0f;
+  const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(-n, 0.693115234375f, x);
+  r = __fmaf_rn(-n, __uint_as_float(0x3805fdf4u), r);
+  float p = __uint_as_float(0x39500d01u);
+  p = __fmaf_rn(p, r, __uint_as_float(0x3ab60b61u));
+  p = __fmaf_rn(p, r, __uint_as_float(0x3c088889u));
+  p = __fmaf_rn(p, r, __uint_as_float(0x3d2aaaabu));
+  p = __fmaf_rn(p, r, __uint_as_float(0x3e2aaaabu));
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int ni = (int)n;
+  if (ni > 127) {
+    p = __fmul_rn(p, 2.0f);
+    ni -= 1;
+  }
+  return __fmul_rn(p, __uint_as_float((uint32_t)(ni + 127) << 23));
+}
+
+// MLX sigmoid form: y = 1/(1+e^-|x|); x < 0 gives 1 - y.
+ASTRO_DEVINL float sigmoid_mlx(float x) {
+  const float y = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cw(-fabsf(x))));
+  return (x < 0.0f) ? __fsub_rn(1.0f, y) : y;
+}
+
+// gate * sigmoid(gate) * up with each intermediate rounded to bf16 (inputs are
+// already bf16 values held in fp32).
+ASTRO_DEVINL float swiglu_bf16(float g, float u) {
+  const float s = round_bf16(sigmoid_mlx(g));
+  const float a = round_bf16(__fmul_rn(g, s));
+  return round_bf16(__fmul_rn(a, u));
+}
+
+ASTRO_DEVINL void record_status(uint32_t* status, uint32_t bits) {
+  if (status) atomicOr(status, bits);
+}
+
+ASTRO_DEVINL uint32_t lanemask_lt() {
+  uint32_t m;
+  asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+  return m;
+}
+
+}  // namespace astro

@@ -1,0 +1,82 @@
+// kernels.h -- internal launch interface between the C ABI (api.cu) and the
+// kernels.  Not installed; the public boundary is include/astro_moe.h.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace astro {
+
+cudaError_t launch_route_experts(const void* logits, int dtype, int64_t tokens, int E, int K,
+                                 int normalize, uint32_t* ids, void* scores, const void* x,
+                                 const void* wg, int H, void* gate_logit, cudaStream_t st);
+
+cudaError_t launch_dense_nt_simt(const void* x, const void* w, int64_t rows, int cols, int depth,
+                                 void* out, int ldo, cudaStream_t st);
+
+cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, int E,
+                                    int64_t shared_rows, uint32_t* sorted_order,
+                                    uint32_t* inverse_order, uint32_t* sorted_ids,
+                                    uint32_t* sorted_tokens, uint32_t* offsets, uint32_t* status,
+                                    cudaStream_t st);
+
+cudaError_t launch_take_rows(const void* src, int64_t src_rows, const uint32_t* rows, int64_t n,
+                             int hidden, void* out, uint32_t* status, cudaStream_t st);
+
+cudaError_t launch_block_combine(const void* rows, const uint32_t* inverse, const void* scores,
+                                 const void* gate_logit, int64_t shared_base, int64_t tokens,
+                                 int K, int H, int sorted, void* out, cudaStream_t st);
+
+cudaError_t launch_sorted_weighted_sum(const void* rows, int out_dtype, const uint32_t* inverse,
+                                       const void* scores, int score_dtype, int64_t tokens, int K,
+                                       int64_t dim, void* out, cudaStream_t st);
+
+cudaError_t launch_unsorted_weighted_sum(const void* outputs, int out_dtype, const void* scores,
+                                         int score_dtype, int64_t tokens, int K, int64_t dim,
+                                         void* out, cudaStream_t st);
+
+cudaError_t launch_combine_shared(const void* sparse, const void* shared, const void* gate,
+                                  int dtype, int64_t tokens, int64_t dim, void* out,
+                                  cudaStream_t st);
+
+cudaError_t launch_swiglu(const void* gate, const void* up, int64_t n, void* out, cudaStream_t st);
+
+cudaError_t launch_numerics_probe(const float* x, int64_t n, int which, float* out,
+                                  cudaStream_t st);
+
+// One stacked affine tensor seen as rows: row (e, f) = e * expert_rows + row_offset + f.
+struct AffineRef {
+  const void* q = nullptr;  // uint32 packed
+  const void* s = nullptr;  // bf16 scales
+  const void* b = nullptr;  // bf16 biases
+  int64_t expert_rows = 0;
+  int64_t row_offset = 0;
+};
+
+struct GroupedGemvDesc {
+  const void* x = nullptr;           // bf16 activations
+  const uint32_t* x_rows = nullptr;  // sorted position -> activation row
+  int64_t x_limit = 0;               // activation rows available
+  int in_features = 0;
+  const uint32_t* seg_offsets = nullptr;  // [nseg + 1], device
+  int nseg = 0;
+  int shared_seg = -1;
+  int64_t rows_total = 0;            // upper bound on seg_offsets[nseg]
+  AffineRef wa[2], wb[2];            // [routed, shared]; wb for SwiGLU mode
+  int out_features = 0, group = 64, bits = 4;
+  bool swiglu = false;
+  void* y = nullptr;
+  const uint32_t* y_rows = nullptr;  // sorted position -> output row
+  int64_t y_limit = 0;               // output rows available
+  int64_t ldy = 0;
+  uint32_t* status = nullptr;
+};
+
+cudaError_t launch_grouped_gemv(const GroupedGemvDesc& d, cudaStream_t st);
+
+cudaError_t launch_offsets_from_sorted(const uint32_t* ids, int64_t n, int E, uint32_t* offsets,
+                                       uint32_t* status, cudaStream_t st);
+cudaError_t launch_compose_rows(const uint32_t* lhs, const uint32_t* order, int64_t n,
+                                uint32_t* rows_out, cudaStream_t st);
+
+}  // namespace astro

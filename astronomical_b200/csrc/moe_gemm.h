@@ -1,0 +1,32 @@
+// moe_gemm.h -- interface of the tcgen05 grouped GEMM path (moe_gemm.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/astro_moe.h"
+
+namespace astro {
+
+// Per-layer tensor-core plan: TMA descriptors over the borrowed MLX-layout
+// weights.  `ok` is false when the layer's profile is not handled by the
+// tensor-core kernels (anything but 4-bit, group 64, bf16 scales).
+struct MoeGemmPlan {
+  bool ok = false;
+  void* dev = nullptr;  // device copy of the kernel parameter blocks
+  astro_moe_layer_weights w{};
+};
+
+int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan);
+void moe_gemm_release(MoeGemmPlan& plan);
+bool moe_gemm_enabled(const MoeGemmPlan& plan, int use_tensor_cores_option);
+size_t moe_gemm_scratch_bytes();
+
+cudaError_t moe_gemm_router(const MoeGemmPlan& plan, const void* x, int64_t tokens, void* logits,
+                            void* scratch, cudaStream_t st);
+cudaError_t moe_gemm_gate_up(const MoeGemmPlan& plan, const void* states, int64_t rows,
+                             const uint32_t* offsets, void* act, void* scratch, cudaStream_t st);
+cudaError_t moe_gemm_down(const MoeGemmPlan& plan, const void* act, int64_t rows,
+                          const uint32_t* offsets, void* yrows, void* scratch, cudaStream_t st);
+
+}  // namespace astro

@@ -1,0 +1,253 @@
+// route.cu -- router softmax / top-K / renormalisation, one warp per token.
+//
+// Replaces qwen3_5_moe_route_experts (qwen3_5_moe/model/routing.rs:16-49):
+// softmax(precise) over E in fp32 with probabilities rounded to the logits
+// dtype, argpartition + take_along_axis for the K largest, and (norm_topk_prob)
+// sum/divide.  The K winners are ordered by (probability desc, expert id asc).
+//
+// Reduction order (shared with the CPU restatement): lane l owns experts
+// [l*C, min(E,(l+1)*C)), C = ceil(E/32), sums its exp values in index order;
+// the 32 partial sums meet in a butterfly over xor distances 16..1.  The exp is
+// expf_cw (common.cuh), so bf16 probabilities -- and therefore the selected ids --
+// are bit-identical to the oracle given the same logits.
+//
+// Optionally the same warp computes the shared-expert gate logit
+// bf16(x[t] . wg) (resident_execution.rs:384-388) so the block needs no extra
+// pass over the hidden states for it.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace astro {
+
+template <typename T> struct RouteKey;
+// 16-bit types: probabilities are >= 0, so their bit patterns order like the
+// values; key = (bits << 16) | (0xffff - id) and max gives (value desc, id asc).
+template <> struct RouteKey<__nv_bfloat16> {
+  static ASTRO_DEVINL uint32_t bits(float p) { return f32_to_bf16(p); }
+  static ASTRO_DEVINL float value(uint32_t b) { return bf16_to_f32((uint16_t)b); }
+};
+template <> struct RouteKey<__half> {
+  static ASTRO_DEVINL uint32_t bits(float p) { return __half_as_ushort(__float2half_rn(p)); }
+  static ASTRO_DEVINL float value(uint32_t b) { return __half2float(__ushort_as_half((uint16_t)b)); }
+};
+
+template <typename T, int CMAX>
+__global__ void __launch_bounds__(256) route_experts_kernel(
+    const T* __restrict__ logits, int64_t tokens, int E, int K, int normalize,
+    uint32_t* __restrict__ out_ids, T* __restrict__ out_scores,
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wg, int H,
+    __nv_bfloat16* __restrict__ gate_logit) {
+  const int lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  const int C = (E + 31) >> 5;
+  const int i0 = lane * C;
+  const T* row = logits + t * E;
+
+  float v[CMAX];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < CMAX; ++c) {
+    const int i = i0 + c;
+    v[c] = (c < C && i < E) ? Num<T>::load(row, i) : -INFINITY;
+    mx = (v[c] > mx) ? v[c] : mx;
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, mx, m);
+    mx = (o > mx) ? o : mx;
+  }
+  float part = 0.0f;
+#pragma unroll
+  for (int c = 0; c < CMAX; ++c) {
+    const int i = i0 + c;
+    if (c < C && i < E) {
+      v[c] = expf_cw(__fsub_rn(v[c], mx));
+      part = __fadd_rn(part, v[c]);
+    }
+  }
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, m));
+  const float inv = __fdiv_rn(1.0f, part);
+
+  // probabilities rounded to the logits dtype; top-K selection
+  uint32_t key[CMAX];
+#pragma unroll
+  for (int c = 0; c < CMAX; ++c) {
+    const int i = i0 + c;
+    const bool valid = (c < C && i < E);
+    const float p = Num<T>::round(__fmul_rn(v[c], inv));
+    if constexpr (sizeof(T) == 2) {
+      key[c] = valid ? ((RouteKey<T>::bits(p) << 16) | (0xffffu - (uint32_t)i)) : 0u;
+    } else {
+      v[c] = valid ? p : -1.0f;
+      key[c] = valid ? 1u : 0u;  // liveness only
+    }
+  }
+
+  float sel_val = 0.0f;  // lane k keeps winner k
+  uint32_t sel_id = 0;
+  float sum_sel = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    uint32_t wid;
+    float wval;
+    if constexpr (sizeof(T) == 2) {
+      uint32_t best = 0;
+#pragma unroll
+      for (int c = 0; c < CMAX; ++c) best = (key[c] > best) ? key[c] : best;
+      best = __reduce_max_sync(0xffffffffu, best);
+      wid = 0xffffu - (best & 0xffffu);
+      wval = RouteKey<T>::value(best >> 16);
+#pragma unroll
+      for (int c = 0; c < CMAX; ++c)
+        if (key[c] == best) key[c] = 0u;
+    } else {
+      // fp32 probabilities: (value desc, id asc) with a 64-bit key
+      uint64_t best = 0;
+#pragma unroll
+      for (int c = 0; c < CMAX; ++c) {
+        if (key[c]) {
+          const uint64_t kk = ((uint64_t)__float_as_uint(v[c]) << 32) |
+                              (uint64_t)(0xffffffffu - (uint32_t)(i0 + c));
+          best = (kk > best) ? kk : best;
+        }
+      }
+#pragma unroll
+      for (int m = 16; m >= 1; m >>= 1) {
+        const uint64_t o = __shfl_xor_sync(0xffffffffu, best, m);
+        best = (o > best) ? o : best;
+      }
+      wid = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+      wval = __uint_as_float((uint32_t)(best >> 32));
+#pragma unroll
+      for (int c = 0; c < CMAX; ++c)
+        if (key[c] && (uint32_t)(i0 + c) == wid) key[c] = 0u;
+    }
+    if (lane == k) {
+      sel_val = wval;
+      sel_id = wid;
+    }
+    sum_sel = __fadd_rn(sum_sel, wval);
+  }
+  if (lane < K) {
+    float s = sel_val;
+    if (normalize) s = Num<T>::round(__fdiv_rn(sel_val, Num<T>::round(sum_sel)));
+    out_ids[t * K + lane] = sel_id;
+    Num<T>::store(out_scores, t * K + lane, s);
+  }
+
+  if (gate_logit != nullptr) {
+    // bf16(x[t] . wg): 16-byte chunks strided over the warp, fp32 fma, butterfly.
+    const uint4* xr = reinterpret_cast<const uint4*>(x + t * (int64_t)H);
+    const uint4* wr = reinterpret_cast<const uint4*>(wg);
+    float acc = 0.0f;
+    for (int c = lane; c < H / 8; c += 32) {
+      const uint4 a = xr[c], b = __ldg(wr + c);
+      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc = __fmaf_rn(__uint_as_float(av[j] << 16), __uint_as_float(bv[j] << 16), acc);
+        acc = __fmaf_rn(__uint_as_float(av[j] & 0xffff0000u), __uint_as_float(bv[j] & 0xffff0000u),
+                        acc);
+      }
+    }
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, m));
+    if (lane == 0) gate_logit[t] = __float2bfloat16_rn(acc);
+  }
+}
+
+template <typename T>
+static cudaError_t launch_route_t(const void* logits, int64_t tokens, int E, int K, int normalize,
+                                  uint32_t* ids, void* scores, const void* x, const void* wg,
+                                  int H, void* gate_logit, cudaStream_t st) {
+  if (tokens == 0) return cudaSuccess;
+  const int warps = 8;
+  const dim3 grid((unsigned)((tokens + warps - 1) / warps)), block(warps * 32);
+  const int C = (E + 31) / 32;
+  auto args = [&](auto kern) {
+    kern<<<grid, block, 0, st>>>((const T*)logits, tokens, E, K, normalize, ids, (T*)scores,
+                                 (const __nv_bfloat16*)x, (const __nv_bfloat16*)wg, H,
+                                 (__nv_bfloat16*)gate_logit);
+  };
+  if (C <= 4) args(route_experts_kernel<T, 4>);
+  else if (C <= 8) args(route_experts_kernel<T, 8>);
+  else if (C <= 16) args(route_experts_kernel<T, 16>);
+  else args(route_experts_kernel<T, 32>);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_experts(const void* logits, int dtype, int64_t tokens, int E, int K,
+                                 int normalize, uint32_t* ids, void* scores, const void* x,
+                                 const void* wg, int H, void* gate_logit, cudaStream_t st) {
+  switch (dtype) {
+    case kBF16:
+      return launch_route_t<__nv_bfloat16>(logits, tokens, E, K, normalize, ids, scores, x, wg, H,
+                                           gate_logit, st);
+    case kF16:
+      return launch_route_t<__half>(logits, tokens, E, K, normalize, ids, scores, x, wg, H,
+                                    gate_logit, st);
+    default:
+      return launch_route_t<float>(logits, tokens, E, K, normalize, ids, scores, x, wg, H,
+                                   gate_logit, st);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Dense bf16 projection out[r, c] = bf16(sum_k x[r,k] w[c,k]) for the router
+// when the tensor-core path is not used (portable SIMT tile kernel: 64x64
+// output tile, K step 32, fp32 accumulation).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) dense_nt_simt_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w, int64_t rows,
+    int cols, int depth, __nv_bfloat16* __restrict__ out, int ldo) {
+  __shared__ float xs[32][65];
+  __shared__ float ws[32][65];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t r0 = (int64_t)blockIdx.y * 64;
+  const int c0 = blockIdx.x * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < depth; k0 += 32) {
+    for (int i = threadIdx.x; i < 64 * 32; i += 256) {
+      const int rr = i / 32, kk = i % 32;
+      const int64_t gr = r0 + rr;
+      const int gc = c0 + rr;
+      xs[kk][rr] = (gr < rows && k0 + kk < depth) ? __bfloat162float(x[gr * depth + k0 + kk]) : 0.f;
+      ws[kk][rr] = (gc < cols && k0 + kk < depth) ? __bfloat162float(w[(int64_t)gc * depth + k0 + kk])
+                                                  : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < 32; ++kk) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = xs[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = ws[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t gr = r0 + ty * 4 + i;
+      const int gc = c0 + tx * 4 + j;
+      if (gr < rows && gc < cols) out[gr * ldo + gc] = __float2bfloat16_rn(acc[i][j]);
+    }
+}
+
+cudaError_t launch_dense_nt_simt(const void* x, const void* w, int64_t rows, int cols, int depth,
+                                 void* out, int ldo, cudaStream_t st) {
+  if (rows == 0 || cols == 0) return cudaSuccess;
+  const dim3 grid((cols + 63) / 64, (unsigned)((rows + 63) / 64));
+  dense_nt_simt_kernel<<<grid, 256, 0, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w,
+                                             rows, cols, depth, (__nv_bfloat16*)out, ldo);
+  return cudaGetLastError();
+}
+
+}  // namespace astro

@@ -1,0 +1,238 @@
+/*
+ * astro_moe.h -- C ABI of libastro_moe, the B200 (sm_100a) implementation of
+ * Astronomical's sorted mixture-of-experts block.
+ *
+ * Conventions (mirroring the MLX-C convention the reference binds through
+ * crates/runtime-integration/src/mlx_runtime/error_handling.rs:19-60):
+ *   - every entry point returns an int status (ASTRO_MOE_OK == 0); the message
+ *     of the last failure on the calling thread is astro_moe_last_error();
+ *   - array arguments are caller-owned DEVICE pointers unless the name says
+ *     host; calls are stream-ordered and asynchronous on the given cudaStream_t
+ *     (passed as void*, NULL = the legacy default stream);
+ *   - geometry is validated on the host before any kernel runs (as
+ *     sparse_experts/error.rs:1-22 does); index errors found on the device
+ *     (expert id >= E, bad row) are recorded in a per-device status word, read
+ *     with astro_moe_device_status(), and the offending access is skipped;
+ *   - weights are borrowed, never copied (StackedExpertProjection<'a>,
+ *     sparse_experts/gathered_projection.rs:45-71): the caller keeps them alive.
+ *
+ * Weight layout is MLX's affine layout, unchanged, so checkpoints drop in:
+ * packed uint32 [E, out, in*bits/32] with element j of a row at bit j*bits of
+ * the row's little-endian bit stream, scales/biases bf16 [E, out, in/group],
+ * w = scale * q + bias.  Paths below are relative to the reference project root.
+ */
+#ifndef ASTRO_MOE_H
+#define ASTRO_MOE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ASTRO_MOE_ABI_VERSION 1
+
+enum {
+  ASTRO_MOE_OK = 0,
+  ASTRO_MOE_ERR_INVALID_ARGUMENT = 1, /* MlxRuntimeError::RuntimeOperation, geometry */
+  ASTRO_MOE_ERR_CUDA = 2,
+  ASTRO_MOE_ERR_OUT_OF_MEMORY = 3,
+  ASTRO_MOE_ERR_UNSUPPORTED = 4,
+  ASTRO_MOE_ERR_DEVICE_STATUS = 5,    /* a kernel recorded a bad index or a wait timeout */
+  ASTRO_MOE_ERR_NOT_REGISTERED = 6,
+  ASTRO_MOE_ERR_NCCL = 7,
+  ASTRO_MOE_ERR_DUPLICATE_SLOT = 8,   /* assignment_permutation.rs:26-31 */
+  ASTRO_MOE_ERR_OUT_OF_RANGE_SLOT = 9,/* assignment_permutation.rs:20-25 */
+  ASTRO_MOE_ERR_MEMORY_LIMIT = 10     /* MlxRuntimeError::ActiveMemoryLimitExceeded, mlx_runtime_types.rs:129-133 */
+};
+
+enum { ASTRO_MOE_DTYPE_BF16 = 1, ASTRO_MOE_DTYPE_F16 = 2, ASTRO_MOE_DTYPE_F32 = 3 };
+
+/* device status bits (astro_moe_device_status) */
+enum {
+  ASTRO_MOE_DEVICE_BAD_EXPERT_ID = 1,
+  ASTRO_MOE_DEVICE_WAIT_TIMEOUT = 2,
+  ASTRO_MOE_DEVICE_BAD_SHAPE = 4
+};
+
+/* Thread-local message of the last failed call; replaces the handler installed
+ * by crates/runtime-integration/src/mlx_runtime/error_handling.rs:10-44. */
+const char* astro_moe_last_error(void);
+int astro_moe_abi_version(void);
+
+/* Reads (and with reset != 0 clears) the device status word of `device`;
+ * synchronises that device first. */
+int astro_moe_device_status(int32_t device, uint32_t* status, int32_t reset);
+
+/* ------------------------------------------------------------------------ */
+/* Stage entry points: one per MlxRuntime call the reference's MoE path makes */
+/* ------------------------------------------------------------------------ */
+
+/* qwen3_5_moe_route_experts, crates/model-serving/src/qwen3_5_moe/model/routing.rs:16-49
+ * (softmax_axis mlx_operations.rs:314, argpartition_axis :364, take_along_axis,
+ * sum/divide).  router_logits [tokens, experts] of `dtype`; selected_indices
+ * uint32 [tokens, top_k]; selected_scores [tokens, top_k] of `dtype`.  The K
+ * winners are ordered by (probability desc, expert id asc).  top_k <= 32,
+ * experts <= 1024. */
+int astro_moe_route_experts(const void* router_logits, int32_t dtype, int64_t tokens,
+                            int32_t experts, int32_t top_k, int32_t normalize,
+                            uint32_t* selected_indices, void* selected_scores, void* stream);
+
+/* sort_expert_assignments, crates/model-serving/src/sparse_experts/assignment_sort.rs:36-97
+ * (argsort_axis mlx_operations.rs:377 twice, floor_divide :178).  Stable.  Any
+ * output pointer may be NULL.  expert_offsets has experts+1 entries (the
+ * per-expert row ranges gather_qmm derives internally).  experts <= 1024. */
+int astro_moe_sort_expert_assignments(const uint32_t* selected_indices, int64_t tokens,
+                                      int32_t top_k, int32_t experts, uint32_t* sorted_order,
+                                      uint32_t* inverse_order, uint32_t* sorted_indices,
+                                      uint32_t* sorted_tokens, uint32_t* expert_offsets,
+                                      void* stream);
+
+/* take_axis(states, rows, 0), crates/runtime-integration/src/mlx_shape_operations.rs:34
+ * as used at assignment_sort.rs:88: out[p] = states[rows[p]] (bf16 rows of
+ * `hidden` elements, hidden % 8 == 0). */
+int astro_moe_take_rows(const void* states, int64_t state_rows, int32_t hidden,
+                        const uint32_t* rows, int64_t n, void* out, void* stream);
+
+/* MlxRuntime::gather_quantized_matmul_affine,
+ * crates/runtime-integration/src/mlx_quantized_operations.rs:100-157 (transpose=true,
+ * validation :226-330).  out[n] = activations[lhs_indices[n]] .
+ * dequant(W[rhs_indices[n]])^T; lhs_indices NULL = identity, rhs_indices NULL
+ * = expert 0.  activations bf16 [activation_rows, in_features]; out bf16
+ * [n_rows, out_features].  sorted_indices != 0 promises ascending rhs indices
+ * (gathered_projection.rs:24-38); otherwise rows are grouped internally.
+ * group_size in {32,64,128}, bits in {2,3,4,5,6,8}. */
+int astro_moe_gather_qmm(const void* activations, int64_t activation_rows, int32_t in_features,
+                         const uint32_t* lhs_indices, const uint32_t* rhs_indices, int64_t n_rows,
+                         const uint32_t* packed, const void* scales, const void* biases,
+                         int32_t experts, int32_t out_features, int32_t group_size, int32_t bits,
+                         int32_t sorted_indices, void* out, void* stream);
+
+/* MlxRuntime::quantized_matmul_affine, mlx_quantized_operations.rs:49-98
+ * (transpose=true): out = activations . dequant(W)^T. */
+int astro_moe_quantized_matmul(const void* activations, int64_t rows, int32_t in_features,
+                               const uint32_t* packed, const void* scales, const void* biases,
+                               int32_t out_features, int32_t group_size, int32_t bits, void* out,
+                               void* stream);
+
+/* MlxRuntime::apply_compiled_swiglu, crates/runtime-integration/src/mlx_compiled_swiglu.rs:32-89:
+ * out = gate * sigmoid(gate) * up, bf16, n elements. */
+int astro_moe_swiglu(const void* gate, const void* up, int64_t n, void* out, void* stream);
+
+/* sorted_expert_weighted_sum, crates/model-serving/src/sparse_experts/weighted_sum.rs:75-190
+ * (kernel source :16-33).  sorted_outputs [tokens*top_k, dim] and out
+ * [tokens, dim] of output_dtype; scores [tokens, top_k] of score_dtype. */
+int astro_moe_sorted_expert_weighted_sum(const void* sorted_outputs, int32_t output_dtype,
+                                         const uint32_t* inverse_order, const void* scores,
+                                         int32_t score_dtype, int64_t tokens, int32_t top_k,
+                                         int64_t dim, void* out, void* stream);
+
+/* unsorted_expert_weighted_sum, weighted_sum.rs:46-60 and :94-120.
+ * outputs [tokens, top_k, dim]. */
+int astro_moe_unsorted_expert_weighted_sum(const void* outputs, int32_t output_dtype,
+                                           const void* scores, int32_t score_dtype,
+                                           int64_t tokens, int32_t top_k, int64_t dim, void* out,
+                                           void* stream);
+
+/* combine_sparse_and_shared_experts, crates/model-serving/src/qwen3_5_moe/model/output_combination.rs:34-43,
+ * and the compiled graph runtime-integration/src/mlx_compiled_sparse_shared_expert_combination.rs:9-75:
+ * out = sparse + sigmoid(gate_logits) * shared; gate_logits [tokens, 1]. */
+int astro_moe_combine_sparse_and_shared(const void* sparse, const void* shared,
+                                        const void* gate_logits, int32_t dtype, int64_t tokens,
+                                        int64_t dim, void* out, void* stream);
+
+/* invert_assignment_order, crates/model-serving/src/sparse_experts/assignment_permutation.rs:10-41.
+ * HOST arrays; returns ASTRO_MOE_ERR_DUPLICATE_SLOT / _OUT_OF_RANGE_SLOT. */
+int astro_moe_invert_assignment_order(const uint32_t* host_sorted_order, int64_t n,
+                                      uint32_t* host_inverse_order);
+
+/* ------------------------------------------------------------------------ */
+/* Block level: Qwen3_5Model::forward_qwen3_5_moe, resident branch            */
+/* (crates/model-serving/src/qwen3_5_moe/model/forward.rs:19-28, :111-127;    */
+/*  resident_execution.rs:70-143, :352-400)                                  */
+/* ------------------------------------------------------------------------ */
+
+typedef struct astro_moe_ctx astro_moe_ctx;
+
+typedef struct {
+  int64_t max_tokens;        /* workspace is sized for this many tokens per call */
+  int32_t sorted_threshold;  /* 0 = 64, MINIMUM_SORTED_EXPERT_ASSIGNMENTS (routing.rs:13) */
+  int32_t use_tensor_cores;  /* 0 = auto (tcgen05 path for 4-bit g64), -1 = never */
+  int64_t reserved[6];
+} astro_moe_options;
+
+/* One stacked affine projection in MLX layout (Qwen3_5AffineWeights::Quantized,
+ * qwen3_5/model/decoder_layer_weights.rs:15-26). */
+typedef struct {
+  const uint32_t* packed;
+  const void* scales;  /* bf16 */
+  const void* biases;  /* bf16 */
+} astro_moe_affine;
+
+/* Qwen3_5MoEFeedForwardWeights (qwen3_5_moe/model/feed_forward_weights.rs:16-24)
+ * plus the resident expert stacks (expert_residency).  With gate_up_fused the
+ * `gate` tensor is the [E, 2I, .] concatenation of resident_gate_up_fusion.rs:221-260
+ * (gate rows first) and `up` is ignored.  shared_intermediate == 0: no shared expert. */
+typedef struct {
+  int32_t hidden, experts, top_k, intermediate, shared_intermediate;
+  int32_t group_size, bits, normalize_top_k, gate_up_fused;
+  const void* router_weight;       /* bf16 [E, H] (Qwen3_5MoERouterGateWeights::Unquantized) */
+  astro_moe_affine gate, up;       /* [E, I, H*bits/32] */
+  astro_moe_affine down;           /* [E, H, I*bits/32] */
+  astro_moe_affine shared_gate, shared_up; /* [Is, H*bits/32] */
+  astro_moe_affine shared_down;    /* [H, Is*bits/32] */
+  const void* shared_expert_gate;  /* bf16 [1, H] */
+} astro_moe_layer_weights;
+
+/* Optional device outputs of one block call, for parity checks. */
+typedef struct {
+  void* router_logits;        /* bf16 [tokens, E] */
+  uint32_t* selected_indices; /* [tokens, K] */
+  void* selected_scores;      /* bf16 [tokens, K] */
+  uint32_t* expert_offsets;   /* [E + 2] (segment E = shared expert rows) */
+} astro_moe_block_taps;
+
+int astro_moe_ctx_create(int32_t device, void* stream, const astro_moe_options* options,
+                         astro_moe_ctx** out_ctx);
+int astro_moe_ctx_destroy(astro_moe_ctx* ctx);
+int astro_moe_ctx_set_stream(astro_moe_ctx* ctx, void* stream);
+/* synchronises the context stream and turns a non-zero device status into
+ * ASTRO_MOE_ERR_DEVICE_STATUS */
+int astro_moe_ctx_synchronize(astro_moe_ctx* ctx);
+
+/* Borrows the weights of one decoder layer (bind_qwen3_5_moe_feed_forward_weights,
+ * feed_forward_weights.rs:50-84); validates every shape. */
+int astro_moe_register_layer(astro_moe_ctx* ctx, int32_t layer,
+                             const astro_moe_layer_weights* weights);
+
+/* forward_qwen3_5_moe: hidden_states bf16 [tokens, H] -> out bf16 [tokens, H]. */
+int astro_moe_block_forward(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                            int64_t tokens, void* out);
+int astro_moe_block_forward_taps(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                                 int64_t tokens, void* out, const astro_moe_block_taps* taps);
+/* Per-stage device time of block calls, measured with CUDA events on the context
+ * stream; the stage names follow PerformanceOperation
+ * (crates/model-serving/src/performance_attribution/catalog.rs:89-92), which in
+ * the reference times only host graph construction. */
+typedef struct {
+  int64_t calls;                     /* block calls measured */
+  int64_t kernel_launches;           /* kernels those calls launched */
+  double router_projection_ms;
+  double assignment_preparation_ms;  /* ExpertAssignmentPreparation: route, sort, row gather */
+  double gate_up_ms;                 /* GatheredExpertExecution: gate/up projection + SwiGLU */
+  double down_ms;                    /* GatheredExpertExecution: down projection */
+  double weighted_reduction_ms;      /* ExpertWeightedReduction, fused with the shared expert */
+} astro_moe_attribution;
+
+int astro_moe_ctx_set_attribution(astro_moe_ctx* ctx, int32_t enabled);
+/* Synchronises, adds up the pending measurements and optionally resets them. */
+int astro_moe_ctx_read_attribution(astro_moe_ctx* ctx, astro_moe_attribution* out, int32_t reset);
+
+/* Same with HOST buffers: copies in, runs, copies out, synchronises. */
+int astro_moe_block_forward_host(astro_moe_ctx* ctx, int32_t layer, const void* host_hidden,
+                                 int64_t tokens, void* host_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

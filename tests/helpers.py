@@ -1,0 +1,75 @@
+"""Shared helpers for the parity tests (comparison metrics and array plumbing)."""
+from __future__ import annotations
+
+import numpy as np
+
+from astronomical_b200.synthetic import bf16_to_f32, f32_to_bf16
+
+# north-star tolerances for block outputs in bf16
+MAX_ABS = 2e-2
+REL_L2 = 1e-3
+
+
+def to_np_bf16(t) -> np.ndarray:
+    """torch bf16 tensor -> uint16 bit patterns."""
+    import torch
+
+    return t.detach().contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+
+
+def to_np_u32(t) -> np.ndarray:
+    import torch
+
+    return t.detach().contiguous().view(torch.int32).cpu().numpy().view(np.uint32)
+
+
+def bf16_tensor(a, device="cuda"):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint16).view(np.int16)).view(
+        torch.bfloat16).to(device)
+
+
+def u32_tensor(a, device="cuda"):
+    import torch
+
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.uint32).view(np.int32)).to(device)
+
+
+def bf16_ulp(x: np.ndarray) -> np.ndarray:
+    """Spacing of bf16 numbers at |x| (8 significant bits)."""
+    ax = np.abs(x.astype(np.float64))
+    ax = np.maximum(ax, np.float64(np.finfo(np.float32).tiny))
+    return np.exp2(np.floor(np.log2(ax)) - 7)
+
+
+def assert_bf16_ulps(a_bits, b_bits, ulps: float = 1.0, max_frac: float = 0.02):
+    """Every element within `ulps` bf16 ulps, and at most `max_frac` differing."""
+    a = bf16_to_f32(a_bits).astype(np.float64)
+    b = bf16_to_f32(b_bits).astype(np.float64)
+    assert a.shape == b.shape
+    diff = np.abs(a - b)
+    tol = ulps * bf16_ulp(np.maximum(np.abs(a), np.abs(b)))
+    bad = diff > tol
+    assert not bad.any(), f"{bad.sum()} elements beyond {ulps} ulp; worst {diff.max()}"
+    frac = float((diff > 0).mean()) if diff.size else 0.0
+    assert frac <= max_frac, f"{frac:.4f} of elements differ"
+
+
+def block_metrics(got_bits, ref_bits):
+    g = bf16_to_f32(got_bits).astype(np.float64)
+    r = bf16_to_f32(ref_bits).astype(np.float64)
+    max_abs = float(np.max(np.abs(g - r))) if g.size else 0.0
+    rel_l2 = float(np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)) if g.size else 0.0
+    return max_abs, rel_l2
+
+
+def assert_block_close(got_bits, ref_bits):
+    max_abs, rel_l2 = block_metrics(got_bits, ref_bits)
+    assert max_abs <= MAX_ABS and rel_l2 <= REL_L2, (max_abs, rel_l2)
+    return max_abs, rel_l2
+
+
+__all__ = ["to_np_bf16", "to_np_u32", "bf16_tensor", "u32_tensor", "assert_bf16_ulps",
+           "block_metrics", "assert_block_close", "bf16_to_f32", "f32_to_bf16", "MAX_ABS",
+           "REL_L2"]
