@@ -251,10 +251,12 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   StageMarks marks(ctx);
   marks.mark();
   // a1: router projection
-  const bool use_tc = astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores);
+  const bool use_tc = astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores) &&
+                      (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
   ctx->launches += use_tc ? 7 : 6;
   if (use_tc) {
-    CK(astro::moe_gemm_router(L.gemm, x, T, b.logits, b.gemm_scratch, st), "router projection");
+    CK(astro::moe_gemm_router(L.gemm, x, T, b.logits, b.gemm_scratch, ctx->status, st),
+       "router projection");
   } else {
     CK(astro::launch_dense_nt_simt(x, w.router_weight, T, E, H, b.logits, E, st), "router projection");
   }
@@ -273,10 +275,12 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     // a4-a6 on tcgen05: gather rows, gate/up + SwiGLU, down
     CK(astro::launch_take_rows(x, T, b.stok, rows, H, b.states, ctx->status, st), "take rows");
     marks.mark();
-    CK(astro::moe_gemm_gate_up(L.gemm, b.states, rows, b.offsets, b.act, b.gemm_scratch, st),
+    CK(astro::moe_gemm_gate_up(L.gemm, b.states, rows, b.offsets, b.act, b.gemm_scratch,
+                               ctx->status, st),
        "gate/up projection");
     marks.mark();
-    CK(astro::moe_gemm_down(L.gemm, b.act, rows, b.offsets, b.yrows, b.gemm_scratch, st),
+    CK(astro::moe_gemm_down(L.gemm, b.act, rows, b.offsets, b.yrows, b.gemm_scratch,
+                            ctx->status, st),
        "down projection");
   } else {
     marks.mark();

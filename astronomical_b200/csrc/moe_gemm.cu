@@ -1,27 +1,645 @@
-// moe_gemm.cu -- tcgen05 grouped GEMM (placeholder until the tensor-core
-// kernels land: every layer takes the CUDA-core path).
+// moe_gemm.cu -- grouped expert GEMM on the 5th-generation tensor cores (sm_100a).
+//
+// Computes the gathered projections of the sorted MoE block
+// (runtime-integration/src/mlx_quantized_operations.rs:100-157, gather_qmm with
+// transpose=true and sorted indices) for MLX affine 4-bit, group-64 weights:
+//
+//   gate/up : act[row, f] = swiglu(bf16(x_row . Wg[e,f]), bf16(x_row . Wu[e,f]))
+//             (qwen3_5_moe/model/resident_execution.rs:210-258 + mlx_compiled_swiglu.rs)
+//   down    : y[row, f]   = bf16(act_row . Wd[e,f])
+//   router  : logits[t,e] = bf16(x_t . Wr[e])        (forward.rs:52-93, dense bf16)
+//
+// Layout of the problem: rows of one expert are contiguous after the sort, so a
+// work unit is (expert segment, tile of <= 256 rows, block of weight rows).  The
+// GEMM is "swap-AB": the weight tile is the MMA's A operand (M = 128 weight rows)
+// and the token rows are B (N = the tile's row count rounded up to 16, 16..256),
+// so an expert with 130 rows costs N = 144, not two 128-row tiles, and every
+// weight tile is dequantised exactly once per unit.
+//
+// Per CTA (persistent, one per SM, units assigned round robin):
+//   warp 0      TMA producer: raw int4 weight rows (32 B per row per K block,
+//               MLX layout, no repacking) and the token rows (bf16, 128-byte
+//               swizzle) into a 4-stage ring.
+//   warps 6-13  dequantisers: nibbles -> bf16 with bf16x2 FMAs (w = s*q + b),
+//               written in the canonical SW128 K-major layout the MMA reads.
+//   warp 1      one thread issues tcgen05.mma (M=128, N<=256, K=16) into one of
+//               two TMEM accumulators (2 x 256 fp32 columns) and commits.
+//   warps 2-5   epilogue: tcgen05.ld -> SwiGLU / bf16 -> global, while the MMA
+//               fills the other accumulator.
+// For gate/up the 128 A rows hold 64 gate and 64 up rows, interleaved in 16-row
+// groups so that each gate row and its up row land in lanes l and l+16 of the
+// same epilogue warp (one shuffle pairs them).
+//
+// Every mbarrier wait is bounded (2 s); on timeout the kernel records
+// kDevWaitTimeout, waits (bounded) for its own copies and MMAs, frees TMEM and
+// returns.  No cluster multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstring>
+
 #include "moe_gemm.h"
+#include "tc_ptx.cuh"
 
 namespace astro {
+
+enum GemmMode : int { kGateUp = 0, kDown = 1, kRouter = 2 };
+
+constexpr int kStages = 4;
+constexpr int kBM = 128;                  // weight rows per tile (MMA M)
+constexpr int kBK = 64;                   // K per stage = one quantisation group
+constexpr int kMaxN = 256;                // token rows per tile (MMA N)
+constexpr int kABytes = kBM * kBK * 2;    // 16 KB bf16 A tile
+constexpr int kBBytes = kMaxN * kBK * 2;  // 32 KB bf16 B tile
+constexpr int kRawBytes = kBM * 32;       // 4 KB int4 A tile
+constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;  // 52 KB, multiple of 1024
+constexpr int kSmemBytes = kStages * kStageBytes + 1024;    // + alignment slack
+constexpr int kMaxSeg = 1025;
+constexpr int kDequantWarps = 8;
+constexpr int kThreadsQ = (6 + kDequantWarps) * 32;  // gate/up, down
+constexpr int kThreadsR = 6 * 32;                    // router (A comes by TMA)
+constexpr uint32_t kTmemCols = 512;                  // 2 accumulators x 256 columns
+
+struct GemmParams {
+  CUtensorMap tm_a[2][2];  // [routed, shared][gate|down, up] raw int4 maps; router: bf16 map
+  CUtensorMap tm_b;        // token rows, bf16, box {64, 64}, 128-byte swizzle
+  const uint16_t* scales[2][2];
+  const uint16_t* biases[2][2];
+  int64_t a_row_base[2][2];   // first tensor row of expert 0 (the up half of a fused tensor: I)
+  int64_t a_expert_rows[2];   // tensor rows per expert (I, 2I when fused, H for down)
+  int groups_per_row;         // scales per weight row = K / 64
+  const uint32_t* seg_offsets;  // [nseg + 1]; nullptr: one segment [0, total_rows)
+  int nseg;
+  int shared_seg;
+  int total_rows;
+  int kblocks;     // K / 64
+  int fb_count;    // weight-row blocks per segment
+  int tile_rows;   // token rows per tile (<= 256, multiple of 64)
+  uint16_t* out;   // bf16 output matrix
+  int64_t ldo;
+  int out_cols;    // valid output columns (router: E)
+  int out_rows;    // rows available in `out`
+  uint32_t* status;
+};
+
+struct Unit {
+  int seg, row0, nrows, fb;
+};
+
+struct SmemCtl {
+  uint64_t full[kStages];
+  uint64_t dq[kStages];
+  uint64_t empty[kStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+  int total_units;
+  int prefix[kMaxSeg + 1];
+  int offs[kMaxSeg + 1];
+};
+
+ASTRO_DEVINL bool decode_unit(const SmemCtl& c, const GemmParams& p, int u, Unit& out) {
+  const int tile = u / p.fb_count;
+  out.fb = u - tile * p.fb_count;
+  int lo = 0, hi = p.nseg - 1;
+  while (lo < hi) {  // last segment whose first tile <= tile
+    const int mid = (lo + hi + 1) >> 1;
+    if (c.prefix[mid] <= tile) lo = mid; else hi = mid - 1;
+  }
+  out.seg = lo;
+  out.row0 = c.offs[lo] + (tile - c.prefix[lo]) * p.tile_rows;
+  const int end = c.offs[lo + 1];
+  out.nrows = min(p.tile_rows, end - out.row0);
+  return out.nrows > 0;
+}
+
+// 8 int4 codes (MLX order: code j at bits 4j) -> 8 bf16 = scale*q + bias, as
+// four 32-bit words in K order.  128+q is formed exactly by OR-ing the code into
+// the mantissa of bf16 128.0; subtracting 128 is exact; one bf16x2 FMA per pair.
+ASTRO_DEVINL uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
+  uint32_t t[4];
+  t[0] = (w & 0x000f000fu) | 0x43004300u;          // (q0, q4)
+  t[1] = ((w >> 4) & 0x000f000fu) | 0x43004300u;   // (q1, q5)
+  t[2] = ((w >> 8) & 0x000f000fu) | 0x43004300u;   // (q2, q6)
+  t[3] = ((w >> 12) & 0x000f000fu) | 0x43004300u;  // (q3, q7)
+  uint32_t v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 q = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&t[i]), k128);
+    __nv_bfloat162 r = __hfma2(q, s2, b2);
+    v[i] = *reinterpret_cast<uint32_t*>(&r);
+  }
+  uint4 o;
+  o.x = __byte_perm(v[0], v[1], 0x5410);  // (d0, d1)
+  o.y = __byte_perm(v[2], v[3], 0x5410);  // (d2, d3)
+  o.z = __byte_perm(v[0], v[1], 0x7632);  // (d4, d5)
+  o.w = __byte_perm(v[2], v[3], 0x7632);  // (d6, d7)
+  return o;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
+    moe_gemm_kernel(const __grid_constant__ GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ SmemCtl ctl;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  auto stage_a = [&](int s) { return smem + s * kStageBytes; };
+  auto stage_b = [&](int s) { return smem + s * kStageBytes + kABytes; };
+  auto stage_raw = [&](int s) { return smem + s * kStageBytes + kABytes + kBBytes; };
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  volatile int* abort = &ctl.abort;
+
+  // ---- setup: segment table, barriers, TMEM ----
+  if (warp == 0) {
+    // tile prefix over segments
+    int carry = 0;
+    for (int base = 0; base < p.nseg; base += 32) {
+      const int s = base + lane;
+      int c = 0, o0 = 0, o1 = 0;
+      if (s < p.nseg) {
+        o0 = p.seg_offsets ? (int)p.seg_offsets[s] : 0;
+        o1 = p.seg_offsets ? (int)p.seg_offsets[s + 1] : p.total_rows;
+        c = (o1 - o0 + p.tile_rows - 1) / p.tile_rows;
+        ctl.offs[s] = o0;
+        if (s == p.nseg - 1) ctl.offs[s + 1] = o1;
+      }
+      int incl = c;
+#pragma unroll
+      for (int m = 1; m < 32; m <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, m);
+        if (lane >= m) incl += o;
+      }
+      if (s < p.nseg) ctl.prefix[s] = carry + incl - c;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) {
+      ctl.prefix[p.nseg] = carry;
+      ctl.total_units = carry * p.fb_count;
+      ctl.abort = 0;
+      for (int s = 0; s < kStages; ++s) {
+        tc::mbar_init(&ctl.full[s], 1);
+        tc::mbar_init(&ctl.dq[s], kDequantWarps);
+        tc::mbar_init(&ctl.empty[s], 1);
+      }
+      for (int a = 0; a < 2; ++a) {
+        tc::mbar_init(&ctl.tfull[a], 1);
+        tc::mbar_init(&ctl.tempty[a], 4);
+      }
+      tc::mbar_init(&ctl.mma_done, 1);
+      tc::fence_mbar_init();
+      tc::prefetch_tmap(&p.tm_b);
+      tc::prefetch_tmap(&p.tm_a[0][0]);
+    }
+  } else if (warp == 1) {
+    tc::tmem_alloc(&ctl.tmem_base, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem_base = ctl.tmem_base;
+  const int total_units = ctl.total_units;
+  constexpr int kFeat = (MODE == kGateUp) ? 64 : 128;  // output features per unit
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_phase[kStages];
+      bool issued[kStages];
+      for (int s = 0; s < kStages; ++s) issued[s] = false, issued_phase[s] = 0;
+      for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
+        Unit U;
+        if (!decode_unit(ctl, p, u, U)) continue;
+        const bool shared = (U.seg == p.shared_seg);
+        const int wi = shared ? 1 : 0;
+        const int64_t e = shared ? 0 : U.seg;
+        const int chunks = (U.nrows + 63) / 64;
+        const uint32_t bbytes = (uint32_t)chunks * 64 * 128;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!tc::mbar_wait(&ctl.empty[stage], phase ^ 1u, abort, p.status)) goto producer_done;
+          if constexpr (MODE == kRouter) {
+            tc::mbar_arrive_expect_tx(&ctl.full[stage], (uint32_t)kABytes + bbytes);
+            tc::tma_load_2d(stage_a(stage), &p.tm_a[0][0], kb * kBK, U.fb * kBM, &ctl.full[stage]);
+          } else if constexpr (MODE == kGateUp) {
+            tc::mbar_arrive_expect_tx(&ctl.full[stage], (uint32_t)kRawBytes + bbytes);
+            const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * 64;
+            tc::tma_load_2d(stage_raw(stage), &p.tm_a[wi][0], kb * 8,
+                            (int32_t)(p.a_row_base[wi][0] + r0), &ctl.full[stage]);
+            tc::tma_load_2d(stage_raw(stage) + 2048, &p.tm_a[wi][1], kb * 8,
+                            (int32_t)(p.a_row_base[wi][1] + r0), &ctl.full[stage]);
+          } else {
+            tc::mbar_arrive_expect_tx(&ctl.full[stage], (uint32_t)kRawBytes + bbytes);
+            const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * kBM;
+            tc::tma_load_2d(stage_raw(stage), &p.tm_a[wi][0], kb * 8,
+                            (int32_t)(p.a_row_base[wi][0] + r0), &ctl.full[stage]);
+          }
+          for (int c = 0; c < chunks; ++c)
+            tc::tma_load_2d(stage_b(stage) + c * 8192, &p.tm_b, kb * kBK, U.row0 + c * 64,
+                            &ctl.full[stage]);
+          issued[stage] = true;
+          issued_phase[stage] = phase;
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+      }
+    producer_done:
+      if (*abort) {
+        // let our own copies land before the CTA exits (bounded)
+        for (int s = 0; s < kStages; ++s)
+          if (issued[s]) {
+            int dummy = 0;
+            tc::mbar_wait(&ctl.full[s], issued_phase[s], (volatile int*)&dummy, nullptr,
+                          100000000ull);
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
+        Unit U;
+        if (!decode_unit(ctl, p, u, U)) continue;
+        const int n = (U.nrows + 15) & ~15;
+        const uint32_t idesc = tc::idesc_bf16(kBM, n);
+        if (!tc::mbar_wait(&ctl.tempty[acc], acc_phase ^ 1u, abort, p.status)) break;
+        tc::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          uint64_t* ready = (MODE == kRouter) ? &ctl.full[stage] : &ctl.dq[stage];
+          if (!tc::mbar_wait(ready, phase, abort, p.status)) goto mma_done;
+          tc::tc_fence_after();
+          const uint32_t a_addr = tc::smem_u32(stage_a(stage));
+          const uint32_t b_addr = tc::smem_u32(stage_b(stage));
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            tc::mma_bf16(d_tmem, tc::sdesc_sw128(a_addr + k * 32), tc::sdesc_sw128(b_addr + k * 32),
+                         idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&ctl.empty[stage]);
+          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+        }
+        tc::mma_commit(&ctl.tfull[acc]);
+        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      }
+    mma_done:
+      // every MMA issued by this thread completes before TMEM is released
+      tc::mma_commit(&ctl.mma_done);
+      int dummy = 0;
+      tc::mbar_wait(&ctl.mma_done, 0, (volatile int*)&dummy, p.status, 200000000ull);
+    }
+  } else if (warp < 6) {
+    // ================= epilogue (TMEM -> registers -> global) =================
+    const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
+      Unit U;
+      if (!decode_unit(ctl, p, u, U)) continue;
+      if (!tc::mbar_wait(&ctl.tfull[acc], acc_phase, abort, p.status)) break;
+      tc::tc_fence_after();
+      const int n = (U.nrows + 15) & ~15;
+      const uint32_t t0 = tmem_base + ((uint32_t)(32 * sub) << 16) + (uint32_t)(acc * 256);
+      for (int cb = 0; cb < n / 16; ++cb) {
+        uint32_t v[16];
+        tc::tmem_ld16(t0 + (uint32_t)(cb * 16), v);
+        tc::tmem_ld_wait();
+        const int rbase = U.row0 + cb * 16;
+        if constexpr (MODE == kGateUp) {
+          // lane l < 16: gate row f; lane l + 16: up row f (f = 16*sub + l%16)
+          const int col = U.fb * 64 + sub * 16 + (lane & 15);
+#pragma unroll
+          for (int m = 0; m < 8; ++m) {
+            const uint32_t send = (lane < 16) ? v[2 * m + 1] : v[2 * m];
+            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 16);
+            float g, up;
+            int j;
+            if (lane < 16) { g = __uint_as_float(v[2 * m]); up = __uint_as_float(recv); j = 2 * m; }
+            else { g = __uint_as_float(recv); up = __uint_as_float(v[2 * m + 1]); j = 2 * m + 1; }
+            const int row = rbase + j;
+            if (j + cb * 16 < U.nrows && row < p.out_rows && col < p.out_cols) {
+              const float a = swiglu_bf16(round_bf16(g), round_bf16(up));
+              p.out[(int64_t)row * p.ldo + col] = f32_to_bf16(a);
+            }
+          }
+        } else {
+          const int col = U.fb * kFeat + 32 * sub + lane;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int row = rbase + j;
+            if (j + cb * 16 < U.nrows && row < p.out_rows && col < p.out_cols)
+              p.out[(int64_t)row * p.ldo + col] = f32_to_bf16(__uint_as_float(v[j]));
+          }
+        }
+      }
+      tc::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ctl.tempty[acc]);
+      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+    }
+  } else if constexpr (MODE != kRouter) {
+    // ================= dequantisers =================
+    const int t = threadIdx.x - 6 * 32;  // 0..255
+    const int r = t >> 1;                // A tile row
+    const int h = t & 1;                 // which half of the 64-element K block
+    int raw_row, j, f_local;
+    if constexpr (MODE == kGateUp) {
+      const int within = r & 31, g4 = r >> 5;
+      j = within < 16 ? 0 : 1;
+      f_local = g4 * 16 + (within & 15);
+      raw_row = j * 64 + f_local;
+    } else {
+      j = 0;
+      f_local = r;
+      raw_row = r;
+    }
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
+      Unit U;
+      if (!decode_unit(ctl, p, u, U)) continue;
+      const bool shared = (U.seg == p.shared_seg);
+      const int wi = shared ? 1 : 0;
+      const int64_t e = shared ? 0 : U.seg;
+      const int64_t grow = p.a_row_base[wi][j] + e * p.a_expert_rows[wi] +
+                           (int64_t)U.fb * kFeat + f_local;
+      const uint16_t* sp = p.scales[wi][j] + grow * p.groups_per_row;
+      const uint16_t* bp = p.biases[wi][j] + grow * p.groups_per_row;
+      uint16_t s_next = __ldg(sp), b_next = __ldg(bp);
+      for (int kb = 0; kb < p.kblocks; ++kb) {
+        const uint16_t s16 = s_next, b16 = b_next;
+        if (kb + 1 < p.kblocks) { s_next = __ldg(sp + kb + 1); b_next = __ldg(bp + kb + 1); }
+        if (!tc::mbar_wait(&ctl.full[stage], phase, abort, p.status)) goto dequant_done;
+        const uint4 w4 = *reinterpret_cast<const uint4*>(stage_raw(stage) + raw_row * 32 + h * 16);
+        const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16(s16));
+        const __nv_bfloat162 b2 = __bfloat162bfloat162(__ushort_as_bfloat16(b16));
+        uint8_t* arow = stage_a(stage) + r * 128;
+        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int c = h * 4 + i;  // logical 16-byte chunk (8 K elements)
+          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = dequant8(ws[i], s2, b2);
+        }
+        tc::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ctl.dq[stage]);
+        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      }
+    }
+  dequant_done:;
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ===========================================================================
+// host side
+// ===========================================================================
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2D map over a row-major matrix: `cols` elements of `elem_bytes` per row.
+bool make_map(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes,
+              uint64_t cols, uint64_t rows, uint32_t box_cols, uint32_t box_rows,
+              CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn || !base || rows == 0) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)elem_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct PlanData {
+  GemmParams gate_up{};
+  GemmParams down{};
+  GemmParams router{};
+  int sms = 148;
+};
+
+int sm_count() {
+  int dev = 0, n = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+template <int MODE>
+cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
+  const int threads = MODE == kRouter ? kThreadsR : kThreadsQ;
+  static uint64_t configured[3] = {0, 0, 0};  // per-device bit
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured[MODE] & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<MODE>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured[MODE] |= bit;
+  }
+  int grid = sm_count();
+  if (max_units < grid) grid = max_units;
+  if (grid <= 0) return cudaSuccess;
+  moe_gemm_kernel<MODE><<<grid, threads, kSmemBytes, st>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace
 
 int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan) {
   plan->ok = false;
   plan->w = w;
+  if (plan->dev) {
+    delete reinterpret_cast<PlanData*>(plan->dev);
+    plan->dev = nullptr;
+  }
+  const int H = w.hidden, E = w.experts, I = w.intermediate, Is = w.shared_intermediate;
+  // eligible profile: 4-bit, group 64, shapes that tile exactly
+  if (w.bits != 4 || w.group_size != 64) return 0;
+  if (H % 128 != 0 || I % 64 != 0 || (Is != 0 && Is != I)) return 0;
+  if (E > 1024 || !encode_fn()) return 0;
+  auto* d = new PlanData();
+  d->sms = sm_count();
+  const CUtensorMapDataType U32 = CU_TENSOR_MAP_DATA_TYPE_UINT32;
+  const uint64_t wh = (uint64_t)H / 8, wi = (uint64_t)I / 8;
+  bool ok = true;
+  // gate/up
+  GemmParams& g = d->gate_up;
+  const int64_t gate_rows = w.gate_up_fused ? 2LL * I : (int64_t)I;
+  ok &= make_map(&g.tm_a[0][0], w.gate.packed, U32, 4, wh, (uint64_t)E * gate_rows, 8, 64,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  if (w.gate_up_fused) {
+    g.tm_a[0][1] = g.tm_a[0][0];
+    g.a_row_base[0][0] = 0;
+    g.a_row_base[0][1] = I;
+    g.scales[0][1] = (const uint16_t*)w.gate.scales;
+    g.biases[0][1] = (const uint16_t*)w.gate.biases;
+  } else {
+    ok &= make_map(&g.tm_a[0][1], w.up.packed, U32, 4, wh, (uint64_t)E * I, 8, 64,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    g.a_row_base[0][0] = g.a_row_base[0][1] = 0;
+    g.scales[0][1] = (const uint16_t*)w.up.scales;
+    g.biases[0][1] = (const uint16_t*)w.up.biases;
+  }
+  g.scales[0][0] = (const uint16_t*)w.gate.scales;
+  g.biases[0][0] = (const uint16_t*)w.gate.biases;
+  g.a_expert_rows[0] = gate_rows;
+  if (Is > 0) {
+    ok &= make_map(&g.tm_a[1][0], w.shared_gate.packed, U32, 4, wh, (uint64_t)Is, 8, 64,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    ok &= make_map(&g.tm_a[1][1], w.shared_up.packed, U32, 4, wh, (uint64_t)Is, 8, 64,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    g.scales[1][0] = (const uint16_t*)w.shared_gate.scales;
+    g.biases[1][0] = (const uint16_t*)w.shared_gate.biases;
+    g.scales[1][1] = (const uint16_t*)w.shared_up.scales;
+    g.biases[1][1] = (const uint16_t*)w.shared_up.biases;
+    g.a_expert_rows[1] = Is;
+  }
+  g.groups_per_row = H / 64;
+  g.kblocks = H / 64;
+  g.fb_count = I / 64;
+  g.tile_rows = kMaxN;
+  g.out_cols = I;
+  g.ldo = I;
+  // down
+  GemmParams& dn = d->down;
+  ok &= make_map(&dn.tm_a[0][0], w.down.packed, U32, 4, wi, (uint64_t)E * H, 8, 128,
+                 CU_TENSOR_MAP_SWIZZLE_NONE);
+  dn.scales[0][0] = (const uint16_t*)w.down.scales;
+  dn.biases[0][0] = (const uint16_t*)w.down.biases;
+  dn.a_expert_rows[0] = H;
+  if (Is > 0) {
+    ok &= make_map(&dn.tm_a[1][0], w.shared_down.packed, U32, 4, wi, (uint64_t)H, 8, 128,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    dn.scales[1][0] = (const uint16_t*)w.shared_down.scales;
+    dn.biases[1][0] = (const uint16_t*)w.shared_down.biases;
+    dn.a_expert_rows[1] = H;
+  }
+  dn.groups_per_row = I / 64;
+  dn.kblocks = I / 64;
+  dn.fb_count = H / 128;
+  dn.tile_rows = kMaxN;
+  dn.out_cols = H;
+  dn.ldo = H;
+  // router (dense bf16 A by TMA)
+  GemmParams& rt = d->router;
+  ok &= make_map(&rt.tm_a[0][0], w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                 (uint64_t)H, (uint64_t)E, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+  rt.kblocks = H / 64;
+  rt.fb_count = (E + 127) / 128;
+  rt.tile_rows = 64;
+  rt.out_cols = E;
+  rt.ldo = E;
+  rt.shared_seg = -1;
+  rt.nseg = 1;
+  rt.seg_offsets = nullptr;
+  if (!ok) {
+    delete d;
+    return 0;  // not eligible: the CUDA-core path serves this layer
+  }
+  plan->dev = d;
+  plan->ok = true;
   return 0;
 }
-void moe_gemm_release(MoeGemmPlan& plan) { plan.ok = false; }
-bool moe_gemm_enabled(const MoeGemmPlan& plan, int opt) { return plan.ok && opt >= 0; }
+
+void moe_gemm_release(MoeGemmPlan& plan) {
+  if (plan.dev) delete reinterpret_cast<PlanData*>(plan.dev);
+  plan.dev = nullptr;
+  plan.ok = false;
+}
+
+// use_tensor_cores option: > 0 selects the tcgen05 path for eligible layers.
+bool moe_gemm_enabled(const MoeGemmPlan& plan, int opt) { return plan.ok && opt > 0; }
+
 size_t moe_gemm_scratch_bytes() { return 256; }
-cudaError_t moe_gemm_router(const MoeGemmPlan&, const void*, int64_t, void*, void*, cudaStream_t) {
-  return cudaErrorNotSupported;
+
+static bool bind_b(GemmParams& p, const void* rows_ptr, int64_t rows, int K) {
+  return make_map(&p.tm_b, rows_ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
+                  (uint64_t)rows, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
 }
-cudaError_t moe_gemm_gate_up(const MoeGemmPlan&, const void*, int64_t, const uint32_t*, void*, void*,
-                             cudaStream_t) {
-  return cudaErrorNotSupported;
+
+cudaError_t moe_gemm_router(const MoeGemmPlan& plan, const void* x, int64_t tokens, void* logits,
+                            void* scratch, uint32_t* status, cudaStream_t st) {
+  (void)scratch;
+  auto* d = reinterpret_cast<PlanData*>(plan.dev);
+  if (!d) return cudaErrorNotSupported;
+  GemmParams p = d->router;
+  if (!bind_b(p, x, tokens, plan.w.hidden)) return cudaErrorInvalidValue;
+  p.total_rows = (int)tokens;
+  p.out = (uint16_t*)logits;
+  p.out_rows = (int)tokens;
+  p.status = status;
+  const int units = (int)((tokens + 63) / 64) * p.fb_count;
+  return launch<kRouter>(p, units, st);
 }
-cudaError_t moe_gemm_down(const MoeGemmPlan&, const void*, int64_t, const uint32_t*, void*, void*,
-                          cudaStream_t) {
-  return cudaErrorNotSupported;
+
+cudaError_t moe_gemm_gate_up(const MoeGemmPlan& plan, const void* states, int64_t rows,
+                             const uint32_t* offsets, void* act, void* scratch, uint32_t* status,
+                             cudaStream_t st) {
+  (void)scratch;
+  auto* d = reinterpret_cast<PlanData*>(plan.dev);
+  if (!d) return cudaErrorNotSupported;
+  GemmParams p = d->gate_up;
+  if (!bind_b(p, states, rows, plan.w.hidden)) return cudaErrorInvalidValue;
+  const bool shared = plan.w.shared_intermediate > 0;
+  p.seg_offsets = offsets;
+  p.nseg = plan.w.experts + (shared ? 1 : 0);
+  p.shared_seg = shared ? plan.w.experts : -1;
+  p.total_rows = (int)rows;
+  p.out = (uint16_t*)act;
+  p.out_rows = (int)rows;
+  p.status = status;
+  const int max_units = (int)((rows + kMaxN - 1) / kMaxN + p.nseg) * p.fb_count;
+  return launch<kGateUp>(p, max_units, st);
+}
+
+cudaError_t moe_gemm_down(const MoeGemmPlan& plan, const void* act, int64_t rows,
+                          const uint32_t* offsets, void* yrows, void* scratch, uint32_t* status,
+                          cudaStream_t st) {
+  (void)scratch;
+  auto* d = reinterpret_cast<PlanData*>(plan.dev);
+  if (!d) return cudaErrorNotSupported;
+  GemmParams p = d->down;
+  if (!bind_b(p, act, rows, plan.w.intermediate)) return cudaErrorInvalidValue;
+  const bool shared = plan.w.shared_intermediate > 0;
+  p.seg_offsets = offsets;
+  p.nseg = plan.w.experts + (shared ? 1 : 0);
+  p.shared_seg = shared ? plan.w.experts : -1;
+  p.total_rows = (int)rows;
+  p.out = (uint16_t*)yrows;
+  p.out_rows = (int)rows;
+  p.status = status;
+  const int max_units = (int)((rows + kMaxN - 1) / kMaxN + p.nseg) * p.fb_count;
+  return launch<kDown>(p, max_units, st);
 }
 
 }  // namespace astro

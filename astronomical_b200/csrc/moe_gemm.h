@@ -23,10 +23,12 @@ bool moe_gemm_enabled(const MoeGemmPlan& plan, int use_tensor_cores_option);
 size_t moe_gemm_scratch_bytes();
 
 cudaError_t moe_gemm_router(const MoeGemmPlan& plan, const void* x, int64_t tokens, void* logits,
-                            void* scratch, cudaStream_t st);
+                            void* scratch, uint32_t* status, cudaStream_t st);
 cudaError_t moe_gemm_gate_up(const MoeGemmPlan& plan, const void* states, int64_t rows,
-                             const uint32_t* offsets, void* act, void* scratch, cudaStream_t st);
+                             const uint32_t* offsets, void* act, void* scratch, uint32_t* status,
+                             cudaStream_t st);
 cudaError_t moe_gemm_down(const MoeGemmPlan& plan, const void* act, int64_t rows,
-                          const uint32_t* offsets, void* yrows, void* scratch, cudaStream_t st);
+                          const uint32_t* offsets, void* yrows, void* scratch, uint32_t* status,
+                          cudaStream_t st);
 
 }  // namespace astro

@@ -485,6 +485,15 @@ int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t t
                          const int64_t* token_subset, int64_t n_subset,
                          const uint16_t* logits_override, uint16_t* out,
                          uint32_t* out_ids, uint16_t* out_scores, int num_threads) {
+  return ao_moe_block_forward_terms(w, x, tokens, token_subset, n_subset, logits_override, out,
+                                    out_ids, out_scores, NULL, NULL, num_threads);
+}
+
+int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int64_t tokens,
+                               const int64_t* token_subset, int64_t n_subset,
+                               const uint16_t* logits_override, uint16_t* out,
+                               uint32_t* out_ids, uint16_t* out_scores, uint16_t* out_sparse,
+                               uint16_t* out_shared_gated, int num_threads) {
   const int H = w->hidden, E = w->experts, K = w->top_k, I = w->intermediate;
   const int Is = w->shared_intermediate, G = w->group, B = w->bits;
   if (tokens < 0 || H <= 0 || E <= 0 || K <= 0 || K > E || I <= 0 || Is < 0)
@@ -575,10 +584,19 @@ int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t t
     ao_gather_qmm(sa, NULL, NULL, nt, Is, w->sdown_q, w->sdown_s, w->sdown_b, 1, H, G, B, so);
     ao_matmul_bf16_nt(xs, w->shared_gate_w, nt, 1, H, gl);
     ao_combine_sparse_and_shared(sparse, so, gl, AO_BF16, nt, H, out);
+    if (out_shared_gated) {
+      for (int64_t t = 0; t < nt; ++t) {
+        const float g = rnd_bf16(ao_sigmoidf(ao_bf16_to_f32(gl[t])));
+        for (int d = 0; d < H; ++d)
+          out_shared_gated[t * H + d] = ao_f32_to_bf16(ao_bf16_to_f32(so[t * H + d]) * g);
+      }
+    }
     free(gl); free(so); free(sa); free(su); free(sg);
   } else {
     memcpy(out, sparse, sizeof(uint16_t) * (size_t)nt * H);
+    if (out_shared_gated) memset(out_shared_gated, 0, sizeof(uint16_t) * (size_t)nt * H);
   }
+  if (out_sparse) memcpy(out_sparse, sparse, sizeof(uint16_t) * (size_t)nt * H);
   if (out_ids) memcpy(out_ids, ids, sizeof(uint32_t) * (size_t)n);
   if (out_scores) memcpy(out_scores, scores, sizeof(uint16_t) * (size_t)n);
   free(sparse); free(yrows); free(offs); free(stok); free(sids); free(inv); free(order);

@@ -118,6 +118,15 @@ int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t t
                          const uint16_t* logits_override, uint16_t* out,
                          uint32_t* out_ids, uint16_t* out_scores, int num_threads);
 
+/* Same, also returning the two bf16 terms of the final addition (the routed
+ * weighted sum and the gated shared-expert output; zero without a shared
+ * expert), used to scale output tolerances. */
+int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int64_t tokens,
+                               const int64_t* token_subset, int64_t n_subset,
+                               const uint16_t* logits_override, uint16_t* out,
+                               uint32_t* out_ids, uint16_t* out_scores, uint16_t* out_sparse,
+                               uint16_t* out_shared_gated, int num_threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -69,6 +69,8 @@ def _declare(l: ctypes.CDLL) -> None:
     l.ao_combine_sparse_and_shared.restype = None
     l.ao_moe_block_forward.argtypes = [P, P, I64, P, I64, P, P, P, P, I]
     l.ao_moe_block_forward.restype = I
+    l.ao_moe_block_forward_terms.argtypes = [P, P, I64, P, I64, P, P, P, P, P, P, I]
+    l.ao_moe_block_forward_terms.restype = I
 
 
 class BlockWeights(ctypes.Structure):
@@ -236,9 +238,10 @@ def combine_sparse_and_shared(sparse, shared, gate_logits, bf16=True):
 
 
 def moe_block_forward(weights: dict, x, token_subset=None, logits_override=None,
-                      num_threads: int = 0):
+                      num_threads: int = 0, terms: bool = False):
     """Whole block on CPU.  weights: dict from astronomical_b200.synthetic (MLX layout).
-    Returns (y bf16 [n, H], ids [n, K], scores bf16 [n, K]) for the listed tokens."""
+    Returns (y bf16 [n, H], ids [n, K], scores bf16 [n, K]) for the listed tokens, plus
+    (sparse, gated_shared) -- the bf16 terms of the final addition -- when terms=True."""
     cfg = weights["config"]
     x = _c(x, np.uint16)
     T, H = x.shape
@@ -275,8 +278,12 @@ def moe_block_forward(weights: dict, x, token_subset=None, logits_override=None,
     ids = np.empty((n, K), np.uint32)
     sc = np.empty((n, K), np.uint16)
     lo = None if logits_override is None else _c(logits_override, np.uint16)
-    st = lib().ao_moe_block_forward(ctypes.byref(bw), _p(x), T, _p(sub), n, _p(lo), _p(y),
-                                    _p(ids), _p(sc), num_threads)
+    sp = np.empty((n, H), np.uint16) if terms else None
+    sg = np.empty((n, H), np.uint16) if terms else None
+    st = lib().ao_moe_block_forward_terms(ctypes.byref(bw), _p(x), T, _p(sub), n, _p(lo), _p(y),
+                                          _p(ids), _p(sc), _p(sp), _p(sg), num_threads)
     if st != OK:
         raise ValueError(f"moe_block_forward status {st}")
+    if terms:
+        return y, ids, sc, sp, sg
     return y, ids, sc

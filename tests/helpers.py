@@ -56,18 +56,35 @@ def assert_bf16_ulps(a_bits, b_bits, ulps: float = 1.0, max_frac: float = 0.02):
     assert frac <= max_frac, f"{frac:.4f} of elements differ"
 
 
-def block_metrics(got_bits, ref_bits):
+def block_metrics(got_bits, ref_bits, terms=None):
+    """(raw max-abs, scaled max-abs, relative L2).
+
+    The scaled error divides by max(1, magnitude): the comparison convention of
+    the reference's own bf16 tests (crates/model-serving/tests/direct_mlx/
+    sparse_expert_projection.rs:33-44, assert_f32_close scales by
+    max(|expected|, 1)).  The magnitude is that of the terms entering the block's
+    last addition, |sparse| + |gated shared| (both bf16 values of the oracle), when
+    they are given: y can cancel to ~1 while the gated shared term is ~15, and one
+    bf16 ulp of that term (0.06) then moves y by more than 2e-2 absolute."""
     g = bf16_to_f32(got_bits).astype(np.float64)
     r = bf16_to_f32(ref_bits).astype(np.float64)
-    max_abs = float(np.max(np.abs(g - r))) if g.size else 0.0
-    rel_l2 = float(np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)) if g.size else 0.0
-    return max_abs, rel_l2
+    if not g.size:
+        return 0.0, 0.0, 0.0
+    d = np.abs(g - r)
+    max_abs = float(d.max())
+    mag = np.abs(r)
+    if terms is not None:
+        mag = np.maximum(mag, sum(np.abs(bf16_to_f32(t).astype(np.float64)) for t in terms))
+    scaled = float((d / np.maximum(mag, 1.0)).max())
+    rel_l2 = float(np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30))
+    return max_abs, scaled, rel_l2
 
 
-def assert_block_close(got_bits, ref_bits):
-    max_abs, rel_l2 = block_metrics(got_bits, ref_bits)
-    assert max_abs <= MAX_ABS and rel_l2 <= REL_L2, (max_abs, rel_l2)
-    return max_abs, rel_l2
+def assert_block_close(got_bits, ref_bits, terms=None):
+    """max-abs 2e-2 (scaled, see block_metrics) and rel-L2 1e-3."""
+    max_abs, scaled, rel_l2 = block_metrics(got_bits, ref_bits, terms)
+    assert scaled <= MAX_ABS and rel_l2 <= REL_L2, (max_abs, scaled, rel_l2)
+    return max_abs, scaled, rel_l2
 
 
 __all__ = ["to_np_bf16", "to_np_u32", "bf16_tensor", "u32_tensor", "assert_bf16_ulps",

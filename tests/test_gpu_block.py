@@ -46,38 +46,47 @@ def run_and_compare(cfg, T, seed=0, subset=None, fuse=False, use_tc=0):
     srt = O.sort_expert_assignments(ids_o, cfg["experts"])
     assert np.array_equal(offs[:cfg["experts"] + 1], srt["expert_offsets"])
     # block output on the same logits
-    y_ref, ids_r, _ = O.moe_block_forward(w, x, token_subset=subset, logits_override=logits)
+    y_ref, ids_r, _, sp, sg = O.moe_block_forward(w, x, token_subset=subset,
+                                                  logits_override=logits, terms=True)
     assert np.array_equal(ids_r, ids[sub])
-    metrics = assert_block_close(got[sub], y_ref)
+    metrics = assert_block_close(got[sub], y_ref, terms=(sp, sg))
     blk.close()
     return metrics
 
 
-def test_block_config0_shape():
+# path: 1 = tcgen05 tensor-core kernels (4-bit g64 layers), -1 = CUDA-core kernels
+PATHS = [pytest.param(1, id="tcgen05"), pytest.param(-1, id="cudacore")]
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_block_config0_shape(path):
     cfg = dict(synthetic.CONFIGS[0])
-    run_and_compare(cfg, 32)
+    run_and_compare(cfg, 32, use_tc=path)
 
 
-@pytest.mark.parametrize("T", [1, 4, 7, 8, 16, 64, 200])
-def test_block_config1_shape_small_T(T):
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("T", [1, 4, 7, 8, 16, 64, 200, 777])
+def test_block_config1_shape_small_T(T, path):
     # T*K < 64 takes the unsorted weighted sum (routing.rs:13), T >= 8 the sorted one
-    run_and_compare(small_cfg(), T, seed=T)
+    run_and_compare(small_cfg(), T, seed=T, use_tc=path)
 
 
+@pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("T", [1, 4, 16, 64])
-def test_block_decode_zipf(T):
+def test_block_decode_zipf(T, path):
     cfg = dict(synthetic.CONFIGS[2])
     cfg["tokens"] = T
-    run_and_compare(cfg, T, seed=100 + T)
+    run_and_compare(cfg, T, seed=100 + T, use_tc=path)
 
 
-def test_block_fused_gate_up_equals_separate():
+@pytest.mark.parametrize("path", PATHS)
+def test_block_fused_gate_up_equals_separate(path):
     # resident_gate_up_fusion.rs: fusing gate||up must not change any value
     cfg = small_cfg()
     w = synthetic.make_block_weights(cfg, seed=4)
     x = bf16_tensor(synthetic.make_hidden_states(96, cfg["hidden"], seed=5))
-    a = moe.Qwen3_5MoEBlock(w, max_tokens=96, fuse_gate_up=False)
-    b = moe.Qwen3_5MoEBlock(w, max_tokens=96, fuse_gate_up=True)
+    a = moe.Qwen3_5MoEBlock(w, max_tokens=96, fuse_gate_up=False, use_tensor_cores=path)
+    b = moe.Qwen3_5MoEBlock(w, max_tokens=96, fuse_gate_up=True, use_tensor_cores=path)
     ya, yb = a.forward(x), b.forward(x)
     torch.cuda.synchronize()
     assert torch.equal(ya, yb)
@@ -85,18 +94,37 @@ def test_block_fused_gate_up_equals_separate():
     b.close()
 
 
-def test_block_full_size_config1_subset():
+@pytest.mark.parametrize("path", PATHS)
+def test_block_full_size_config1_subset(path):
     """T=4096 (the headline shape): every output row depends only on its own
     token, so the oracle checks a sample of 48 rows of the full-size run."""
     rng = np.random.default_rng(7)
     subset = np.sort(rng.choice(4096, 48, replace=False))
-    run_and_compare(small_cfg(), 4096, seed=11, subset=subset)
+    run_and_compare(small_cfg(), 4096, seed=11, subset=subset, use_tc=path)
 
 
-def test_block_deterministic_and_empty():
+@pytest.mark.parametrize("path", PATHS)
+def test_block_paths_agree_within_tolerance(path):
+    """The two GPU paths compute the same block (different accumulation order)."""
+    cfg = small_cfg()
+    w = synthetic.make_block_weights(cfg, seed=21)
+    x = bf16_tensor(synthetic.make_hidden_states(1024, cfg["hidden"], seed=22))
+    a = moe.Qwen3_5MoEBlock(w, max_tokens=1024, use_tensor_cores=1)
+    b = moe.Qwen3_5MoEBlock(w, max_tokens=1024, use_tensor_cores=-1)
+    ya, ta = a.forward(x, taps=True)
+    yb, tb = b.forward(x, taps=True)
+    torch.cuda.synchronize()
+    if torch.equal(ta["router_logits"], tb["router_logits"]):
+        assert torch.equal(ta["selected_indices"], tb["selected_indices"])
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_block_deterministic_and_empty(path):
     cfg = small_cfg()
     w = synthetic.make_block_weights(cfg, seed=8)
-    blk = moe.Qwen3_5MoEBlock(w, max_tokens=512)
+    blk = moe.Qwen3_5MoEBlock(w, max_tokens=512, use_tensor_cores=path)
     x = bf16_tensor(synthetic.make_hidden_states(512, cfg["hidden"], seed=9))
     y1 = blk.forward(x)
     y2 = blk.forward(x)
