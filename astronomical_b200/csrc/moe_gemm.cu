@@ -577,8 +577,9 @@ void moe_gemm_release(MoeGemmPlan& plan) {
   plan.ok = false;
 }
 
-// use_tensor_cores option: > 0 selects the tcgen05 path for eligible layers.
-bool moe_gemm_enabled(const MoeGemmPlan& plan, int opt) { return plan.ok && opt > 0; }
+// use_tensor_cores option: >= 0 (auto/on) selects the tcgen05 path for eligible
+// layers; < 0 forces the CUDA-core kernels.
+bool moe_gemm_enabled(const MoeGemmPlan& plan, int opt) { return plan.ok && opt >= 0; }
 
 size_t moe_gemm_scratch_bytes() { return 256; }
 

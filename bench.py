@@ -48,6 +48,8 @@ def parse():
                     help="tokens per CPU-baseline sample (0 = size it to ~10 s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--use-tensor-cores", type=int, default=0)
+    ap.add_argument("--profile", action="store_true",
+                    help="only W warm-up and K plain steps (for ncu captures; prints nothing)")
     return ap.parse_args()
 
 
@@ -197,6 +199,12 @@ def run_ours(args):
     for _ in range(args.warmup):
         blk.forward(x)
     torch.cuda.synchronize()
+    if args.profile:
+        for _ in range(args.steps):
+            blk.forward(x)
+        torch.cuda.synchronize()
+        blk.close()
+        return
 
     clocks = ClockSampler(local)
     clocks.start()
