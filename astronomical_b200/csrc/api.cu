@@ -133,6 +133,7 @@ struct BlockWorkspace {
   uint32_t* sids;
   uint32_t* stok;
   uint32_t* offsets;
+  void* sort_scratch;
   uint16_t* states;  // gathered activation rows [rows, H] (tensor-core path)
   uint16_t* act;     // [rows, I]
   uint16_t* yrows;   // [rows, H]
@@ -163,6 +164,7 @@ size_t plan_workspace(const astro_moe_layer_weights& w, int64_t T, BlockWorkspac
   b.sids = (uint32_t*)take(sizeof(uint32_t) * rows);
   b.stok = (uint32_t*)take(sizeof(uint32_t) * rows);
   b.offsets = (uint32_t*)take(sizeof(uint32_t) * (E + 2));
+  b.sort_scratch = take(astro::sort_scratch_bytes(N, (int)E));
   b.states = (uint16_t*)take(sizeof(uint16_t) * rows * H);
   b.act = (uint16_t*)take(sizeof(uint16_t) * rows * Imax);
   b.yrows = (uint16_t*)take(sizeof(uint16_t) * rows * H);
@@ -253,7 +255,7 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   // a1: router projection
   const bool use_tc = astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores) &&
                       (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-  ctx->launches += use_tc ? 7 : 6;
+  ctx->launches += use_tc ? 8 : 7;
   if (use_tc) {
     CK(astro::moe_gemm_router(L.gemm, x, T, b.logits, b.gemm_scratch, ctx->status, st),
        "router projection");
@@ -268,7 +270,7 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
      "route experts");
   // a3: sort (+ shared segment E)
   CK(astro::launch_sort_assignments(b.ids, T, K, E, has_shared ? T : 0, b.order, b.inverse,
-                                    b.sids, b.stok, b.offsets, ctx->status, st),
+                                    b.sids, b.stok, b.offsets, ctx->status, b.sort_scratch, st),
      "sort expert assignments");
 
   if (use_tc) {
@@ -408,16 +410,16 @@ int astro_moe_sort_expert_assignments(const uint32_t* ids, int64_t tokens, int32
   if (tokens * top_k > 0 && !ids) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null ids", op);
   uint32_t* status = nullptr;
   if (int rc = device_status_ptr(&status)) return rc;
-  uint32_t* offs = expert_offsets;
-  bool tmp = false;
-  if (!offs) {
-    CK(cudaMallocAsync(&offs, sizeof(uint32_t) * (experts + 1), S(stream)), "cudaMallocAsync");
-    tmp = true;
-  }
+  const int64_t n = tokens * (int64_t)top_k;
+  const size_t scratch_bytes = astro::sort_scratch_bytes(n, experts);
+  char* tmp = nullptr;
+  CK(cudaMallocAsync((void**)&tmp, scratch_bytes + sizeof(uint32_t) * (experts + 1), S(stream)),
+     "cudaMallocAsync");
+  uint32_t* offs = expert_offsets ? expert_offsets : (uint32_t*)(tmp + scratch_bytes);
   CK(astro::launch_sort_assignments(ids, tokens, top_k, experts, 0, sorted_order, inverse_order,
-                                    sorted_ids, sorted_tokens, offs, status, S(stream)),
+                                    sorted_ids, sorted_tokens, offs, status, tmp, S(stream)),
      op);
-  if (tmp) CK(cudaFreeAsync(offs, S(stream)), "cudaFreeAsync");
+  CK(cudaFreeAsync(tmp, S(stream)), "cudaFreeAsync");
   return ASTRO_MOE_OK;
 }
 
@@ -482,12 +484,14 @@ int astro_moe_gather_qmm(const void* x, int64_t x_rows, int32_t in_features,
     // group rows by expert with the stable sort, gather through the order and
     // write every result back to its original row
     const size_t n = (size_t)n_rows;
-    CK(cudaMallocAsync(&buf, sizeof(uint32_t) * (2 * n + experts + 1), st), "cudaMallocAsync");
+    const size_t sb = astro::sort_scratch_bytes(n_rows, experts);
+    CK(cudaMallocAsync(&buf, sizeof(uint32_t) * (2 * n + experts + 1) + sb, st), "cudaMallocAsync");
     uint32_t* order = buf;
     uint32_t* xr = buf + n;
     uint32_t* offs = buf + 2 * n;
+    void* sscratch = buf + 2 * n + experts + 1;
     CK(astro::launch_sort_assignments(rhs, n_rows, 1, experts, 0, order, nullptr, nullptr, nullptr,
-                                      offs, status, st),
+                                      offs, status, sscratch, st),
        op);
     CK(astro::launch_compose_rows(lhs, order, n_rows, xr, st), op);
     d.seg_offsets = offs;

@@ -14,11 +14,13 @@ cudaError_t launch_route_experts(const void* logits, int dtype, int64_t tokens, 
 cudaError_t launch_dense_nt_simt(const void* x, const void* w, int64_t rows, int cols, int depth,
                                  void* out, int ldo, cudaStream_t st);
 
+// scratch: sort_scratch_bytes(tokens * K, E) bytes of device memory
+size_t sort_scratch_bytes(int64_t n, int E);
 cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, int E,
                                     int64_t shared_rows, uint32_t* sorted_order,
                                     uint32_t* inverse_order, uint32_t* sorted_ids,
                                     uint32_t* sorted_tokens, uint32_t* offsets, uint32_t* status,
-                                    cudaStream_t st);
+                                    void* scratch, cudaStream_t st);
 
 cudaError_t launch_take_rows(const void* src, int64_t src_rows, const uint32_t* rows, int64_t n,
                              int hidden, void* out, uint32_t* status, cudaStream_t st);

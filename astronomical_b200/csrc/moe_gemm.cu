@@ -20,8 +20,9 @@
 //   warp 0      TMA producer: raw int4 weight rows (32 B per row per K block,
 //               MLX layout, no repacking) and the token rows (bf16, 128-byte
 //               swizzle) into a 4-stage ring.
-//   warps 6-13  dequantisers: nibbles -> bf16 with bf16x2 FMAs (w = s*q + b),
-//               written in the canonical SW128 K-major layout the MMA reads.
+//   warps 6-21  dequantisers (two groups of 8 taking alternate K blocks): nibbles
+//               -> bf16 with bf16x2 FMAs (w = s*q + b), written in the canonical
+//               SW128 K-major layout the MMA reads.
 //   warp 1      one thread issues tcgen05.mma (M=128, N<=256, K=16) into one of
 //               two TMEM accumulators (2 x 256 fp32 columns) and commits.
 //   warps 2-5   epilogue: tcgen05.ld -> SwiGLU / bf16 -> global, while the MMA
@@ -37,6 +38,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstring>
+#include <initializer_list>
 
 #include "moe_gemm.h"
 #include "tc_ptx.cuh"
@@ -55,7 +57,8 @@ constexpr int kRawBytes = kBM * 32;       // 4 KB int4 A tile
 constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;  // 52 KB, multiple of 1024
 constexpr int kSmemBytes = kStages * kStageBytes + 1024;    // + alignment slack
 constexpr int kMaxSeg = 1025;
-constexpr int kDequantWarps = 8;
+constexpr int kDequantWarps = 16;  // two groups of 8, alternate K blocks
+constexpr int kDqArrivals = 8;     // warps of one group arrive per stage
 constexpr int kThreadsQ = (6 + kDequantWarps) * 32;  // gate/up, down
 constexpr int kThreadsR = 6 * 32;                    // router (A comes by TMA)
 constexpr uint32_t kTmemCols = 512;                  // 2 accumulators x 256 columns
@@ -68,6 +71,7 @@ struct GemmParams {
   int64_t a_row_base[2][2];   // first tensor row of expert 0 (the up half of a fused tensor: I)
   int64_t a_expert_rows[2];   // tensor rows per expert (I, 2I when fused, H for down)
   int groups_per_row;         // scales per weight row = K / 64
+  int scale_vec;              // groups fetched per vector load: 8, 4 or 1
   const uint32_t* seg_offsets;  // [nseg + 1]; nullptr: one segment [0, total_rows)
   int nseg;
   int shared_seg;
@@ -183,7 +187,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       ctl.abort = 0;
       for (int s = 0; s < kStages; ++s) {
         tc::mbar_init(&ctl.full[s], 1);
-        tc::mbar_init(&ctl.dq[s], kDequantWarps);
+        tc::mbar_init(&ctl.dq[s], kDqArrivals);
         tc::mbar_init(&ctl.empty[s], 1);
       }
       for (int a = 0; a < 2; ++a) {
@@ -348,9 +352,15 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     }
   } else if constexpr (MODE != kRouter) {
     // ================= dequantisers =================
-    const int t = threadIdx.x - 6 * 32;  // 0..255
-    const int r = t >> 1;                // A tile row
-    const int h = t & 1;                 // which half of the 64-element K block
+    // Two groups of 8 warps take alternate K blocks (items), so each warp has two
+    // stage-times per item.  Thread (row r, half h) converts 32 codes per item.
+    // The row's scales/biases are fetched VEC groups at a time, one vector ahead
+    // (8 K blocks of lead for VEC = 8), so no item waits on a global load.
+    const int t = threadIdx.x - 6 * 32;
+    const int grp = t >> 8;              // item parity handled by this thread
+    const int tt = t & 255;
+    const int r = tt >> 1;               // A tile row
+    const int h = tt & 1;                // which half of the 64-element K block
     int raw_row, j, f_local;
     if constexpr (MODE == kGateUp) {
       const int within = r & 31, g4 = r >> 5;
@@ -362,40 +372,94 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       f_local = r;
       raw_row = r;
     }
-    int stage = 0;
-    uint32_t phase = 0;
-    for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
+    const int VEC = p.scale_vec;  // 8, 4 or 1 groups per vector load
+    const int KB = p.kblocks;
+    auto row_of = [&](int ui, int64_t& grow, int& wsel) -> bool {
+      const int u = blockIdx.x + ui * gridDim.x;
+      if (u >= total_units) return false;
       Unit U;
-      if (!decode_unit(ctl, p, u, U)) continue;
+      if (!decode_unit(ctl, p, u, U)) return false;
       const bool shared = (U.seg == p.shared_seg);
-      const int wi = shared ? 1 : 0;
+      wsel = shared ? 1 : 0;
       const int64_t e = shared ? 0 : U.seg;
-      const int64_t grow = p.a_row_base[wi][j] + e * p.a_expert_rows[wi] +
-                           (int64_t)U.fb * kFeat + f_local;
-      const uint16_t* sp = p.scales[wi][j] + grow * p.groups_per_row;
-      const uint16_t* bp = p.biases[wi][j] + grow * p.groups_per_row;
-      uint16_t s_next = __ldg(sp), b_next = __ldg(bp);
-      for (int kb = 0; kb < p.kblocks; ++kb) {
-        const uint16_t s16 = s_next, b16 = b_next;
-        if (kb + 1 < p.kblocks) { s_next = __ldg(sp + kb + 1); b_next = __ldg(bp + kb + 1); }
-        if (!tc::mbar_wait(&ctl.full[stage], phase, abort, p.status)) goto dequant_done;
-        const uint4 w4 = *reinterpret_cast<const uint4*>(stage_raw(stage) + raw_row * 32 + h * 16);
-        const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16(s16));
-        const __nv_bfloat162 b2 = __bfloat162bfloat162(__ushort_as_bfloat16(b16));
-        uint8_t* arow = stage_a(stage) + r * 128;
-        const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int c = h * 4 + i;  // logical 16-byte chunk (8 K elements)
-          *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = dequant8(ws[i], s2, b2);
-        }
-        tc::fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&ctl.dq[stage]);
-        if (++stage == kStages) { stage = 0; phase ^= 1u; }
+      grow = p.a_row_base[wsel][j] + e * p.a_expert_rows[wsel] + (int64_t)U.fb * kFeat + f_local;
+      return true;
+    };
+    auto load_vec = [&](int wsel, int64_t grow, int vid, uint4& vs, uint4& vb) {
+      const int64_t off = grow * p.groups_per_row + (int64_t)vid * VEC;
+      const uint16_t* sp = p.scales[wsel][j] + off;
+      const uint16_t* bp = p.biases[wsel][j] + off;
+      if (VEC == 8) {
+        vs = __ldg(reinterpret_cast<const uint4*>(sp));
+        vb = __ldg(reinterpret_cast<const uint4*>(bp));
+      } else if (VEC == 4) {
+        const uint2 a = __ldg(reinterpret_cast<const uint2*>(sp));
+        const uint2 c = __ldg(reinterpret_cast<const uint2*>(bp));
+        vs = make_uint4(a.x, a.y, 0u, 0u);
+        vb = make_uint4(c.x, c.y, 0u, 0u);
+      } else {
+        vs = make_uint4(__ldg(sp), 0u, 0u, 0u);
+        vb = make_uint4(__ldg(bp), 0u, 0u, 0u);
       }
+    };
+    auto pick = [](const uint4& v, int q) -> uint16_t {
+      const uint32_t w = (q < 4) ? ((q < 2) ? v.x : v.y) : ((q < 6) ? v.z : v.w);
+      return (uint16_t)((q & 1) ? (w >> 16) : (w & 0xffffu));
+    };
+    int ui = 0, kb = grp;
+    while (kb >= KB) { kb -= KB; ++ui; }
+    int cu = -1, cw = 0;          // decoded unit of the current item
+    int64_t cg = 0;
+    int c_ui = -1, c_vid = -1;    // vector in use
+    uint4 cs = make_uint4(0, 0, 0, 0), cb = cs;
+    int n_ui = -1, n_vid = -1;    // prefetched vector
+    uint4 ns = cs, nb = cs;
+    while (!*abort) {
+      if (ui != cu) {
+        if (!row_of(ui, cg, cw)) break;
+        cu = ui;
+      }
+      const int vid = kb / VEC;
+      if (ui != c_ui || vid != c_vid) {
+        if (ui == n_ui && vid == n_vid) { cs = ns; cb = nb; }
+        else load_vec(cw, cg, vid, cs, cb);
+        c_ui = ui;
+        c_vid = vid;
+        // prefetch the following vector of this thread's item sequence
+        int pui = ui, pvid = vid + 1;
+        if (pvid * VEC >= KB) { pui = ui + 1; pvid = 0; }
+        int64_t pg = cg;
+        int pw = cw;
+        if (pui == ui || row_of(pui, pg, pw)) {
+          load_vec(pw, pg, pvid, ns, nb);
+          n_ui = pui;
+          n_vid = pvid;
+        } else {
+          n_ui = -1;
+        }
+      }
+      const int q = kb - vid * VEC;
+      const uint16_t s16 = pick(cs, q), b16 = pick(cb, q);
+      const int item = ui * KB + kb;
+      const int stage = item % kStages;
+      const uint32_t phase = (uint32_t)(item / kStages) & 1u;
+      if (!tc::mbar_wait(&ctl.full[stage], phase, abort, p.status)) break;
+      const uint4 w4 = *reinterpret_cast<const uint4*>(stage_raw(stage) + raw_row * 32 + h * 16);
+      const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16(s16));
+      const __nv_bfloat162 b2 = __bfloat162bfloat162(__ushort_as_bfloat16(b16));
+      uint8_t* arow = stage_a(stage) + r * 128;
+      const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int c = h * 4 + i;  // logical 16-byte chunk (8 K elements)
+        *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = dequant8(ws[i], s2, b2);
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ctl.dq[stage]);
+      kb += 2;
+      while (kb >= KB) { kb -= KB; ++ui; }
     }
-  dequant_done:;
   }
 
   tc::tc_fence_before();
@@ -445,6 +509,18 @@ struct PlanData {
   GemmParams router{};
   int sms = 148;
 };
+
+// widest scale vector (8 or 4 groups) that every scale/bias row allows
+int vec_for(int groups, std::initializer_list<const void*> ptrs) {
+  for (int v : {8, 4}) {
+    if (groups % v) continue;
+    bool ok = true;
+    for (const void* ptr : ptrs)
+      if (ptr && (reinterpret_cast<uintptr_t>(ptr) & (uintptr_t)(2 * v - 1))) ok = false;
+    if (ok) return v;
+  }
+  return 1;
+}
 
 int sm_count() {
   int dev = 0, n = 148;
@@ -525,6 +601,9 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan) {
     g.a_expert_rows[1] = Is;
   }
   g.groups_per_row = H / 64;
+  g.scale_vec = vec_for(H / 64, {w.gate.scales, w.gate.biases, w.up.scales, w.up.biases,
+                                 w.shared_gate.scales, w.shared_gate.biases, w.shared_up.scales,
+                                 w.shared_up.biases});
   g.kblocks = H / 64;
   g.fb_count = I / 64;
   g.tile_rows = kMaxN;
@@ -545,6 +624,8 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan) {
     dn.a_expert_rows[1] = H;
   }
   dn.groups_per_row = I / 64;
+  dn.scale_vec = vec_for(I / 64, {w.down.scales, w.down.biases, w.shared_down.scales,
+                                  w.shared_down.biases});
   dn.kblocks = I / 64;
   dn.fb_count = H / 128;
   dn.tile_rows = kMaxN;

@@ -6,11 +6,11 @@
 // offsets that MLX derives inside gather_qmm are materialised as the exclusive
 // scan of the histogram; the grouped GEMMs consume them directly.
 //
-// One CTA of 32 warps: warp w owns a contiguous slice of the assignments, so
-// stability only needs per-warp histograms (phase 1), an (expert, warp) scan
-// (phase 2) and an in-order scatter where equal ids inside one 32-wide step get
-// their rank from __match_any_sync (phase 3).  Ids >= E set a status bit and
-// are skipped, so no write ever leaves the output arrays.
+// Two passes over tiles of 2048 assignments: per-tile histograms, then each
+// tile computes its bases (global exclusive scan over experts, plus earlier
+// tiles, plus earlier warps of the tile) and scatters its assignments in order;
+// equal ids inside one 32-wide step get their rank from __match_any_sync.  Ids
+// >= E set a status bit and are skipped, so no write leaves the output arrays.
 //
 // With shared_rows > 0 the shared expert is appended as segment E: rows
 // [n, n + shared_rows) with token t and id E, offsets[E+1] = n + shared_rows.
@@ -19,100 +19,128 @@
 
 namespace astro {
 
-constexpr int kSortWarps = 32;
+// Tiles of kSortTile assignments; inside a tile warp w owns a contiguous run of
+// kSortTile / kSortWarps assignments, so stability needs only per-warp counts.
+constexpr int kSortWarps = 16;
+constexpr int kSortTile = 2048;
+constexpr int kPerWarp = kSortTile / kSortWarps;  // 128
 
-__global__ void __launch_bounds__(kSortWarps * 32, 1) sort_assignments_kernel(
-    const uint32_t* __restrict__ ids, int64_t n, int K, int E, int64_t shared_rows,
-    uint32_t* __restrict__ sorted_order, uint32_t* __restrict__ inverse_order,
-    uint32_t* __restrict__ sorted_ids, uint32_t* __restrict__ sorted_tokens,
-    uint32_t* __restrict__ offsets, uint32_t* __restrict__ status) {
-  extern __shared__ int smem_i[];
-  int* cnt = smem_i;                      // [kSortWarps][E]
-  int* tot = smem_i + kSortWarps * E;     // [E]
-  __shared__ int warp_sums[32];
+int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
+
+size_t sort_scratch_bytes(int64_t n, int E) {
+  return sizeof(int) * (size_t)(sort_tiles(n) > 0 ? sort_tiles(n) : 1) * (size_t)E;
+}
+
+// pass 1: histogram of each tile -> tile_hist[g][e]
+__global__ void __launch_bounds__(kSortWarps * 32) sort_hist_kernel(
+    const uint32_t* __restrict__ ids, int64_t n, int E, int* __restrict__ tile_hist,
+    uint32_t* __restrict__ status) {
+  extern __shared__ int hist[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int64_t chunk = (n + kSortWarps - 1) / kSortWarps;
-  const int64_t beg = (int64_t)w * chunk;
-  const int64_t end = (beg + chunk < n) ? beg + chunk : n;
-
-  for (int i = threadIdx.x; i < kSortWarps * E; i += blockDim.x) cnt[i] = 0;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
   __syncthreads();
-
-  // phase 1: per-warp histogram
-  for (int64_t base = beg; base < end; base += 32) {
-    const int64_t i = base + lane;
-    const bool act = i < end;
-    uint32_t id = act ? ids[i] : 0xffffffffu;
+  const int64_t beg = (int64_t)blockIdx.x * kSortTile + (int64_t)w * kPerWarp;
+  for (int it = 0; it < kPerWarp; it += 32) {
+    const int64_t i = beg + it + lane;
+    const bool act = i < n;
+    const uint32_t id = act ? ids[i] : 0xffffffffu;
     const bool ok = act && id < (uint32_t)E;
     if (act && !ok) record_status(status, kDevBadExpertId);
-    const uint32_t key = ok ? id : 0xffffffffu;
-    const uint32_t peers = __match_any_sync(0xffffffffu, key);
+    const uint32_t peers = __match_any_sync(0xffffffffu, ok ? id : 0xffffffffu);
+    if (ok && (__ffs(peers) - 1) == lane) atomicAdd(&hist[id], __popc(peers));
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    tile_hist[(int64_t)blockIdx.x * E + e] = hist[e];
+}
+
+// pass 2: every tile derives its bases (global exclusive scan over experts of
+// all tiles' counts + counts of earlier tiles + counts of earlier warps of the
+// tile) and scatters its assignments in order.
+__global__ void __launch_bounds__(kSortWarps * 32) sort_scatter_kernel(
+    const uint32_t* __restrict__ ids, int64_t n, int K, int E, int tiles,
+    const int* __restrict__ tile_hist, int64_t shared_rows, uint32_t* __restrict__ sorted_order,
+    uint32_t* __restrict__ inverse_order, uint32_t* __restrict__ sorted_ids,
+    uint32_t* __restrict__ sorted_tokens, uint32_t* __restrict__ offsets) {
+  extern __shared__ int sm[];
+  int* cnt = sm;                             // [kSortWarps][E]
+  int* base = sm + kSortWarps * E;           // [E] counts of earlier tiles
+  int* totals = sm + (kSortWarps + 1) * E;   // [E] counts of all tiles
+  __shared__ int warp_sums[32];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int g = blockIdx.x;
+  for (int i = threadIdx.x; i < kSortWarps * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  const int64_t beg = (int64_t)g * kSortTile + (int64_t)w * kPerWarp;
+  for (int it = 0; it < kPerWarp; it += 32) {
+    const int64_t i = beg + it + lane;
+    const uint32_t id = (i < n) ? ids[i] : 0xffffffffu;
+    const bool ok = id < (uint32_t)E;
+    const uint32_t peers = __match_any_sync(0xffffffffu, ok ? id : 0xffffffffu);
     if (ok && (__ffs(peers) - 1) == lane) cnt[w * E + id] += __popc(peers);
   }
-  __syncthreads();
-
-  // phase 2: per expert, exclusive scan over warps; then scan of totals over experts
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int run = 0;
-    for (int ww = 0; ww < kSortWarps; ++ww) {
-      const int c = cnt[ww * E + e];
-      cnt[ww * E + e] = run;
-      run += c;
+  // totals over all tiles and the count of earlier tiles, per expert
+  const int per = (E + blockDim.x - 1) / blockDim.x;
+  const int e0 = threadIdx.x * per;
+  int local = 0;
+  for (int q = 0; q < per && e0 + q < E; ++q) {
+    const int e = e0 + q;
+    int total = 0, before = 0;
+    for (int t = 0; t < tiles; ++t) {
+      const int c = tile_hist[(int64_t)t * E + e];
+      total += c;
+      if (t < g) before += c;
     }
-    tot[e] = run;
+    base[e] = before;
+    local += total;
+    totals[e] = total;
   }
   __syncthreads();
-  // block-wide exclusive scan of tot[0..E), E <= 32 * blockDim.x
-  {
-    const int per = (E + blockDim.x - 1) / blockDim.x;
-    const int e0 = threadIdx.x * per;
-    int local = 0;
-    for (int j = 0; j < per && e0 + j < E; ++j) local += tot[e0 + j];
-    int incl = local;
+  // block-wide exclusive scan of the totals
+  int incl = local;
+#pragma unroll
+  for (int m = 1; m < 32; m <<= 1) {
+    const int o = __shfl_up_sync(0xffffffffu, incl, m);
+    if (lane >= m) incl += o;
+  }
+  if (lane == 31) warp_sums[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    int s = lane < kSortWarps ? warp_sums[lane] : 0;
 #pragma unroll
     for (int m = 1; m < 32; m <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, m);
-      if (lane >= m) incl += o;
+      const int o = __shfl_up_sync(0xffffffffu, s, m);
+      if (lane >= m) s += o;
     }
-    if (lane == 31) warp_sums[w] = incl;
-    __syncthreads();
-    if (w == 0) {
-      int s = warp_sums[lane];
-#pragma unroll
-      for (int m = 1; m < 32; m <<= 1) {
-        const int o = __shfl_up_sync(0xffffffffu, s, m);
-        if (lane >= m) s += o;
-      }
-      warp_sums[lane] = s;  // inclusive
-    }
-    __syncthreads();
-    int run = incl - local + (w > 0 ? warp_sums[w - 1] : 0);
-    for (int j = 0; j < per && e0 + j < E; ++j) {
-      const int c = tot[e0 + j];
-      tot[e0 + j] = run;  // now the exclusive offset
-      run += c;
-    }
+    if (lane < kSortWarps) warp_sums[lane] = s;
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    offsets[e] = (uint32_t)tot[e];
-    for (int ww = 0; ww < kSortWarps; ++ww) cnt[ww * E + e] += tot[e];
+  {
+    int run = incl - local + (w > 0 ? warp_sums[w - 1] : 0);
+    for (int q = 0; q < per && e0 + q < E; ++q) {
+      const int e = e0 + q;
+      const int total = totals[e];
+      if (g == 0) offsets[e] = (uint32_t)run;
+      int b = run + base[e];
+      for (int ww = 0; ww < kSortWarps; ++ww) {
+        const int c = cnt[ww * E + e];
+        cnt[ww * E + e] = b;
+        b += c;
+      }
+      run += total;
+    }
   }
-  if (threadIdx.x == 0) {
-    const int total = warp_sums[31];
+  if (g == 0 && threadIdx.x == blockDim.x - 1) {
+    const int total = warp_sums[kSortWarps - 1];
     offsets[E] = (uint32_t)total;
     if (shared_rows > 0) offsets[E + 1] = (uint32_t)(total + shared_rows);
   }
   __syncthreads();
-
-  // phase 3: stable scatter in original order
-  for (int64_t base = beg; base < end; base += 32) {
-    const int64_t i = base + lane;
-    const bool act = i < end;
-    const uint32_t id = act ? ids[i] : 0xffffffffu;
-    const bool ok = act && id < (uint32_t)E;
-    const uint32_t key = ok ? id : 0xffffffffu;
-    const uint32_t peers = __match_any_sync(0xffffffffu, key);
+  for (int it = 0; it < kPerWarp; it += 32) {
+    const int64_t i = beg + it + lane;
+    const uint32_t id = (i < n) ? ids[i] : 0xffffffffu;
+    const bool ok = id < (uint32_t)E;
+    const uint32_t peers = __match_any_sync(0xffffffffu, ok ? id : 0xffffffffu);
     int pos = 0;
     if (ok) pos = cnt[w * E + id] + __popc(peers & lanemask_lt());
     __syncwarp();
@@ -125,9 +153,10 @@ __global__ void __launch_bounds__(kSortWarps * 32, 1) sort_assignments_kernel(
       if (sorted_tokens) sorted_tokens[pos] = (uint32_t)(i / K);
     }
   }
-  // shared-expert segment (token order)
+  // shared-expert segment (token order), split over the tiles
   if (shared_rows > 0) {
-    for (int64_t t = threadIdx.x; t < shared_rows; t += blockDim.x) {
+    for (int64_t t = (int64_t)g * blockDim.x + threadIdx.x; t < shared_rows;
+         t += (int64_t)tiles * blockDim.x) {
       if (sorted_tokens) sorted_tokens[n + t] = (uint32_t)t;
       if (sorted_ids) sorted_ids[n + t] = (uint32_t)E;
     }
@@ -138,15 +167,19 @@ cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, 
                                     int64_t shared_rows, uint32_t* sorted_order,
                                     uint32_t* inverse_order, uint32_t* sorted_ids,
                                     uint32_t* sorted_tokens, uint32_t* offsets, uint32_t* status,
-                                    cudaStream_t st) {
+                                    void* scratch, cudaStream_t st) {
   const int64_t n = tokens * (int64_t)K;
-  const size_t smem = sizeof(int) * (size_t)(kSortWarps + 1) * E;
-  if (smem > 48 * 1024)
-    cudaFuncSetAttribute(sort_assignments_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)smem);
-  sort_assignments_kernel<<<1, kSortWarps * 32, smem, st>>>(
-      ids, n, K > 0 ? K : 1, E, shared_rows, sorted_order, inverse_order, sorted_ids,
-      sorted_tokens, offsets, status);
+  const int tiles = (int)(n > 0 ? sort_tiles(n) : 1);
+  int* tile_hist = reinterpret_cast<int*>(scratch);
+  const size_t smem1 = sizeof(int) * (size_t)E;
+  const size_t smem2 = sizeof(int) * (size_t)(kSortWarps + 2) * E;
+  if (smem2 > 48 * 1024)
+    cudaFuncSetAttribute(sort_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)smem2);
+  sort_hist_kernel<<<tiles, kSortWarps * 32, smem1, st>>>(ids, n, E, tile_hist, status);
+  sort_scatter_kernel<<<tiles, kSortWarps * 32, smem2, st>>>(
+      ids, n, K > 0 ? K : 1, E, tiles, tile_hist, shared_rows, sorted_order, inverse_order,
+      sorted_ids, sorted_tokens, offsets);
   return cudaGetLastError();
 }
 
