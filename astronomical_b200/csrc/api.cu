@@ -21,7 +21,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/astro_moe.h"
+#include "astro_moe.h"
 #include "kernels.h"
 #include "moe_gemm.h"
 

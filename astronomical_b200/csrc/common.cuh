@@ -79,9 +79,11 @@ ASTRO_DEVINL float expf_cw(float x) {
   return __fmul_rn(p, __uint_as_float((uint32_t)(ni + 127) << 23));
 }
 
-// MLX sigmoid form: y = 1/(1+e^-|x|); x < 0 gives 1 - y.
+// MLX sigmoid form: y = 1/(1+e^-|x|); x < 0 gives 1 - y.  The correctly rounded
+// reciprocal equals the correctly rounded quotient 1/d, so this matches an IEEE
+// division bit for bit.
 ASTRO_DEVINL float sigmoid_mlx(float x) {
-  const float y = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cw(-fabsf(x))));
+  const float y = __frcp_rn(__fadd_rn(1.0f, expf_cw(-fabsf(x))));
   return (x < 0.0f) ? __fsub_rn(1.0f, y) : y;
 }
 

@@ -9,27 +9,27 @@
 //   down    : y[row, f]   = bf16(act_row . Wd[e,f])
 //   router  : logits[t,e] = bf16(x_t . Wr[e])        (forward.rs:52-93, dense bf16)
 //
-// Layout of the problem: rows of one expert are contiguous after the sort, so a
-// work unit is (expert segment, tile of <= 256 rows, block of weight rows).  The
-// GEMM is "swap-AB": the weight tile is the MMA's A operand (M = 128 weight rows)
-// and the token rows are B (N = the tile's row count rounded up to 16, 16..256),
-// so an expert with 130 rows costs N = 144, not two 128-row tiles, and every
-// weight tile is dequantised exactly once per unit.
+// Rows of one expert are contiguous after the sort, so a work unit is (expert
+// segment, tile of <= kMaxN rows, block of weight rows).  The GEMM is "swap-AB":
+// the weight tile is the MMA's A operand (M = 128 weight rows) and the token rows
+// are B (N = the tile's row count rounded up to 16), so an expert with 130 rows
+// costs N = 144, not two 128-row tiles, and every weight tile is dequantised once
+// per unit.  A work item is one 64-wide K block (one quantisation group).
 //
-// Per CTA (persistent, one per SM, units assigned round robin):
-//   warp 0      TMA producer: raw int4 weight rows (32 B per row per K block,
-//               MLX layout, no repacking) and the token rows (bf16, 128-byte
-//               swizzle) into a 4-stage ring.
-//   warps 6-21  dequantisers (two groups of 8 taking alternate K blocks): nibbles
-//               -> bf16 with bf16x2 FMAs (w = s*q + b), written in the canonical
-//               SW128 K-major layout the MMA reads.
-//   warp 1      one thread issues tcgen05.mma (M=128, N<=256, K=16) into one of
-//               two TMEM accumulators (2 x 256 fp32 columns) and commits.
-//   warps 2-5   epilogue: tcgen05.ld -> SwiGLU / bf16 -> global, while the MMA
-//               fills the other accumulator.
-// For gate/up the 128 A rows hold 64 gate and 64 up rows, interleaved in 16-row
-// groups so that each gate row and its up row land in lanes l and l+16 of the
-// same epilogue warp (one shuffle pairs them).
+// Three decoupled shared-memory rings (per CTA, persistent, one CTA per SM):
+//   raw  (kRawStages x 4 KB)   int4 weight rows, MLX layout, by TMA    <- warp 0
+//   B    (kBStages x 24 KB)    token rows, bf16, 128-byte swizzle, TMA <- warp 2
+//   A    (kAStages x 16 KB)    dequantised weights, SW128 K-major      <- warps 12-19
+// The token-row stream is the latency-critical one (the variants that dropped
+// each stream showed it), so it gets the deepest ring, loaded in 16-row boxes so
+// only rows the MMA reads are fetched.  Two groups of 4 dequant warps take
+// alternate items (nibbles -> bf16 with bf16x2 FMAs, w = s*q + b); each thread
+// converts one 64-element weight row per item.  Warp 1 (one thread) issues
+// tcgen05.mma (M=128, N<=192, K=16) into one of two TMEM accumulators and
+// commits; warps 4-11 (two per TMEM sub-partition) drain the other accumulator:
+// tcgen05.ld -> SwiGLU / bf16 -> global.  For gate/up the 128 A rows hold 64
+// gate and 64 up rows, interleaved in 16-row groups so each gate row and its up
+// row land in lanes l and l+16 of the same epilogue warp (one shuffle pairs them).
 //
 // Every mbarrier wait is bounded (2 s); on timeout the kernel records
 // kDevWaitTimeout, waits (bounded) for its own copies and MMAs, frees TMEM and
@@ -47,25 +47,34 @@ namespace astro {
 
 enum GemmMode : int { kGateUp = 0, kDown = 1, kRouter = 2 };
 
-constexpr int kStages = 4;
 constexpr int kBM = 128;                  // weight rows per tile (MMA M)
-constexpr int kBK = 64;                   // K per stage = one quantisation group
-constexpr int kMaxN = 256;                // token rows per tile (MMA N)
+constexpr int kBK = 64;                   // K per item = one quantisation group
+constexpr int kMaxN = 192;                // token rows per tile (MMA N)
+constexpr int kBoxRows = 16;              // token rows per TMA box
 constexpr int kABytes = kBM * kBK * 2;    // 16 KB bf16 A tile
-constexpr int kBBytes = kMaxN * kBK * 2;  // 32 KB bf16 B tile
+constexpr int kBBytes = kMaxN * kBK * 2;  // 24 KB bf16 B tile
 constexpr int kRawBytes = kBM * 32;       // 4 KB int4 A tile
-constexpr int kStageBytes = kABytes + kBBytes + kRawBytes;  // 52 KB, multiple of 1024
-constexpr int kSmemBytes = kStages * kStageBytes + 1024;    // + alignment slack
+constexpr int kRawStages = 8;
+constexpr int kBStages = 6;
+constexpr int kAStages = 2;
+constexpr int kSmemBytes = kBStages * kBBytes + kAStages * kABytes + kRawStages * kRawBytes + 1024;
 constexpr int kMaxSeg = 1025;
-constexpr int kDequantWarps = 16;  // two groups of 8, alternate K blocks
-constexpr int kDqArrivals = 8;     // warps of one group arrive per stage
-constexpr int kThreadsQ = (6 + kDequantWarps) * 32;  // gate/up, down
-constexpr int kThreadsR = 6 * 32;                    // router (A comes by TMA)
-constexpr uint32_t kTmemCols = 512;                  // 2 accumulators x 256 columns
+constexpr int kRawWarp = 0, kMmaWarp = 1, kBWarp = 2;
+constexpr int kEpiFirst = 4;       // warps 4..11: epilogue, two per TMEM sub-partition
+constexpr int kEpiWarps = 8;
+constexpr int kDqFirst = kEpiFirst + kEpiWarps;  // warps 12..19: dequantisers
+constexpr int kDqGroups = 2;       // groups taking alternate items
+constexpr int kDqGroupWarps = 4;   // 128 threads = one per A row
+constexpr int kDequantWarps = kDqGroups * kDqGroupWarps;
+constexpr int kThreadsQ = (kDqFirst + kDequantWarps) * 32;  // gate/up, down
+constexpr int kThreadsR = kDqFirst * 32;                    // router (A comes by TMA)
+constexpr uint32_t kTmemCols = 512;                         // 2 accumulators x 256 columns
+static_assert(kAStages % kDqGroups == 0 && kRawStages % kDqGroups == 0, "ring/group parity");
+static_assert(kBBytes % 1024 == 0 && kABytes % 1024 == 0, "SW128 tiles need 1024-byte alignment");
 
 struct GemmParams {
   CUtensorMap tm_a[2][2];  // [routed, shared][gate|down, up] raw int4 maps; router: bf16 map
-  CUtensorMap tm_b;        // token rows, bf16, box {64, 64}, 128-byte swizzle
+  CUtensorMap tm_b;        // token rows, bf16, box {64, 16}, 128-byte swizzle
   const uint16_t* scales[2][2];
   const uint16_t* biases[2][2];
   int64_t a_row_base[2][2];   // first tensor row of expert 0 (the up half of a fused tensor: I)
@@ -78,7 +87,7 @@ struct GemmParams {
   int total_rows;
   int kblocks;     // K / 64
   int fb_count;    // weight-row blocks per segment
-  int tile_rows;   // token rows per tile (<= 256, multiple of 64)
+  int tile_rows;   // token rows per tile (<= kMaxN)
   uint16_t* out;   // bf16 output matrix
   int64_t ldo;
   int out_cols;    // valid output columns (router: E)
@@ -91,11 +100,10 @@ struct Unit {
 };
 
 struct SmemCtl {
-  uint64_t full[kStages];
-  uint64_t dq[kStages];
-  uint64_t empty[kStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+  uint64_t a_full[kAStages], a_empty[kAStages];
+  uint64_t b_full[kBStages], b_empty[kBStages];
+  uint64_t tfull[2], tempty[2];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
@@ -144,6 +152,11 @@ ASTRO_DEVINL uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
   return o;
 }
 
+// ring bookkeeping for item k in a ring of S slots
+ASTRO_DEVINL int slot_of(int k, int S) { return k % S; }
+ASTRO_DEVINL uint32_t full_parity(int k, int S) { return (uint32_t)(k / S) & 1u; }
+ASTRO_DEVINL uint32_t empty_parity(int k, int S) { return ((uint32_t)(k / S) & 1u) ^ 1u; }
+
 template <int MODE>
 __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p) {
@@ -151,23 +164,27 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
   __shared__ SmemCtl ctl;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  auto stage_a = [&](int s) { return smem + s * kStageBytes; };
-  auto stage_b = [&](int s) { return smem + s * kStageBytes + kABytes; };
-  auto stage_raw = [&](int s) { return smem + s * kStageBytes + kABytes + kBBytes; };
+  uint8_t* ring_b = smem;                                  // kBStages x kBBytes
+  uint8_t* ring_a = ring_b + kBStages * kBBytes;           // kAStages x kABytes
+  uint8_t* ring_raw = ring_a + kAStages * kABytes;         // kRawStages x kRawBytes
+  auto b_at = [&](int s) { return ring_b + s * kBBytes; };
+  auto a_at = [&](int s) { return ring_a + s * kABytes; };
+  auto raw_at = [&](int s) { return ring_raw + s * kRawBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort = &ctl.abort;
+  const int KB = p.kblocks;
+  constexpr int kFeat = (MODE == kGateUp) ? 64 : 128;  // output features per unit
 
   // ---- setup: segment table, barriers, TMEM ----
   if (warp == 0) {
-    // tile prefix over segments
     int carry = 0;
     for (int base = 0; base < p.nseg; base += 32) {
       const int s = base + lane;
-      int c = 0, o0 = 0, o1 = 0;
+      int c = 0;
       if (s < p.nseg) {
-        o0 = p.seg_offsets ? (int)p.seg_offsets[s] : 0;
-        o1 = p.seg_offsets ? (int)p.seg_offsets[s + 1] : p.total_rows;
+        const int o0 = p.seg_offsets ? (int)p.seg_offsets[s] : 0;
+        const int o1 = p.seg_offsets ? (int)p.seg_offsets[s + 1] : p.total_rows;
         c = (o1 - o0 + p.tile_rows - 1) / p.tile_rows;
         ctl.offs[s] = o0;
         if (s == p.nseg - 1) ctl.offs[s + 1] = o1;
@@ -185,21 +202,28 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       ctl.prefix[p.nseg] = carry;
       ctl.total_units = carry * p.fb_count;
       ctl.abort = 0;
-      for (int s = 0; s < kStages; ++s) {
-        tc::mbar_init(&ctl.full[s], 1);
-        tc::mbar_init(&ctl.dq[s], kDqArrivals);
-        tc::mbar_init(&ctl.empty[s], 1);
+      for (int s = 0; s < kRawStages; ++s) {
+        tc::mbar_init(&ctl.raw_full[s], 1);
+        tc::mbar_init(&ctl.raw_empty[s], kDqGroupWarps);
+      }
+      for (int s = 0; s < kAStages; ++s) {
+        tc::mbar_init(&ctl.a_full[s], MODE == kRouter ? 1 : kDqGroupWarps);
+        tc::mbar_init(&ctl.a_empty[s], 1);
+      }
+      for (int s = 0; s < kBStages; ++s) {
+        tc::mbar_init(&ctl.b_full[s], 1);
+        tc::mbar_init(&ctl.b_empty[s], 1);
       }
       for (int a = 0; a < 2; ++a) {
         tc::mbar_init(&ctl.tfull[a], 1);
-        tc::mbar_init(&ctl.tempty[a], 4);
+        tc::mbar_init(&ctl.tempty[a], kEpiWarps);
       }
       tc::mbar_init(&ctl.mma_done, 1);
       tc::fence_mbar_init();
       tc::prefetch_tmap(&p.tm_b);
       tc::prefetch_tmap(&p.tm_a[0][0]);
     }
-  } else if (warp == 1) {
+  } else if (warp == kMmaWarp) {
     tc::tmem_alloc(&ctl.tmem_base, kTmemCols);
     tc::tmem_relinquish();
   }
@@ -208,66 +232,94 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
   tc::tc_fence_after();
   const uint32_t tmem_base = ctl.tmem_base;
   const int total_units = ctl.total_units;
-  constexpr int kFeat = (MODE == kGateUp) ? 64 : 128;  // output features per unit
 
-  if (warp == 0) {
-    // ================= TMA producer =================
+  if (warp == kRawWarp) {
+    // ================= weight producer (raw int4 rows; router: bf16 A) =================
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      uint32_t issued_phase[kStages];
-      bool issued[kStages];
-      for (int s = 0; s < kStages; ++s) issued[s] = false, issued_phase[s] = 0;
+      int k = 0;
+      int last_k = -1;
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
         Unit U;
         if (!decode_unit(ctl, p, u, U)) continue;
         const bool shared = (U.seg == p.shared_seg);
         const int wi = shared ? 1 : 0;
         const int64_t e = shared ? 0 : U.seg;
-        const int chunks = (U.nrows + 63) / 64;
-        const uint32_t bbytes = (uint32_t)chunks * 64 * 128;
-        for (int kb = 0; kb < p.kblocks; ++kb) {
-          if (!tc::mbar_wait(&ctl.empty[stage], phase ^ 1u, abort, p.status)) goto producer_done;
+        for (int kb = 0; kb < KB; ++kb, ++k) {
           if constexpr (MODE == kRouter) {
-            tc::mbar_arrive_expect_tx(&ctl.full[stage], (uint32_t)kABytes + bbytes);
-            tc::tma_load_2d(stage_a(stage), &p.tm_a[0][0], kb * kBK, U.fb * kBM, &ctl.full[stage]);
-          } else if constexpr (MODE == kGateUp) {
-            tc::mbar_arrive_expect_tx(&ctl.full[stage], (uint32_t)kRawBytes + bbytes);
-            const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * 64;
-            tc::tma_load_2d(stage_raw(stage), &p.tm_a[wi][0], kb * 8,
-                            (int32_t)(p.a_row_base[wi][0] + r0), &ctl.full[stage]);
-            tc::tma_load_2d(stage_raw(stage) + 2048, &p.tm_a[wi][1], kb * 8,
-                            (int32_t)(p.a_row_base[wi][1] + r0), &ctl.full[stage]);
+            const int s = slot_of(k, kAStages);
+            if (!tc::mbar_wait(&ctl.a_empty[s], empty_parity(k, kAStages), abort, p.status))
+              goto raw_done;
+            tc::mbar_arrive_expect_tx(&ctl.a_full[s], (uint32_t)kABytes);
+            tc::tma_load_2d(a_at(s), &p.tm_a[0][0], kb * kBK, U.fb * kBM, &ctl.a_full[s]);
           } else {
-            tc::mbar_arrive_expect_tx(&ctl.full[stage], (uint32_t)kRawBytes + bbytes);
-            const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * kBM;
-            tc::tma_load_2d(stage_raw(stage), &p.tm_a[wi][0], kb * 8,
-                            (int32_t)(p.a_row_base[wi][0] + r0), &ctl.full[stage]);
+            const int s = slot_of(k, kRawStages);
+            if (!tc::mbar_wait(&ctl.raw_empty[s], empty_parity(k, kRawStages), abort, p.status))
+              goto raw_done;
+            tc::mbar_arrive_expect_tx(&ctl.raw_full[s], (uint32_t)kRawBytes);
+            if constexpr (MODE == kGateUp) {
+              const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * 64;
+              tc::tma_load_2d(raw_at(s), &p.tm_a[wi][0], kb * 8,
+                              (int32_t)(p.a_row_base[wi][0] + r0), &ctl.raw_full[s]);
+              tc::tma_load_2d(raw_at(s) + 2048, &p.tm_a[wi][1], kb * 8,
+                              (int32_t)(p.a_row_base[wi][1] + r0), &ctl.raw_full[s]);
+            } else {
+              const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * kBM;
+              tc::tma_load_2d(raw_at(s), &p.tm_a[wi][0], kb * 8,
+                              (int32_t)(p.a_row_base[wi][0] + r0), &ctl.raw_full[s]);
+            }
           }
-          for (int c = 0; c < chunks; ++c)
-            tc::tma_load_2d(stage_b(stage) + c * 8192, &p.tm_b, kb * kBK, U.row0 + c * 64,
-                            &ctl.full[stage]);
-          issued[stage] = true;
-          issued_phase[stage] = phase;
-          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          last_k = k;
         }
       }
-    producer_done:
+    raw_done:
       if (*abort) {
-        // let our own copies land before the CTA exits (bounded)
-        for (int s = 0; s < kStages; ++s)
-          if (issued[s]) {
-            int dummy = 0;
-            tc::mbar_wait(&ctl.full[s], issued_phase[s], (volatile int*)&dummy, nullptr,
-                          100000000ull);
-          }
+        // let this thread's own copies land before the CTA exits (bounded)
+        int dummy = 0;
+        // only the last issue of each slot can still be in flight
+        const int ring = (MODE == kRouter) ? kAStages : kRawStages;
+        for (int k2 = (last_k - ring + 1 > 0 ? last_k - ring + 1 : 0); k2 <= last_k; ++k2) {
+          if (MODE == kRouter)
+            tc::mbar_wait(&ctl.a_full[slot_of(k2, kAStages)], full_parity(k2, kAStages),
+                          (volatile int*)&dummy, nullptr, 50000000ull);
+          else
+            tc::mbar_wait(&ctl.raw_full[slot_of(k2, kRawStages)], full_parity(k2, kRawStages),
+                          (volatile int*)&dummy, nullptr, 50000000ull);
+        }
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kBWarp) {
+    // ================= token-row producer =================
+    if (lane == 0) {
+      int k = 0;
+      int last_k = -1;
+      for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
+        Unit U;
+        if (!decode_unit(ctl, p, u, U)) continue;
+        const int boxes = (U.nrows + kBoxRows - 1) / kBoxRows;
+        const uint32_t bytes = (uint32_t)boxes * kBoxRows * 128;
+        for (int kb = 0; kb < KB; ++kb, ++k) {
+          const int s = slot_of(k, kBStages);
+          if (!tc::mbar_wait(&ctl.b_empty[s], empty_parity(k, kBStages), abort, p.status))
+            goto b_done;
+          tc::mbar_arrive_expect_tx(&ctl.b_full[s], bytes);
+          for (int c = 0; c < boxes; ++c)
+            tc::tma_load_2d(b_at(s) + c * (kBoxRows * 128), &p.tm_b, kb * kBK,
+                            U.row0 + c * kBoxRows, &ctl.b_full[s]);
+          last_k = k;
+        }
+      }
+    b_done:
+      if (*abort) {
+        int dummy = 0;
+        for (int k2 = (last_k - kBStages + 1 > 0 ? last_k - kBStages + 1 : 0); k2 <= last_k; ++k2)
+          tc::mbar_wait(&ctl.b_full[slot_of(k2, kBStages)], full_parity(k2, kBStages),
+                        (volatile int*)&dummy, nullptr, 50000000ull);
+      }
+    }
+  } else if (warp == kMmaWarp) {
     // ================= MMA issuer =================
     if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
+      int k = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
@@ -278,19 +330,21 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         if (!tc::mbar_wait(&ctl.tempty[acc], acc_phase ^ 1u, abort, p.status)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
-        for (int kb = 0; kb < p.kblocks; ++kb) {
-          uint64_t* ready = (MODE == kRouter) ? &ctl.full[stage] : &ctl.dq[stage];
-          if (!tc::mbar_wait(ready, phase, abort, p.status)) goto mma_done;
+        for (int kb = 0; kb < KB; ++kb, ++k) {
+          const int sa = slot_of(k, kAStages), sb = slot_of(k, kBStages);
+          if (!tc::mbar_wait(&ctl.a_full[sa], full_parity(k, kAStages), abort, p.status))
+            goto mma_done;
+          if (!tc::mbar_wait(&ctl.b_full[sb], full_parity(k, kBStages), abort, p.status))
+            goto mma_done;
           tc::tc_fence_after();
-          const uint32_t a_addr = tc::smem_u32(stage_a(stage));
-          const uint32_t b_addr = tc::smem_u32(stage_b(stage));
+          const uint32_t a_addr = tc::smem_u32(a_at(sa));
+          const uint32_t b_addr = tc::smem_u32(b_at(sb));
 #pragma unroll
-          for (int k = 0; k < kBK / 16; ++k) {
-            tc::mma_bf16(d_tmem, tc::sdesc_sw128(a_addr + k * 32), tc::sdesc_sw128(b_addr + k * 32),
-                         idesc, (kb > 0 || k > 0) ? 1u : 0u);
-          }
-          tc::mma_commit(&ctl.empty[stage]);
-          if (++stage == kStages) { stage = 0; phase ^= 1u; }
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            tc::mma_bf16(d_tmem, tc::sdesc_sw128(a_addr + kk * 32),
+                         tc::sdesc_sw128(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_commit(&ctl.a_empty[sa]);
+          tc::mma_commit(&ctl.b_empty[sb]);
         }
         tc::mma_commit(&ctl.tfull[acc]);
         if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
@@ -301,49 +355,77 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       int dummy = 0;
       tc::mbar_wait(&ctl.mma_done, 0, (volatile int*)&dummy, p.status, 200000000ull);
     }
-  } else if (warp < 6) {
+  } else if (warp >= kEpiFirst && warp < kEpiFirst + kEpiWarps) {
     // ================= epilogue (TMEM -> registers -> global) =================
-    const int sub = warp & 3;  // TMEM sub-partition this warp may access
+    // Two warps per TMEM sub-partition take alternate 16-column chunks; the
+    // load of the next chunk is in flight while the current one is converted.
+    const int sub = warp & 3;                    // TMEM sub-partition this warp may access
+    const int half = (warp - kEpiFirst) >> 2;    // which alternate chunks
     int acc = 0;
     uint32_t acc_phase = 0;
+    auto process = [&](const uint32_t (&v)[16], const Unit& U, int cb) {
+      const int rbase = U.row0 + cb * 16;
+      if constexpr (MODE == kGateUp) {
+        // lane l < 16: gate row f; lane l + 16: up row f (f = 16*sub + l%16)
+        const int col = U.fb * 64 + sub * 16 + (lane & 15);
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const uint32_t send = (lane < 16) ? v[2 * m + 1] : v[2 * m];
+          const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 16);
+          const float g = __uint_as_float(lane < 16 ? v[2 * m] : recv);
+          const float up = __uint_as_float(lane < 16 ? recv : v[2 * m + 1]);
+          const int j = 2 * m + (lane >> 4);
+          const int row = rbase + j;
+          if (j + cb * 16 < U.nrows && row < p.out_rows && col < p.out_cols) {
+            const float a = swiglu_bf16(round_bf16(g), round_bf16(up));
+            p.out[(int64_t)row * p.ldo + col] = f32_to_bf16(a);
+          }
+        }
+      } else {
+        // lanes l and l^1 trade one value so each stores a bf16 pair of
+        // adjacent features: even lanes token 2m, odd lanes token 2m+1
+        const int colbase = U.fb * kFeat + 32 * sub + (lane & ~1);
+        const bool odd = lane & 1;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+          const uint32_t send = odd ? v[2 * m] : v[2 * m + 1];
+          const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+          const float lo = __uint_as_float(odd ? recv : v[2 * m]);
+          const float hi = __uint_as_float(odd ? v[2 * m + 1] : recv);
+          const int j = 2 * m + (odd ? 1 : 0);
+          const int row = rbase + j;
+          if (j + cb * 16 < U.nrows && row < p.out_rows && colbase < p.out_cols) {
+            uint16_t* dst = p.out + (int64_t)row * p.ldo + colbase;
+            if (colbase + 1 < p.out_cols) {
+              const __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
+              *reinterpret_cast<__nv_bfloat162*>(dst) = pr;
+            } else {
+              dst[0] = f32_to_bf16(lo);
+            }
+          }
+        }
+      }
+    };
     for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
       Unit U;
       if (!decode_unit(ctl, p, u, U)) continue;
       if (!tc::mbar_wait(&ctl.tfull[acc], acc_phase, abort, p.status)) break;
       tc::tc_fence_after();
-      const int n = (U.nrows + 15) & ~15;
+      const int nch = ((U.nrows + 15) & ~15) / 16;
       const uint32_t t0 = tmem_base + ((uint32_t)(32 * sub) << 16) + (uint32_t)(acc * 256);
-      for (int cb = 0; cb < n / 16; ++cb) {
-        uint32_t v[16];
-        tc::tmem_ld16(t0 + (uint32_t)(cb * 16), v);
-        tc::tmem_ld_wait();
-        const int rbase = U.row0 + cb * 16;
-        if constexpr (MODE == kGateUp) {
-          // lane l < 16: gate row f; lane l + 16: up row f (f = 16*sub + l%16)
-          const int col = U.fb * 64 + sub * 16 + (lane & 15);
-#pragma unroll
-          for (int m = 0; m < 8; ++m) {
-            const uint32_t send = (lane < 16) ? v[2 * m + 1] : v[2 * m];
-            const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 16);
-            float g, up;
-            int j;
-            if (lane < 16) { g = __uint_as_float(v[2 * m]); up = __uint_as_float(recv); j = 2 * m; }
-            else { g = __uint_as_float(recv); up = __uint_as_float(v[2 * m + 1]); j = 2 * m + 1; }
-            const int row = rbase + j;
-            if (j + cb * 16 < U.nrows && row < p.out_rows && col < p.out_cols) {
-              const float a = swiglu_bf16(round_bf16(g), round_bf16(up));
-              p.out[(int64_t)row * p.ldo + col] = f32_to_bf16(a);
-            }
-          }
-        } else {
-          const int col = U.fb * kFeat + 32 * sub + lane;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int row = rbase + j;
-            if (j + cb * 16 < U.nrows && row < p.out_rows && col < p.out_cols)
-              p.out[(int64_t)row * p.ldo + col] = f32_to_bf16(__uint_as_float(v[j]));
-          }
-        }
+      uint32_t va[16], vb[16];
+      int cb = half;
+      if (cb < nch) tc::tmem_ld16(t0 + (uint32_t)(cb * 16), va);
+      while (cb < nch) {
+        tc::tmem_ld_wait16(va);
+        if (cb + 2 < nch) tc::tmem_ld16(t0 + (uint32_t)((cb + 2) * 16), vb);
+        process(va, U, cb);
+        cb += 2;
+        if (cb >= nch) break;
+        tc::tmem_ld_wait16(vb);
+        if (cb + 2 < nch) tc::tmem_ld16(t0 + (uint32_t)((cb + 2) * 16), va);
+        process(vb, U, cb);
+        cb += 2;
       }
       tc::tc_fence_before();
       __syncwarp();
@@ -351,16 +433,14 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
     }
   } else if constexpr (MODE != kRouter) {
+    if (warp >= kDqFirst) {
     // ================= dequantisers =================
-    // Two groups of 8 warps take alternate K blocks (items), so each warp has two
-    // stage-times per item.  Thread (row r, half h) converts 32 codes per item.
-    // The row's scales/biases are fetched VEC groups at a time, one vector ahead
-    // (8 K blocks of lead for VEC = 8), so no item waits on a global load.
-    const int t = threadIdx.x - 6 * 32;
-    const int grp = t >> 8;              // item parity handled by this thread
-    const int tt = t & 255;
-    const int r = tt >> 1;               // A tile row
-    const int h = tt & 1;                // which half of the 64-element K block
+    // Group g takes items k = g, g + 2, ...  Thread r converts weight row r of the
+    // A tile (64 elements = 8 packed words) per item.  The row's scales/biases
+    // come VEC groups per vector load, one vector ahead of use.
+    const int t = threadIdx.x - kDqFirst * 32;
+    const int grp = t / (kDqGroupWarps * 32);
+    const int r = t % (kDqGroupWarps * 32);  // A tile row
     int raw_row, j, f_local;
     if constexpr (MODE == kGateUp) {
       const int within = r & 31, g4 = r >> 5;
@@ -373,7 +453,6 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       raw_row = r;
     }
     const int VEC = p.scale_vec;  // 8, 4 or 1 groups per vector load
-    const int KB = p.kblocks;
     auto row_of = [&](int ui, int64_t& grow, int& wsel) -> bool {
       const int u = blockIdx.x + ui * gridDim.x;
       if (u >= total_units) return false;
@@ -425,7 +504,6 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         else load_vec(cw, cg, vid, cs, cb);
         c_ui = ui;
         c_vid = vid;
-        // prefetch the following vector of this thread's item sequence
         int pui = ui, pvid = vid + 1;
         if (pvid * VEC >= KB) { pui = ui + 1; pvid = 0; }
         int64_t pg = cg;
@@ -440,31 +518,37 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       }
       const int q = kb - vid * VEC;
       const uint16_t s16 = pick(cs, q), b16 = pick(cb, q);
-      const int item = ui * KB + kb;
-      const int stage = item % kStages;
-      const uint32_t phase = (uint32_t)(item / kStages) & 1u;
-      if (!tc::mbar_wait(&ctl.full[stage], phase, abort, p.status)) break;
-      const uint4 w4 = *reinterpret_cast<const uint4*>(stage_raw(stage) + raw_row * 32 + h * 16);
+      const int k = ui * KB + kb;
+      const int rs = slot_of(k, kRawStages), as = slot_of(k, kAStages);
+      if (!tc::mbar_wait(&ctl.raw_full[rs], full_parity(k, kRawStages), abort, p.status)) break;
+      const uint4 w0 = *reinterpret_cast<const uint4*>(raw_at(rs) + raw_row * 32);
+      const uint4 w1 = *reinterpret_cast<const uint4*>(raw_at(rs) + raw_row * 32 + 16);
       const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16(s16));
       const __nv_bfloat162 b2 = __bfloat162bfloat162(__ushort_as_bfloat16(b16));
-      uint8_t* arow = stage_a(stage) + r * 128;
-      const uint32_t ws[4] = {w4.x, w4.y, w4.z, w4.w};
+      uint4 o[8];
+      const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int c = h * 4 + i;  // logical 16-byte chunk (8 K elements)
-        *reinterpret_cast<uint4*>(arow + ((c ^ (r & 7)) << 4)) = dequant8(ws[i], s2, b2);
-      }
+      for (int i = 0; i < 8; ++i) o[i] = dequant8(ws[i], s2, b2);
+      // the raw slot is free once its words are consumed
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&ctl.raw_empty[rs]);
+      if (!tc::mbar_wait(&ctl.a_empty[as], empty_parity(k, kAStages), abort, p.status)) break;
+      uint8_t* arow = a_at(as) + r * 128;
+#pragma unroll
+      for (int i = 0; i < 8; ++i)  // logical 16-byte chunk i (8 K elements)
+        *reinterpret_cast<uint4*>(arow + ((i ^ (r & 7)) << 4)) = o[i];
       tc::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&ctl.dq[stage]);
-      kb += 2;
+      if (lane == 0) tc::mbar_arrive(&ctl.a_full[as]);
+      kb += kDqGroups;
       while (kb >= KB) { kb -= KB; ++ui; }
+    }
     }
   }
 
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 1) {
+  if (warp == kMmaWarp) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem_base, kTmemCols);
   }
@@ -532,6 +616,7 @@ int sm_count() {
 template <int MODE>
 cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
   const int threads = MODE == kRouter ? kThreadsR : kThreadsQ;
+  static_assert(kSmemBytes + sizeof(SmemCtl) <= 227 * 1024, "shared memory budget");
   static uint64_t configured[3] = {0, 0, 0};  // per-device bit
   int dev = 0;
   cudaGetDevice(&dev);
@@ -666,7 +751,7 @@ size_t moe_gemm_scratch_bytes() { return 256; }
 
 static bool bind_b(GemmParams& p, const void* rows_ptr, int64_t rows, int K) {
   return make_map(&p.tm_b, rows_ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                  (uint64_t)rows, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+                  (uint64_t)rows, 64, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 cudaError_t moe_gemm_router(const MoeGemmPlan& plan, const void* x, int64_t tokens, void* logits,

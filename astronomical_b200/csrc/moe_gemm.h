@@ -4,7 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#include "../../include/astro_moe.h"
+#include "astro_moe.h"
 
 namespace astro {
 

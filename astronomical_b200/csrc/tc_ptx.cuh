@@ -142,6 +142,16 @@ ASTRO_DEVINL void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
       : "r"(taddr));
 }
 ASTRO_DEVINL void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Wait that also ties the destination registers of the outstanding load, so the
+// compiler cannot schedule any use of them before the wait.
+ASTRO_DEVINL void tmem_ld_wait16(uint32_t (&v)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(v[0]), "+r"(v[1]), "+r"(v[2]), "+r"(v[3]), "+r"(v[4]), "+r"(v[5]),
+                 "+r"(v[6]), "+r"(v[7]), "+r"(v[8]), "+r"(v[9]), "+r"(v[10]), "+r"(v[11]),
+                 "+r"(v[12]), "+r"(v[13]), "+r"(v[14]), "+r"(v[15])
+               :
+               : "memory");
+}
 
 // Shared-memory matrix descriptor: K-major tile of 128-byte rows with the
 // 128-byte swizzle (8-row atoms of 1024 bytes), tile base 1024-byte aligned.
