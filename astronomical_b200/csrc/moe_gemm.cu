@@ -16,17 +16,21 @@
 // costs N = 144, not two 128-row tiles, and every weight tile is dequantised once
 // per unit.  A work item is one 64-wide K block (one quantisation group).
 //
-// Three decoupled shared-memory rings (per CTA, persistent, one CTA per SM):
-//   raw  (kRawStages x 4 KB)   int4 weight rows, MLX layout, by TMA    <- warp 0
-//   B    (kBStages x 24 KB)    token rows, bf16, 128-byte swizzle, TMA <- warp 2
-//   A    (kAStages x 16 KB)    dequantised weights, SW128 K-major      <- warps 12-19
-// The token-row stream is the latency-critical one (the variants that dropped
-// each stream showed it), so it gets the deepest ring, loaded in 16-row boxes so
-// only rows the MMA reads are fetched.  Two groups of 4 dequant warps take
+// Rings (per CTA, persistent, one CTA per SM):
+//   raw  smem (kRawStages x 4 KB)  int4 weight rows, MLX layout, by TMA  <- warp 0
+//   B    smem (kOpStages x 20 KB)  token rows, bf16, 128-byte swizzle, TMA <- warp 2
+//   A    TMEM (kOpStages x 32 col) dequantised weights, written with one
+//                                  tcgen05.st per row per item <- warps 12-19
+// The MMA reads A from tensor memory, so shared memory only carries the raw
+// codes and the token rows; per operand slot one full barrier (token bytes + 4
+// dequant warps) and one empty barrier (one MMA commit).
+// The token-row stream is the critical one, so it gets the deepest ring; a tile
+// is covered by the fewest 128/64/32/16-row boxes (each TMA issue has a fixed
+// cost) and only rows the MMA reads are fetched.  Two groups of 4 dequant warps take
 // alternate items (nibbles -> bf16 with bf16x2 FMAs, w = s*q + b); each thread
 // converts one 64-element weight row per item.  Warp 1 (one thread) issues
-// tcgen05.mma (M=128, N<=192, K=16) into one of two TMEM accumulators and
-// commits; warps 4-11 (two per TMEM sub-partition) drain the other accumulator:
+// tcgen05.mma (M=128, N<=160, K=16) into one of three TMEM accumulators and
+// commits; eight epilogue warps (two per TMEM sub-partition) drain the others:
 // tcgen05.ld -> SwiGLU / bf16 -> global.  For gate/up the 128 A rows hold 64
 // gate and 64 up rows, interleaved in 16-row groups so each gate row and its up
 // row land in lanes l and l+16 of the same epilogue warp (one shuffle pairs them).
@@ -49,32 +53,53 @@ enum GemmMode : int { kGateUp = 0, kDown = 1, kRouter = 2 };
 
 constexpr int kBM = 128;                  // weight rows per tile (MMA M)
 constexpr int kBK = 64;                   // K per item = one quantisation group
-constexpr int kMaxN = 192;                // token rows per tile (MMA N)
-constexpr int kBoxRows = 16;              // token rows per TMA box
+constexpr int kMaxN = 160;                // token rows per tile (MMA N)
+constexpr int kBoxRows = 16;              // granularity of token rows per TMA box
+constexpr int kBoxKinds = 4;              // token-row boxes of 128, 64, 32 and 16 rows
 constexpr int kABytes = kBM * kBK * 2;    // 16 KB bf16 A tile
-constexpr int kBBytes = kMaxN * kBK * 2;  // 24 KB bf16 B tile
+constexpr int kBBytes = kMaxN * kBK * 2;  // 20 KB bf16 B tile
 constexpr int kRawBytes = kBM * 32;       // 4 KB int4 A tile
 constexpr int kRawStages = 8;
-constexpr int kBStages = 6;
-constexpr int kAStages = 2;
-constexpr int kSmemBytes = kBStages * kBBytes + kAStages * kABytes + kRawStages * kRawBytes + 1024;
+constexpr int kOpStages = 6;              // operand slots: B tile in smem (+ A tile, see below)
+// Dequantised weights go to TMEM (A from tensor memory), so an operand slot of the
+// quantised modes is just the B tile; the router's bf16 A comes by TMA into smem.
+template <int MODE> constexpr int op_bytes() { return MODE == 2 ? kABytes + kBBytes : kBBytes; }
+template <int MODE> constexpr int smem_bytes() {
+  return kOpStages * op_bytes<MODE>() + (MODE == 2 ? 0 : kRawStages * kRawBytes) + 1024;
+}
 constexpr int kMaxSeg = 1025;
+// Warp roles.  A warp can only reach the TMEM lanes of its own SM sub-partition
+// (warp % 4), so the dequantisers, which write A rows 32*(warp%4).. into TMEM,
+// and the epilogue warps, which read accumulator rows the same way, each cover
+// all four sub-partitions.
 constexpr int kRawWarp = 0, kMmaWarp = 1, kBWarp = 2;
 constexpr int kEpiFirst = 4;       // warps 4..11: epilogue, two per TMEM sub-partition
 constexpr int kEpiWarps = 8;
 constexpr int kDqFirst = kEpiFirst + kEpiWarps;  // warps 12..19: dequantisers
 constexpr int kDqGroups = 2;       // groups taking alternate items
-constexpr int kDqGroupWarps = 4;   // 128 threads = one per A row
+constexpr int kDqGroupWarps = 4;   // one warp per sub-partition = 32 A rows each
 constexpr int kDequantWarps = kDqGroups * kDqGroupWarps;
-constexpr int kThreadsQ = (kDqFirst + kDequantWarps) * 32;  // gate/up, down
-constexpr int kThreadsR = kDqFirst * 32;                    // router (A comes by TMA)
-constexpr uint32_t kTmemCols = 512;                         // 2 accumulators x 256 columns
-static_assert(kAStages % kDqGroups == 0 && kRawStages % kDqGroups == 0, "ring/group parity");
+constexpr int kThreadsQ = (kDqFirst + kDequantWarps) * 32;
+constexpr int kThreadsR = kDqFirst * 32;  // router: no dequantisers (A comes by TMA)
+
+// epilogue: which half of the chunks (0/1) this warp drains, or -1
+ASTRO_DEVINL int epi_half(int w) {
+  return (w >= kEpiFirst && w < kEpiFirst + kEpiWarps) ? (w - kEpiFirst) / 4 : -1;
+}
+// dequant: group * 4 + warp-in-group, or -1 (warp-in-group == warp % 4)
+ASTRO_DEVINL int dq_slot(int w) { return w >= kDqFirst ? w - kDqFirst : -1; }
+constexpr int kAccs = 2;                                    // TMEM accumulators in flight
+constexpr int kAColsPerStage = kBK / 2;                     // 64 bf16 per row = 32 columns
+constexpr int kACol0 = kAccs * kMaxN;                       // first TMEM column of the A ring
+constexpr uint32_t kTmemCols = 512;
+static_assert(kACol0 + kOpStages * kAColsPerStage <= (int)kTmemCols,
+              "accumulators and the A ring must fit in TMEM");
+static_assert(kRawStages % kDqGroups == 0, "raw ring must split evenly over dequant groups");
 static_assert(kBBytes % 1024 == 0 && kABytes % 1024 == 0, "SW128 tiles need 1024-byte alignment");
 
 struct GemmParams {
   CUtensorMap tm_a[2][2];  // [routed, shared][gate|down, up] raw int4 maps; router: bf16 map
-  CUtensorMap tm_b;        // token rows, bf16, box {64, 16}, 128-byte swizzle
+  CUtensorMap tm_b[kBoxKinds];  // token rows, bf16, boxes {64, 128|64|32|16}, 128-byte swizzle
   const uint16_t* scales[2][2];
   const uint16_t* biases[2][2];
   int64_t a_row_base[2][2];   // first tensor row of expert 0 (the up half of a fused tensor: I)
@@ -101,9 +126,8 @@ struct Unit {
 
 struct SmemCtl {
   uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-  uint64_t a_full[kAStages], a_empty[kAStages];
-  uint64_t b_full[kBStages], b_empty[kBStages];
-  uint64_t tfull[2], tempty[2];
+  uint64_t op_full[kOpStages], op_empty[kOpStages];
+  uint64_t tfull[kAccs], tempty[kAccs];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
@@ -157,18 +181,18 @@ ASTRO_DEVINL int slot_of(int k, int S) { return k % S; }
 ASTRO_DEVINL uint32_t full_parity(int k, int S) { return (uint32_t)(k / S) & 1u; }
 ASTRO_DEVINL uint32_t empty_parity(int k, int S) { return ((uint32_t)(k / S) & 1u) ^ 1u; }
 
-template <int MODE>
+template <int MODE, int VEC>
 __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   __shared__ SmemCtl ctl;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* ring_b = smem;                                  // kBStages x kBBytes
-  uint8_t* ring_a = ring_b + kBStages * kBBytes;           // kAStages x kABytes
-  uint8_t* ring_raw = ring_a + kAStages * kABytes;         // kRawStages x kRawBytes
-  auto b_at = [&](int s) { return ring_b + s * kBBytes; };
-  auto a_at = [&](int s) { return ring_a + s * kABytes; };
+  constexpr int kOpBytes = op_bytes<MODE>();
+  uint8_t* ring_op = smem;                                 // kOpStages x ([A tile,] B tile)
+  uint8_t* ring_raw = ring_op + kOpStages * kOpBytes;      // kRawStages x kRawBytes
+  auto a_at = [&](int s) { return ring_op + s * kOpBytes; };           // router only
+  auto b_at = [&](int s) { return ring_op + s * kOpBytes + (kOpBytes - kBBytes); };
   auto raw_at = [&](int s) { return ring_raw + s * kRawBytes; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -176,8 +200,8 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
   const int KB = p.kblocks;
   constexpr int kFeat = (MODE == kGateUp) ? 64 : 128;  // output features per unit
 
-  // ---- setup: segment table, barriers, TMEM ----
-  if (warp == 0) {
+  // ---- setup: segment table, barriers (warp kRawWarp), TMEM (warp kMmaWarp) ----
+  if (warp == kRawWarp) {
     int carry = 0;
     for (int base = 0; base < p.nseg; base += 32) {
       const int s = base + lane;
@@ -206,21 +230,20 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         tc::mbar_init(&ctl.raw_full[s], 1);
         tc::mbar_init(&ctl.raw_empty[s], kDqGroupWarps);
       }
-      for (int s = 0; s < kAStages; ++s) {
-        tc::mbar_init(&ctl.a_full[s], MODE == kRouter ? 1 : kDqGroupWarps);
-        tc::mbar_init(&ctl.a_empty[s], 1);
+      // an operand slot is full after the token producer's expect-tx arrival
+      // (+ its bytes) and the A tile: 4 dequant warps, or the weight producer's
+      // expect-tx arrival for the router's TMA-loaded bf16 A
+      for (int s = 0; s < kOpStages; ++s) {
+        tc::mbar_init(&ctl.op_full[s], 1 + (MODE == kRouter ? 1 : kDqGroupWarps));
+        tc::mbar_init(&ctl.op_empty[s], 1);
       }
-      for (int s = 0; s < kBStages; ++s) {
-        tc::mbar_init(&ctl.b_full[s], 1);
-        tc::mbar_init(&ctl.b_empty[s], 1);
-      }
-      for (int a = 0; a < 2; ++a) {
+      for (int a = 0; a < kAccs; ++a) {
         tc::mbar_init(&ctl.tfull[a], 1);
         tc::mbar_init(&ctl.tempty[a], kEpiWarps);
       }
       tc::mbar_init(&ctl.mma_done, 1);
       tc::fence_mbar_init();
-      tc::prefetch_tmap(&p.tm_b);
+      for (int b = 0; b < kBoxKinds; ++b) tc::prefetch_tmap(&p.tm_b[b]);
       tc::prefetch_tmap(&p.tm_a[0][0]);
     }
   } else if (warp == kMmaWarp) {
@@ -246,11 +269,11 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         const int64_t e = shared ? 0 : U.seg;
         for (int kb = 0; kb < KB; ++kb, ++k) {
           if constexpr (MODE == kRouter) {
-            const int s = slot_of(k, kAStages);
-            if (!tc::mbar_wait(&ctl.a_empty[s], empty_parity(k, kAStages), abort, p.status))
+            const int s = slot_of(k, kOpStages);
+            if (!tc::mbar_wait(&ctl.op_empty[s], empty_parity(k, kOpStages), abort, p.status))
               goto raw_done;
-            tc::mbar_arrive_expect_tx(&ctl.a_full[s], (uint32_t)kABytes);
-            tc::tma_load_2d(a_at(s), &p.tm_a[0][0], kb * kBK, U.fb * kBM, &ctl.a_full[s]);
+            tc::mbar_arrive_expect_tx(&ctl.op_full[s], (uint32_t)kABytes);
+            tc::tma_load_2d(a_at(s), &p.tm_a[0][0], kb * kBK, U.fb * kBM, &ctl.op_full[s]);
           } else {
             const int s = slot_of(k, kRawStages);
             if (!tc::mbar_wait(&ctl.raw_empty[s], empty_parity(k, kRawStages), abort, p.status))
@@ -276,10 +299,10 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         // let this thread's own copies land before the CTA exits (bounded)
         int dummy = 0;
         // only the last issue of each slot can still be in flight
-        const int ring = (MODE == kRouter) ? kAStages : kRawStages;
+        const int ring = (MODE == kRouter) ? kOpStages : kRawStages;
         for (int k2 = (last_k - ring + 1 > 0 ? last_k - ring + 1 : 0); k2 <= last_k; ++k2) {
           if (MODE == kRouter)
-            tc::mbar_wait(&ctl.a_full[slot_of(k2, kAStages)], full_parity(k2, kAStages),
+            tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages)], full_parity(k2, kOpStages),
                           (volatile int*)&dummy, nullptr, 50000000ull);
           else
             tc::mbar_wait(&ctl.raw_full[slot_of(k2, kRawStages)], full_parity(k2, kRawStages),
@@ -295,31 +318,41 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
         Unit U;
         if (!decode_unit(ctl, p, u, U)) continue;
-        const int boxes = (U.nrows + kBoxRows - 1) / kBoxRows;
-        const uint32_t bytes = (uint32_t)boxes * kBoxRows * 128;
+        // cover the rows the MMA reads with the fewest boxes (each TMA issue has a
+        // fixed cost): 144 rows -> one 128-row box and one 16-row box
+        const int rows16 = (U.nrows + kBoxRows - 1) / kBoxRows * kBoxRows;
+        const uint32_t bytes = (uint32_t)rows16 * 128;
         for (int kb = 0; kb < KB; ++kb, ++k) {
-          const int s = slot_of(k, kBStages);
-          if (!tc::mbar_wait(&ctl.b_empty[s], empty_parity(k, kBStages), abort, p.status))
+          const int s = slot_of(k, kOpStages);
+          if (!tc::mbar_wait(&ctl.op_empty[s], empty_parity(k, kOpStages), abort, p.status))
             goto b_done;
-          tc::mbar_arrive_expect_tx(&ctl.b_full[s], bytes);
-          for (int c = 0; c < boxes; ++c)
-            tc::tma_load_2d(b_at(s) + c * (kBoxRows * 128), &p.tm_b, kb * kBK,
-                            U.row0 + c * kBoxRows, &ctl.b_full[s]);
+          tc::mbar_arrive_expect_tx(&ctl.op_full[s], bytes);
+          int off = 0;
+#pragma unroll
+          for (int b = 0; b < kBoxKinds; ++b) {
+            const int box = 128 >> b;
+            while (rows16 - off >= box) {
+              tc::tma_load_2d(b_at(s) + off * 128, &p.tm_b[b], kb * kBK, U.row0 + off,
+                              &ctl.op_full[s]);
+              off += box;
+            }
+          }
           last_k = k;
         }
       }
     b_done:
       if (*abort) {
         int dummy = 0;
-        for (int k2 = (last_k - kBStages + 1 > 0 ? last_k - kBStages + 1 : 0); k2 <= last_k; ++k2)
-          tc::mbar_wait(&ctl.b_full[slot_of(k2, kBStages)], full_parity(k2, kBStages),
+        for (int k2 = (last_k - kOpStages + 1 > 0 ? last_k - kOpStages + 1 : 0); k2 <= last_k; ++k2)
+          tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages)], full_parity(k2, kOpStages),
                         (volatile int*)&dummy, nullptr, 50000000ull);
       }
     }
   } else if (warp == kMmaWarp) {
     // ================= MMA issuer =================
     if (lane == 0) {
-      int k = 0;
+      int os = 0;          // operand slot of the next item
+      uint32_t oph = 0;    // its round parity
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
@@ -329,25 +362,29 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         const uint32_t idesc = tc::idesc_bf16(kBM, n);
         if (!tc::mbar_wait(&ctl.tempty[acc], acc_phase ^ 1u, abort, p.status)) break;
         tc::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
-        for (int kb = 0; kb < KB; ++kb, ++k) {
-          const int sa = slot_of(k, kAStages), sb = slot_of(k, kBStages);
-          if (!tc::mbar_wait(&ctl.a_full[sa], full_parity(k, kAStages), abort, p.status))
-            goto mma_done;
-          if (!tc::mbar_wait(&ctl.b_full[sb], full_parity(k, kBStages), abort, p.status))
-            goto mma_done;
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kMaxN);
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!tc::mbar_wait(&ctl.op_full[os], oph, abort, p.status)) goto mma_done;
           tc::tc_fence_after();
-          const uint32_t a_addr = tc::smem_u32(a_at(sa));
-          const uint32_t b_addr = tc::smem_u32(b_at(sb));
+          const uint32_t b_addr = tc::smem_u32(b_at(os));
+          if constexpr (MODE == kRouter) {
+            const uint32_t a_addr = tc::smem_u32(a_at(os));
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            tc::mma_bf16(d_tmem, tc::sdesc_sw128(a_addr + kk * 32),
-                         tc::sdesc_sw128(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-          tc::mma_commit(&ctl.a_empty[sa]);
-          tc::mma_commit(&ctl.b_empty[sb]);
+            for (int kk = 0; kk < kBK / 16; ++kk)
+              tc::mma_bf16(d_tmem, tc::sdesc_sw128(a_addr + kk * 32),
+                           tc::sdesc_sw128(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          } else {
+            const uint32_t a_tmem = tmem_base + (uint32_t)(kACol0 + os * kAColsPerStage);
+#pragma unroll
+            for (int kk = 0; kk < kBK / 16; ++kk)  // K = 16 bf16 = 8 TMEM columns per MMA
+              tc::mma_bf16_ts(d_tmem, a_tmem + (uint32_t)(kk * 8), tc::sdesc_sw128(b_addr + kk * 32),
+                              idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc::mma_commit(&ctl.op_empty[os]);
+          if (++os == kOpStages) { os = 0; oph ^= 1u; }
         }
         tc::mma_commit(&ctl.tfull[acc]);
-        if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+        if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
       }
     mma_done:
       // every MMA issued by this thread completes before TMEM is released
@@ -355,12 +392,12 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       int dummy = 0;
       tc::mbar_wait(&ctl.mma_done, 0, (volatile int*)&dummy, p.status, 200000000ull);
     }
-  } else if (warp >= kEpiFirst && warp < kEpiFirst + kEpiWarps) {
+  } else if (epi_half(warp) >= 0) {
     // ================= epilogue (TMEM -> registers -> global) =================
     // Two warps per TMEM sub-partition take alternate 16-column chunks; the
     // load of the next chunk is in flight while the current one is converted.
     const int sub = warp & 3;                    // TMEM sub-partition this warp may access
-    const int half = (warp - kEpiFirst) >> 2;    // which alternate chunks
+    const int half = epi_half(warp);             // which alternate chunks
     int acc = 0;
     uint32_t acc_phase = 0;
     auto process = [&](const uint32_t (&v)[16], const Unit& U, int cb) {
@@ -412,7 +449,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       if (!tc::mbar_wait(&ctl.tfull[acc], acc_phase, abort, p.status)) break;
       tc::tc_fence_after();
       const int nch = ((U.nrows + 15) & ~15) / 16;
-      const uint32_t t0 = tmem_base + ((uint32_t)(32 * sub) << 16) + (uint32_t)(acc * 256);
+      const uint32_t t0 = tmem_base + ((uint32_t)(32 * sub) << 16) + (uint32_t)(acc * kMaxN);
       uint32_t va[16], vb[16];
       int cb = half;
       if (cb < nch) tc::tmem_ld16(t0 + (uint32_t)(cb * 16), va);
@@ -430,17 +467,17 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&ctl.tempty[acc]);
-      if (++acc == 2) { acc = 0; acc_phase ^= 1u; }
+      if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
     }
   } else if constexpr (MODE != kRouter) {
-    if (warp >= kDqFirst) {
+    if (dq_slot(warp) >= 0) {
     // ================= dequantisers =================
     // Group g takes items k = g, g + 2, ...  Thread r converts weight row r of the
     // A tile (64 elements = 8 packed words) per item.  The row's scales/biases
     // come VEC groups per vector load, one vector ahead of use.
-    const int t = threadIdx.x - kDqFirst * 32;
-    const int grp = t / (kDqGroupWarps * 32);
-    const int r = t % (kDqGroupWarps * 32);  // A tile row
+    const int grp = dq_slot(warp) / kDqGroupWarps;
+    const int r = (warp & 3) * 32 + lane;  // A tile row = TMEM lane this thread may write
+    const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
     int raw_row, j, f_local;
     if constexpr (MODE == kGateUp) {
       const int within = r & 31, g4 = r >> 5;
@@ -452,7 +489,6 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       f_local = r;
       raw_row = r;
     }
-    const int VEC = p.scale_vec;  // 8, 4 or 1 groups per vector load
     auto row_of = [&](int ui, int64_t& grow, int& wsel) -> bool {
       const int u = blockIdx.x + ui * gridDim.x;
       if (u >= total_units) return false;
@@ -468,10 +504,10 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       const int64_t off = grow * p.groups_per_row + (int64_t)vid * VEC;
       const uint16_t* sp = p.scales[wsel][j] + off;
       const uint16_t* bp = p.biases[wsel][j] + off;
-      if (VEC == 8) {
+      if constexpr (VEC == 8) {
         vs = __ldg(reinterpret_cast<const uint4*>(sp));
         vb = __ldg(reinterpret_cast<const uint4*>(bp));
-      } else if (VEC == 4) {
+      } else if constexpr (VEC == 4) {
         const uint2 a = __ldg(reinterpret_cast<const uint2*>(sp));
         const uint2 c = __ldg(reinterpret_cast<const uint2*>(bp));
         vs = make_uint4(a.x, a.y, 0u, 0u);
@@ -487,6 +523,8 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     };
     int ui = 0, kb = grp;
     while (kb >= KB) { kb -= KB; ++ui; }
+    int rs = grp, os = grp;       // ring slots of item k = grp, grp + kDqGroups, ...
+    uint32_t rph = 0, oph = 0;    // their round parities
     int cu = -1, cw = 0;          // decoded unit of the current item
     int64_t cg = 0;
     int c_ui = -1, c_vid = -1;    // vector in use
@@ -518,30 +556,34 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       }
       const int q = kb - vid * VEC;
       const uint16_t s16 = pick(cs, q), b16 = pick(cb, q);
-      const int k = ui * KB + kb;
-      const int rs = slot_of(k, kRawStages), as = slot_of(k, kAStages);
-      if (!tc::mbar_wait(&ctl.raw_full[rs], full_parity(k, kRawStages), abort, p.status)) break;
+      if (!tc::mbar_wait(&ctl.raw_full[rs], rph, abort, p.status)) break;
       const uint4 w0 = *reinterpret_cast<const uint4*>(raw_at(rs) + raw_row * 32);
       const uint4 w1 = *reinterpret_cast<const uint4*>(raw_at(rs) + raw_row * 32 + 16);
       const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16(s16));
       const __nv_bfloat162 b2 = __bfloat162bfloat162(__ushort_as_bfloat16(b16));
-      uint4 o[8];
+      uint32_t o[32];  // 64 bf16 of row r in K order, two per TMEM column
       const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = dequant8(ws[i], s2, b2);
+      for (int i = 0; i < 8; ++i) {
+        const uint4 d = dequant8(ws[i], s2, b2);
+        o[4 * i] = d.x; o[4 * i + 1] = d.y; o[4 * i + 2] = d.z; o[4 * i + 3] = d.w;
+      }
       // the raw slot is free once its words are consumed
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&ctl.raw_empty[rs]);
-      if (!tc::mbar_wait(&ctl.a_empty[as], empty_parity(k, kAStages), abort, p.status)) break;
-      uint8_t* arow = a_at(as) + r * 128;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)  // logical 16-byte chunk i (8 K elements)
-        *reinterpret_cast<uint4*>(arow + ((i ^ (r & 7)) << 4)) = o[i];
-      tc::fence_proxy_async_smem();
+      if (!tc::mbar_wait(&ctl.op_empty[os], oph ^ 1u, abort, p.status)) break;
+      tc::tc_fence_after();
+      tc::tmem_st32(tmem_base + lane_addr + (uint32_t)(kACol0 + os * kAColsPerStage), o);
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&ctl.a_full[as]);
+      if (lane == 0) tc::mbar_arrive(&ctl.op_full[os]);
       kb += kDqGroups;
       while (kb >= KB) { kb -= KB; ++ui; }
+      rs += kDqGroups;
+      if (rs >= kRawStages) { rs -= kRawStages; rph ^= 1u; }
+      os += kDqGroups;
+      if (os >= kOpStages) { os -= kOpStages; oph ^= 1u; }
     }
     }
   }
@@ -613,25 +655,34 @@ int sm_count() {
   return n;
 }
 
-template <int MODE>
-cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
+template <int MODE, int VEC>
+cudaError_t launch_vec(const GemmParams& p, int max_units, cudaStream_t st) {
   const int threads = MODE == kRouter ? kThreadsR : kThreadsQ;
-  static_assert(kSmemBytes + sizeof(SmemCtl) <= 227 * 1024, "shared memory budget");
-  static uint64_t configured[3] = {0, 0, 0};  // per-device bit
+  constexpr int kSmem = smem_bytes<MODE>();
+  static_assert(kSmem + sizeof(SmemCtl) <= 227 * 1024, "shared memory budget");
+  static uint64_t configured = 0;  // per-device bit
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
-  if (!(configured[MODE] & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<MODE>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (!(configured & bit)) {
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<MODE, VEC>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
-    configured[MODE] |= bit;
+    configured |= bit;
   }
   int grid = sm_count();
   if (max_units < grid) grid = max_units;
   if (grid <= 0) return cudaSuccess;
-  moe_gemm_kernel<MODE><<<grid, threads, kSmemBytes, st>>>(p);
+  moe_gemm_kernel<MODE, VEC><<<grid, threads, kSmem, st>>>(p);
   return cudaGetLastError();
+}
+
+template <int MODE>
+cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
+  if constexpr (MODE == kRouter) return launch_vec<MODE, 1>(p, max_units, st);
+  if (p.scale_vec == 8) return launch_vec<MODE, 8>(p, max_units, st);
+  if (p.scale_vec == 4) return launch_vec<MODE, 4>(p, max_units, st);
+  return launch_vec<MODE, 1>(p, max_units, st);
 }
 
 }  // namespace
@@ -750,8 +801,11 @@ bool moe_gemm_enabled(const MoeGemmPlan& plan, int opt) { return plan.ok && opt 
 size_t moe_gemm_scratch_bytes() { return 256; }
 
 static bool bind_b(GemmParams& p, const void* rows_ptr, int64_t rows, int K) {
-  return make_map(&p.tm_b, rows_ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
-                  (uint64_t)rows, 64, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B);
+  bool ok = true;
+  for (int b = 0; b < kBoxKinds; ++b)
+    ok &= make_map(&p.tm_b[b], rows_ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)K,
+                   (uint64_t)rows, 64, (uint32_t)(128 >> b), CU_TENSOR_MAP_SWIZZLE_128B);
+  return ok;
 }
 
 cudaError_t moe_gemm_router(const MoeGemmPlan& plan, const void* x, int64_t tokens, void* logits,
