@@ -59,7 +59,7 @@ constexpr int kBoxKinds = 4;              // token-row boxes of 128, 64, 32 and 
 constexpr int kABytes = kBM * kBK * 2;    // 16 KB bf16 A tile
 constexpr int kBBytes = kMaxN * kBK * 2;  // 20 KB bf16 B tile
 constexpr int kRawBytes = kBM * 32;       // 4 KB int4 A tile
-constexpr int kRawStages = 8;
+constexpr int kRawStages = 8;   // multiple of kDqGroups
 constexpr int kOpStages = 6;              // operand slots: B tile in smem (+ A tile, see below)
 // Dequantised weights go to TMEM (A from tensor memory), so an operand slot of the
 // quantised modes is just the B tile; the router's bf16 A comes by TMA into smem.
@@ -76,7 +76,7 @@ constexpr int kRawWarp = 0, kMmaWarp = 1, kBWarp = 2;
 constexpr int kEpiFirst = 4;       // warps 4..11: epilogue, two per TMEM sub-partition
 constexpr int kEpiWarps = 8;
 constexpr int kDqFirst = kEpiFirst + kEpiWarps;  // warps 12..19: dequantisers
-constexpr int kDqGroups = 2;       // groups taking alternate items
+constexpr int kDqGroups = 4;       // groups taking items round robin
 constexpr int kDqGroupWarps = 4;   // one warp per sub-partition = 32 A rows each
 constexpr int kDequantWarps = kDqGroups * kDqGroupWarps;
 constexpr int kThreadsQ = (kDqFirst + kDequantWarps) * 32;
