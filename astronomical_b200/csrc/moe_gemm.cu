@@ -20,16 +20,16 @@
 //   raw  smem (kRawStages x 4 KB)  int4 weight rows, MLX layout, by TMA  <- warp 0
 //   B    smem (kOpStages x 20 KB)  token rows, bf16, 128-byte swizzle, TMA <- warp 2
 //   A    TMEM (kOpStages x 32 col) dequantised weights, written with one
-//                                  tcgen05.st per row per item <- warps 12-19
+//                                  tcgen05.st per row per item <- warps 12-27
 // The MMA reads A from tensor memory, so shared memory only carries the raw
 // codes and the token rows; per operand slot one full barrier (token bytes + 4
 // dequant warps) and one empty barrier (one MMA commit).
 // The token-row stream is the critical one, so it gets the deepest ring; a tile
 // is covered by the fewest 128/64/32/16-row boxes (each TMA issue has a fixed
-// cost) and only rows the MMA reads are fetched.  Two groups of 4 dequant warps take
-// alternate items (nibbles -> bf16 with bf16x2 FMAs, w = s*q + b); each thread
+// cost) and only rows the MMA reads are fetched.  Four groups of 4 dequant warps take
+// items round robin (nibbles -> bf16 with bf16x2 FMAs, w = s*q + b); each thread
 // converts one 64-element weight row per item.  Warp 1 (one thread) issues
-// tcgen05.mma (M=128, N<=160, K=16) into one of three TMEM accumulators and
+// tcgen05.mma (M=128, N<=160, K=16) into one of two TMEM accumulators and
 // commits; eight epilogue warps (two per TMEM sub-partition) drain the others:
 // tcgen05.ld -> SwiGLU / bf16 -> global.  For gate/up the 128 A rows hold 64
 // gate and 64 up rows, interleaved in 16-row groups so each gate row and its up
@@ -75,7 +75,7 @@ constexpr int kMaxSeg = 1025;
 constexpr int kRawWarp = 0, kMmaWarp = 1, kBWarp = 2;
 constexpr int kEpiFirst = 4;       // warps 4..11: epilogue, two per TMEM sub-partition
 constexpr int kEpiWarps = 8;
-constexpr int kDqFirst = kEpiFirst + kEpiWarps;  // warps 12..19: dequantisers
+constexpr int kDqFirst = kEpiFirst + kEpiWarps;  // warps 12..27: dequantisers
 constexpr int kDqGroups = 4;       // groups taking items round robin
 constexpr int kDqGroupWarps = 4;   // one warp per sub-partition = 32 A rows each
 constexpr int kDequantWarps = kDqGroups * kDqGroupWarps;

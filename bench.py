@@ -239,16 +239,24 @@ def run_ours(args):
                                              "gate_up_ms", "down_ms", "weighted_reduction_ms")}
     rows = T * K + (T if Is else 0)
     flops_gate_up = 2.0 * rows * H * 2 * I
+    segs = E + (1 if Is else 0)  # expert segments the gate/up GEMM reads (+ shared)
+    bytes_gate_up = (segs * 2 * I * H // 2 + segs * 2 * I * (H // 64) * 2 * 2
+                     + rows * H * 2 + rows * I * 2)
     flops_block = 2.0 * T * K * 3 * H * I + 2.0 * T * 3 * H * Is + 2.0 * T * H * E + 2.0 * T * H
     peaks, kind = load_peaks()
     gu_s = stage_ms["gate_up_ms"] / 1e3
     achieved = flops_gate_up / gu_s / 1e12 if gu_s > 0 else 0.0
     peak = float(peaks["bf16_tflops"])
     traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
+    # DRAM bytes (read + write) of one gate/up launch from the committed ncu
+    # capture of this workload
+    tp = os.path.join(ROOT, "profiles", "moe_gemm_config1_t4096_traffic.txt")
+    if os.path.exists(tp) and T == 4096:
         with open(tp) as f:
-            traffic = json.load(f).get("gate_up_bytes_per_launch")
+            for line in f:
+                key, _, val = line.partition(" ")
+                if key == "gate_up_bytes_per_launch":
+                    traffic = int(val)
 
     # e2e through the host-buffer entry point
     hx = x.cpu().pin_memory()
@@ -283,7 +291,8 @@ def run_ours(args):
                      "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                      "frac": achieved / peak if peak else None, "peak_kind": f"{kind} burst",
                      "traffic": traffic,
-                     "algorithmic_flop_per_launch": flops_gate_up},
+                     "algorithmic_flop_per_launch": flops_gate_up,
+                     "algorithmic_bytes_per_launch": bytes_gate_up},
         "block_tflops": flops_block / (ms / 1e3) / 1e12 * world,
         "stages_ms": stage_ms,
         "clocks": clk,
