@@ -77,6 +77,8 @@ SIGNATURES = {
     "astro_moe_route_experts": ([_P, _I32, _I64, _I32, _I32, _I32, _P, _P, _P], ctypes.c_int),
     "astro_moe_sort_expert_assignments": ([_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P],
                                           ctypes.c_int),
+    "astro_moe_sort_expert_assignments_no_alloc": (
+        [_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P], ctypes.c_int),
     "astro_moe_take_rows": ([_P, _I64, _I32, _P, _I64, _P, _P], ctypes.c_int),
     "astro_moe_gather_qmm": ([_P, _I64, _I32, _P, _P, _I64, _P, _P, _P, _I32, _I32, _I32, _I32,
                               _I32, _P, _P], ctypes.c_int),

@@ -360,6 +360,11 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
 
 }  // namespace
 
+int astro::set_last_error(int status, const char* message) {
+  g_last_error = message;
+  return status;
+}
+
 extern "C" {
 
 const char* astro_moe_last_error(void) { return g_last_error.c_str(); }

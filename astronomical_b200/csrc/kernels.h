@@ -81,4 +81,8 @@ cudaError_t launch_offsets_from_sorted(const uint32_t* ids, int64_t n, int E, ui
 cudaError_t launch_compose_rows(const uint32_t* lhs, const uint32_t* order, int64_t n,
                                 uint32_t* rows_out, cudaStream_t st);
 
+// Sets the calling thread's astro_moe_last_error() message and returns `status`
+// (for entry points defined outside api.cu).
+int set_last_error(int status, const char* message);
+
 }  // namespace astro

@@ -88,6 +88,29 @@ int astro_moe_sort_expert_assignments(const uint32_t* selected_indices, int64_t 
                                       uint32_t* sorted_tokens, uint32_t* expert_offsets,
                                       void* stream);
 
+/* No counterpart in the reference.  The same sort for callers that cannot
+ * allocate device memory: a process whose own caching allocator has reserved
+ * all of HBM (cudaMalloc/cudaMallocAsync would fail), or a latency-bound loop
+ * that cannot accept the device synchronisation cudaMalloc/cudaFree may cause.
+ * Outputs equal astro_moe_sort_expert_assignments's.  Its scratch is a fixed
+ * ASTRO_MOE_NO_ALLOC_SCRATCH_BYTES (256 KiB) device array per GPU, kept until
+ * the process exits: a call needs 4*experts*ceil(tokens*top_k/2048) bytes, plus
+ * 4*(experts+1) when expert_offsets is NULL, and larger calls fail with
+ * ASTRO_MOE_ERR_UNSUPPORTED before any work is queued.  Nothing in the array
+ * must start at zero.  All calls on a device share the array: calls whose
+ * kernels overlap on the GPU race, so order them on one stream.  The first call
+ * on each device (with that device current) looks up the array's device address
+ * once; make that first call before any stream capture.  device_status is an
+ * optional caller-owned device word that receives ASTRO_MOE_DEVICE_BAD_EXPERT_ID
+ * (OR'ed in) for ids >= experts; NULL records nothing.  Such ids are skipped. */
+#define ASTRO_MOE_NO_ALLOC_SCRATCH_BYTES 262144
+int astro_moe_sort_expert_assignments_no_alloc(const uint32_t* selected_indices, int64_t tokens,
+                                               int32_t top_k, int32_t experts,
+                                               uint32_t* sorted_order, uint32_t* inverse_order,
+                                               uint32_t* sorted_indices, uint32_t* sorted_tokens,
+                                               uint32_t* expert_offsets, uint32_t* device_status,
+                                               void* stream);
+
 /* take_axis(states, rows, 0), crates/runtime-integration/src/mlx_shape_operations.rs:34
  * as used at assignment_sort.rs:88: out[p] = states[rows[p]] (bf16 rows of
  * `hidden` elements, hidden % 8 == 0). */
