@@ -34,7 +34,8 @@ class AstroMoeError(RuntimeError):
 
 class Options(ctypes.Structure):
     _fields_ = [("max_tokens", ctypes.c_int64), ("sorted_threshold", ctypes.c_int32),
-                ("use_tensor_cores", ctypes.c_int32), ("reserved", ctypes.c_int64 * 6)]
+                ("use_tensor_cores", ctypes.c_int32), ("decode_max_tokens", ctypes.c_int64),
+                ("decode_fused", ctypes.c_int64), ("reserved", ctypes.c_int64 * 4)]
 
 
 class Affine(ctypes.Structure):

@@ -100,6 +100,8 @@ struct LayerState {
   astro_moe_layer_weights w{};
   bool registered = false;
   astro::MoeGemmPlan gemm{};  // tensor-core plan (TMA descriptors), when eligible
+  bool decode_ok = false;     // the small-batch GEMVs cover this layer's geometry
+  bool router_gemv_ok = false;
 };
 
 struct astro_moe_ctx {
@@ -124,6 +126,7 @@ struct astro_moe_ctx {
 namespace {
 
 struct BlockWorkspace {
+  uint32_t* barrier;  // fused decode grid barrier; first in the workspace (fixed address)
   uint16_t* logits;
   uint32_t* ids;
   uint16_t* scores;
@@ -155,6 +158,7 @@ size_t plan_workspace(const astro_moe_layer_weights& w, int64_t T, BlockWorkspac
     return p;
   };
   BlockWorkspace b{};
+  b.barrier = (uint32_t*)take(2 * sizeof(uint32_t));
   b.logits = (uint16_t*)take(sizeof(uint16_t) * T * E);
   b.ids = (uint32_t*)take(sizeof(uint32_t) * N);
   b.scores = (uint16_t*)take(sizeof(uint16_t) * N);
@@ -183,6 +187,8 @@ int ensure_ws(astro_moe_ctx* ctx, size_t bytes) {
   }
   CK(cudaMalloc(&ctx->ws, bytes), "cudaMalloc(workspace)");
   ctx->ws_bytes = bytes;
+  // the fused decode kernel's barrier words (workspace offset 0) start at zero
+  CK(cudaMemset(ctx->ws, 0, 256), "cudaMemset(workspace barrier)");
   return ASTRO_MOE_OK;
 }
 
@@ -226,12 +232,68 @@ struct StageMarks {
     cudaEventRecord(e, ctx->stream);
     ev.push_back(e);
   }
+  // forgets the last n marks (recorded before a launch that did not happen)
+  void drop(size_t n) {
+    while (n-- > 0 && !ev.empty()) {
+      ctx->event_pool.push_back(ev.back());
+      ev.pop_back();
+    }
+  }
   void commit() {
     if (ctx->attribution && ev.size() == 6) ctx->pending.push_back(ev);
     else for (auto e : ev) ctx->event_pool.push_back(e);
     ev.clear();
   }
 };
+
+// Stacked projections of a layer as row views: [routed, shared] gate, up, down.
+void fill_projections(const astro_moe_layer_weights& w, astro::AffineRef (&gate)[2],
+                      astro::AffineRef (&up)[2], astro::AffineRef (&down)[2]) {
+  const int64_t I = w.intermediate, Is = w.shared_intermediate, H = w.hidden;
+  if (w.gate_up_fused) {
+    gate[0] = astro::AffineRef{w.gate.packed, w.gate.scales, w.gate.biases, 2 * I, 0};
+    up[0] = astro::AffineRef{w.gate.packed, w.gate.scales, w.gate.biases, 2 * I, I};
+  } else {
+    gate[0] = astro::AffineRef{w.gate.packed, w.gate.scales, w.gate.biases, I, 0};
+    up[0] = astro::AffineRef{w.up.packed, w.up.scales, w.up.biases, I, 0};
+  }
+  down[0] = astro::AffineRef{w.down.packed, w.down.scales, w.down.biases, H, 0};
+  gate[1] = up[1] = down[1] = astro::AffineRef{};
+  if (Is > 0) {
+    gate[1] = astro::AffineRef{w.shared_gate.packed, w.shared_gate.scales, w.shared_gate.biases, Is, 0};
+    up[1] = astro::AffineRef{w.shared_up.packed, w.shared_up.scales, w.shared_up.biases, Is, 0};
+    down[1] = astro::AffineRef{w.shared_down.packed, w.shared_down.scales, w.shared_down.biases, H, 0};
+  }
+}
+
+// Copies the requested intermediate arrays of a block call to the caller's taps.
+int copy_taps(astro_moe_ctx* ctx, const BlockWorkspace& b, int64_t T, int E, int K,
+              bool has_shared, const astro_moe_block_taps* taps) {
+  if (!taps) return ASTRO_MOE_OK;
+  cudaStream_t st = ctx->stream;
+  const int64_t N = T * K;
+  {
+    if (taps->router_logits)
+      CK(cudaMemcpyAsync(taps->router_logits, b.logits, sizeof(uint16_t) * T * E,
+                         cudaMemcpyDeviceToDevice, st), "taps");
+    if (taps->selected_indices)
+      CK(cudaMemcpyAsync(taps->selected_indices, b.ids, sizeof(uint32_t) * N,
+                         cudaMemcpyDeviceToDevice, st), "taps");
+    if (taps->selected_scores)
+      CK(cudaMemcpyAsync(taps->selected_scores, b.scores, sizeof(uint16_t) * N,
+                         cudaMemcpyDeviceToDevice, st), "taps");
+    if (taps->expert_offsets)
+      CK(cudaMemcpyAsync(taps->expert_offsets, b.offsets,
+                         sizeof(uint32_t) * (E + (has_shared ? 2 : 1)), cudaMemcpyDeviceToDevice, st),
+         "taps");
+  }
+  return ASTRO_MOE_OK;
+}
+
+// batches up to this many tokens take the decode GEMVs unless the options say otherwise
+constexpr int64_t kDefaultDecodeTokens = 8;
+// batches up to this many tokens compute router logits with the router GEMV
+constexpr int64_t kRouterGemvTokens = 64;
 
 int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void* out,
               const astro_moe_block_taps* taps) {
@@ -253,10 +315,65 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   StageMarks marks(ctx);
   marks.mark();
   // a1: router projection
-  const bool use_tc = astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores) &&
-                      (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-  ctx->launches += use_tc ? 8 : 7;
-  if (use_tc) {
+  const bool x_aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  const int64_t decode_max = ctx->opt.decode_max_tokens == 0 ? kDefaultDecodeTokens
+                                                             : ctx->opt.decode_max_tokens;
+  // small batches: GEMVs over the active experts (HBM-bound); otherwise the
+  // tcgen05 grouped GEMMs, or the CUDA-core grouped GEMV when those are off
+  const bool use_decode = decode_max > 0 && T <= decode_max && x_aligned && L.decode_ok;
+  const bool use_tc = !use_decode && astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores) &&
+                      x_aligned;
+  const bool router_gemv = T <= kRouterGemvTokens && x_aligned && L.router_gemv_ok;
+  const bool try_fused = use_decode && ctx->opt.decode_fused >= 0 &&
+                         astro::decode_fused_supported((int)T, H, E, K, I) &&
+                         w.shared_intermediate == (has_shared ? I : 0);
+  if (try_fused) {
+    astro::DecodeFusedArgs a;
+    a.x = x;
+    a.T = (int)T;
+    a.H = H;
+    a.E = E;
+    a.K = K;
+    a.I = I;
+    a.normalize = w.normalize_top_k;
+    a.sorted = sorted_semantics ? 1 : 0;
+    a.has_shared = has_shared ? 1 : 0;
+    a.wr = w.router_weight;
+    a.wg = w.shared_expert_gate;
+    fill_projections(w, a.gate, a.up, a.down);
+    a.logits = b.logits;
+    a.gate_logit = b.gate_logit;
+    a.ids = b.ids;
+    a.scores = b.scores;
+    a.offsets = b.offsets;
+    a.act = b.act;
+    a.yrows = b.yrows;
+    a.out = out;
+    a.barrier = b.barrier;
+    a.status = ctx->status;
+    // one kernel: its whole time is reported under gate_up_ms
+    marks.mark();
+    marks.mark();
+    const cudaError_t e = astro::launch_decode_fused(a, st);
+    if (e == cudaSuccess) {
+      ctx->launches += 1;
+      marks.mark();
+      marks.mark();
+      marks.mark();
+      marks.commit();
+      if (ctx->attribution) ctx->acc.calls += 1;
+      return copy_taps(ctx, b, T, E, K, has_shared, taps);
+    }
+    if (e != cudaErrorCooperativeLaunchTooLarge && e != cudaErrorNotSupported) {
+      return cuda_fail(e, "fused decode block");
+    }
+    cudaGetLastError();  // the device cannot co-schedule the grid: unfused kernels below
+    marks.drop(2);
+  }
+  ctx->launches += 3 + astro::sort_launch_count(N) + (use_tc ? 3 : 2);
+  if (router_gemv) {
+    CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, b.logits, st), "router projection");
+  } else if (use_tc) {
     CK(astro::moe_gemm_router(L.gemm, x, T, b.logits, b.gemm_scratch, ctx->status, st),
        "router projection");
   } else {
@@ -286,7 +403,8 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
        "down projection");
   } else {
     marks.mark();
-    // a4-a6 on CUDA cores (grouped GEMV tiles); the shared expert is segment E
+    // a4-a6 on CUDA cores: the decode GEMVs, or the grouped GEMV tiles; the shared
+    // expert is segment E
     astro::GroupedGemvDesc d;
     d.x = x;
     d.x_rows = b.stok;
@@ -315,7 +433,12 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     d.y_limit = rows;
     d.ldy = I;
     d.status = ctx->status;
-    CK(astro::launch_grouped_gemv(d, st), "gate/up projection");
+    const int64_t max_active = (N < E ? N : E) + (has_shared ? 1 : 0);
+    if (use_decode) {
+      CK(astro::launch_decode_gate_up(d, max_active, st), "gate/up projection");
+    } else {
+      CK(astro::launch_grouped_gemv(d, st), "gate/up projection");
+    }
     marks.mark();
     astro::GroupedGemvDesc dd = d;
     dd.x = b.act;
@@ -330,7 +453,11 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     dd.swiglu = false;
     dd.y = b.yrows;
     dd.ldy = H;
-    CK(astro::launch_grouped_gemv(dd, st), "down projection");
+    if (use_decode) {
+      CK(astro::launch_decode_down(dd, max_active, st), "down projection");
+    } else {
+      CK(astro::launch_grouped_gemv(dd, st), "down projection");
+    }
   }
   marks.mark();
   // a7 + a8: weighted sum fused with the shared expert and its gate
@@ -340,22 +467,7 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   marks.mark();
   marks.commit();
   if (ctx->attribution) ctx->acc.calls += 1;
-  if (taps) {
-    if (taps->router_logits)
-      CK(cudaMemcpyAsync(taps->router_logits, b.logits, sizeof(uint16_t) * T * E,
-                         cudaMemcpyDeviceToDevice, st), "taps");
-    if (taps->selected_indices)
-      CK(cudaMemcpyAsync(taps->selected_indices, b.ids, sizeof(uint32_t) * N,
-                         cudaMemcpyDeviceToDevice, st), "taps");
-    if (taps->selected_scores)
-      CK(cudaMemcpyAsync(taps->selected_scores, b.scores, sizeof(uint16_t) * N,
-                         cudaMemcpyDeviceToDevice, st), "taps");
-    if (taps->expert_offsets)
-      CK(cudaMemcpyAsync(taps->expert_offsets, b.offsets,
-                         sizeof(uint32_t) * (E + (has_shared ? 2 : 1)), cudaMemcpyDeviceToDevice, st),
-         "taps");
-  }
-  return ASTRO_MOE_OK;
+  return copy_taps(ctx, b, T, E, K, has_shared, taps);
 }
 
 }  // namespace
@@ -675,6 +787,15 @@ int astro_moe_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_moe_
     L.registered = false;
     return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);
   }
+  auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  bool weights_aligned = aligned16(w->gate.packed) && aligned16(w->down.packed) &&
+                         (w->gate_up_fused || aligned16(w->up.packed));
+  if (w->shared_intermediate > 0)
+    weights_aligned = weights_aligned && aligned16(w->shared_gate.packed) &&
+                      aligned16(w->shared_up.packed) && aligned16(w->shared_down.packed);
+  L.decode_ok = weights_aligned &&
+                astro::decode_gemv_supported(w->hidden, w->intermediate, w->group_size, w->bits);
+  L.router_gemv_ok = aligned16(w->router_weight) && astro::router_gemv_supported(w->hidden);
   return ASTRO_MOE_OK;
 }
 

@@ -11,6 +11,7 @@
 //   out = bf16(sparse + bf16(shared * bf16(sigmoid(gate_logit)))).
 // Every step rounds where MLX's dtypes round, so the result depends on the
 // expert rows only through their bf16 values: deterministic, no atomics.
+#include "combine_dev.cuh"
 #include "common.cuh"
 #include "kernels.h"
 
@@ -18,55 +19,28 @@ namespace astro {
 
 // Block path: rows bf16 [*, H]; per token t, the K routed rows are found through
 // `inverse` (slot -> row), the shared row is shared_base + t.  8 elements per
-// thread, 16-byte loads.
+// thread, 16-byte loads.  The token's slot rows and scores are staged in shared
+// memory first and combine_chunk issues the row loads of 8 slots before using
+// any, so a token costs two dependent memory round trips, not 2K.
 __global__ void __launch_bounds__(256) block_combine_kernel(
     const uint4* __restrict__ rows, const uint32_t* __restrict__ inverse,
     const __nv_bfloat16* __restrict__ scores, const __nv_bfloat16* __restrict__ gate_logit,
     int64_t shared_base, int64_t tokens, int K, int H, int sorted, uint4* __restrict__ out) {
+  __shared__ uint32_t s_row[32];
+  __shared__ float s_score[32];
   const int chunks = H >> 3;
   for (int64_t t = blockIdx.x; t < tokens; t += gridDim.x) {
+    if (threadIdx.x < K) {
+      s_row[threadIdx.x] = __ldg(inverse + t * K + threadIdx.x);
+      s_score[threadIdx.x] = __bfloat162float(scores[t * K + threadIdx.x]);
+    }
     float sg = 0.f;
     if (gate_logit) sg = round_bf16(sigmoid_mlx(__bfloat162float(gate_logit[t])));
-    for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-      float acc[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-      for (int k = 0; k < K; ++k) {
-        const int64_t a = t * K + k;
-        const uint32_t r = __ldg(inverse + a);
-        const float s = __bfloat162float(scores[a]);
-        const uint4 v = rows[(int64_t)r * chunks + c];
-        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
-          if (sorted) {
-            acc[2 * j] = __fmaf_rn(lo, s, acc[2 * j]);
-            acc[2 * j + 1] = __fmaf_rn(hi, s, acc[2 * j + 1]);
-          } else {
-            acc[2 * j] = __fadd_rn(acc[2 * j], round_bf16(__fmul_rn(lo, s)));
-            acc[2 * j + 1] = __fadd_rn(acc[2 * j + 1], round_bf16(__fmul_rn(hi, s)));
-          }
-        }
-      }
-      uint32_t o[4];
-      if (gate_logit) {
-        const uint4 v = rows[(shared_base + t) * chunks + c];
-        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float lo = __uint_as_float(vv[j] << 16), hi = __uint_as_float(vv[j] & 0xffff0000u);
-          const float y0 = __fadd_rn(round_bf16(acc[2 * j]), round_bf16(__fmul_rn(lo, sg)));
-          const float y1 = __fadd_rn(round_bf16(acc[2 * j + 1]), round_bf16(__fmul_rn(hi, sg)));
-          o[j] = (uint32_t)f32_to_bf16(y0) | ((uint32_t)f32_to_bf16(y1) << 16);
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-          o[j] = (uint32_t)f32_to_bf16(acc[2 * j]) | ((uint32_t)f32_to_bf16(acc[2 * j + 1]) << 16);
-      }
-      out[t * chunks + c] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < chunks; c += blockDim.x)
+      out[t * chunks + c] = combine_chunk(rows, chunks, c, s_row, s_score, K, sorted != 0,
+                                          gate_logit ? shared_base + t : -1, sg);
+    __syncthreads();  // s_row / s_score are rewritten for the next token
   }
 }
 

@@ -1,0 +1,980 @@
+// decode.cu -- the small-batch (decode) kernels of the MoE block: a router GEMV
+// and the gathered int4 gate/up (+SwiGLU) and down GEMVs over the active experts.
+//
+// At decode batch sizes (config 2: T in {1, 4, 16, 64}) each routed expert sees a
+// handful of token rows, so the block is bound by streaming the selected experts'
+// weights from HBM (1,769,472 B per expert) and by fixed per-launch latency, not
+// by MMA throughput.  These kernels therefore:
+//   * stream each weight row exactly once with 128-bit coalesced loads that skip
+//     L1 (a warp reads 512 contiguous bytes per instruction);
+//   * dequantise in registers (MLX affine int4, group 64: w = bf16(s*q + b), the
+//     same rounded weight the oracle and the tensor-core path use) and
+//     accumulate in fp32, reducing across lanes with warp shuffles;
+//   * visit only non-empty expert segments: every block compacts the expert
+//     offsets into a list of active segments in shared memory, so the grid can be
+//     sized for the worst case without launching a block per idle expert;
+//   * read token rows through the sorted-token indirection (no row gather).
+// Semantics are gather_qmm's (mlx_quantized_operations.rs:100-157) and the
+// router projection's (qwen3_5_moe/model/forward.rs:52-93); the accumulation
+// order is defined here (lane-strided partial sums, butterfly reduction), so
+// outputs match the oracle to the block tolerance, not bit for bit.
+#include "combine_dev.cuh"
+#include "common.cuh"
+#include "kernels.h"
+#include "route_dev.cuh"
+
+namespace astro {
+namespace {
+
+constexpr int kThreads = 256;      // router blocks
+constexpr int kWarps = kThreads / 32;
+constexpr int kGemvThreads = 512;  // GEMV blocks: one per SM, 16 warps
+constexpr int kGemvWarps = kGemvThreads / 32;
+constexpr int kMaxSegs = 1025;  // 1024 routed experts + the shared expert
+constexpr int kRouterTokens = 8;  // tokens per router block
+
+// Weights are read once: bypass L1.
+ASTRO_DEVINL uint4 ld_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+ASTRO_DEVINL uint4 ld_cached(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+ASTRO_DEVINL float lo_f(uint32_t v) { return __uint_as_float(v << 16); }
+ASTRO_DEVINL float hi_f(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// 8 bf16 in a uint4 -> fp32
+ASTRO_DEVINL void bf16x8_to_f32(const uint4& v, float (&f)[8]) {
+  f[0] = lo_f(v.x); f[1] = hi_f(v.x); f[2] = lo_f(v.y); f[3] = hi_f(v.y);
+  f[4] = lo_f(v.z); f[5] = hi_f(v.z); f[6] = lo_f(v.w); f[7] = hi_f(v.w);
+}
+
+// One packed word (8 nibbles, element i at bits 4i) -> 4 bf16x2 pairs
+// (element i, element i + 4) of w = bf16(s * q + b).
+ASTRO_DEVINL void dequant_word(uint32_t v, __nv_bfloat162 s2, __nv_bfloat162 b2,
+                               uint32_t (&out)[4]) {
+  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t t = ((v >> (4 * i)) & 0x000f000fu) | 0x43004300u;  // bf16 (128 + q)
+    __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&t), k128);
+    __nv_bfloat162 w = __hfma2(q, s2, b2);
+    out[i] = *reinterpret_cast<uint32_t*>(&w);
+  }
+}
+
+// 32 consecutive elements (a uint4 of packed words) -> 16 bf16x2 pairs; pair
+// 4c + i holds elements (8c + i, 8c + i + 4).
+ASTRO_DEVINL void dequant32(const uint4& q, uint16_t s, uint16_t b, uint32_t (&w)[16]) {
+  const __nv_bfloat162 s2 = __halves2bfloat162(__ushort_as_bfloat16(s), __ushort_as_bfloat16(s));
+  const __nv_bfloat162 b2 = __halves2bfloat162(__ushort_as_bfloat16(b), __ushort_as_bfloat16(b));
+  uint32_t t[4];
+  dequant_word(q.x, s2, b2, t);
+  w[0] = t[0]; w[1] = t[1]; w[2] = t[2]; w[3] = t[3];
+  dequant_word(q.y, s2, b2, t);
+  w[4] = t[0]; w[5] = t[1]; w[6] = t[2]; w[7] = t[3];
+  dequant_word(q.z, s2, b2, t);
+  w[8] = t[0]; w[9] = t[1]; w[10] = t[2]; w[11] = t[3];
+  dequant_word(q.w, s2, b2, t);
+  w[12] = t[0]; w[13] = t[1]; w[14] = t[2]; w[15] = t[3];
+}
+
+// acc += sum over the 8 elements of chunk c of w * x
+ASTRO_DEVINL float dot8(const uint32_t (&w)[16], int c, const float (&x)[8], float acc) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t p = w[4 * c + i];
+    acc = __fmaf_rn(lo_f(p), x[i], acc);
+    acc = __fmaf_rn(hi_f(p), x[i + 4], acc);
+  }
+  return acc;
+}
+
+ASTRO_DEVINL float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+ASTRO_DEVINL float half_warp_sum(float v) {
+#pragma unroll
+  for (int m = 8; m > 0; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+// Compacts the non-empty segments of offsets[0..nseg] (ascending) into `list`;
+// returns their count.  Called by every thread of the block.
+template <int NT>
+ASTRO_DEVINL int active_segments(const uint32_t* __restrict__ offsets, int nseg, uint16_t* list,
+                                 int* warp_cnt) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int base = 0;
+  for (int s0 = 0; s0 < nseg; s0 += NT) {
+    const int s = s0 + threadIdx.x;
+    const bool ne = s < nseg && offsets[s + 1] > offsets[s];
+    const uint32_t bal = __ballot_sync(0xffffffffu, ne);
+    if (lane == 0) warp_cnt[w] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int i = 0; i < NT / 32; ++i) {
+      const int c = warp_cnt[i];
+      before += i < w ? c : 0;
+      total += c;
+    }
+    if (ne) list[base + before + __popc(bal & lanemask_lt())] = (uint16_t)s;
+    base += total;
+    __syncthreads();
+  }
+  return base;
+}
+
+// ---------------------------------------------------------------------------
+// router: logits[t, e] = bf16(x_t . Wr[e]); block = 8 experts x 8 tokens, the
+// tokens' rows staged in shared memory, one warp per expert row.
+template <int J>  // H = 256 * J
+__global__ void __launch_bounds__(kThreads) router_gemv_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t T, const __nv_bfloat16* __restrict__ wr, int E,
+    __nv_bfloat16* __restrict__ logits) {
+  constexpr int H = 256 * J;
+  constexpr int kRowVec = H / 8;  // uint4 per row
+  extern __shared__ uint4 xs[];   // [kRouterTokens][kRowVec]
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t t0 = (int64_t)blockIdx.y * kRouterTokens;
+  const int nt = (int)(T - t0 < kRouterTokens ? T - t0 : kRouterTokens);
+  const uint4* xsrc = reinterpret_cast<const uint4*>(x + t0 * H);
+  for (int i = threadIdx.x; i < nt * kRowVec; i += kThreads) xs[i] = ld_cached(xsrc + i);
+  __syncthreads();
+  const int e = blockIdx.x * kWarps + w;
+  if (e >= E) return;
+  uint4 wv[J];
+  const uint4* wrow = reinterpret_cast<const uint4*>(wr + (int64_t)e * H);
+#pragma unroll
+  for (int j = 0; j < J; ++j) wv[j] = ld_stream(wrow + j * 32 + lane);
+  float acc[kRouterTokens];
+#pragma unroll
+  for (int t = 0; t < kRouterTokens; ++t) acc[t] = 0.0f;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    float wf[8];
+    bf16x8_to_f32(wv[j], wf);
+#pragma unroll
+    for (int t = 0; t < kRouterTokens; ++t) {
+      if (t < nt) {
+        float xf[8];
+        bf16x8_to_f32(xs[t * kRowVec + j * 32 + lane], xf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(wf[i], xf[i], acc[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < kRouterTokens; ++t) {
+    if (t < nt) {
+      const float v = warp_sum(acc[t]);
+      if (lane == 0) logits[(t0 + t) * E + e] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Token rows of the current segment are staged in shared memory, kRowChunk rows
+// per pass.  Lane l reads 16-byte chunks 4l..4l+3 of a 1024-element (or
+// 512-element) step, so 8 lanes of one access phase would hit two bank groups;
+// storing chunk q at q ^ ((q >> 3) & 7) spreads them over all eight.
+constexpr int kRowChunk = 8;
+constexpr int kRowChunkGU = 4;  // gate/up: fewer accumulators, no register spills
+
+ASTRO_DEVINL int swz(int q) { return q ^ ((q >> 3) & 7); }
+
+// Cooperative copy of rows p .. p+n-1 (row index through `rows` when given) of
+// a bf16 matrix with `vecs` uint4 per row into xs[n][vecs] (swizzled).  Rows
+// outside [0, limit) record kDevBadShape and are read as row 0.
+ASTRO_DEVINL void stage_rows(uint4* xs, const uint4* __restrict__ src, const uint32_t* rows,
+                             uint32_t p, int n, int vecs, int64_t limit, uint32_t* status) {
+  for (int i = threadIdx.x; i < n * vecs; i += kGemvThreads) {
+    const int j = i / vecs, q = i - j * vecs;
+    int64_t r = rows ? (int64_t)rows[p + j] : (int64_t)(p + j);
+    if (r >= limit) {
+      record_status(status, kDevBadShape);
+      r = 0;
+    }
+    xs[j * vecs + swz(q)] = ld_cached(src + r * vecs + q);
+  }
+}
+
+// Packed codes and scales of one lane's share of a weight row: STEPS 16-byte
+// code vectors and, per step, (scale | bias << 16).
+template <int STEPS> struct RowRegs {
+  uint4 q[STEPS];
+  uint32_t sb[STEPS];
+};
+
+// Issues the loads of one row share (nothing waits on them until use).
+template <int STEPS>
+ASTRO_DEVINL void load_row(RowRegs<STEPS>& r, const AffineRef& W, int64_t row, int words,
+                           int groups, int qoff, int goff, int qstride, int gstride) {
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(W.q) + row * words + qoff;
+  const uint16_t* ps = reinterpret_cast<const uint16_t*>(W.s) + row * groups + goff;
+  const uint16_t* pb = reinterpret_cast<const uint16_t*>(W.b) + row * groups + goff;
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s) r.q[s] = ld_stream(q + s * qstride);
+#pragma unroll
+  for (int s = 0; s < STEPS; ++s)
+    r.sb[s] = (uint32_t)__ldg(ps + s * gstride) | ((uint32_t)__ldg(pb + s * gstride) << 16);
+}
+
+// gate/up + SwiGLU.  Item = (active segment, 16 consecutive features); warp w
+// owns feature f = base + w: its gate row and up row.  Lane l holds elements
+// [1024 s + 32 l, +32) of a row, inside quantisation group 16 s + l / 2.  The
+// next item's codes are loaded while the current one is computed.
+template <int STEPS>  // in_features = 1024 * STEPS
+__global__ void __launch_bounds__(kGemvThreads, 1) decode_gate_up_kernel(GroupedGemvDesc d) {
+  extern __shared__ uint4 xs[];  // [kRowChunkGU][H / 8]
+  __shared__ uint16_t list[kMaxSegs];
+  __shared__ int warp_cnt[kGemvWarps];
+  const int n_act = active_segments<kGemvThreads>(d.seg_offsets, d.nseg, list, warp_cnt);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  constexpr int H = 1024 * STEPS;
+  constexpr int kVecs = H / 8, kWords = H / 8, kGroups = H / 64;
+  const int per_seg = d.out_features / kGemvWarps;
+  const int64_t items = (int64_t)n_act * per_seg;
+  const uint4* xsrc = reinterpret_cast<const uint4*>(d.x);
+  __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(d.y);
+  auto load_item = [&](int64_t it, RowRegs<STEPS>& ga, RowRegs<STEPS>& ua) {
+    const int seg = list[it / per_seg];
+    const int f = (int)(it % per_seg) * kGemvWarps + w;
+    const int sh = seg == d.shared_seg ? 1 : 0;
+    // select by value (a dynamic index into the parameter block would copy it to local memory)
+    const AffineRef A = sh ? d.wa[1] : d.wa[0];
+    const AffineRef B = sh ? d.wb[1] : d.wb[0];
+    const int64_t e = sh ? 0 : seg;
+    load_row<STEPS>(ga, A, e * A.expert_rows + A.row_offset + f, kWords, kGroups, lane * 4,
+                    lane / 2, 128, 16);
+    load_row<STEPS>(ua, B, e * B.expert_rows + B.row_offset + f, kWords, kGroups, lane * 4,
+                    lane / 2, 128, 16);
+  };
+  RowRegs<STEPS> ga, ua, gn, un;
+  int64_t it = blockIdx.x;
+  if (it < items) load_item(it, ga, ua);
+  for (; it < items; it += gridDim.x) {
+    if (it + gridDim.x < items) load_item(it + gridDim.x, gn, un);
+    const int seg = list[it / per_seg];
+    const int f = (int)(it % per_seg) * kGemvWarps + w;
+    uint32_t p0 = d.seg_offsets[seg], p1 = d.seg_offsets[seg + 1];
+    if (p1 > (uint64_t)d.rows_total) p1 = (uint32_t)d.rows_total;
+    for (uint32_t p = p0; p < p1; p += kRowChunkGU) {
+      const int n = (int)(p1 - p < (uint32_t)kRowChunkGU ? p1 - p : (uint32_t)kRowChunkGU);
+      __syncthreads();  // the previous pass is done with xs
+      stage_rows(xs, xsrc, d.x_rows, p, n, kVecs, d.x_limit, d.status);
+      __syncthreads();
+      float g[kRowChunkGU], u[kRowChunkGU];
+#pragma unroll
+      for (int j = 0; j < kRowChunkGU; ++j) g[j] = u[j] = 0.f;
+#pragma unroll
+      for (int s = 0; s < STEPS; ++s) {
+        uint32_t wg[16], wu[16];
+        dequant32(ga.q[s], (uint16_t)ga.sb[s], (uint16_t)(ga.sb[s] >> 16), wg);
+        dequant32(ua.q[s], (uint16_t)ua.sb[s], (uint16_t)(ua.sb[s] >> 16), wu);
+#pragma unroll
+        for (int j = 0; j < kRowChunkGU; ++j) {
+          if (j < n) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float xf[8];
+              bf16x8_to_f32(xs[j * kVecs + swz(s * 128 + lane * 4 + c)], xf);
+              g[j] = dot8(wg, c, xf, g[j]);
+              u[j] = dot8(wu, c, xf, u[j]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kRowChunkGU; ++j) {
+        if (j < n) {
+          const float gs = warp_sum(g[j]), us = warp_sum(u[j]);
+          if (lane == 0 && p + j < (uint64_t)d.y_limit)
+            y[(int64_t)(p + j) * d.ldy + f] =
+                __float2bfloat16_rn(swiglu_bf16(round_bf16(gs), round_bf16(us)));
+        }
+      }
+    }
+    ga = gn;
+    ua = un;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// down projection.  Item = (active segment, 64 output rows); warp w owns rows
+// base + 4w .. base + 4w + 3, half-warp h rows 4w + 2h and 4w + 2h + 1.  Lane l
+// of a half holds elements [512 s + 32 l, +32) of a row (group 8 s + l / 2).
+// Activation rows are read by sorted position; the next item's codes are
+// loaded while the current one is computed.
+template <int STEPS>  // in_features = 512 * STEPS
+__global__ void __launch_bounds__(kGemvThreads, 1) decode_down_kernel(GroupedGemvDesc d) {
+  extern __shared__ uint4 xs[];  // [kRowChunk][K / 8]
+  __shared__ uint16_t list[kMaxSegs];
+  __shared__ int warp_cnt[kGemvWarps];
+  const int n_act = active_segments<kGemvThreads>(d.seg_offsets, d.nseg, list, warp_cnt);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int half = lane >> 4, li = lane & 15;
+  constexpr int K = 512 * STEPS;
+  constexpr int kVecs = K / 8, kWords = K / 8, kGroups = K / 64;
+  constexpr int kRowsPerHalf = 2;
+  constexpr int kRowsPerItem = 2 * kRowsPerHalf * kGemvWarps;  // 64
+  const int per_seg = d.out_features / kRowsPerItem;
+  const int64_t items = (int64_t)n_act * per_seg;
+  const uint4* xsrc = reinterpret_cast<const uint4*>(d.x);
+  __nv_bfloat16* y = reinterpret_cast<__nv_bfloat16*>(d.y);
+  auto first_row = [&](int64_t it) {
+    return (int)(it % per_seg) * kRowsPerItem + w * 2 * kRowsPerHalf + half * kRowsPerHalf;
+  };
+  auto load_item = [&](int64_t it, RowRegs<STEPS> (&rr)[kRowsPerHalf]) {
+    const int seg = list[it / per_seg];
+    const int sh = seg == d.shared_seg ? 1 : 0;
+    const AffineRef A = sh ? d.wa[1] : d.wa[0];
+    const int64_t e = sh ? 0 : seg;
+    const int64_t rbase = e * A.expert_rows + A.row_offset + first_row(it);
+#pragma unroll
+    for (int r = 0; r < kRowsPerHalf; ++r)
+      load_row<STEPS>(rr[r], A, rbase + r, kWords, kGroups, li * 4, li / 2, 64, 8);
+  };
+  RowRegs<STEPS> cur[kRowsPerHalf], nxt[kRowsPerHalf];
+  int64_t it = blockIdx.x;
+  if (it < items) load_item(it, cur);
+  for (; it < items; it += gridDim.x) {
+    if (it + gridDim.x < items) load_item(it + gridDim.x, nxt);
+    const int seg = list[it / per_seg];
+    const int r0 = first_row(it);
+    uint32_t p0 = d.seg_offsets[seg], p1 = d.seg_offsets[seg + 1];
+    if (p1 > (uint64_t)d.rows_total) p1 = (uint32_t)d.rows_total;
+    for (uint32_t p = p0; p < p1; p += kRowChunk) {
+      const int n = (int)(p1 - p < (uint32_t)kRowChunk ? p1 - p : (uint32_t)kRowChunk);
+      __syncthreads();
+      stage_rows(xs, xsrc, nullptr, p, n, kVecs, d.x_limit, d.status);
+      __syncthreads();
+#pragma unroll
+      for (int r = 0; r < kRowsPerHalf; ++r) {
+        float a[kRowChunk];
+#pragma unroll
+        for (int j = 0; j < kRowChunk; ++j) a[j] = 0.f;
+#pragma unroll
+        for (int s = 0; s < STEPS; ++s) {
+          uint32_t wd[16];
+          dequant32(cur[r].q[s], (uint16_t)cur[r].sb[s], (uint16_t)(cur[r].sb[s] >> 16), wd);
+#pragma unroll
+          for (int j = 0; j < kRowChunk; ++j) {
+            if (j < n) {
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float xf[8];
+                bf16x8_to_f32(xs[j * kVecs + swz(s * 64 + li * 4 + c)], xf);
+                a[j] = dot8(wd, c, xf, a[j]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kRowChunk; ++j) {
+          if (j < n) {
+            const float v = half_warp_sum(a[j]);
+            if (li == 0 && p + j < (uint64_t)d.y_limit)
+              y[(int64_t)(p + j) * d.ldy + r0 + r] = __float2bfloat16_rn(v);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kRowsPerHalf; ++r) cur[r] = nxt[r];
+  }
+}
+
+int grid_for(int64_t items_upper) {
+  const int64_t cap = 148;  // one 16-warp block per SM
+  return (int)(items_upper < 1 ? 1 : (items_upper < cap ? items_upper : cap));
+}
+
+// ===========================================================================
+// Fused decode block: the whole MoE block for T <= kFusedMaxTokens tokens in one
+// cooperative launch (one 16-warp block per SM).  Phases:
+//   1. router logits and the shared-expert gate logit (x staged in shared
+//      memory); idle lanes prefetch the shared expert's weights into L2;
+//   -- grid barrier --
+//   2. every block routes all T tokens and sorts the T*K assignments in its own
+//      shared memory (identical inputs give identical results in every block, so
+//      no barrier follows); block 0 publishes ids, scores and offsets;
+//   3. gate/up + SwiGLU over (active segment, 16 features) items -> act rows;
+//   -- grid barrier --
+//   4. down over (active segment, 64 output rows) items -> expert rows;
+//   -- grid barrier --
+//   5. weighted combine with the gated shared expert -> out.
+// Launch gaps and the per-kernel dependency chains of the multi-kernel path
+// disappear; the arithmetic of every phase is the multi-kernel path's (same
+// routing, sort order, dequantisation, fp32 accumulation and combine), so the
+// two paths agree to the block tolerance and routing is bit-identical.
+constexpr int kFusedMaxTokens = 16;
+constexpr int kFusedMaxExperts = 256;
+constexpr int kFusedMaxAssign = 512;
+
+struct FusedDecodeParams {
+  const __nv_bfloat16* x;  // [T, H]
+  static FusedDecodeParams from(const DecodeFusedArgs& a) {
+    FusedDecodeParams p;
+    p.x = reinterpret_cast<const __nv_bfloat16*>(a.x);
+    p.T = a.T;
+    p.E = a.E;
+    p.K = a.K;
+    p.normalize = a.normalize;
+    p.sorted = a.sorted;
+    p.has_shared = a.has_shared;
+    p.wr = reinterpret_cast<const __nv_bfloat16*>(a.wr);
+    p.wg = reinterpret_cast<const __nv_bfloat16*>(a.wg);
+    for (int i = 0; i < 2; ++i) {
+      p.gate[i] = a.gate[i];
+      p.up[i] = a.up[i];
+      p.down[i] = a.down[i];
+    }
+    p.logits = reinterpret_cast<__nv_bfloat16*>(a.logits);
+    p.gate_logit = reinterpret_cast<__nv_bfloat16*>(a.gate_logit);
+    p.ids = a.ids;
+    p.scores = reinterpret_cast<__nv_bfloat16*>(a.scores);
+    p.offsets = a.offsets;
+    p.act = reinterpret_cast<__nv_bfloat16*>(a.act);
+    p.yrows = reinterpret_cast<__nv_bfloat16*>(a.yrows);
+    p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    p.barrier = a.barrier;
+    p.status = a.status;
+    return p;
+  }
+  int T, E, K, normalize, sorted, has_shared;
+  const __nv_bfloat16* wr;  // [E, H]
+  const __nv_bfloat16* wg;  // [H] shared-expert gate (has_shared)
+  AffineRef gate[2], up[2], down[2];  // [routed, shared]
+  __nv_bfloat16* logits;      // [T, E]
+  __nv_bfloat16* gate_logit;  // [T]
+  uint32_t* ids;              // [T * K]
+  __nv_bfloat16* scores;      // [T * K]
+  uint32_t* offsets;          // [E + 2]
+  __nv_bfloat16* act;         // [T * K + T, I]
+  __nv_bfloat16* yrows;       // [T * K + T, H]
+  __nv_bfloat16* out;         // [T, H]
+  uint32_t* barrier;          // {count, generation}; count is zero between launches
+  uint32_t* status;
+};
+
+// Grid-wide barrier for a cooperative launch: the last block to arrive resets
+// the count and advances the generation (release); the others poll the
+// generation with acquire loads and a short back-off.  The wait is bounded
+// (2 s): on timeout it records kDevWaitTimeout and returns false, and the
+// caller skips the rest of the kernel.
+ASTRO_DEVINL bool grid_barrier(uint32_t* bar, uint32_t* status, int* flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t gen, old, v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(bar) : "memory");
+    int ok = 1;
+    if (old == gridDim.x - 1) {
+      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
+      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar + 1) : "memory");
+    } else {
+      uint64_t t0;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+      uint32_t spins = 0;
+      while (true) {
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar + 1) : "memory");
+        if (v != gen) break;
+        __nanosleep(32);
+        if ((++spins & 255u) == 0) {
+          uint64_t t1;
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+          if (t1 - t0 > 2000000000ull) {
+            record_status(status, kDevWaitTimeout);
+            ok = 0;
+            break;
+          }
+        }
+      }
+    }
+    *flag = ok;
+  }
+  __syncthreads();
+  return *flag != 0;
+}
+
+// prefetch one 128-byte line into L2
+ASTRO_DEVINL void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
+
+template <int H, int I>
+__global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDecodeParams P) {
+  constexpr int kVecs = H / 8;            // uint4 per x row
+  constexpr int J = H / 256;              // router: uint4 per lane per row
+  constexpr int SGU = H / 1024, SD = I / 512;
+  constexpr int kWordsGU = H / 8, kGroupsGU = H / 64, kWordsD = I / 8, kGroupsD = I / 64;
+  constexpr int kDVecs = I / 8;
+  extern __shared__ uint4 smem[];
+  uint4* xs = smem;                                   // [T][kVecs], swizzled
+  uint4* ys = xs + kFusedMaxTokens * kVecs;           // [kRowChunk][kDVecs], swizzled
+  __nv_bfloat16* s_logits = reinterpret_cast<__nv_bfloat16*>(ys + kRowChunk * kDVecs);  // [T][E]
+  __shared__ uint32_t s_ids[kFusedMaxAssign];
+  __shared__ __nv_bfloat16 s_sc16[kFusedMaxAssign];
+  __shared__ float s_score[kFusedMaxAssign];
+  __shared__ uint32_t s_inv[kFusedMaxAssign];
+  __shared__ uint32_t s_stok[kFusedMaxAssign + kFusedMaxTokens];
+  __shared__ int s_cnt[kFusedMaxExperts + 1];
+  __shared__ uint32_t s_offs[kFusedMaxExperts + 2];
+  __shared__ uint16_t s_list[kFusedMaxExperts + 1];
+  __shared__ float s_sg[kFusedMaxTokens];
+  __shared__ int s_warp[kGemvWarps];
+  __shared__ int s_flag;
+  __shared__ int s_nact;
+
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int T = P.T, E = P.E, K = P.K, N = T * K;
+  const int gwarp = blockIdx.x * kGemvWarps + w, nwarps = gridDim.x * kGemvWarps;
+  const int gtid = blockIdx.x * kGemvThreads + threadIdx.x, nthreads = gridDim.x * kGemvThreads;
+
+  // ---- phase 1: router logits (+ shared gate logit) ----
+  {
+    const uint4* xsrc = reinterpret_cast<const uint4*>(P.x);
+    for (int i = threadIdx.x; i < T * kVecs; i += kGemvThreads) {
+      const int t = i / kVecs, q = i - t * kVecs;
+      xs[t * kVecs + swz(q)] = ld_cached(xsrc + (int64_t)t * kVecs + q);
+    }
+    if (P.has_shared) {
+      // the shared expert is always used: start pulling its weights into L2
+      const AffineRef* sw[3] = {&P.gate[1], &P.up[1], &P.down[1]};
+      const int64_t qbytes[3] = {(int64_t)I * H / 2, (int64_t)I * H / 2, (int64_t)H * I / 2};
+      const int64_t sbytes[3] = {(int64_t)I * (H / 64) * 2, (int64_t)I * (H / 64) * 2,
+                                 (int64_t)H * (I / 64) * 2};
+#pragma unroll
+      for (int m = 0; m < 3; ++m) {
+        const char* q = reinterpret_cast<const char*>(sw[m]->q);
+        for (int64_t l = gtid; l * 128 < qbytes[m]; l += nthreads) prefetch_l2(q + l * 128);
+        const char* sc = reinterpret_cast<const char*>(sw[m]->s);
+        const char* bi = reinterpret_cast<const char*>(sw[m]->b);
+        for (int64_t l = gtid; l * 128 < sbytes[m]; l += nthreads) {
+          prefetch_l2(sc + l * 128);
+          prefetch_l2(bi + l * 128);
+        }
+      }
+    }
+    __syncthreads();
+    const int tgroups = (T + kRouterTokens - 1) / kRouterTokens;
+    const int rows = E + (P.has_shared ? 1 : 0);
+    // unit u runs on block u % grid (warp u / grid): the rows are spread over all SMs
+    const int gw_spread = w * gridDim.x + blockIdx.x;
+    for (int u = gw_spread; u < rows * tgroups; u += nwarps) {
+      const int r = u / tgroups, t0 = (u - r * tgroups) * kRouterTokens;
+      const int nt = T - t0 < kRouterTokens ? T - t0 : kRouterTokens;
+      const uint4* wrow = reinterpret_cast<const uint4*>(r < E ? P.wr + (int64_t)r * H : P.wg);
+      uint4 wv[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) wv[j] = ld_stream(wrow + j * 32 + lane);
+      float acc[kRouterTokens];
+#pragma unroll
+      for (int t = 0; t < kRouterTokens; ++t) acc[t] = 0.f;
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        float wf[8];
+        bf16x8_to_f32(wv[j], wf);
+#pragma unroll
+        for (int t = 0; t < kRouterTokens; ++t) {
+          if (t < nt) {
+            float xf[8];
+            bf16x8_to_f32(xs[(t0 + t) * kVecs + swz(j * 32 + lane)], xf);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(wf[i], xf[i], acc[t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int t = 0; t < kRouterTokens; ++t) {
+        if (t < nt) {
+          const float v = warp_sum(acc[t]);
+          if (lane == 0) {
+            if (r < E) P.logits[(int64_t)(t0 + t) * E + r] = __float2bfloat16_rn(v);
+            else P.gate_logit[t0 + t] = __float2bfloat16_rn(v);
+          }
+        }
+      }
+    }
+  }
+  if (!grid_barrier(P.barrier, P.status, &s_flag)) return;
+
+  // ---- phase 2: route + sort, redundantly in every block ----
+  for (int i = threadIdx.x; i < T * E; i += kGemvThreads)
+    s_logits[i] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(P.logits) + i));
+  for (int e = threadIdx.x; e <= E; e += kGemvThreads) s_cnt[e] = 0;
+  if (threadIdx.x < T)
+    s_sg[threadIdx.x] =
+        P.has_shared
+            ? round_bf16(sigmoid_mlx(bf16_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(P.gate_logit) + threadIdx.x))))
+            : 0.f;
+  __syncthreads();
+  if (w < T) route_token<__nv_bfloat16, 8>(s_logits + w * E, E, K, P.normalize, s_ids + w * K, s_sc16 + w * K);
+  __syncthreads();
+  int rank = 0;
+  uint32_t my_id = 0xffffffffu;
+  if (threadIdx.x < N) {
+    s_inv[threadIdx.x] = 0;  // an id >= E keeps slot row 0 (recorded, never used for output)
+    my_id = s_ids[threadIdx.x];
+    s_score[threadIdx.x] = __bfloat162float(s_sc16[threadIdx.x]);
+    if (my_id < (uint32_t)E) {
+      for (int j = 0; j < (int)threadIdx.x; ++j) rank += s_ids[j] == my_id ? 1 : 0;
+      atomicAdd(&s_cnt[my_id], 1);
+    } else {
+      record_status(P.status, kDevBadExpertId);
+    }
+    if (blockIdx.x == 0) {
+      P.ids[threadIdx.x] = my_id;
+      P.scores[threadIdx.x] = s_sc16[threadIdx.x];
+    }
+  }
+  __syncthreads();
+  if (w == 0) {
+    // exclusive scan of the E counts: lane l owns experts [l*C, l*C + C)
+    const int C = (E + 31) / 32;
+    int part = 0;
+    for (int i = 0; i < C; ++i) part += (lane * C + i < E) ? s_cnt[lane * C + i] : 0;
+    int incl = part;
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, m);
+      if (lane >= m) incl += o;
+    }
+    int run = incl - part;
+    for (int i = 0; i < C; ++i) {
+      const int e = lane * C + i;
+      if (e < E) {
+        s_offs[e] = (uint32_t)run;
+        run += s_cnt[e];
+      }
+    }
+    if (lane == 31) {
+      s_offs[E] = (uint32_t)incl;
+      s_offs[E + 1] = (uint32_t)(incl + (P.has_shared ? T : 0));
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < N && my_id < (uint32_t)E) {
+    const uint32_t pos = s_offs[my_id] + (uint32_t)rank;
+    s_stok[pos] = threadIdx.x / K;
+    s_inv[threadIdx.x] = pos;
+  }
+  if (P.has_shared && threadIdx.x < T) s_stok[s_offs[E] + threadIdx.x] = threadIdx.x;
+  if (blockIdx.x == 0)
+    for (int e = threadIdx.x; e < E + 2; e += kGemvThreads) P.offsets[e] = s_offs[e];
+  __syncthreads();
+  {
+    const int nseg = E + (P.has_shared ? 1 : 0);
+    const int s = threadIdx.x;
+    const bool ne = s < nseg && s_offs[s + 1] > s_offs[s];
+    const uint32_t bal = __ballot_sync(0xffffffffu, ne);
+    if (lane == 0) s_warp[w] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+#pragma unroll
+    for (int i = 0; i < kGemvWarps; ++i) {
+      before += i < w ? s_warp[i] : 0;
+      total += s_warp[i];
+    }
+    if (ne) s_list[before + __popc(bal & lanemask_lt())] = (uint16_t)s;
+    if (threadIdx.x == 0) s_nact = total;
+    __syncthreads();
+  }
+  const int n_act = s_nact;
+  const uint32_t rows_total = s_offs[E + 1];
+  {
+    // the experts are known: pull this block's gate/up and down weight rows into
+    // L2 now, so the loads of phases 3 and 4 do not each wait a full HBM trip
+    const int per_gu = I / kGemvWarps, per_d = H / (4 * kGemvWarps);
+    const int items_gu = n_act * per_gu, items_d = n_act * per_d;
+    constexpr int kLinesGU = kGemvWarps * (H / 2) / 128;       // 16 rows of packed codes
+    constexpr int kLinesGUs = (kGemvWarps * (H / 64) * 2 + 127) / 128;
+    constexpr int kLinesD = 4 * kGemvWarps * (I / 2) / 128;    // 64 rows of packed codes
+    constexpr int kLinesDs = (4 * kGemvWarps * (I / 64) * 2 + 127) / 128;
+    constexpr int kPerGU = 2 * (kLinesGU + 2 * kLinesGUs), kPerD = kLinesD + 2 * kLinesDs;
+    const int n_gu = (items_gu - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int n_d = (items_d - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    for (int i = threadIdx.x; i < n_gu * kPerGU + n_d * kPerD; i += kGemvThreads) {
+      const char* line;
+      if (i < n_gu * kPerGU) {
+        const int k = i / kPerGU, l = i - k * kPerGU;
+        const int it = (int)blockIdx.x + k * (int)gridDim.x;
+        const int seg = s_list[it / per_gu];
+        const int f0 = (it % per_gu) * kGemvWarps;
+        const int sh = seg == E ? 1 : 0;
+        const int which = l / (kLinesGU + 2 * kLinesGUs), ll = l - which * (kLinesGU + 2 * kLinesGUs);
+        const AffineRef W = which ? (sh ? P.up[1] : P.up[0]) : (sh ? P.gate[1] : P.gate[0]);
+        const int64_t row = (sh ? 0 : (int64_t)seg) * W.expert_rows + W.row_offset + f0;
+        if (ll < kLinesGU)
+          line = reinterpret_cast<const char*>(W.q) + row * (H / 2) + (int64_t)ll * 128;
+        else if (ll < kLinesGU + kLinesGUs)
+          line = reinterpret_cast<const char*>(W.s) + row * (H / 64) * 2 + (int64_t)(ll - kLinesGU) * 128;
+        else
+          line = reinterpret_cast<const char*>(W.b) + row * (H / 64) * 2 +
+                 (int64_t)(ll - kLinesGU - kLinesGUs) * 128;
+      } else {
+        const int i2 = i - n_gu * kPerGU;
+        const int k = i2 / kPerD, l = i2 - k * kPerD;
+        const int it = (int)blockIdx.x + k * (int)gridDim.x;
+        const int seg = s_list[it / per_d];
+        const int r0 = (it % per_d) * 4 * kGemvWarps;
+        const int sh = seg == E ? 1 : 0;
+        const AffineRef W = sh ? P.down[1] : P.down[0];
+        const int64_t row = (sh ? 0 : (int64_t)seg) * W.expert_rows + W.row_offset + r0;
+        if (l < kLinesD)
+          line = reinterpret_cast<const char*>(W.q) + row * (I / 2) + (int64_t)l * 128;
+        else if (l < kLinesD + kLinesDs)
+          line = reinterpret_cast<const char*>(W.s) + row * (I / 64) * 2 + (int64_t)(l - kLinesD) * 128;
+        else
+          line = reinterpret_cast<const char*>(W.b) + row * (I / 64) * 2 +
+                 (int64_t)(l - kLinesD - kLinesDs) * 128;
+      }
+      prefetch_l2(line);
+    }
+  }
+
+  // ---- phase 3: gate/up + SwiGLU ----
+  {
+    const int per_seg = I / kGemvWarps;
+    const int items = n_act * per_seg;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+      const int seg = s_list[it / per_seg];
+      const int f = (it % per_seg) * kGemvWarps + w;
+      const int sh = seg == E ? 1 : 0;
+      const AffineRef A = sh ? P.gate[1] : P.gate[0];
+      const AffineRef B = sh ? P.up[1] : P.up[0];
+      const int64_t e = sh ? 0 : seg;
+      RowRegs<SGU> ga, ua;
+      load_row<SGU>(ga, A, e * A.expert_rows + A.row_offset + f, kWordsGU, kGroupsGU, lane * 4,
+                    lane / 2, 128, 16);
+      load_row<SGU>(ua, B, e * B.expert_rows + B.row_offset + f, kWordsGU, kGroupsGU, lane * 4,
+                    lane / 2, 128, 16);
+      const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
+      for (uint32_t p = p0; p < p1; p += kRowChunkGU) {
+        const int n = (int)(p1 - p < (uint32_t)kRowChunkGU ? p1 - p : (uint32_t)kRowChunkGU);
+        float g[kRowChunkGU], u[kRowChunkGU];
+#pragma unroll
+        for (int j = 0; j < kRowChunkGU; ++j) g[j] = u[j] = 0.f;
+#pragma unroll
+        for (int st = 0; st < SGU; ++st) {
+          uint32_t wg[16], wu[16];
+          dequant32(ga.q[st], (uint16_t)ga.sb[st], (uint16_t)(ga.sb[st] >> 16), wg);
+          dequant32(ua.q[st], (uint16_t)ua.sb[st], (uint16_t)(ua.sb[st] >> 16), wu);
+#pragma unroll
+          for (int j = 0; j < kRowChunkGU; ++j) {
+            if (j < n) {
+              const int t = (int)s_stok[p + j];
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                float xf[8];
+                bf16x8_to_f32(xs[t * kVecs + swz(st * 128 + lane * 4 + c)], xf);
+                g[j] = dot8(wg, c, xf, g[j]);
+                u[j] = dot8(wu, c, xf, u[j]);
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kRowChunkGU; ++j) {
+          if (j < n) {
+            const float gs = warp_sum(g[j]), us = warp_sum(u[j]);
+            if (lane == 0)
+              P.act[(int64_t)(p + j) * I + f] =
+                  __float2bfloat16_rn(swiglu_bf16(round_bf16(gs), round_bf16(us)));
+          }
+        }
+      }
+    }
+  }
+  if (!grid_barrier(P.barrier, P.status, &s_flag)) return;
+
+  // ---- phase 4: down ----
+  {
+    const int half = lane >> 4, li = lane & 15;
+    constexpr int kRowsPerHalf = 2;
+    constexpr int kRowsPerItem = 2 * kRowsPerHalf * kGemvWarps;  // 64
+    const int per_seg = H / kRowsPerItem;
+    const int items = n_act * per_seg;
+    const uint4* asrc = reinterpret_cast<const uint4*>(P.act);
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+      const int seg = s_list[it / per_seg];
+      const int r0 = (it % per_seg) * kRowsPerItem + w * 2 * kRowsPerHalf + half * kRowsPerHalf;
+      const int sh = seg == E ? 1 : 0;
+      const AffineRef A = sh ? P.down[1] : P.down[0];
+      const int64_t e = sh ? 0 : seg;
+      RowRegs<SD> rr[kRowsPerHalf];
+#pragma unroll
+      for (int r = 0; r < kRowsPerHalf; ++r)
+        load_row<SD>(rr[r], A, e * A.expert_rows + A.row_offset + r0 + r, kWordsD, kGroupsD,
+                     li * 4, li / 2, 64, 8);
+      const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
+      for (uint32_t p = p0; p < p1; p += kRowChunk) {
+        const int n = (int)(p1 - p < (uint32_t)kRowChunk ? p1 - p : (uint32_t)kRowChunk);
+        __syncthreads();
+        for (int i = threadIdx.x; i < n * kDVecs; i += kGemvThreads) {
+          const int j = i / kDVecs, q = i - j * kDVecs;
+          ys[j * kDVecs + swz(q)] = __ldcg(asrc + (int64_t)(p + j) * kDVecs + q);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int r = 0; r < kRowsPerHalf; ++r) {
+          float a[kRowChunk];
+#pragma unroll
+          for (int j = 0; j < kRowChunk; ++j) a[j] = 0.f;
+#pragma unroll
+          for (int st = 0; st < SD; ++st) {
+            uint32_t wd[16];
+            dequant32(rr[r].q[st], (uint16_t)rr[r].sb[st], (uint16_t)(rr[r].sb[st] >> 16), wd);
+#pragma unroll
+            for (int j = 0; j < kRowChunk; ++j) {
+              if (j < n) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                  float xf[8];
+                  bf16x8_to_f32(ys[j * kDVecs + swz(st * 64 + li * 4 + c)], xf);
+                  a[j] = dot8(wd, c, xf, a[j]);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < kRowChunk; ++j) {
+            if (j < n) {
+              const float v = half_warp_sum(a[j]);
+              if (li == 0) P.yrows[(int64_t)(p + j) * H + r0 + r] = __float2bfloat16_rn(v);
+            }
+          }
+        }
+      }
+    }
+  }
+  if (!grid_barrier(P.barrier, P.status, &s_flag)) return;
+
+  // ---- phase 5: weighted combine + gated shared expert ----
+  {
+    const uint4* rows = reinterpret_cast<const uint4*>(P.yrows);
+    uint4* out = reinterpret_cast<uint4*>(P.out);
+    for (int u = gtid; u < T * kVecs; u += nthreads) {
+      const int t = u / kVecs, c = u - t * kVecs;
+      out[u] = combine_chunk(rows, kVecs, c, s_inv + t * K, s_score + t * K, K, P.sorted != 0,
+                             P.has_shared ? (int64_t)(s_offs[E] + t) : -1, s_sg[t]);
+    }
+  }
+  (void)rows_total;
+}
+
+}  // namespace
+
+bool router_gemv_supported(int H) { return H == 1024 || H == 2048 || H == 4096; }
+
+cudaError_t launch_router_gemv(const void* x, int64_t T, const void* wr, int E, int H, void* logits,
+                               cudaStream_t st) {
+  if (T <= 0) return cudaSuccess;
+  const dim3 grid((unsigned)((E + kWarps - 1) / kWarps),
+                  (unsigned)((T + kRouterTokens - 1) / kRouterTokens));
+  const size_t smem = (size_t)kRouterTokens * H * 2;
+  auto* xx = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto* ww = reinterpret_cast<const __nv_bfloat16*>(wr);
+  auto* out = reinterpret_cast<__nv_bfloat16*>(logits);
+  switch (H) {
+    case 1024:
+      router_gemv_kernel<4><<<grid, kThreads, smem, st>>>(xx, T, ww, E, out);
+      break;
+    case 2048:
+      router_gemv_kernel<8><<<grid, kThreads, smem, st>>>(xx, T, ww, E, out);
+      break;
+    case 4096:
+      cudaFuncSetAttribute(router_gemv_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      router_gemv_kernel<16><<<grid, kThreads, smem, st>>>(xx, T, ww, E, out);
+      break;
+    default:
+      return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+bool decode_gemv_supported(int H, int I, int group, int bits) {
+  return bits == 4 && group == 64 && (H == 1024 || H == 2048 || H == 4096) &&
+         (I == 512 || I == 1024 || I == 2048) && I % kGemvWarps == 0 && H % (4 * kGemvWarps) == 0;
+}
+
+cudaError_t launch_decode_gate_up(const GroupedGemvDesc& d, int64_t max_active, cudaStream_t st) {
+  if (d.rows_total == 0) return cudaSuccess;
+  if (d.nseg > kMaxSegs - 1) return cudaErrorInvalidValue;
+  const int grid = grid_for(max_active * (d.out_features / kGemvWarps));
+  const size_t smem = (size_t)kRowChunkGU * d.in_features * 2;
+  switch (d.in_features) {
+    case 1024: decode_gate_up_kernel<1><<<grid, kGemvThreads, smem, st>>>(d); break;
+    case 2048: decode_gate_up_kernel<2><<<grid, kGemvThreads, smem, st>>>(d); break;
+    case 4096:
+      cudaFuncSetAttribute(decode_gate_up_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem);
+      decode_gate_up_kernel<4><<<grid, kGemvThreads, smem, st>>>(d);
+      break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_decode_down(const GroupedGemvDesc& d, int64_t max_active, cudaStream_t st) {
+  if (d.rows_total == 0) return cudaSuccess;
+  if (d.nseg > kMaxSegs - 1) return cudaErrorInvalidValue;
+  const int grid = grid_for(max_active * (d.out_features / (4 * kGemvWarps)));
+  const size_t smem = (size_t)kRowChunk * d.in_features * 2;
+  switch (d.in_features) {
+    case 512: decode_down_kernel<1><<<grid, kGemvThreads, smem, st>>>(d); break;
+    case 1024: decode_down_kernel<2><<<grid, kGemvThreads, smem, st>>>(d); break;
+    case 2048: decode_down_kernel<4><<<grid, kGemvThreads, smem, st>>>(d); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace astro
+
+namespace astro {
+
+bool decode_fused_supported(int T, int H, int E, int K, int I) {
+  return T >= 1 && T <= kFusedMaxTokens && E >= 1 && E <= kFusedMaxExperts && K >= 1 && K <= 32 &&
+         T * K <= kFusedMaxAssign && (H == 1024 || H == 2048) && (I == 512 || I == 1024);
+}
+
+namespace {
+template <int H, int I>
+cudaError_t launch_fused_t(const FusedDecodeParams& p, cudaStream_t st) {
+  auto kern = decode_fused_kernel<H, I>;
+  const size_t smem = (size_t)(kFusedMaxTokens * (H / 8) + kRowChunk * (I / 8)) * 16 +
+                      (size_t)kFusedMaxTokens * kFusedMaxExperts * 2;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, sms = 0, per_sm = 0;
+  if ((e = cudaGetDevice(&dev)) != cudaSuccess) return e;
+  if ((e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return e;
+  if ((e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kGemvThreads, smem)) !=
+      cudaSuccess)
+    return e;
+  if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+  FusedDecodeParams arg = p;
+  void* args[] = {&arg};
+  return cudaLaunchCooperativeKernel((const void*)kern, dim3(sms), dim3(kGemvThreads), args, smem, st);
+}
+}  // namespace
+
+cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t st) {
+  if (!decode_fused_supported(a.T, a.H, a.E, a.K, a.I)) return cudaErrorInvalidValue;
+  const FusedDecodeParams p = FusedDecodeParams::from(a);
+  if (a.H == 2048 && a.I == 512) return launch_fused_t<2048, 512>(p, st);
+  if (a.H == 2048 && a.I == 1024) return launch_fused_t<2048, 1024>(p, st);
+  if (a.H == 1024 && a.I == 512) return launch_fused_t<1024, 512>(p, st);
+  return launch_fused_t<1024, 1024>(p, st);
+}
+
+}  // namespace astro

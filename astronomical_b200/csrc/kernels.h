@@ -16,6 +16,8 @@ cudaError_t launch_dense_nt_simt(const void* x, const void* w, int64_t rows, int
 
 // scratch: sort_scratch_bytes(tokens * K, E) bytes of device memory
 size_t sort_scratch_bytes(int64_t n, int E);
+// kernels one launch_sort_assignments call issues (1 when all n fit one tile)
+int sort_launch_count(int64_t n);
 cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, int E,
                                     int64_t shared_rows, uint32_t* sorted_order,
                                     uint32_t* inverse_order, uint32_t* sorted_ids,
@@ -75,6 +77,44 @@ struct GroupedGemvDesc {
 };
 
 cudaError_t launch_grouped_gemv(const GroupedGemvDesc& d, cudaStream_t st);
+
+// Small-batch kernels (decode.cu).  Router GEMV: logits [T, E] bf16 = x [T, H] .
+// Wr [E, H]^T for H in {1024, 2048, 4096}; x and Wr 16-byte aligned.
+bool router_gemv_supported(int H);
+cudaError_t launch_router_gemv(const void* x, int64_t T, const void* wr, int E, int H, void* logits,
+                               cudaStream_t st);
+// Gathered int4 g64 GEMVs over the non-empty segments of d.seg_offsets
+// (max_active bounds their number): gate/up writes SwiGLU(gate, up) rows
+// (d.wa = gate, d.wb = up, in_features 1024/2048/4096); down reads rows of
+// d.x by sorted position (in_features 512/1024/2048).
+bool decode_gemv_supported(int H, int I, int group, int bits);
+cudaError_t launch_decode_gate_up(const GroupedGemvDesc& d, int64_t max_active, cudaStream_t st);
+cudaError_t launch_decode_down(const GroupedGemvDesc& d, int64_t max_active, cudaStream_t st);
+
+// Fused decode block (decode.cu): router, route, sort, gate/up, down and
+// combine of T <= 16 tokens in one cooperative launch (one block per SM, grid
+// barriers between dependent phases).  `barrier` is two words that must be zero
+// before the first launch; the kernel leaves them reusable.  Returns
+// cudaErrorCooperativeLaunchTooLarge when the device cannot hold the grid.
+struct DecodeFusedArgs {
+  const void* x = nullptr;  // bf16 [T, H]
+  int T = 0, H = 0, E = 0, K = 0, I = 0, normalize = 1, sorted = 0, has_shared = 0;
+  const void* wr = nullptr;  // bf16 [E, H]
+  const void* wg = nullptr;  // bf16 [H]
+  AffineRef gate[2], up[2], down[2];  // [routed, shared]
+  void* logits = nullptr;
+  void* gate_logit = nullptr;
+  uint32_t* ids = nullptr;
+  void* scores = nullptr;
+  uint32_t* offsets = nullptr;
+  void* act = nullptr;
+  void* yrows = nullptr;
+  void* out = nullptr;
+  uint32_t* barrier = nullptr;
+  uint32_t* status = nullptr;
+};
+bool decode_fused_supported(int T, int H, int E, int K, int I);
+cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t st);
 
 cudaError_t launch_offsets_from_sorted(const uint32_t* ids, int64_t n, int E, uint32_t* offsets,
                                        uint32_t* status, cudaStream_t st);

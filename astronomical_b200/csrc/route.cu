@@ -16,20 +16,9 @@
 // pass over the hidden states for it.
 #include "common.cuh"
 #include "kernels.h"
+#include "route_dev.cuh"
 
 namespace astro {
-
-template <typename T> struct RouteKey;
-// 16-bit types: probabilities are >= 0, so their bit patterns order like the
-// values; key = (bits << 16) | (0xffff - id) and max gives (value desc, id asc).
-template <> struct RouteKey<__nv_bfloat16> {
-  static ASTRO_DEVINL uint32_t bits(float p) { return f32_to_bf16(p); }
-  static ASTRO_DEVINL float value(uint32_t b) { return bf16_to_f32((uint16_t)b); }
-};
-template <> struct RouteKey<__half> {
-  static ASTRO_DEVINL uint32_t bits(float p) { return __half_as_ushort(__float2half_rn(p)); }
-  static ASTRO_DEVINL float value(uint32_t b) { return __half2float(__ushort_as_half((uint16_t)b)); }
-};
 
 template <typename T, int CMAX>
 __global__ void __launch_bounds__(256) route_experts_kernel(
@@ -40,101 +29,7 @@ __global__ void __launch_bounds__(256) route_experts_kernel(
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= tokens) return;
-  const int C = (E + 31) >> 5;
-  const int i0 = lane * C;
-  const T* row = logits + t * E;
-
-  float v[CMAX];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int c = 0; c < CMAX; ++c) {
-    const int i = i0 + c;
-    v[c] = (c < C && i < E) ? Num<T>::load(row, i) : -INFINITY;
-    mx = (v[c] > mx) ? v[c] : mx;
-  }
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) {
-    const float o = __shfl_xor_sync(0xffffffffu, mx, m);
-    mx = (o > mx) ? o : mx;
-  }
-  float part = 0.0f;
-#pragma unroll
-  for (int c = 0; c < CMAX; ++c) {
-    const int i = i0 + c;
-    if (c < C && i < E) {
-      v[c] = expf_cw(__fsub_rn(v[c], mx));
-      part = __fadd_rn(part, v[c]);
-    }
-  }
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) part = __fadd_rn(part, __shfl_xor_sync(0xffffffffu, part, m));
-  const float inv = __fdiv_rn(1.0f, part);
-
-  // probabilities rounded to the logits dtype; top-K selection
-  uint32_t key[CMAX];
-#pragma unroll
-  for (int c = 0; c < CMAX; ++c) {
-    const int i = i0 + c;
-    const bool valid = (c < C && i < E);
-    const float p = Num<T>::round(__fmul_rn(v[c], inv));
-    if constexpr (sizeof(T) == 2) {
-      key[c] = valid ? ((RouteKey<T>::bits(p) << 16) | (0xffffu - (uint32_t)i)) : 0u;
-    } else {
-      v[c] = valid ? p : -1.0f;
-      key[c] = valid ? 1u : 0u;  // liveness only
-    }
-  }
-
-  float sel_val = 0.0f;  // lane k keeps winner k
-  uint32_t sel_id = 0;
-  float sum_sel = 0.0f;
-  for (int k = 0; k < K; ++k) {
-    uint32_t wid;
-    float wval;
-    if constexpr (sizeof(T) == 2) {
-      uint32_t best = 0;
-#pragma unroll
-      for (int c = 0; c < CMAX; ++c) best = (key[c] > best) ? key[c] : best;
-      best = __reduce_max_sync(0xffffffffu, best);
-      wid = 0xffffu - (best & 0xffffu);
-      wval = RouteKey<T>::value(best >> 16);
-#pragma unroll
-      for (int c = 0; c < CMAX; ++c)
-        if (key[c] == best) key[c] = 0u;
-    } else {
-      // fp32 probabilities: (value desc, id asc) with a 64-bit key
-      uint64_t best = 0;
-#pragma unroll
-      for (int c = 0; c < CMAX; ++c) {
-        if (key[c]) {
-          const uint64_t kk = ((uint64_t)__float_as_uint(v[c]) << 32) |
-                              (uint64_t)(0xffffffffu - (uint32_t)(i0 + c));
-          best = (kk > best) ? kk : best;
-        }
-      }
-#pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) {
-        const uint64_t o = __shfl_xor_sync(0xffffffffu, best, m);
-        best = (o > best) ? o : best;
-      }
-      wid = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
-      wval = __uint_as_float((uint32_t)(best >> 32));
-#pragma unroll
-      for (int c = 0; c < CMAX; ++c)
-        if (key[c] && (uint32_t)(i0 + c) == wid) key[c] = 0u;
-    }
-    if (lane == k) {
-      sel_val = wval;
-      sel_id = wid;
-    }
-    sum_sel = __fadd_rn(sum_sel, wval);
-  }
-  if (lane < K) {
-    float s = sel_val;
-    if (normalize) s = Num<T>::round(__fdiv_rn(sel_val, Num<T>::round(sum_sel)));
-    out_ids[t * K + lane] = sel_id;
-    Num<T>::store(out_scores, t * K + lane, s);
-  }
+  route_token<T, CMAX>(logits + t * E, E, K, normalize, out_ids + t * K, out_scores + t * K);
 
   if (gate_logit != nullptr) {
     // bf16(x[t] . wg): 16-byte chunks strided over the warp, fp32 fma, butterfly.

@@ -11,6 +11,8 @@
 // tiles, plus earlier warps of the tile) and scatters its assignments in order;
 // equal ids inside one 32-wide step get their rank from __match_any_sync.  Ids
 // >= E set a status bit and are skipped, so no write leaves the output arrays.
+// When all assignments fit one tile (decode batches, n <= 2048) the histogram
+// pass is skipped: the single scatter block counts for itself.
 //
 // With shared_rows > 0 the shared expert is appended as segment E: rows
 // [n, n + shared_rows) with token t and id E, offsets[E+1] = n + shared_rows.
@@ -26,6 +28,8 @@ constexpr int kSortTile = 2048;
 constexpr int kPerWarp = kSortTile / kSortWarps;  // 128
 
 int64_t sort_tiles(int64_t n) { return (n + kSortTile - 1) / kSortTile; }
+
+int sort_launch_count(int64_t n) { return sort_tiles(n) > 1 ? 2 : 1; }
 
 size_t sort_scratch_bytes(int64_t n, int E) {
   return sizeof(int) * (size_t)(sort_tiles(n) > 0 ? sort_tiles(n) : 1) * (size_t)E;
@@ -61,7 +65,8 @@ __global__ void __launch_bounds__(kSortWarps * 32) sort_scatter_kernel(
     const uint32_t* __restrict__ ids, int64_t n, int K, int E, int tiles,
     const int* __restrict__ tile_hist, int64_t shared_rows, uint32_t* __restrict__ sorted_order,
     uint32_t* __restrict__ inverse_order, uint32_t* __restrict__ sorted_ids,
-    uint32_t* __restrict__ sorted_tokens, uint32_t* __restrict__ offsets) {
+    uint32_t* __restrict__ sorted_tokens, uint32_t* __restrict__ offsets,
+    uint32_t* __restrict__ status) {
   extern __shared__ int sm[];
   int* cnt = sm;                             // [kSortWarps][E]
   int* base = sm + kSortWarps * E;           // [E] counts of earlier tiles
@@ -76,20 +81,27 @@ __global__ void __launch_bounds__(kSortWarps * 32) sort_scatter_kernel(
     const int64_t i = beg + it + lane;
     const uint32_t id = (i < n) ? ids[i] : 0xffffffffu;
     const bool ok = id < (uint32_t)E;
+    if (!tile_hist && i < n && !ok) record_status(status, kDevBadExpertId);
     const uint32_t peers = __match_any_sync(0xffffffffu, ok ? id : 0xffffffffu);
     if (ok && (__ffs(peers) - 1) == lane) cnt[w * E + id] += __popc(peers);
   }
-  // totals over all tiles and the count of earlier tiles, per expert
+  // totals over all tiles and the count of earlier tiles, per expert; a single
+  // tile (tile_hist == nullptr) takes its totals from its own warp counts
+  if (!tile_hist) __syncthreads();
   const int per = (E + blockDim.x - 1) / blockDim.x;
   const int e0 = threadIdx.x * per;
   int local = 0;
   for (int q = 0; q < per && e0 + q < E; ++q) {
     const int e = e0 + q;
     int total = 0, before = 0;
-    for (int t = 0; t < tiles; ++t) {
-      const int c = tile_hist[(int64_t)t * E + e];
-      total += c;
-      if (t < g) before += c;
+    if (tile_hist) {
+      for (int t = 0; t < tiles; ++t) {
+        const int c = tile_hist[(int64_t)t * E + e];
+        total += c;
+        if (t < g) before += c;
+      }
+    } else {
+      for (int ww = 0; ww < kSortWarps; ++ww) total += cnt[ww * E + e];
     }
     base[e] = before;
     local += total;
@@ -176,10 +188,14 @@ cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, 
   if (smem2 > 48 * 1024)
     cudaFuncSetAttribute(sort_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)smem2);
-  sort_hist_kernel<<<tiles, kSortWarps * 32, smem1, st>>>(ids, n, E, tile_hist, status);
+  if (tiles > 1) {
+    sort_hist_kernel<<<tiles, kSortWarps * 32, smem1, st>>>(ids, n, E, tile_hist, status);
+  } else {
+    tile_hist = nullptr;  // one tile: the scatter pass counts (and checks ids) itself
+  }
   sort_scatter_kernel<<<tiles, kSortWarps * 32, smem2, st>>>(
       ids, n, K > 0 ? K : 1, E, tiles, tile_hist, shared_rows, sorted_order, inverse_order,
-      sorted_ids, sorted_tokens, offsets);
+      sorted_ids, sorted_tokens, offsets, status);
   return cudaGetLastError();
 }
 

@@ -293,7 +293,8 @@ class Qwen3_5MoEBlock:
     """
 
     def __init__(self, weights: dict, device: int = 0, max_tokens: int = 4096,
-                 use_tensor_cores: int = 0, fuse_gate_up: bool = False, layer: int = 0):
+                 use_tensor_cores: int = 0, fuse_gate_up: bool = False, layer: int = 0,
+                 decode_max_tokens: int = 0, decode_fused: int = 0):
         cfg = weights["config"]
         self.cfg = dict(cfg)
         self.device = torch.device("cuda", device)
@@ -316,6 +317,8 @@ class Qwen3_5MoEBlock:
         opts.max_tokens = max_tokens
         opts.sorted_threshold = 0
         opts.use_tensor_cores = use_tensor_cores
+        opts.decode_max_tokens = decode_max_tokens
+        opts.decode_fused = decode_fused
         ctx = ctypes.c_void_p()
         with torch.cuda.device(dev):
             check(_lib.lib().astro_moe_ctx_create(device, ctypes.c_void_p(

@@ -48,6 +48,8 @@ def parse():
                     help="tokens per CPU-baseline sample (0 = size it to ~10 s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--use-tensor-cores", type=int, default=0)
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode sweep")
+    ap.add_argument("--decode-layers", type=int, default=16)
     ap.add_argument("--profile", action="store_true",
                     help="only W warm-up and K plain steps (for ncu captures; prints nothing)")
     return ap.parse_args()
@@ -160,6 +162,66 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- GPU
+EXPERT_BYTES = 1769472  # one routed expert: gate + up + down, int4 g64 with bf16 scales/biases
+
+
+def measure_decode(args, dev, rank, hbm_peak, max_over_ranks):
+    """Config 2: decode batches T in {1, 4, 16, 64} of the config-1 block with
+    Zipf(1.1) routing skew, over a stack of `decode_layers` independent layers
+    replayed as one CUDA graph (the weights of a step do not fit L2, as in a
+    40-layer model).  Reports device time per layer and achieved HBM bandwidth
+    against the algorithmic bytes: (distinct routed experts + shared) x 1,769,472
+    + router 1 MiB + shared gate 4 KiB + activations in/out."""
+    import torch
+
+    from astronomical_b200 import moe, synthetic
+
+    cfg = dict(synthetic.CONFIGS[2])
+    L = args.decode_layers
+    blocks = [moe.Qwen3_5MoEBlock(synthetic.make_block_weights_torch(cfg, seed=500 + 17 * l + rank,
+                                                                     device=dev),
+                                  device=dev.index, max_tokens=64) for l in range(L)]
+    out = {"workload": "config2_decode_zipf1.1", "layers_in_graph": L,
+           "path": "fused decode kernel for T<=8, tcgen05 grouped GEMMs above", "sweep": {}}
+    for T in (1, 4, 16, 64):
+        g = torch.Generator(device=dev)
+        g.manual_seed(700 + T)
+        x = torch.randn((T, 2048), generator=g, device=dev).to(torch.bfloat16)
+        x[:, 0] = 1.0  # the Zipf bias enters through router column 0
+        distinct = 0
+        for b in blocks:
+            _, tp = b.forward(x, taps=True)
+            distinct += int(torch.unique(tp["selected_indices"]).numel())
+        for _ in range(3):
+            for b in blocks:
+                b.forward(x)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for b in blocks:
+                b.forward(x)
+        for _ in range(3):
+            graph.replay()
+        reps = 20
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(reps):
+            graph.replay()
+        e.record()
+        torch.cuda.synchronize()
+        us = max_over_ranks(s.elapsed_time(e) * 1e3 / (reps * L))
+        byts = (distinct + L) * EXPERT_BYTES / L + 256 * 2048 * 2 + 2048 * 2 + 2 * T * 2048 * 2
+        gbs = byts / us / 1e3
+        out["sweep"][f"T{T}"] = {"us_per_layer": us, "hbm_gbs": gbs, "hbm_frac": gbs / hbm_peak,
+                                 "distinct_experts_per_layer": distinct / L,
+                                 "algorithmic_bytes_per_layer": byts}
+        del graph
+    for b in blocks:
+        b.close()
+    return out
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -300,6 +362,9 @@ def run_ours(args):
                 "d2h_bytes_per_step": T * H * 2},
         "gpu_launches": launches,
     }
+    if not args.no_decode:
+        line["decode"] = measure_decode(args, dev, rank, float(peaks["hbm_gbs"]), max_over_ranks)
+        line["decode"]["hbm_peak_gbs"] = float(peaks["hbm_gbs"])
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as O
 

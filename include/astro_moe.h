@@ -181,7 +181,11 @@ typedef struct {
   int64_t max_tokens;        /* workspace is sized for this many tokens per call */
   int32_t sorted_threshold;  /* 0 = 64, MINIMUM_SORTED_EXPERT_ASSIGNMENTS (routing.rs:13) */
   int32_t use_tensor_cores;  /* 0 = auto (tcgen05 path for 4-bit g64), -1 = never */
-  int64_t reserved[6];
+  int64_t decode_max_tokens; /* batches of at most this many tokens take the decode
+                                GEMVs (4-bit g64 layers); 0 = 8, -1 = never */
+  int64_t decode_fused;      /* decode batches of <= 16 tokens run as one cooperative
+                                kernel; 0 = auto, -1 = never (separate kernels) */
+  int64_t reserved[4];
 } astro_moe_options;
 
 /* One stacked affine projection in MLX layout (Qwen3_5AffineWeights::Quantized,
@@ -234,7 +238,7 @@ int astro_moe_block_forward(astro_moe_ctx* ctx, int32_t layer, const void* hidde
 int astro_moe_block_forward_taps(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
                                  int64_t tokens, void* out, const astro_moe_block_taps* taps);
 /* Per-stage device time of block calls, measured with CUDA events on the context
- * stream; the stage names follow PerformanceOperation
+ * stream (a fused decode call is one kernel; its time is reported as gate_up_ms); the stage names follow PerformanceOperation
  * (crates/model-serving/src/performance_attribution/catalog.rs:89-92), which in
  * the reference times only host graph construction. */
 typedef struct {

@@ -23,10 +23,16 @@ def small_cfg(**kw):
     return cfg
 
 
-def run_and_compare(cfg, T, seed=0, subset=None, fuse=False, use_tc=0):
+def block(w, path, **kw):
+    use_tc, decode, fused = path
+    return moe.Qwen3_5MoEBlock(w, use_tensor_cores=use_tc, decode_max_tokens=decode,
+                               decode_fused=fused, **kw)
+
+
+def run_and_compare(cfg, T, seed=0, subset=None, fuse=False, path=(0, 0, 0)):
     w = synthetic.make_block_weights(cfg, seed=seed)
     x = synthetic.make_hidden_states(T, cfg["hidden"], seed=seed + 1, zipf=bool(cfg.get("zipf")))
-    blk = moe.Qwen3_5MoEBlock(w, max_tokens=T, fuse_gate_up=fuse, use_tensor_cores=use_tc)
+    blk = block(w, path, max_tokens=T, fuse_gate_up=fuse)
     y, taps = blk.forward(bf16_tensor(x), taps=True)
     blk.synchronize()
     logits = to_np_bf16(taps["router_logits"])
@@ -54,21 +60,25 @@ def run_and_compare(cfg, T, seed=0, subset=None, fuse=False, use_tc=0):
     return metrics
 
 
-# path: 1 = tcgen05 tensor-core kernels (4-bit g64 layers), -1 = CUDA-core kernels
-PATHS = [pytest.param(1, id="tcgen05"), pytest.param(-1, id="cudacore")]
+# path = (use_tensor_cores, decode_max_tokens, decode_fused): the tcgen05 grouped
+# GEMMs, the CUDA-core grouped GEMV, the separate decode kernels (taken here up
+# to 1024 tokens so that segments of many rows are covered too), and the fused
+# decode kernel (T <= 16; larger T falls through to the separate decode kernels)
+PATHS = [pytest.param((1, -1, -1), id="tcgen05"), pytest.param((-1, -1, -1), id="cudacore"),
+         pytest.param((0, 1024, -1), id="decode"), pytest.param((0, 1024, 0), id="fused")]
 
 
 @pytest.mark.parametrize("path", PATHS)
 def test_block_config0_shape(path):
     cfg = dict(synthetic.CONFIGS[0])
-    run_and_compare(cfg, 32, use_tc=path)
+    run_and_compare(cfg, 32, path=path)
 
 
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("T", [1, 4, 7, 8, 16, 64, 200, 777])
 def test_block_config1_shape_small_T(T, path):
     # T*K < 64 takes the unsorted weighted sum (routing.rs:13), T >= 8 the sorted one
-    run_and_compare(small_cfg(), T, seed=T, use_tc=path)
+    run_and_compare(small_cfg(), T, seed=T, path=path)
 
 
 @pytest.mark.parametrize("path", PATHS)
@@ -76,7 +86,7 @@ def test_block_config1_shape_small_T(T, path):
 def test_block_decode_zipf(T, path):
     cfg = dict(synthetic.CONFIGS[2])
     cfg["tokens"] = T
-    run_and_compare(cfg, T, seed=100 + T, use_tc=path)
+    run_and_compare(cfg, T, seed=100 + T, path=path)
 
 
 @pytest.mark.parametrize("path", PATHS)
@@ -85,8 +95,8 @@ def test_block_fused_gate_up_equals_separate(path):
     cfg = small_cfg()
     w = synthetic.make_block_weights(cfg, seed=4)
     x = bf16_tensor(synthetic.make_hidden_states(96, cfg["hidden"], seed=5))
-    a = moe.Qwen3_5MoEBlock(w, max_tokens=96, fuse_gate_up=False, use_tensor_cores=path)
-    b = moe.Qwen3_5MoEBlock(w, max_tokens=96, fuse_gate_up=True, use_tensor_cores=path)
+    a = block(w, path, max_tokens=96, fuse_gate_up=False)
+    b = block(w, path, max_tokens=96, fuse_gate_up=True)
     ya, yb = a.forward(x), b.forward(x)
     torch.cuda.synchronize()
     assert torch.equal(ya, yb)
@@ -100,7 +110,7 @@ def test_block_full_size_config1_subset(path):
     token, so the oracle checks a sample of 48 rows of the full-size run."""
     rng = np.random.default_rng(7)
     subset = np.sort(rng.choice(4096, 48, replace=False))
-    run_and_compare(small_cfg(), 4096, seed=11, subset=subset, use_tc=path)
+    run_and_compare(small_cfg(), 4096, seed=11, subset=subset, path=path)
 
 
 @pytest.mark.parametrize("path", PATHS)
@@ -109,8 +119,8 @@ def test_block_paths_agree_within_tolerance(path):
     cfg = small_cfg()
     w = synthetic.make_block_weights(cfg, seed=21)
     x = bf16_tensor(synthetic.make_hidden_states(1024, cfg["hidden"], seed=22))
-    a = moe.Qwen3_5MoEBlock(w, max_tokens=1024, use_tensor_cores=1)
-    b = moe.Qwen3_5MoEBlock(w, max_tokens=1024, use_tensor_cores=-1)
+    a = block(w, (1, -1, -1), max_tokens=1024)
+    b = block(w, path, max_tokens=1024)
     ya, ta = a.forward(x, taps=True)
     yb, tb = b.forward(x, taps=True)
     torch.cuda.synchronize()
@@ -124,7 +134,7 @@ def test_block_paths_agree_within_tolerance(path):
 def test_block_deterministic_and_empty(path):
     cfg = small_cfg()
     w = synthetic.make_block_weights(cfg, seed=8)
-    blk = moe.Qwen3_5MoEBlock(w, max_tokens=512, use_tensor_cores=path)
+    blk = block(w, path, max_tokens=512)
     x = bf16_tensor(synthetic.make_hidden_states(512, cfg["hidden"], seed=9))
     y1 = blk.forward(x)
     y2 = blk.forward(x)
