@@ -102,6 +102,15 @@ struct LayerState {
   astro::MoeGemmPlan gemm{};  // tensor-core plan (TMA descriptors), when eligible
   bool decode_ok = false;     // the small-batch GEMVs cover this layer's geometry
   bool router_gemv_ok = false;
+  // expert-parallel layer: w.experts counts the local stacks, ep_total all experts
+  bool ep = false;
+  int ep_first = 0, ep_total = 0;
+};
+
+// Grow-only device buffer (synchronises the stream before replacing memory).
+struct DevBuf {
+  void* p = nullptr;
+  size_t bytes = 0;
 };
 
 struct astro_moe_ctx {
@@ -121,6 +130,10 @@ struct astro_moe_ctx {
   std::vector<std::vector<cudaEvent_t>> pending;  // 6 events per measured call
   astro_moe_attribution acc{};
   int64_t launches = 0;
+  // expert-parallel block in flight (dispatch -> experts -> combine)
+  DevBuf ep_disp, ep_exp, ep_shared;
+  int ep_layer = -1;
+  int64_t ep_tokens = -1;
 };
 
 namespace {
@@ -470,6 +483,128 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   return copy_taps(ctx, b, T, E, K, has_shared, taps);
 }
 
+// geometry and pointer checks of one layer's weights (register_layer and the
+// expert-parallel registration)
+int validate_layer(const char* op, const astro_moe_layer_weights* w) {
+  if (w->hidden <= 0 || w->experts <= 0 || w->top_k <= 0 || w->top_k > w->experts ||
+      w->intermediate <= 0 || w->shared_intermediate < 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid geometry", op);
+  if (w->top_k > 32 || w->experts > 1024)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: top_k <= 32 and experts <= 1024 are supported", op);
+  if (w->hidden % 8 != 0) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: hidden must be a multiple of 8", op);
+  if (int rc = check_affine(op, w->hidden, w->group_size, w->bits)) return rc;
+  if (int rc = check_affine(op, w->intermediate, w->group_size, w->bits)) return rc;
+  if (w->shared_intermediate > 0)
+    if (int rc = check_affine(op, w->shared_intermediate, w->group_size, w->bits)) return rc;
+  if (w->shared_intermediate != 0 && w->shared_intermediate != w->intermediate)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED,
+                "%s: the shared expert must have the routed intermediate width (or be absent)", op);
+  if (!w->router_weight) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight", op);
+  if (int rc = validate_affine_tensor("gate", w->gate)) return rc;
+  if (!w->gate_up_fused)
+    if (int rc = validate_affine_tensor("up", w->up)) return rc;
+  if (int rc = validate_affine_tensor("down", w->down)) return rc;
+  if (w->shared_intermediate > 0) {
+    if (int rc = validate_affine_tensor("shared gate", w->shared_gate)) return rc;
+    if (int rc = validate_affine_tensor("shared up", w->shared_up)) return rc;
+    if (int rc = validate_affine_tensor("shared down", w->shared_down)) return rc;
+    if (!w->shared_expert_gate) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate", op);
+  }
+  return ASTRO_MOE_OK;
+}
+
+int devbuf_ensure(astro_moe_ctx* ctx, DevBuf& b, size_t bytes) {
+  if (b.bytes >= bytes) return ASTRO_MOE_OK;
+  if (b.p) {
+    CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    cudaFree(b.p);
+    b.p = nullptr;
+    b.bytes = 0;
+  }
+  CK(cudaMalloc(&b.p, bytes), "cudaMalloc(expert-parallel buffers)");
+  b.bytes = bytes;
+  return ASTRO_MOE_OK;
+}
+
+// dispatch-side arrays of an expert-parallel layer for T tokens
+struct EpDispatch {
+  uint16_t* logits;
+  uint32_t* ids;
+  uint16_t* scores;
+  uint16_t* gate_logit;
+  uint32_t* order;
+  uint32_t* inverse;
+  uint32_t* sids;
+  uint32_t* stok;
+  void* sort_scratch;
+};
+size_t plan_ep_dispatch(int64_t T, int E, int K, EpDispatch* out, char* base) {
+  const int64_t N = T * K;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off = align_up(off + bytes, 256);
+    return p;
+  };
+  EpDispatch d{};
+  d.logits = (uint16_t*)take(sizeof(uint16_t) * T * E);
+  d.ids = (uint32_t*)take(sizeof(uint32_t) * N);
+  d.scores = (uint16_t*)take(sizeof(uint16_t) * N);
+  d.gate_logit = (uint16_t*)take(sizeof(uint16_t) * T);
+  d.order = (uint32_t*)take(sizeof(uint32_t) * N);
+  d.inverse = (uint32_t*)take(sizeof(uint32_t) * N);
+  d.sids = (uint32_t*)take(sizeof(uint32_t) * N);
+  d.stok = (uint32_t*)take(sizeof(uint32_t) * N);
+  d.sort_scratch = take(astro::sort_scratch_bytes(N, E));
+  if (out) *out = d;
+  return off;
+}
+
+// expert-side arrays for `rows` expert-major rows (received + shared)
+struct EpExperts {
+  uint16_t* states;
+  uint16_t* act;
+  uint16_t* yrows;
+  uint32_t* src_start;
+  uint32_t* exp_start;
+  uint32_t* offsets;
+  uint32_t* dest;
+  uint32_t* src_of;
+  void* gemm_scratch;
+};
+size_t plan_ep_experts(int64_t rows, int64_t n_recv, int H, int I, int runs, int El, EpExperts* out,
+                       char* base) {
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    char* p = base ? base + off : nullptr;
+    off = align_up(off + bytes, 256);
+    return p;
+  };
+  EpExperts e{};
+  e.states = (uint16_t*)take(sizeof(uint16_t) * rows * H);
+  e.act = (uint16_t*)take(sizeof(uint16_t) * rows * I);
+  e.yrows = (uint16_t*)take(sizeof(uint16_t) * rows * H);
+  e.src_start = (uint32_t*)take(sizeof(uint32_t) * runs);
+  e.exp_start = (uint32_t*)take(sizeof(uint32_t) * runs);
+  e.offsets = (uint32_t*)take(sizeof(uint32_t) * (El + 2));
+  e.dest = (uint32_t*)take(sizeof(uint32_t) * (n_recv > 0 ? n_recv : 1));
+  e.src_of = (uint32_t*)take(sizeof(uint32_t) * (n_recv > 0 ? n_recv : 1));
+  e.gemm_scratch = take(astro::moe_gemm_scratch_bytes());
+  if (out) *out = e;
+  return off;
+}
+
+int ep_layer(astro_moe_ctx* ctx, int32_t layer, const char* op, LayerState** out) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null ctx", op);
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.registered)
+    return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "%s: layer %d is not registered", op, layer);
+  if (!it->second.ep)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: layer %d is not an expert-parallel layer", op, layer);
+  *out = &it->second;
+  return ASTRO_MOE_OK;
+}
+
 }  // namespace
 
 int astro::set_last_error(int status, const char* message) {
@@ -754,30 +889,7 @@ int astro_moe_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_moe_
   const char* op = "register layer";
   if (!ctx || !w) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null argument", op);
   if (layer < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: negative layer index", op);
-  if (w->hidden <= 0 || w->experts <= 0 || w->top_k <= 0 || w->top_k > w->experts ||
-      w->intermediate <= 0 || w->shared_intermediate < 0)
-    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid geometry", op);
-  if (w->top_k > 32 || w->experts > 1024)
-    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: top_k <= 32 and experts <= 1024 are supported", op);
-  if (w->hidden % 8 != 0) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: hidden must be a multiple of 8", op);
-  if (int rc = check_affine(op, w->hidden, w->group_size, w->bits)) return rc;
-  if (int rc = check_affine(op, w->intermediate, w->group_size, w->bits)) return rc;
-  if (w->shared_intermediate > 0)
-    if (int rc = check_affine(op, w->shared_intermediate, w->group_size, w->bits)) return rc;
-  if (w->shared_intermediate != 0 && w->shared_intermediate != w->intermediate)
-    return fail(ASTRO_MOE_ERR_UNSUPPORTED,
-                "%s: the shared expert must have the routed intermediate width (or be absent)", op);
-  if (!w->router_weight) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight", op);
-  if (int rc = validate_affine_tensor("gate", w->gate)) return rc;
-  if (!w->gate_up_fused)
-    if (int rc = validate_affine_tensor("up", w->up)) return rc;
-  if (int rc = validate_affine_tensor("down", w->down)) return rc;
-  if (w->shared_intermediate > 0) {
-    if (int rc = validate_affine_tensor("shared gate", w->shared_gate)) return rc;
-    if (int rc = validate_affine_tensor("shared up", w->shared_up)) return rc;
-    if (int rc = validate_affine_tensor("shared down", w->shared_down)) return rc;
-    if (!w->shared_expert_gate) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate", op);
-  }
+  if (int rc = validate_layer(op, w)) return rc;
   DeviceGuard g(ctx->device);
   LayerState& L = ctx->layers[layer];
   astro::moe_gemm_release(L.gemm);
@@ -805,6 +917,9 @@ int astro_moe_block_forward_taps(astro_moe_ctx* ctx, int32_t layer, const void* 
   auto it = ctx->layers.find(layer);
   if (it == ctx->layers.end() || !it->second.registered)
     return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "block forward: layer %d is not registered", layer);
+  if (it->second.ep)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "block forward: layer %d is expert-parallel (use astro_moe_ep_dispatch/experts/combine)", layer);
   if (T < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: negative token count");
   if (T * (int64_t)it->second.w.top_k + T > 0x7fffffffLL)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: too many tokens");
@@ -853,6 +968,8 @@ int astro_moe_block_forward_host(astro_moe_ctx* ctx, int32_t layer, const void* 
   auto it = ctx->layers.find(layer);
   if (it == ctx->layers.end() || !it->second.registered)
     return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "block forward: layer %d is not registered", layer);
+  if (it->second.ep)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: layer %d is expert-parallel", layer);
   if (T <= 0) return T == 0 ? ASTRO_MOE_OK : fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "negative tokens");
   DeviceGuard g(ctx->device);
   const size_t bytes = sizeof(uint16_t) * (size_t)T * it->second.w.hidden;
@@ -872,6 +989,201 @@ int astro_moe_block_forward_host(astro_moe_ctx* ctx, int32_t layer, const void* 
   if (int rc = run_block(ctx, it->second, dx, T, dy, nullptr)) return rc;
   CK(cudaMemcpyAsync(host_out, dy, bytes, cudaMemcpyDeviceToHost, ctx->stream), "copy output out");
   return astro_moe_ctx_synchronize(ctx);
+}
+
+
+// ===========================================================================
+// expert parallelism
+// ===========================================================================
+int astro_moe_ep_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_moe_layer_weights* w,
+                                int32_t expert_first, int32_t expert_count) {
+  const char* op = "register expert-parallel layer";
+  if (!ctx || !w) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null argument", op);
+  if (layer < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: negative layer index", op);
+  if (int rc = validate_layer(op, w)) return rc;
+  if (expert_first < 0 || expert_count < 1 || expert_first + expert_count > w->experts)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: local experts [%d, %d) outside [0, %d)", op,
+                expert_first, expert_first + expert_count, w->experts);
+  DeviceGuard g(ctx->device);
+  LayerState& L = ctx->layers[layer];
+  astro::moe_gemm_release(L.gemm);
+  astro_moe_layer_weights local = *w;
+  local.experts = expert_count;
+  L.w = local;
+  L.ep = true;
+  L.ep_first = expert_first;
+  L.ep_total = w->experts;
+  L.registered = true;
+  L.decode_ok = false;
+  if (int st = astro::moe_gemm_plan(local, &L.gemm, w->experts)) {
+    L.registered = false;
+    return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);
+  }
+  L.router_gemv_ok = (reinterpret_cast<uintptr_t>(w->router_weight) & 15u) == 0 &&
+                     astro::router_gemv_supported(w->hidden);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_dispatch(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T,
+                          void* send_rows, uint32_t* expert_offsets) {
+  const char* op = "expert-parallel dispatch";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_layer(ctx, layer, op, &Lp)) return rc;
+  LayerState& L = *Lp;
+  const astro_moe_layer_weights& w = L.w;
+  const int H = w.hidden, E = L.ep_total, K = w.top_k;
+  if (T < 0 || T * (int64_t)K > 0x7fffffffLL)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid token count", op);
+  if (T > 0 && (!x || !send_rows || !expert_offsets))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: hidden states must be 16-byte aligned", op);
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = ctx->stream;
+  const bool has_shared = w.shared_intermediate > 0;
+  EpDispatch d{};
+  if (int rc = devbuf_ensure(ctx, ctx->ep_disp, plan_ep_dispatch(T > 0 ? T : 1, E, K, nullptr, nullptr)))
+    return rc;
+  plan_ep_dispatch(T > 0 ? T : 1, E, K, &d, (char*)ctx->ep_disp.p);
+  ctx->ep_layer = layer;
+  ctx->ep_tokens = T;
+  if (T == 0) {
+    CK(cudaMemsetAsync(expert_offsets, 0, sizeof(uint32_t) * (E + 1), st), op);
+    return ASTRO_MOE_OK;
+  }
+  if (T <= kRouterGemvTokens && L.router_gemv_ok) {
+    CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, d.logits, st), "router projection");
+  } else if (astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores)) {
+    CK(astro::moe_gemm_router(L.gemm, x, T, d.logits, nullptr, ctx->status, st), "router projection");
+  } else {
+    CK(astro::launch_dense_nt_simt(x, w.router_weight, T, E, H, d.logits, E, st), "router projection");
+  }
+  CK(astro::launch_route_experts(d.logits, ASTRO_MOE_DTYPE_BF16, T, E, K, w.normalize_top_k, d.ids,
+                                 d.scores, x, has_shared ? w.shared_expert_gate : nullptr, H,
+                                 has_shared ? d.gate_logit : nullptr, st),
+     "route experts");
+  CK(astro::launch_sort_assignments(d.ids, T, K, E, 0, d.order, d.inverse, d.sids, d.stok,
+                                    expert_offsets, ctx->status, d.sort_scratch, st),
+     "sort expert assignments");
+  CK(astro::launch_take_rows(x, T, d.stok, T * K, H, send_rows, ctx->status, st), "gather rows");
+  ctx->launches += 3 + astro::sort_launch_count(T * K);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_rows,
+                         const uint32_t* recv_counts, int32_t world, int64_t recv_total,
+                         const void* x, int64_t T, void* out_rows) {
+  const char* op = "expert-parallel experts";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_layer(ctx, layer, op, &Lp)) return rc;
+  LayerState& L = *Lp;
+  const astro_moe_layer_weights& w = L.w;
+  const int H = w.hidden, El = w.experts, I = w.intermediate;
+  if (world < 1 || world * El > 2048)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: world * local experts must be <= 2048", op);
+  if (recv_total < 0 || T < 0 || recv_total + T > 0x7fffffffLL)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid row counts", op);
+  if (!recv_counts || (recv_total > 0 && (!recv_rows || !out_rows)) || (T > 0 && !x))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = ctx->stream;
+  const bool has_shared = w.shared_intermediate > 0;
+  const int64_t shared_rows = has_shared ? T : 0;
+  const int64_t rows = recv_total + shared_rows;
+  EpExperts e{};
+  if (int rc = devbuf_ensure(ctx, ctx->ep_exp,
+                             plan_ep_experts(rows, recv_total, H, I, world * El, El, nullptr, nullptr)))
+    return rc;
+  plan_ep_experts(rows, recv_total, H, I, world * El, El, &e, (char*)ctx->ep_exp.p);
+  if (has_shared)
+    if (int rc = devbuf_ensure(ctx, ctx->ep_shared, sizeof(uint16_t) * (size_t)(T > 0 ? T : 1) * H))
+      return rc;
+  CK(astro::launch_ep_permutation(recv_counts, world, El, (int)shared_rows, e.src_start, e.exp_start,
+                                  e.offsets, e.dest, e.src_of, st),
+     "expert-major permutation");
+  CK(astro::launch_take_rows(recv_rows, recv_total, e.src_of, recv_total, H, e.states, ctx->status, st),
+     "expert-major rows");
+  if (shared_rows > 0)
+    CK(cudaMemcpyAsync(e.states + recv_total * H, x, sizeof(uint16_t) * shared_rows * H,
+                       cudaMemcpyDeviceToDevice, st),
+       "shared-expert rows");
+  ctx->launches += 3;
+  if (rows > 0) {
+    if (astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores)) {
+      CK(astro::moe_gemm_gate_up(L.gemm, e.states, rows, e.offsets, e.act, e.gemm_scratch,
+                                 ctx->status, st),
+         "gate/up projection");
+      CK(astro::moe_gemm_down(L.gemm, e.act, rows, e.offsets, e.yrows, e.gemm_scratch, ctx->status,
+                              st),
+         "down projection");
+    } else {
+      astro::GroupedGemvDesc d;
+      d.x = e.states;
+      d.x_limit = rows;
+      d.in_features = H;
+      d.seg_offsets = e.offsets;
+      d.nseg = El + (has_shared ? 1 : 0);
+      d.shared_seg = has_shared ? El : -1;
+      d.rows_total = rows;
+      astro::AffineRef down[2];
+      fill_projections(w, d.wa, d.wb, down);
+      d.out_features = I;
+      d.group = w.group_size;
+      d.bits = w.bits;
+      d.swiglu = true;
+      d.y = e.act;
+      d.y_limit = rows;
+      d.ldy = I;
+      d.status = ctx->status;
+      CK(astro::launch_grouped_gemv(d, st), "gate/up projection");
+      astro::GroupedGemvDesc dd = d;
+      dd.x = e.act;
+      dd.in_features = I;
+      dd.wa[0] = down[0];
+      dd.wa[1] = down[1];
+      dd.wb[0] = dd.wb[1] = astro::AffineRef{};
+      dd.out_features = H;
+      dd.swiglu = false;
+      dd.y = e.yrows;
+      dd.ldy = H;
+      CK(astro::launch_grouped_gemv(dd, st), "down projection");
+    }
+    ctx->launches += 2;
+  }
+  CK(astro::launch_take_rows(e.yrows, rows, e.dest, recv_total, H, out_rows, ctx->status, st),
+     "received order");
+  if (shared_rows > 0)
+    CK(cudaMemcpyAsync(ctx->ep_shared.p, e.yrows + recv_total * H, sizeof(uint16_t) * shared_rows * H,
+                       cudaMemcpyDeviceToDevice, st),
+       "shared-expert rows");
+  ctx->launches += 1;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_combine(astro_moe_ctx* ctx, int32_t layer, const void* returned_rows, int64_t T,
+                         void* out) {
+  const char* op = "expert-parallel combine";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_layer(ctx, layer, op, &Lp)) return rc;
+  const astro_moe_layer_weights& w = Lp->w;
+  if (ctx->ep_layer != layer || ctx->ep_tokens != T)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "%s: layer %d with %lld tokens does not match the dispatch in flight", op, layer,
+                (long long)T);
+  if (T == 0) return ASTRO_MOE_OK;
+  if (!returned_rows || !out) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  const int H = w.hidden, E = Lp->ep_total, K = w.top_k;
+  const bool has_shared = w.shared_intermediate > 0;
+  DeviceGuard g(ctx->device);
+  EpDispatch d{};
+  plan_ep_dispatch(T, E, K, &d, (char*)ctx->ep_disp.p);
+  const int threshold = ctx->opt.sorted_threshold > 0 ? ctx->opt.sorted_threshold : 64;
+  CK(astro::launch_block_combine_split(returned_rows, has_shared ? ctx->ep_shared.p : returned_rows,
+                                       d.inverse, d.scores, has_shared ? d.gate_logit : nullptr, T, K,
+                                       H, T * K >= threshold ? 1 : 0, out, ctx->stream),
+     "weighted combine");
+  ctx->launches += 1;
+  return ASTRO_MOE_OK;
 }
 
 }  // extern "C"

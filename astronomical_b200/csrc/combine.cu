@@ -23,9 +23,10 @@ namespace astro {
 // memory first and combine_chunk issues the row loads of 8 slots before using
 // any, so a token costs two dependent memory round trips, not 2K.
 __global__ void __launch_bounds__(256) block_combine_kernel(
-    const uint4* __restrict__ rows, const uint32_t* __restrict__ inverse,
-    const __nv_bfloat16* __restrict__ scores, const __nv_bfloat16* __restrict__ gate_logit,
-    int64_t shared_base, int64_t tokens, int K, int H, int sorted, uint4* __restrict__ out) {
+    const uint4* __restrict__ rows, const uint4* __restrict__ shared_rows,
+    const uint32_t* __restrict__ inverse, const __nv_bfloat16* __restrict__ scores,
+    const __nv_bfloat16* __restrict__ gate_logit, int64_t shared_base, int64_t tokens, int K,
+    int H, int sorted, uint4* __restrict__ out) {
   __shared__ uint32_t s_row[32];
   __shared__ float s_score[32];
   const int chunks = H >> 3;
@@ -38,8 +39,8 @@ __global__ void __launch_bounds__(256) block_combine_kernel(
     if (gate_logit) sg = round_bf16(sigmoid_mlx(__bfloat162float(gate_logit[t])));
     __syncthreads();
     for (int c = threadIdx.x; c < chunks; c += blockDim.x)
-      out[t * chunks + c] = combine_chunk(rows, chunks, c, s_row, s_score, K, sorted != 0,
-                                          gate_logit ? shared_base + t : -1, sg);
+      out[t * chunks + c] = combine_chunk(rows, shared_rows, chunks, c, s_row, s_score, K,
+                                          sorted != 0, gate_logit ? shared_base + t : -1, sg);
     __syncthreads();  // s_row / s_score are rewritten for the next token
   }
 }
@@ -51,8 +52,21 @@ cudaError_t launch_block_combine(const void* rows, const uint32_t* inverse, cons
   int64_t blocks = tokens < 148 * 64 ? tokens : 148 * 64;
   const int threads = (H / 8) < 256 ? ((H / 8 + 31) / 32) * 32 : 256;
   block_combine_kernel<<<(unsigned)blocks, threads, 0, st>>>(
-      (const uint4*)rows, inverse, (const __nv_bfloat16*)scores,
+      (const uint4*)rows, (const uint4*)rows, inverse, (const __nv_bfloat16*)scores,
       (const __nv_bfloat16*)gate_logit, shared_base, tokens, K, H, sorted, (uint4*)out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_block_combine_split(const void* rows, const void* shared_rows,
+                                       const uint32_t* inverse, const void* scores,
+                                       const void* gate_logit, int64_t tokens, int K, int H,
+                                       int sorted, void* out, cudaStream_t st) {
+  if (tokens == 0) return cudaSuccess;
+  int64_t blocks = tokens < 148 * 64 ? tokens : 148 * 64;
+  const int threads = (H / 8) < 256 ? ((H / 8 + 31) / 32) * 32 : 256;
+  block_combine_kernel<<<(unsigned)blocks, threads, 0, st>>>(
+      (const uint4*)rows, (const uint4*)shared_rows, inverse, (const __nv_bfloat16*)scores,
+      (const __nv_bfloat16*)gate_logit, 0, tokens, K, H, sorted, (uint4*)out);
   return cudaGetLastError();
 }
 

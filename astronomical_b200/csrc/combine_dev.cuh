@@ -14,13 +14,14 @@ namespace astro {
 constexpr int kCombineSlots = 8;  // slot rows whose loads are issued together
 
 // rows: bf16 expert rows as uint4 [*, chunks]; slot_rows / slot_scores: the
-// token's K (row, score) pairs; shared_row < 0 means no shared expert.  Row
-// loads bypass L1 (the rows may have been written earlier in the same kernel).
-ASTRO_DEVINL uint4 combine_chunk(const uint4* rows, int chunks, int c, const uint32_t* slot_rows,
-                                 const float* slot_scores, int K, bool sorted, int64_t shared_row,
-                                 float sg) {
+// token's K (row, score) pairs; the shared expert's row is shared_rows[shared_row]
+// (shared_row < 0: no shared expert).  Row loads bypass L1 (the rows may have
+// been written earlier in the same kernel).
+ASTRO_DEVINL uint4 combine_chunk(const uint4* rows, const uint4* shared_rows, int chunks, int c,
+                                 const uint32_t* slot_rows, const float* slot_scores, int K,
+                                 bool sorted, int64_t shared_row, float sg) {
   uint4 sh = make_uint4(0, 0, 0, 0);
-  if (shared_row >= 0) sh = __ldcg(rows + shared_row * chunks + c);
+  if (shared_row >= 0) sh = __ldcg(shared_rows + shared_row * chunks + c);
   float acc[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) acc[j] = 0.f;

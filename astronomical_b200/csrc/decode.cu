@@ -863,8 +863,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
     uint4* out = reinterpret_cast<uint4*>(P.out);
     for (int u = gtid; u < T * kVecs; u += nthreads) {
       const int t = u / kVecs, c = u - t * kVecs;
-      out[u] = combine_chunk(rows, kVecs, c, s_inv + t * K, s_score + t * K, K, P.sorted != 0,
-                             P.has_shared ? (int64_t)(s_offs[E] + t) : -1, s_sg[t]);
+      out[u] = combine_chunk(rows, rows, kVecs, c, s_inv + t * K, s_score + t * K, K,
+                             P.sorted != 0, P.has_shared ? (int64_t)(s_offs[E] + t) : -1, s_sg[t]);
     }
   }
   (void)rows_total;

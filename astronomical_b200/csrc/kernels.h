@@ -31,6 +31,13 @@ cudaError_t launch_block_combine(const void* rows, const uint32_t* inverse, cons
                                  const void* gate_logit, int64_t shared_base, int64_t tokens,
                                  int K, int H, int sorted, void* out, cudaStream_t st);
 
+// Same with the shared expert's rows in their own array: shared_rows[t] (row t
+// of the token), routed rows through `inverse` into `rows`.
+cudaError_t launch_block_combine_split(const void* rows, const void* shared_rows,
+                                       const uint32_t* inverse, const void* scores,
+                                       const void* gate_logit, int64_t tokens, int K, int H,
+                                       int sorted, void* out, cudaStream_t st);
+
 cudaError_t launch_sorted_weighted_sum(const void* rows, int out_dtype, const uint32_t* inverse,
                                        const void* scores, int score_dtype, int64_t tokens, int K,
                                        int64_t dim, void* out, cudaStream_t st);
@@ -120,6 +127,14 @@ cudaError_t launch_offsets_from_sorted(const uint32_t* ids, int64_t n, int E, ui
                                        uint32_t* status, cudaStream_t st);
 cudaError_t launch_compose_rows(const uint32_t* lhs, const uint32_t* order, int64_t n,
                                 uint32_t* rows_out, cudaStream_t st);
+
+// Expert parallelism (ep.cu): from the received counts [world][El] (device),
+// the (source, expert) run starts in received and expert-major order, the
+// expert-major offsets [El + 2] (segment El: shared_rows rows), and the row maps
+// dest[received q] = expert-major position, src_of[dest[q]] = q.
+cudaError_t launch_ep_permutation(const uint32_t* counts, int world, int El, int shared_rows,
+                                  uint32_t* src_start, uint32_t* exp_start, uint32_t* offsets,
+                                  uint32_t* dest, uint32_t* src_of, cudaStream_t st);
 
 // Sets the calling thread's astro_moe_last_error() message and returns `status`
 // (for entry points defined outside api.cu).

@@ -687,7 +687,7 @@ cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
 
 }  // namespace
 
-int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan) {
+int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int router_rows) {
   plan->ok = false;
   plan->w = w;
   if (plan->dev) {
@@ -767,15 +767,17 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan) {
   dn.tile_rows = kMaxN;
   dn.out_cols = H;
   dn.ldo = H;
-  // router (dense bf16 A by TMA)
+  // router (dense bf16 A by TMA); its row count may exceed the stacked experts'
+  // (expert parallelism: all experts are routed, only the local ones are stacked)
   GemmParams& rt = d->router;
+  const int R = router_rows > 0 ? router_rows : E;
   ok &= make_map(&rt.tm_a[0][0], w.router_weight, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                 (uint64_t)H, (uint64_t)E, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+                 (uint64_t)H, (uint64_t)R, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   rt.kblocks = H / 64;
-  rt.fb_count = (E + 127) / 128;
+  rt.fb_count = (R + 127) / 128;
   rt.tile_rows = 64;
-  rt.out_cols = E;
-  rt.ldo = E;
+  rt.out_cols = R;
+  rt.ldo = R;
   rt.shared_seg = -1;
   rt.nseg = 1;
   rt.seg_offsets = nullptr;

@@ -17,7 +17,9 @@ struct MoeGemmPlan {
   astro_moe_layer_weights w{};
 };
 
-int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan);
+// router_rows > 0: the router projection has this many output rows (all experts
+// of an expert-parallel layer) while w.experts counts the stacked local experts.
+int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int router_rows = 0);
 void moe_gemm_release(MoeGemmPlan& plan);
 bool moe_gemm_enabled(const MoeGemmPlan& plan, int use_tensor_cores_option);
 size_t moe_gemm_scratch_bytes();

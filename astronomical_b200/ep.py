@@ -1,0 +1,233 @@
+"""Expert-parallel MoE block over the GPUs of one node (config 3).
+
+The reference runs the sorted MoE block on one device (MLX); this module splits
+the same block, ``Qwen3_5Model::forward_qwen3_5_moe`` (qwen3_5_moe/model/
+forward.rs:19-127), across ``world`` ranks with one process per GPU:
+
+* experts are block-partitioned: rank r owns experts [r*E/world, (r+1)*E/world);
+  the router and the shared expert are replicated, tokens stay data-parallel;
+* each rank routes and stably sorts its own tokens over all experts; since the
+  sort groups rows by expert, the rows bound for each rank are contiguous;
+* per-expert counts go out with one all-to-all, then the token rows with an
+  all-to-all-v (NCCL over NVLink/NVSwitch through torch.distributed);
+* the receiving rank permutes the rows into expert-major order, appends its own
+  tokens as the shared expert's segment and runs the grouped GEMMs;
+* the outputs travel back with the reverse all-to-all-v, and the source rank
+  forms the router-weighted sum plus the gated shared expert.
+
+Every token's output is computed with the single-GPU block's arithmetic, so an
+expert-parallel run reproduces ``Qwen3_5MoEBlock`` on the same tokens.
+
+The exchange logic (``ExpertParallelBlock``) is independent of where the expert
+arithmetic runs: it drives any object with ``dispatch`` / ``experts`` /
+``combine`` (``CudaExpertShard`` here, an oracle-backed stand-in in the CPU
+tests, which run it over gloo ranks).
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .moe import _ptr, _to_dev, check
+
+__all__ = ["expert_range", "local_expert_weights", "CudaExpertShard", "ExpertParallelBlock",
+           "ExpertParallelStack"]
+
+
+def expert_range(rank: int, world: int, experts: int) -> Tuple[int, int]:
+    """(first, count) of the experts rank `rank` owns; experts % world == 0."""
+    if experts % world != 0:
+        raise ValueError(f"{experts} experts do not split evenly over {world} ranks")
+    n = experts // world
+    return rank * n, n
+
+
+def local_expert_weights(weights: dict, first: int, count: int) -> dict:
+    """The layer's weights with only experts [first, first + count) in the routed
+    stacks (router, shared expert and its gate unchanged)."""
+    out = {"config": dict(weights["config"])}
+    for k, v in weights.items():
+        if k == "config" or v is None:
+            continue
+        if k.split("_")[0] in ("gate", "up", "down"):
+            out[k] = v[first:first + count]
+            if isinstance(out[k], torch.Tensor):
+                out[k] = out[k].contiguous()
+        else:
+            out[k] = v
+    return out
+
+
+class CudaExpertShard:
+    """This rank's part of expert-parallel MoE layers on its GPU (libastro_moe).
+
+    ``layers``: per layer, the weights dict of astronomical_b200.synthetic (full
+    router, shared expert; routed stacks may be full or already local)."""
+
+    def __init__(self, layers: Sequence[dict], rank: int, world: int, device: int = 0,
+                 use_tensor_cores: int = 0, max_tokens: int = 4096):
+        self.rank, self.world = rank, world
+        self.device = torch.device("cuda", device)
+        cfg = layers[0]["config"]
+        self.cfg = dict(cfg)
+        self.E = cfg["experts"]
+        self.first, self.count = expert_range(rank, world, self.E)
+        opts = _lib.Options()
+        opts.max_tokens = max_tokens
+        opts.use_tensor_cores = use_tensor_cores
+        ctx = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(_lib.lib().astro_moe_ctx_create(device, ctypes.c_void_p(
+                torch.cuda.current_stream(self.device).cuda_stream), ctypes.byref(opts),
+                ctypes.byref(ctx)))
+        self.ctx = ctx
+        self._keep = []
+        for li, w in enumerate(layers):
+            if w["gate_q"].shape[0] != self.count:
+                w = local_expert_weights(w, self.first, self.count)
+            self._register(li, w)
+
+    def _register(self, layer: int, w: dict):
+        dev = self.device
+        t = {k: _to_dev(v, dev, bf16=k.endswith("_s") or k.endswith("_b") or
+                        k in ("router_w", "shared_gate_w"))
+             for k, v in w.items() if k != "config" and v is not None}
+        self._keep.append(t)
+        cfg = self.cfg
+
+        def aff(prefix):
+            if prefix + "_q" not in t:
+                return _lib.Affine()
+            return _lib.Affine(t[prefix + "_q"].data_ptr(), t[prefix + "_s"].data_ptr(),
+                               t[prefix + "_b"].data_ptr())
+
+        lw = _lib.LayerWeights()
+        lw.hidden, lw.experts, lw.top_k = cfg["hidden"], self.E, cfg["top_k"]
+        lw.intermediate = cfg["intermediate"]
+        lw.shared_intermediate = cfg.get("shared_intermediate", 0)
+        lw.group_size, lw.bits = cfg["group"], cfg["bits"]
+        lw.normalize_top_k = int(cfg.get("normalize", True))
+        lw.gate_up_fused = 0
+        lw.router_weight = t["router_w"].data_ptr()
+        lw.gate, lw.up, lw.down = aff("gate"), aff("up"), aff("down")
+        lw.shared_gate, lw.shared_up, lw.shared_down = aff("sgate"), aff("sup"), aff("sdown")
+        lw.shared_expert_gate = t["shared_gate_w"].data_ptr() if "shared_gate_w" in t else None
+        check(_lib.lib().astro_moe_ep_register_layer(self.ctx, layer, ctypes.byref(lw),
+                                                     self.first, self.count))
+
+    def _bind(self):
+        check(_lib.lib().astro_moe_ctx_set_stream(
+            self.ctx, ctypes.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)))
+
+    # -- the three compute steps of one layer ------------------------------------
+    def dispatch(self, layer: int, x: torch.Tensor):
+        T, H = x.shape
+        K = self.cfg["top_k"]
+        send = torch.empty((T * K, H), dtype=torch.bfloat16, device=x.device)
+        offsets = torch.empty(self.E + 1, dtype=torch.int32, device=x.device)
+        self._bind()
+        check(_lib.lib().astro_moe_ep_dispatch(self.ctx, layer, _ptr(x), T, _ptr(send),
+                                               _ptr(offsets)))
+        return send, offsets
+
+    def experts(self, layer: int, recv_rows: torch.Tensor, recv_counts: torch.Tensor,
+                recv_total: int, x: torch.Tensor) -> torch.Tensor:
+        out = torch.empty_like(recv_rows)
+        self._bind()
+        check(_lib.lib().astro_moe_ep_experts(self.ctx, layer, _ptr(recv_rows), _ptr(recv_counts),
+                                              self.world, recv_total, _ptr(x), x.shape[0],
+                                              _ptr(out)))
+        return out
+
+    def combine(self, layer: int, returned: torch.Tensor, T: int) -> torch.Tensor:
+        out = torch.empty((T, self.cfg["hidden"]), dtype=torch.bfloat16, device=returned.device)
+        self._bind()
+        check(_lib.lib().astro_moe_ep_combine(self.ctx, layer, _ptr(returned), T, _ptr(out)))
+        return out
+
+    def kernel_launches(self, reset: bool = True) -> int:
+        a = _lib.Attribution()
+        check(_lib.lib().astro_moe_ctx_read_attribution(self.ctx, ctypes.byref(a), int(reset)))
+        return int(a.kernel_launches)
+
+    def close(self):
+        if getattr(self, "ctx", None):
+            _lib.lib().astro_moe_ctx_destroy(self.ctx)
+            self.ctx = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class ExpertParallelBlock:
+    """One layer's exchange: dispatch -> all-to-all -> experts -> all-to-all -> combine.
+
+    ``shard`` provides dispatch/experts/combine for this rank; ``group`` is the
+    process group of the `world` ranks (default: the world group)."""
+
+    def __init__(self, shard, rank: int, world: int, experts: int, group=None):
+        self.shard, self.rank, self.world, self.E = shard, rank, world, experts
+        self.El = expert_range(rank, world, experts)[1]
+        self.group = group
+        self.last_splits: Optional[Tuple[List[int], List[int]]] = None
+
+    def plan(self, offsets: torch.Tensor):
+        """Per-expert counts out, per-source counts in; returns host splits and the
+        device counts [world][El] this rank receives."""
+        counts = (offsets[1:] - offsets[:-1]).to(torch.int32).contiguous()
+        if self.world == 1:
+            recv_counts = counts
+        else:
+            recv_counts = torch.empty(self.world * self.El, dtype=torch.int32, device=offsets.device)
+            dist.all_to_all_single(recv_counts, counts, group=self.group)
+        offs_h = offsets.cpu()
+        rc_h = recv_counts.cpu()
+        send_splits = [int(offs_h[(r + 1) * self.El] - offs_h[r * self.El]) for r in range(self.world)]
+        recv_splits = [int(v) for v in rc_h.view(self.world, self.El).sum(1)]
+        return send_splits, recv_splits, recv_counts
+
+    def forward(self, layer: int, x: torch.Tensor, marks=None) -> torch.Tensor:
+        """``marks``: optional callable recording a named point (stage timing)."""
+        T = x.shape[0]
+        mark = marks or (lambda name: None)
+        send, offsets = self.shard.dispatch(layer, x)
+        mark("dispatch")
+        send_splits, recv_splits, recv_counts = self.plan(offsets)
+        self.last_splits = (send_splits, recv_splits)
+        recv_total = sum(recv_splits)
+        if self.world == 1:
+            recv = send
+        else:
+            recv = send.new_empty((recv_total,) + tuple(send.shape[1:]))
+            dist.all_to_all_single(recv, send, recv_splits, send_splits, group=self.group)
+        mark("exchange_out")
+        out_rows = self.shard.experts(layer, recv, recv_counts, recv_total, x)
+        mark("experts")
+        if self.world == 1:
+            returned = out_rows
+        else:
+            returned = torch.empty_like(send)
+            dist.all_to_all_single(returned, out_rows, send_splits, recv_splits, group=self.group)
+        mark("exchange_back")
+        y = self.shard.combine(layer, returned, T)
+        mark("combine")
+        return y
+
+
+class ExpertParallelStack:
+    """A stack of expert-parallel MoE layers (config 3: the decoder's attention is
+    replaced by identity, so every layer reads the same hidden states)."""
+
+    def __init__(self, shard, rank: int, world: int, experts: int, layers: int, group=None):
+        self.block = ExpertParallelBlock(shard, rank, world, experts, group)
+        self.layers = layers
+
+    def forward(self, x: torch.Tensor) -> List[torch.Tensor]:
+        return [self.block.forward(l, x) for l in range(self.layers)]

@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--use-tensor-cores", type=int, default=0)
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode sweep")
+    ap.add_argument("--no-stack", action="store_true", help="skip the config-3 40-layer stack")
+    ap.add_argument("--stack-layers", type=int, default=40)
+    ap.add_argument("--stack-tokens", type=int, default=16384)
     ap.add_argument("--decode-layers", type=int, default=16)
     ap.add_argument("--profile", action="store_true",
                     help="only W warm-up and K plain steps (for ncu captures; prints nothing)")
@@ -221,6 +224,189 @@ def measure_decode(args, dev, rank, hbm_peak, max_over_ranks):
         b.close()
     return out
 
+NVLINK_GBS = 770.0  # measured peer copy per direction per GPU on this pool (900 nominal)
+
+
+def stage_marker(dev):
+    """Records CUDA events on the current stream at named points; .ms() gives the
+    per-stage device time between consecutive points."""
+    import torch
+
+    class M:
+        def __init__(self):
+            self.ev = []
+
+        def __call__(self, name):
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.ev.append((name, e))
+
+        def ms(self):
+            torch.cuda.synchronize(dev)
+            out = {}
+            for (_, a), (n, b) in zip(self.ev, self.ev[1:]):
+                out[n + "_ms"] = out.get(n + "_ms", 0.0) + a.elapsed_time(b)
+            return out
+    return M()
+
+
+def run_ep(args, rank, world, local, dev):
+    """N > 1: the config-1 block expert-parallel over N GPUs (256/N experts and
+    4096 tokens per GPU: weak scaling, so N = 1 is the single-GPU headline), then
+    the config-3 stack."""
+    import torch
+    import torch.distributed as dist
+
+    from astronomical_b200 import synthetic
+    from astronomical_b200.ep import CudaExpertShard, ExpertParallelBlock
+
+    cfg = dict(synthetic.CONFIGS[1])
+    T, H, E, K, I = args.tokens, cfg["hidden"], cfg["experts"], cfg["top_k"], cfg["intermediate"]
+    Is = cfg["shared_intermediate"]
+    w = synthetic.make_block_weights_torch(cfg, seed=1234, device=dev)  # one model, all ranks
+    shard = CudaExpertShard([w], rank, world, device=local, max_tokens=T)
+    del w
+    torch.cuda.empty_cache()
+    block = ExpertParallelBlock(shard, rank, world, E)
+    g = torch.Generator(device=dev)
+    g.manual_seed(99 + rank)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        block.forward(0, x)
+    shard.kernel_launches(reset=True)
+    clocks = ClockSampler(local)
+    clocks.start()
+    t_end = time.time() + 1.0
+    while time.time() < t_end:
+        block.forward(0, x)
+    dist.barrier()
+    torch.cuda.synchronize()
+    shard.kernel_launches(reset=True)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        block.forward(0, x)
+    end.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    launches = shard.kernel_launches(reset=True)
+    ms = max_over_ranks(start.elapsed_time(end) / args.steps)
+    value = T * world / (ms / 1e3)
+    sent_remote = sum(v for r, v in enumerate(block.last_splits[0]) if r != rank)
+    nvlink_bytes = max_over_ranks(2.0 * sent_remote * H * 2)  # rows out and back, per rank
+    # stage attribution (events on the launching stream), a separate pass
+    m = stage_marker(dev)
+    for _ in range(args.steps):
+        m("start")
+        block.forward(0, x, marks=m)
+    stages = {k: v / args.steps for k, v in m.ms().items() if k != "start_ms"}
+    rows = T * K + T
+    flops = 2.0 * T * K * 3 * H * I + 2.0 * T * 3 * H * Is + 2.0 * T * H * E + 2.0 * T * H
+    peaks, kind = load_peaks()
+    t_tensor = flops / (float(peaks["bf16_tflops"]) * 1e12)
+    t_link = nvlink_bytes / (NVLINK_GBS * 1e9)
+    target_ms = max(t_tensor, t_link) * 1e3
+    # e2e through the public API with host buffers
+    hx = x.cpu().pin_memory()
+    hy = torch.empty_like(hx).pin_memory()
+    for _ in range(max(1, args.warmup)):
+        hy.copy_(block.forward(0, hx.to(dev, non_blocking=True)), non_blocking=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        hy.copy_(block.forward(0, hx.to(dev, non_blocking=True)), non_blocking=True)
+    e2.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps)
+    line = {
+        "metric": "moe_block_prefill_tokens_per_s", "value": value, "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded; weights int4 affine g64 in MLX layout, q~U{0..15}, "
+                "scales |N(0,0.01)|, biases -8*scale, router N(0,0.02), x~N(0,1))",
+        "config": {"workload": "config1_qwen3.6-35b-a3b_moe_block_prefill_expert_parallel",
+                   "tokens_per_gpu": T, "tokens": T * world, "hidden": H, "experts": E,
+                   "experts_per_gpu": E // world, "top_k": K, "intermediate": I,
+                   "shared_intermediate": Is, "quant": "affine int4 g64",
+                   "parallelism": f"ep{world}", "exchange": "NCCL all-to-all-v (torch.distributed)",
+                   "l2": "inputs larger than L2 (expert weights read per step exceed 126 MB "
+                         "per GPU for N <= 2; L2 not flushed)"},
+        "roofline": {"bound": "nvlink" if t_link > t_tensor else "tensor",
+                     "achieved_ms": ms, "target_ms": target_ms, "frac": target_ms / ms,
+                     "peak": {"bf16_tflops": float(peaks["bf16_tflops"]), "nvlink_gbs": NVLINK_GBS},
+                     "unit": "ms", "flop_per_gpu": flops, "nvlink_bytes_per_gpu": nvlink_bytes,
+                     "peak_kind": kind, "traffic": None},
+        "stages_ms": stages,
+        "clocks": clk,
+        "e2e": {"value": T * world / (e2e_ms / 1e3), "unit": "tokens/s",
+                "h2d_bytes_per_step": T * H * 2 * world, "d2h_bytes_per_step": T * H * 2 * world},
+        "gpu_launches": launches,
+    }
+    shard.close()
+    del block, shard
+    torch.cuda.empty_cache()
+    return line
+
+
+def measure_stack(args, rank, world, local, dev, max_over_ranks):
+    """Config 3: `stack_layers` layers of the config-1 block (attention replaced by
+    identity) expert-parallel over the N GPUs, stack_tokens tokens per step split
+    over the ranks (strong scaling).  N = 1 runs the same stack on one GPU."""
+    import torch
+    import torch.distributed as dist
+
+    from astronomical_b200 import synthetic
+    from astronomical_b200.ep import CudaExpertShard, ExpertParallelBlock, local_expert_weights, expert_range
+
+    cfg = dict(synthetic.CONFIGS[1])
+    L, H, E = args.stack_layers, cfg["hidden"], cfg["experts"]
+    T = args.stack_tokens // world
+    first, count = expert_range(rank, world, E)
+    layers = []
+    for l in range(L):
+        w = synthetic.make_block_weights_torch(cfg, seed=4000 + l, device=dev)
+        layers.append(local_expert_weights(w, first, count))
+        del w
+    torch.cuda.empty_cache()
+    shard = CudaExpertShard(layers, rank, world, device=local, max_tokens=T)
+    del layers
+    torch.cuda.empty_cache()
+    block = ExpertParallelBlock(shard, rank, world, E)
+    g = torch.Generator(device=dev)
+    g.manual_seed(500 + rank)
+    x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
+    for l in range(L):
+        block.forward(l, x)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    steps = 3
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        for l in range(L):
+            block.forward(l, x)
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / steps)
+    shard.close()
+    del block, shard
+    torch.cuda.empty_cache()
+    return {"workload": "config3_40_layer_stack_expert_parallel", "layers": L,
+            "tokens_per_step": args.stack_tokens, "tokens_per_gpu": T, "experts_per_gpu": count,
+            "scaling": "strong", "ms_per_step": ms, "tokens_per_s": args.stack_tokens / (ms / 1e3),
+            "us_per_layer": ms * 1e3 / L, "routing": "near-uniform (router N(0,0.02))"}
+
+
 
 def run_ours(args):
     import numpy as np
@@ -235,7 +421,23 @@ def run_ours(args):
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if world > 1:
-        dist.init_process_group("nccl", device_id=dev)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        line = run_ep(args, rank, world, local, dev)
+
+        def mor(v):
+            t = torch.tensor([v], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        if not args.no_stack:
+            line["stack"] = measure_stack(args, rank, world, local, dev, mor)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
 
     cfg = dict(synthetic.CONFIGS[1])
     T, H, E, K, I = args.tokens, cfg["hidden"], cfg["experts"], cfg["top_k"], cfg["intermediate"]
@@ -365,6 +567,11 @@ def run_ours(args):
     if not args.no_decode:
         line["decode"] = measure_decode(args, dev, rank, float(peaks["hbm_gbs"]), max_over_ranks)
         line["decode"]["hbm_peak_gbs"] = float(peaks["hbm_gbs"])
+    if not args.no_stack:
+        blk.close()
+        del w
+        torch.cuda.empty_cache()
+        line["stack"] = measure_stack(args, rank, world, local, dev, max_over_ranks)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as O
 

@@ -259,6 +259,49 @@ int astro_moe_ctx_read_attribution(astro_moe_ctx* ctx, astro_moe_attribution* ou
 int astro_moe_block_forward_host(astro_moe_ctx* ctx, int32_t layer, const void* host_hidden,
                                  int64_t tokens, void* host_out);
 
+/* ------------------------------------------------------------------------ */
+/* Expert parallelism over the GPUs of one node.  No counterpart in the       */
+/* reference (MLX runs the block on one device); it splits the same block      */
+/* (forward.rs:19-127) so that rank r of `world` holds experts                 */
+/* [r*E/world, (r+1)*E/world) and tokens stay data-parallel.  One layer call    */
+/* is dispatch -> (caller's all-to-all of rows) -> experts -> (all-to-all back) */
+/* -> combine, all stream-ordered on the context stream; the caller moves the   */
+/* rows (NCCL) between the calls.  One layer may be in flight per context.      */
+/* ------------------------------------------------------------------------ */
+
+/* `weights` describes the whole layer for routing (experts = all experts,
+ * router_weight [experts, H], shared expert and its gate), but gate/up/down hold
+ * only this rank's experts [expert_first, expert_first + expert_count) as
+ * stacks of expert_count experts (MLX layout). */
+int astro_moe_ep_register_layer(astro_moe_ctx* ctx, int32_t layer,
+                                const astro_moe_layer_weights* weights, int32_t expert_first,
+                                int32_t expert_count);
+
+/* Router, routing and the stable sort of this rank's tokens over ALL experts,
+ * then the gather of the sorted token rows: send_rows bf16 [tokens*top_k, H]
+ * in expert order, so the rows for each rank's experts are contiguous;
+ * expert_offsets uint32 [experts + 1] (device).  The routing is kept in the
+ * context for astro_moe_ep_combine. */
+int astro_moe_ep_dispatch(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                          int64_t tokens, void* send_rows, uint32_t* expert_offsets);
+
+/* Runs this rank's experts on the rows received from all `world` ranks:
+ * recv_rows bf16 [recv_total, H], source-major and, within a source, in expert
+ * order; recv_counts uint32 [world][expert_count] (device) are the per-source,
+ * per-expert row counts (recv_total = their sum, host value).  out_rows bf16
+ * [recv_total, H] receives the expert outputs in the received order.  The
+ * shared expert runs here on this rank's own `tokens` hidden states and is
+ * kept for the combine. */
+int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_rows,
+                         const uint32_t* recv_counts, int32_t world, int64_t recv_total,
+                         const void* hidden_states, int64_t tokens, void* out_rows);
+
+/* returned_rows bf16 [tokens*top_k, H]: the expert outputs of send_rows, in
+ * send order.  out bf16 [tokens, H] = router-weighted sum + gated shared expert,
+ * the same arithmetic as astro_moe_block_forward. */
+int astro_moe_ep_combine(astro_moe_ctx* ctx, int32_t layer, const void* returned_rows,
+                         int64_t tokens, void* out);
+
 #ifdef __cplusplus
 }
 #endif
