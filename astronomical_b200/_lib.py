@@ -57,6 +57,16 @@ class BlockTaps(ctypes.Structure):
                 ("selected_scores", ctypes.c_void_p), ("expert_offsets", ctypes.c_void_p)]
 
 
+class PagerStats(ctypes.Structure):
+    _fields_ = [("lookups", ctypes.c_int64), ("hits", ctypes.c_int64), ("misses", ctypes.c_int64),
+                ("evictions", ctypes.c_int64), ("bytes_h2d", ctypes.c_int64),
+                ("copy_ms", ctypes.c_double), ("resident_pages", ctypes.c_int64),
+                ("capacity_pages", ctypes.c_int64)]
+
+    def as_dict(self):
+        return {n: getattr(self, n) for n, _ in self._fields_}
+
+
 class Attribution(ctypes.Structure):
     _fields_ = [("calls", ctypes.c_int64), ("kernel_launches", ctypes.c_int64),
                 ("router_projection_ms", ctypes.c_double),
@@ -109,6 +119,13 @@ SIGNATURES = {
     "astro_moe_ep_dispatch": ([_P, _I32, _P, _I64, _P, _P], ctypes.c_int),
     "astro_moe_ep_experts": ([_P, _I32, _P, _P, _I32, _I64, _P, _I64, _P], ctypes.c_int),
     "astro_moe_ep_combine": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
+    "astro_moe_page_bytes": ([_I32, _I32, _I32, _I32], ctypes.c_int64),
+    "astro_moe_pager_create": ([_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64,
+                                ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "astro_moe_pager_destroy": ([_P], ctypes.c_int),
+    "astro_moe_pager_read_stats": ([_P, ctypes.POINTER(PagerStats), _I32], ctypes.c_int),
+    "astro_moe_register_paged_layer": ([_P, _I32, ctypes.POINTER(LayerWeights), _P], ctypes.c_int),
+    "astro_moe_paged_block_forward": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
 }
 
 

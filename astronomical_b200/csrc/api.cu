@@ -16,6 +16,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <list>
 #include <map>
 #include <mutex>
 #include <string>
@@ -105,6 +106,8 @@ struct LayerState {
   // expert-parallel layer: w.experts counts the local stacks, ep_total all experts
   bool ep = false;
   int ep_first = 0, ep_total = 0;
+  // paged layer: routed experts come from the pager's pages of this layer
+  astro_moe_pager* pager = nullptr;
 };
 
 // Grow-only device buffer (synchronises the stream before replacing memory).
@@ -134,6 +137,31 @@ struct astro_moe_ctx {
   DevBuf ep_disp, ep_exp, ep_shared;
   int ep_layer = -1;
   int64_t ep_tokens = -1;
+};
+
+// Expert page cache: pinned host pages, HBM slots, LRU over slots (host side).
+struct astro_moe_pager {
+  int device = 0;
+  int layers = 0, E = 0, H = 0, I = 0, group = 64, bits = 4;
+  int64_t page_bytes = 0;
+  // byte offsets of the nine tensors inside a page
+  int64_t off_q[3] = {0, 0, 0}, off_s[3] = {0, 0, 0}, off_b[3] = {0, 0, 0};
+  const char* host = nullptr;
+  char* pool = nullptr;
+  int64_t slots = 0, used = 0;
+  std::vector<int32_t> slot_of_page;   // [layers * E] -> slot or -1
+  std::vector<int64_t> page_of_slot;   // [slots] -> page or -1
+  std::vector<int64_t> last_call;      // [slots] call that last needed the slot
+  std::list<int64_t> lru;              // slots, most recently used first
+  std::vector<std::list<int64_t>::iterator> lru_pos;
+  int64_t call = 0;
+  cudaStream_t copy = nullptr;
+  cudaEvent_t ready = nullptr;
+  uint32_t* h_offsets = nullptr;  // pinned [E + 2]
+  uint32_t* h_table = nullptr;    // pinned [E]
+  uint32_t* d_table = nullptr;    // device [E]
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending, spare;
+  astro_moe_pager_stats st{};
 };
 
 namespace {
@@ -605,6 +633,161 @@ int ep_layer(astro_moe_ctx* ctx, int32_t layer, const char* op, LayerState** out
   return ASTRO_MOE_OK;
 }
 
+// page-major view of the pager's pool as stacked tensors (slot = expert index)
+astro::AffineRef pool_ref(const astro_moe_pager* pg, int m, int64_t code_row_bytes, int64_t sb_row_bytes) {
+  astro::AffineRef r;
+  r.q = pg->pool + pg->off_q[m];
+  r.s = pg->pool + pg->off_s[m];
+  r.b = pg->pool + pg->off_b[m];
+  r.expert_rows = pg->page_bytes / code_row_bytes;
+  r.sb_expert_rows = pg->page_bytes / sb_row_bytes;
+  r.row_offset = 0;
+  return r;
+}
+
+// LRU admission of the experts one block call routes to; returns the number of
+// page copies issued on the pager's copy stream.
+int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs) {
+  pg->call += 1;
+  int64_t copies = 0;
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  for (int e = 0; e < pg->E; ++e) {
+    pg->h_table[e] = 0;
+    if (offs[e + 1] <= offs[e]) continue;
+    const int64_t page = (int64_t)layer * pg->E + e;
+    pg->st.lookups += 1;
+    int64_t slot = pg->slot_of_page[page];
+    if (slot >= 0) {
+      pg->st.hits += 1;
+      pg->lru.splice(pg->lru.begin(), pg->lru, pg->lru_pos[slot]);
+    } else {
+      pg->st.misses += 1;
+      if (pg->used < pg->slots) {
+        slot = pg->used++;
+        pg->lru.push_front(slot);
+        pg->lru_pos[slot] = pg->lru.begin();
+      } else {
+        // least recently used slot that this call does not need
+        auto it = pg->lru.end();
+        do {
+          --it;
+        } while (pg->last_call[*it] == pg->call && it != pg->lru.begin());
+        slot = *it;
+        pg->slot_of_page[pg->page_of_slot[slot]] = -1;
+        pg->st.evictions += 1;
+        pg->lru.splice(pg->lru.begin(), pg->lru, it);
+      }
+      pg->slot_of_page[page] = (int32_t)slot;
+      pg->page_of_slot[slot] = page;
+      if (copies == 0) {
+        if (pg->spare.empty()) {
+          cudaEventCreate(&e0);
+          cudaEventCreate(&e1);
+        } else {
+          e0 = pg->spare.back().first;
+          e1 = pg->spare.back().second;
+          pg->spare.pop_back();
+        }
+        cudaEventRecord(e0, pg->copy);
+      }
+      cudaMemcpyAsync(pg->pool + slot * pg->page_bytes, pg->host + page * pg->page_bytes,
+                      (size_t)pg->page_bytes, cudaMemcpyHostToDevice, pg->copy);
+      pg->st.bytes_h2d += pg->page_bytes;
+      copies += 1;
+    }
+    pg->last_call[slot] = pg->call;
+    pg->h_table[e] = (uint32_t)slot;
+  }
+  if (copies) {
+    cudaEventRecord(e1, pg->copy);
+    pg->pending.emplace_back(e0, e1);
+  }
+  pg->st.resident_pages = pg->used;
+  return copies;
+}
+
+int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x, int64_t T, void* out) {
+  const char* op = "paged block forward";
+  astro_moe_pager* pg = L.pager;
+  const astro_moe_layer_weights& w = L.w;
+  const int H = w.hidden, E = w.experts, K = w.top_k, I = w.intermediate;
+  const bool has_shared = w.shared_intermediate > 0;
+  cudaStream_t st = ctx->stream;
+  if (T == 0) return ASTRO_MOE_OK;
+  const size_t need = plan_workspace(w, T, nullptr, nullptr);
+  if (int rc = ensure_ws(ctx, need)) return rc;
+  BlockWorkspace b{};
+  plan_workspace(w, T, &b, (char*)ctx->ws);
+  const int64_t N = T * K;
+  const int64_t rows = N + (has_shared ? T : 0);
+  const int threshold = ctx->opt.sorted_threshold > 0 ? ctx->opt.sorted_threshold : 64;
+  if (L.router_gemv_ok) {
+    CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, b.logits, st), "router projection");
+  } else {
+    CK(astro::launch_dense_nt_simt(x, w.router_weight, T, E, H, b.logits, E, st), "router projection");
+  }
+  CK(astro::launch_route_experts(b.logits, ASTRO_MOE_DTYPE_BF16, T, E, K, w.normalize_top_k, b.ids,
+                                 b.scores, x, has_shared ? w.shared_expert_gate : nullptr, H,
+                                 has_shared ? b.gate_logit : nullptr, st),
+     "route experts");
+  CK(astro::launch_sort_assignments(b.ids, T, K, E, has_shared ? T : 0, b.order, b.inverse, b.sids,
+                                    b.stok, b.offsets, ctx->status, b.sort_scratch, st),
+     "sort expert assignments");
+  // the routed experts, back on the host (the reference's pager syncs here too)
+  CK(cudaMemcpyAsync(pg->h_offsets, b.offsets, sizeof(uint32_t) * (E + 2), cudaMemcpyDeviceToHost, st),
+     "read back expert offsets");
+  CK(cudaStreamSynchronize(st), "cudaStreamSynchronize");
+  admit_pages(pg, layer, pg->h_offsets);
+  CK(cudaMemcpyAsync(pg->d_table, pg->h_table, sizeof(uint32_t) * E, cudaMemcpyHostToDevice, pg->copy),
+     "slot table");
+  CK(cudaEventRecord(pg->ready, pg->copy), op);
+  CK(cudaStreamWaitEvent(st, pg->ready, 0), op);
+  astro::GroupedGemvDesc d;
+  d.x = x;
+  d.x_rows = b.stok;
+  d.x_limit = T;
+  d.in_features = H;
+  d.seg_offsets = b.offsets;
+  d.nseg = E + (has_shared ? 1 : 0);
+  d.shared_seg = has_shared ? E : -1;
+  d.rows_total = rows;
+  astro::AffineRef g[2], u[2], dn[2];
+  fill_projections(w, g, u, dn);  // shared expert refs (the routed ones are replaced)
+  d.wa[0] = pool_ref(pg, 0, (int64_t)H * pg->bits / 8, (int64_t)(H / pg->group) * 2);
+  d.wb[0] = pool_ref(pg, 1, (int64_t)H * pg->bits / 8, (int64_t)(H / pg->group) * 2);
+  d.wa[1] = g[1];
+  d.wb[1] = u[1];
+  d.out_features = I;
+  d.group = w.group_size;
+  d.bits = w.bits;
+  d.swiglu = true;
+  d.y = b.act;
+  d.y_limit = rows;
+  d.ldy = I;
+  d.status = ctx->status;
+  d.slot_of = pg->d_table;
+  const int64_t max_active = (N < E ? N : E) + (has_shared ? 1 : 0);
+  CK(astro::launch_decode_gate_up(d, max_active, st), "gate/up projection");
+  astro::GroupedGemvDesc dd = d;
+  dd.x = b.act;
+  dd.x_rows = nullptr;
+  dd.x_limit = rows;
+  dd.in_features = I;
+  dd.wa[0] = pool_ref(pg, 2, (int64_t)I * pg->bits / 8, (int64_t)(I / pg->group) * 2);
+  dd.wa[1] = dn[1];
+  dd.wb[0] = dd.wb[1] = astro::AffineRef{};
+  dd.out_features = H;
+  dd.swiglu = false;
+  dd.y = b.yrows;
+  dd.ldy = H;
+  CK(astro::launch_decode_down(dd, max_active, st), "down projection");
+  CK(astro::launch_block_combine(b.yrows, b.inverse, b.scores, has_shared ? b.gate_logit : nullptr,
+                                 N, T, K, H, N >= threshold ? 1 : 0, out, st),
+     "weighted combine");
+  ctx->launches += 6 + astro::sort_launch_count(N);
+  return ASTRO_MOE_OK;
+}
+
 }  // namespace
 
 int astro::set_last_error(int status, const char* message) {
@@ -920,6 +1103,9 @@ int astro_moe_block_forward_taps(astro_moe_ctx* ctx, int32_t layer, const void* 
   if (it->second.ep)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
                 "block forward: layer %d is expert-parallel (use astro_moe_ep_dispatch/experts/combine)", layer);
+  if (it->second.pager)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "block forward: layer %d is paged (use astro_moe_paged_block_forward)", layer);
   if (T < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: negative token count");
   if (T * (int64_t)it->second.w.top_k + T > 0x7fffffffLL)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: too many tokens");
@@ -968,8 +1154,8 @@ int astro_moe_block_forward_host(astro_moe_ctx* ctx, int32_t layer, const void* 
   auto it = ctx->layers.find(layer);
   if (it == ctx->layers.end() || !it->second.registered)
     return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "block forward: layer %d is not registered", layer);
-  if (it->second.ep)
-    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: layer %d is expert-parallel", layer);
+  if (it->second.ep || it->second.pager)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "block forward: layer %d is expert-parallel or paged", layer);
   if (T <= 0) return T == 0 ? ASTRO_MOE_OK : fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "negative tokens");
   DeviceGuard g(ctx->device);
   const size_t bytes = sizeof(uint16_t) * (size_t)T * it->second.w.hidden;
@@ -1184,6 +1370,178 @@ int astro_moe_ep_combine(astro_moe_ctx* ctx, int32_t layer, const void* returned
      "weighted combine");
   ctx->launches += 1;
   return ASTRO_MOE_OK;
+}
+
+
+// ===========================================================================
+// expert paging
+// ===========================================================================
+int64_t astro_moe_page_bytes(int32_t H, int32_t I, int32_t G, int32_t bits) {
+  if (H <= 0 || I <= 0 || G <= 0 || bits <= 0 || H % G || I % G) return 0;
+  return (3LL * I * H) * bits / 8 + (2LL * I * (H / G) + (int64_t)H * (I / G)) * 2 * 2;
+}
+
+int astro_moe_pager_create(astro_moe_ctx* ctx, int32_t layers, int32_t experts, int32_t H,
+                           int32_t I, int32_t G, int32_t bits, const void* host_pages,
+                           int64_t cache_bytes, astro_moe_pager** out) {
+  const char* op = "pager create";
+  if (!ctx || !out || !host_pages) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null argument", op);
+  if (layers <= 0 || experts <= 0 || experts > 1024)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid layer or expert count", op);
+  if (bits != 4 || G != 64 || !astro::decode_gemv_supported(H, I, G, bits))
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: paged experts need 4-bit, group-64 layers of a decode-kernel shape", op);
+  const int64_t page = astro_moe_page_bytes(H, I, G, bits);
+  const int64_t rq_h = (int64_t)H * bits / 8, rs_h = (int64_t)(H / G) * 2;
+  const int64_t rq_i = (int64_t)I * bits / 8, rs_i = (int64_t)(I / G) * 2;
+  if (page % rq_h || page % rs_h || page % rq_i || page % rs_i || page % 16)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: page size does not tile the expert rows", op);
+  const int64_t slots = cache_bytes / page;
+  if (slots < 1) return fail(ASTRO_MOE_ERR_MEMORY_LIMIT, "%s: the cache ceiling holds no page", op);
+  DeviceGuard g(ctx->device);
+  cudaPointerAttributes attr{};
+  CK(cudaPointerGetAttributes(&attr, host_pages), "cudaPointerGetAttributes");
+  if (attr.type != cudaMemoryTypeHost)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: host_pages must be pinned host memory", op);
+  auto* pg = new astro_moe_pager();
+  pg->device = ctx->device;
+  pg->layers = layers;
+  pg->E = experts;
+  pg->H = H;
+  pg->I = I;
+  pg->group = G;
+  pg->bits = bits;
+  pg->page_bytes = page;
+  const int64_t cq = (int64_t)I * rq_h, cd = (int64_t)H * rq_i;
+  const int64_t cs = (int64_t)I * rs_h, cds = (int64_t)H * rs_i;
+  pg->off_q[0] = 0;
+  pg->off_q[1] = cq;
+  pg->off_q[2] = 2 * cq;
+  pg->off_s[0] = 2 * cq + cd;
+  pg->off_b[0] = pg->off_s[0] + cs;
+  pg->off_s[1] = pg->off_b[0] + cs;
+  pg->off_b[1] = pg->off_s[1] + cs;
+  pg->off_s[2] = pg->off_b[1] + cs;
+  pg->off_b[2] = pg->off_s[2] + cds;
+  pg->host = static_cast<const char*>(host_pages);
+  pg->slots = slots;
+  pg->slot_of_page.assign((size_t)layers * experts, -1);
+  pg->page_of_slot.assign((size_t)slots, -1);
+  pg->last_call.assign((size_t)slots, -1);
+  pg->lru_pos.resize((size_t)slots);
+  pg->st.capacity_pages = slots;
+  auto cleanup = [&](cudaError_t e, const char* what) {
+    if (pg->pool) cudaFree(pg->pool);
+    if (pg->d_table) cudaFree(pg->d_table);
+    if (pg->h_table) cudaFreeHost(pg->h_table);
+    if (pg->h_offsets) cudaFreeHost(pg->h_offsets);
+    if (pg->ready) cudaEventDestroy(pg->ready);
+    if (pg->copy) cudaStreamDestroy(pg->copy);
+    delete pg;
+    return cuda_fail(e, what);
+  };
+  cudaError_t e;
+  if ((e = cudaMalloc(&pg->pool, (size_t)(slots * page))) != cudaSuccess) return cleanup(e, "cudaMalloc(page cache)");
+  if ((e = cudaMalloc(&pg->d_table, sizeof(uint32_t) * experts)) != cudaSuccess) return cleanup(e, "cudaMalloc(slot table)");
+  if ((e = cudaHostAlloc(&pg->h_table, sizeof(uint32_t) * experts, cudaHostAllocDefault)) != cudaSuccess)
+    return cleanup(e, "cudaHostAlloc(slot table)");
+  if ((e = cudaHostAlloc(&pg->h_offsets, sizeof(uint32_t) * (experts + 2), cudaHostAllocDefault)) != cudaSuccess)
+    return cleanup(e, "cudaHostAlloc(offsets)");
+  if ((e = cudaEventCreateWithFlags(&pg->ready, cudaEventDisableTiming)) != cudaSuccess) return cleanup(e, "cudaEventCreate");
+  if ((e = cudaStreamCreateWithFlags(&pg->copy, cudaStreamNonBlocking)) != cudaSuccess) return cleanup(e, "cudaStreamCreate");
+  *out = pg;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_pager_destroy(astro_moe_pager* pg) {
+  if (!pg) return ASTRO_MOE_OK;
+  DeviceGuard g(pg->device);
+  cudaStreamSynchronize(pg->copy);
+  for (auto& p : pg->pending) {
+    cudaEventDestroy(p.first);
+    cudaEventDestroy(p.second);
+  }
+  for (auto& p : pg->spare) {
+    cudaEventDestroy(p.first);
+    cudaEventDestroy(p.second);
+  }
+  cudaFree(pg->pool);
+  cudaFree(pg->d_table);
+  cudaFreeHost(pg->h_table);
+  cudaFreeHost(pg->h_offsets);
+  cudaEventDestroy(pg->ready);
+  cudaStreamDestroy(pg->copy);
+  delete pg;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_pager_read_stats(astro_moe_pager* pg, astro_moe_pager_stats* out, int32_t reset) {
+  if (!pg || !out) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "pager stats: null argument");
+  DeviceGuard g(pg->device);
+  CK(cudaStreamSynchronize(pg->copy), "cudaStreamSynchronize");
+  for (auto& p : pg->pending) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, p.first, p.second);
+    pg->st.copy_ms += ms;
+    pg->spare.push_back(p);
+  }
+  pg->pending.clear();
+  *out = pg->st;
+  if (reset) {
+    const int64_t res = pg->st.resident_pages, cap = pg->st.capacity_pages;
+    pg->st = astro_moe_pager_stats{};
+    pg->st.resident_pages = res;
+    pg->st.capacity_pages = cap;
+  }
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_register_paged_layer(astro_moe_ctx* ctx, int32_t layer, const astro_moe_layer_weights* w,
+                                   astro_moe_pager* pg) {
+  const char* op = "register paged layer";
+  if (!ctx || !w || !pg) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null argument", op);
+  if (layer < 0 || layer >= pg->layers)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: layer %d outside the pager's %d layers", op, layer, pg->layers);
+  if (w->experts != pg->E || w->hidden != pg->H || w->intermediate != pg->I ||
+      w->group_size != pg->group || w->bits != pg->bits)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: layer geometry differs from the pager's pages", op);
+  if (w->top_k <= 0 || w->top_k > w->experts || w->top_k > 32)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid top_k", op);
+  if (w->shared_intermediate != 0 && w->shared_intermediate != w->intermediate)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: the shared expert must have the routed width", op);
+  if (!w->router_weight) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight", op);
+  if (w->shared_intermediate > 0) {
+    if (int rc = validate_affine_tensor("shared gate", w->shared_gate)) return rc;
+    if (int rc = validate_affine_tensor("shared up", w->shared_up)) return rc;
+    if (int rc = validate_affine_tensor("shared down", w->shared_down)) return rc;
+    if (!w->shared_expert_gate) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate", op);
+  }
+  DeviceGuard g(ctx->device);
+  LayerState& L = ctx->layers[layer];
+  astro::moe_gemm_release(L.gemm);
+  L = LayerState{};
+  L.w = *w;
+  L.w.gate = L.w.up = L.w.down = astro_moe_affine{};
+  L.w.gate_up_fused = 0;
+  L.registered = true;
+  L.pager = pg;
+  L.router_gemv_ok = (reinterpret_cast<uintptr_t>(w->router_weight) & 15u) == 0 &&
+                     astro::router_gemv_supported(w->hidden);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_paged_block_forward(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T,
+                                  void* out) {
+  const char* op = "paged block forward";
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null ctx", op);
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.registered || !it->second.pager)
+    return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "%s: layer %d is not a registered paged layer", op, layer);
+  if (T < 0 || T > 64) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: 0 <= tokens <= 64", op);
+  if (T > 0 && (!x || !out)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: hidden states must be 16-byte aligned", op);
+  DeviceGuard g(ctx->device);
+  return run_paged_block(ctx, it->second, layer, x, T, out);
 }
 
 }  // extern "C"

@@ -212,13 +212,22 @@ template <int STEPS> struct RowRegs {
   uint32_t sb[STEPS];
 };
 
-// Issues the loads of one row share (nothing waits on them until use).
+// rows of expert e, row f of a stacked tensor: packed codes and scales/biases
+ASTRO_DEVINL int64_t q_row(const AffineRef& W, int64_t e, int64_t f) {
+  return e * W.expert_rows + W.row_offset + f;
+}
+ASTRO_DEVINL int64_t sb_row(const AffineRef& W, int64_t e, int64_t f) {
+  return e * (W.sb_expert_rows ? W.sb_expert_rows : W.expert_rows) + W.row_offset + f;
+}
+
+// Issues the loads of row f of expert e (one lane's share; nothing waits on
+// them until use).
 template <int STEPS>
-ASTRO_DEVINL void load_row(RowRegs<STEPS>& r, const AffineRef& W, int64_t row, int words,
+ASTRO_DEVINL void load_row(RowRegs<STEPS>& r, const AffineRef& W, int64_t e, int64_t f, int words,
                            int groups, int qoff, int goff, int qstride, int gstride) {
-  const uint32_t* q = reinterpret_cast<const uint32_t*>(W.q) + row * words + qoff;
-  const uint16_t* ps = reinterpret_cast<const uint16_t*>(W.s) + row * groups + goff;
-  const uint16_t* pb = reinterpret_cast<const uint16_t*>(W.b) + row * groups + goff;
+  const uint32_t* q = reinterpret_cast<const uint32_t*>(W.q) + q_row(W, e, f) * words + qoff;
+  const uint16_t* ps = reinterpret_cast<const uint16_t*>(W.s) + sb_row(W, e, f) * groups + goff;
+  const uint16_t* pb = reinterpret_cast<const uint16_t*>(W.b) + sb_row(W, e, f) * groups + goff;
 #pragma unroll
   for (int s = 0; s < STEPS; ++s) r.q[s] = ld_stream(q + s * qstride);
 #pragma unroll
@@ -250,11 +259,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_gate_up_kernel(Grouped
     // select by value (a dynamic index into the parameter block would copy it to local memory)
     const AffineRef A = sh ? d.wa[1] : d.wa[0];
     const AffineRef B = sh ? d.wb[1] : d.wb[0];
-    const int64_t e = sh ? 0 : seg;
-    load_row<STEPS>(ga, A, e * A.expert_rows + A.row_offset + f, kWords, kGroups, lane * 4,
-                    lane / 2, 128, 16);
-    load_row<STEPS>(ua, B, e * B.expert_rows + B.row_offset + f, kWords, kGroups, lane * 4,
-                    lane / 2, 128, 16);
+    const int64_t e = sh ? 0 : (d.slot_of ? (int64_t)d.slot_of[seg] : seg);
+    load_row<STEPS>(ga, A, e, f, kWords, kGroups, lane * 4, lane / 2, 128, 16);
+    load_row<STEPS>(ua, B, e, f, kWords, kGroups, lane * 4, lane / 2, 128, 16);
   };
   RowRegs<STEPS> ga, ua, gn, un;
   int64_t it = blockIdx.x;
@@ -335,11 +342,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_down_kernel(GroupedGem
     const int seg = list[it / per_seg];
     const int sh = seg == d.shared_seg ? 1 : 0;
     const AffineRef A = sh ? d.wa[1] : d.wa[0];
-    const int64_t e = sh ? 0 : seg;
-    const int64_t rbase = e * A.expert_rows + A.row_offset + first_row(it);
+    const int64_t e = sh ? 0 : (d.slot_of ? (int64_t)d.slot_of[seg] : seg);
 #pragma unroll
     for (int r = 0; r < kRowsPerHalf; ++r)
-      load_row<STEPS>(rr[r], A, rbase + r, kWords, kGroups, li * 4, li / 2, 64, 8);
+      load_row<STEPS>(rr[r], A, e, first_row(it) + r, kWords, kGroups, li * 4, li / 2, 64, 8);
   };
   RowRegs<STEPS> cur[kRowsPerHalf], nxt[kRowsPerHalf];
   int64_t it = blockIdx.x;
@@ -711,13 +717,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
         const int sh = seg == E ? 1 : 0;
         const int which = l / (kLinesGU + 2 * kLinesGUs), ll = l - which * (kLinesGU + 2 * kLinesGUs);
         const AffineRef W = which ? (sh ? P.up[1] : P.up[0]) : (sh ? P.gate[1] : P.gate[0]);
-        const int64_t row = (sh ? 0 : (int64_t)seg) * W.expert_rows + W.row_offset + f0;
+        const int64_t ex = sh ? 0 : (int64_t)seg;
+        const int64_t row = q_row(W, ex, f0), srow = sb_row(W, ex, f0);
         if (ll < kLinesGU)
           line = reinterpret_cast<const char*>(W.q) + row * (H / 2) + (int64_t)ll * 128;
         else if (ll < kLinesGU + kLinesGUs)
-          line = reinterpret_cast<const char*>(W.s) + row * (H / 64) * 2 + (int64_t)(ll - kLinesGU) * 128;
+          line = reinterpret_cast<const char*>(W.s) + srow * (H / 64) * 2 + (int64_t)(ll - kLinesGU) * 128;
         else
-          line = reinterpret_cast<const char*>(W.b) + row * (H / 64) * 2 +
+          line = reinterpret_cast<const char*>(W.b) + srow * (H / 64) * 2 +
                  (int64_t)(ll - kLinesGU - kLinesGUs) * 128;
       } else {
         const int i2 = i - n_gu * kPerGU;
@@ -727,13 +734,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
         const int r0 = (it % per_d) * 4 * kGemvWarps;
         const int sh = seg == E ? 1 : 0;
         const AffineRef W = sh ? P.down[1] : P.down[0];
-        const int64_t row = (sh ? 0 : (int64_t)seg) * W.expert_rows + W.row_offset + r0;
+        const int64_t ex = sh ? 0 : (int64_t)seg;
+        const int64_t row = q_row(W, ex, r0), srow = sb_row(W, ex, r0);
         if (l < kLinesD)
           line = reinterpret_cast<const char*>(W.q) + row * (I / 2) + (int64_t)l * 128;
         else if (l < kLinesD + kLinesDs)
-          line = reinterpret_cast<const char*>(W.s) + row * (I / 64) * 2 + (int64_t)(l - kLinesD) * 128;
+          line = reinterpret_cast<const char*>(W.s) + srow * (I / 64) * 2 + (int64_t)(l - kLinesD) * 128;
         else
-          line = reinterpret_cast<const char*>(W.b) + row * (I / 64) * 2 +
+          line = reinterpret_cast<const char*>(W.b) + srow * (I / 64) * 2 +
                  (int64_t)(l - kLinesD - kLinesDs) * 128;
       }
       prefetch_l2(line);
@@ -752,10 +760,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       const AffineRef B = sh ? P.up[1] : P.up[0];
       const int64_t e = sh ? 0 : seg;
       RowRegs<SGU> ga, ua;
-      load_row<SGU>(ga, A, e * A.expert_rows + A.row_offset + f, kWordsGU, kGroupsGU, lane * 4,
-                    lane / 2, 128, 16);
-      load_row<SGU>(ua, B, e * B.expert_rows + B.row_offset + f, kWordsGU, kGroupsGU, lane * 4,
-                    lane / 2, 128, 16);
+      load_row<SGU>(ga, A, e, f, kWordsGU, kGroupsGU, lane * 4, lane / 2, 128, 16);
+      load_row<SGU>(ua, B, e, f, kWordsGU, kGroupsGU, lane * 4, lane / 2, 128, 16);
       const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
       for (uint32_t p = p0; p < p1; p += kRowChunkGU) {
         const int n = (int)(p1 - p < (uint32_t)kRowChunkGU ? p1 - p : (uint32_t)kRowChunkGU);
@@ -812,8 +818,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       RowRegs<SD> rr[kRowsPerHalf];
 #pragma unroll
       for (int r = 0; r < kRowsPerHalf; ++r)
-        load_row<SD>(rr[r], A, e * A.expert_rows + A.row_offset + r0 + r, kWordsD, kGroupsD,
-                     li * 4, li / 2, 64, 8);
+        load_row<SD>(rr[r], A, e, r0 + r, kWordsD, kGroupsD, li * 4, li / 2, 64, 8);
       const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
       for (uint32_t p = p0; p < p1; p += kRowChunk) {
         const int n = (int)(p1 - p < (uint32_t)kRowChunk ? p1 - p : (uint32_t)kRowChunk);

@@ -55,13 +55,20 @@ cudaError_t launch_swiglu(const void* gate, const void* up, int64_t n, void* out
 cudaError_t launch_numerics_probe(const float* x, int64_t n, int which, float* out,
                                   cudaStream_t st);
 
-// One stacked affine tensor seen as rows: row (e, f) = e * expert_rows + row_offset + f.
+// One stacked affine tensor seen as rows: row (e, f) = e * expert_rows + row_offset + f
+// of the packed codes, e * sb_expert_rows + row_offset + f of the scales and
+// biases.  sb_expert_rows == 0 means expert_rows (MLX stacks); page-major expert
+// pages (expert paging), where one expert's tensors share one contiguous page,
+// stride the codes and the scales by different row counts.  The decode GEMVs and
+// the fused decode kernel honour sb_expert_rows; the other kernels take MLX
+// stacks only.
 struct AffineRef {
   const void* q = nullptr;  // uint32 packed
   const void* s = nullptr;  // bf16 scales
   const void* b = nullptr;  // bf16 biases
   int64_t expert_rows = 0;
   int64_t row_offset = 0;
+  int64_t sb_expert_rows = 0;
 };
 
 struct GroupedGemvDesc {
@@ -81,6 +88,9 @@ struct GroupedGemvDesc {
   int64_t y_limit = 0;               // output rows available
   int64_t ldy = 0;
   uint32_t* status = nullptr;
+  // decode GEMVs only: routed segment e reads expert slot slot_of[e] of wa/wb
+  // (expert paging); nullptr = slot e
+  const uint32_t* slot_of = nullptr;
 };
 
 cudaError_t launch_grouped_gemv(const GroupedGemvDesc& d, cudaStream_t st);

@@ -50,6 +50,9 @@ def parse():
     ap.add_argument("--use-tensor-cores", type=int, default=0)
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode sweep")
     ap.add_argument("--no-stack", action="store_true", help="skip the config-3 40-layer stack")
+    ap.add_argument("--no-paging", action="store_true", help="skip the config-4 paged decode")
+    ap.add_argument("--paging-layers", type=int, default=40)
+    ap.add_argument("--paging-cache-gb", type=float, default=6.0)
     ap.add_argument("--stack-layers", type=int, default=40)
     ap.add_argument("--stack-tokens", type=int, default=16384)
     ap.add_argument("--decode-layers", type=int, default=16)
@@ -408,6 +411,70 @@ def measure_stack(args, rank, world, local, dev, max_over_ranks):
 
 
 
+def measure_paging(args, dev):
+    """Config 4: the 40-layer stack's 40 x 256 int4 experts (18.1 GB) in pinned
+    host memory, a 6 GB HBM page cache with LRU eviction, decode T=8 with
+    Zipf(1.1) routing skew (new tokens every step).  Device time with CUDA events
+    over whole steps (the per-layer routing read-back included)."""
+    import torch
+
+    from astronomical_b200 import paging, synthetic
+
+    cfg = dict(synthetic.CONFIGS[2])
+    L, T = args.paging_layers, 8
+    E, P = cfg["experts"], paging.page_bytes(cfg)
+    store = torch.empty((L, E, P), dtype=torch.uint8, pin_memory=True)
+    resident = []
+    keep = ("router_w", "shared_gate_w", "sgate_q", "sgate_s", "sgate_b", "sup_q", "sup_s", "sup_b",
+            "sdown_q", "sdown_s", "sdown_b")
+    for l in range(L):
+        w = synthetic.make_block_weights_torch(cfg, seed=9000 + l, device=dev)
+        paging.pack_layer(store[l], w)
+        r = {k: w[k] for k in keep}
+        r["config"] = w["config"]
+        for k in ("gate_q", "gate_s", "gate_b", "up_q", "up_s", "up_b", "down_q", "down_s", "down_b"):
+            r[k] = None
+        resident.append(r)
+        del w
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    cache = int(args.paging_cache_gb * 1e9)
+    stack = paging.PagedMoEStack(resident, store, cache_bytes=cache, device=dev.index)
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+
+    def step():
+        x = torch.randn((T, 2048), generator=g, device=dev).to(torch.bfloat16)
+        x[:, 0] = 1.0  # the Zipf bias enters through router column 0
+        for l in range(L):
+            stack.forward(l, x)
+
+    for _ in range(3):  # fill the cache
+        step()
+    torch.cuda.synchronize()
+    stack.stats(reset=True)
+    steps = 10
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    st = stack.stats(reset=True)
+    stack.close()
+    del store
+    return {"workload": "config4_paged_decode_zipf1.1", "layers": L, "tokens_per_step": T,
+            "pages_total": L * E, "page_bytes": P, "cache_bytes": cache,
+            "cache_pages": st["capacity_pages"], "ms_per_step": ms,
+            "tokens_per_s": T / (ms / 1e3), "us_per_layer": ms * 1e3 / L,
+            "hit_rate": st["hits"] / max(st["lookups"], 1),
+            "misses_per_step": st["misses"] / steps,
+            "pcie_gbs": st["bytes_h2d"] / max(st["copy_ms"], 1e-9) / 1e6,
+            "h2d_bytes_per_step": st["bytes_h2d"] / steps,
+            "copy_ms_per_step": st["copy_ms"] / steps}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -572,6 +639,9 @@ def run_ours(args):
         del w
         torch.cuda.empty_cache()
         line["stack"] = measure_stack(args, rank, world, local, dev, max_over_ranks)
+    if not args.no_paging:
+        torch.cuda.empty_cache()
+        line["paging"] = measure_paging(args, dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from oracle import oracle as O
 

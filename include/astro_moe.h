@@ -302,6 +302,59 @@ int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_row
 int astro_moe_ep_combine(astro_moe_ctx* ctx, int32_t layer, const void* returned_rows,
                          int64_t tokens, void* out);
 
+/* ------------------------------------------------------------------------ */
+/* Expert paging (config 4): Qwen3_5ExpertPager and the paged branch of        */
+/* forward_qwen3_5_moe (qwen3_5_moe/expert_paging/expert_pager/mod.rs:55-224,  */
+/* model/forward.rs:229-312, split_page_route.rs:10-60).  The reference reads  */
+/* missing expert pages from SSD; here every page lives in pinned host memory  */
+/* and an HBM page cache under a byte ceiling keeps the recently used ones      */
+/* (LRU), filled by cudaMemcpyAsync on the pager's own copy stream.            */
+/* ------------------------------------------------------------------------ */
+typedef struct astro_moe_pager astro_moe_pager;
+
+/* Bytes of one expert page: gate, up and down codes, then their scales and
+ * biases, each in MLX layout (see astro_moe_pager_create). */
+int64_t astro_moe_page_bytes(int32_t hidden, int32_t intermediate, int32_t group_size,
+                             int32_t bits);
+
+/* host_pages: PINNED host memory holding layers * experts pages, page
+ * (layer, expert) at byte (layer * experts + expert) * page_bytes; a page is
+ *   gate codes uint32 [I, H*bits/32] | up codes [I, H*bits/32] |
+ *   down codes [H, I*bits/32] | gate scales bf16 [I, H/group] | gate biases |
+ *   up scales | up biases | down scales [H, I/group] | down biases.
+ * cache_bytes: the HBM ceiling of the page cache (whole pages).  4-bit, group 64. */
+int astro_moe_pager_create(astro_moe_ctx* ctx, int32_t layers, int32_t experts, int32_t hidden,
+                           int32_t intermediate, int32_t group_size, int32_t bits,
+                           const void* host_pages, int64_t cache_bytes, astro_moe_pager** out);
+int astro_moe_pager_destroy(astro_moe_pager* pager);
+
+typedef struct {
+  int64_t lookups;          /* (layer, expert) pages a block call needed */
+  int64_t hits;
+  int64_t misses;
+  int64_t evictions;
+  int64_t bytes_h2d;        /* page bytes copied host -> HBM */
+  double copy_ms;           /* device time of those copies (copy-stream events) */
+  int64_t resident_pages;
+  int64_t capacity_pages;
+} astro_moe_pager_stats;
+/* Synchronises the pager's copy stream; reset != 0 clears the counters. */
+int astro_moe_pager_read_stats(astro_moe_pager* pager, astro_moe_pager_stats* out, int32_t reset);
+
+/* A paged layer: `weights` supplies the router, the shared expert and its gate
+ * (resident); gate/up/down are ignored -- the routed experts are the pager's
+ * pages of `layer`. */
+int astro_moe_register_paged_layer(astro_moe_ctx* ctx, int32_t layer,
+                                   const astro_moe_layer_weights* weights,
+                                   astro_moe_pager* pager);
+
+/* forward_qwen3_5_moe for a paged layer: routes, reads the routed experts back
+ * to the host (one stream synchronisation, as the reference's pager does),
+ * admits the missing pages, and runs the experts from the cache.  tokens <= 64
+ * (decode batches). */
+int astro_moe_paged_block_forward(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                                  int64_t tokens, void* out);
+
 #ifdef __cplusplus
 }
 #endif
