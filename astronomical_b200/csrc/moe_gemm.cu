@@ -355,6 +355,14 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       uint32_t oph = 0;    // its round parity
       int acc = 0;
       uint32_t acc_phase = 0;
+      // descriptors of operand slot 0; slot s adds s * (slot bytes >> 4) to the
+      // low word (the 14-bit start-address field cannot carry: smem < 256 KB)
+      const uint64_t bd0 = tc::sdesc_sw128(tc::smem_u32(b_at(0)));
+      const uint32_t b_lo0 = (uint32_t)bd0, b_hi = (uint32_t)(bd0 >> 32);
+      const uint64_t ad0 = tc::sdesc_sw128(tc::smem_u32(a_at(0)));
+      const uint32_t a_lo0 = (uint32_t)ad0, a_hi = (uint32_t)(ad0 >> 32);
+      constexpr uint32_t kSlotStep = (uint32_t)(kOpBytes >> 4);
+      const uint32_t a_tmem0 = tmem_base + (uint32_t)kACol0;
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
         Unit U;
         if (!decode_unit(ctl, p, u, U)) continue;
@@ -366,19 +374,14 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         for (int kb = 0; kb < KB; ++kb) {
           if (!tc::mbar_wait(&ctl.op_full[os], oph, abort, p.status)) goto mma_done;
           tc::tc_fence_after();
-          const uint32_t b_addr = tc::smem_u32(b_at(os));
+          const uint32_t b_lo = b_lo0 + (uint32_t)os * kSlotStep;
           if constexpr (MODE == kRouter) {
-            const uint32_t a_addr = tc::smem_u32(a_at(os));
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)
-              tc::mma_bf16(d_tmem, tc::sdesc_sw128(a_addr + kk * 32),
-                           tc::sdesc_sw128(b_addr + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc::mma4_bf16_ss(d_tmem, a_lo0 + (uint32_t)os * kSlotStep, a_hi, b_lo, b_hi, idesc,
+                             (uint32_t)kb);
           } else {
-            const uint32_t a_tmem = tmem_base + (uint32_t)(kACol0 + os * kAColsPerStage);
-#pragma unroll
-            for (int kk = 0; kk < kBK / 16; ++kk)  // K = 16 bf16 = 8 TMEM columns per MMA
-              tc::mma_bf16_ts(d_tmem, a_tmem + (uint32_t)(kk * 8), tc::sdesc_sw128(b_addr + kk * 32),
-                              idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            // K = 16 bf16 = 8 TMEM columns of A per MMA, 32 bytes of B
+            tc::mma4_bf16_ts(d_tmem, a_tmem0 + (uint32_t)(os * kAColsPerStage), b_lo, b_hi, idesc,
+                             (uint32_t)kb);
           }
           tc::mma_commit(&ctl.op_empty[os]);
           if (++os == kOpStages) { os = 0; oph ^= 1u; }

@@ -135,6 +135,51 @@ ASTRO_DEVINL void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
       : "memory");
 }
 
+// The four K=16 MMAs of one 64-wide K block in one asm block (the issuing thread
+// shares its scheduler with busy warps, so every instruction it saves counts):
+// A from TMEM columns a, a+8, a+16, a+24; B descriptors whose low words are
+// b_lo, b_lo+2, b_lo+4, b_lo+6 (32-byte steps) with high word b_hi; the first
+// MMA accumulates iff acc_first != 0, the rest always do.
+ASTRO_DEVINL void mma4_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo, uint32_t b_hi,
+                               uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .b64 b0, b1, b2, b3;\n\t.reg .b32 l1, l2, l3, a1, a2, a3;\n\t"
+      "setp.ne.b32 p, %5, 0;\n\t"
+      "setp.eq.b32 q, %5, %5;\n\t"
+      "add.u32 l1, %2, 2;\n\tadd.u32 l2, %2, 4;\n\tadd.u32 l3, %2, 6;\n\t"
+      "add.u32 a1, %1, 8;\n\tadd.u32 a2, %1, 16;\n\tadd.u32 a3, %1, 24;\n\t"
+      "mov.b64 b0, {%2, %3};\n\tmov.b64 b1, {l1, %3};\n\t"
+      "mov.b64 b2, {l2, %3};\n\tmov.b64 b3, {l3, %3};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], b0, %4, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a1], b1, %4, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a2], b2, %4, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [a3], b3, %4, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc_first)
+      : "memory");
+}
+
+// Same with A from shared memory: A descriptors a_lo + 2k, B descriptors b_lo + 2k.
+ASTRO_DEVINL void mma4_bf16_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t a_hi, uint32_t b_lo,
+                               uint32_t b_hi, uint32_t idesc, uint32_t acc_first) {
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t.reg .b64 a0, a1, a2, a3, b0, b1, b2, b3;\n\t"
+      ".reg .b32 x1, x2, x3, y1, y2, y3;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "setp.eq.b32 q, %6, %6;\n\t"
+      "add.u32 x1, %1, 2;\n\tadd.u32 x2, %1, 4;\n\tadd.u32 x3, %1, 6;\n\t"
+      "add.u32 y1, %3, 2;\n\tadd.u32 y2, %3, 4;\n\tadd.u32 y3, %3, 6;\n\t"
+      "mov.b64 a0, {%1, %2};\n\tmov.b64 a1, {x1, %2};\n\t"
+      "mov.b64 a2, {x2, %2};\n\tmov.b64 a3, {x3, %2};\n\t"
+      "mov.b64 b0, {%3, %4};\n\tmov.b64 b1, {y1, %4};\n\t"
+      "mov.b64 b2, {y2, %4};\n\tmov.b64 b3, {y3, %4};\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a0, b0, %5, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a1, b1, %5, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a2, b2, %5, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], a3, b3, %5, q;\n\t}" ::"r"(d_tmem),
+      "r"(a_lo), "r"(a_hi), "r"(b_lo), "r"(b_hi), "r"(idesc), "r"(acc_first)
+      : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns from registers: thread i writes lane (base + i).
 ASTRO_DEVINL void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
   asm volatile(

@@ -58,6 +58,12 @@ def parse():
     ap.add_argument("--decode-layers", type=int, default=16)
     ap.add_argument("--profile", action="store_true",
                     help="only W warm-up and K plain steps (for ncu captures; prints nothing)")
+    ap.add_argument("--profile-workload", default="prefill",
+                    choices=["prefill", "decode", "paging"],
+                    help="with --profile: config-1 prefill steps, config-2 decode steps of "
+                         "--decode-tokens tokens over --decode-layers layers (eager), or config-4 "
+                         "paged steps over --paging-layers layers")
+    ap.add_argument("--decode-tokens", type=int, default=1)
     return ap.parse_args()
 
 
@@ -168,6 +174,49 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- GPU
+def run_profile_workload(args, dev):
+    """--profile with a decode or paging workload: W warm-up and K plain steps,
+    nothing printed (for ncu captures of those kernels)."""
+    import torch
+
+    from astronomical_b200 import moe, paging, synthetic
+
+    cfg = dict(synthetic.CONFIGS[2])
+    T = args.decode_tokens
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    if args.profile_workload == "decode":
+        blocks = [moe.Qwen3_5MoEBlock(synthetic.make_block_weights_torch(cfg, seed=500 + l, device=dev),
+                                      device=dev.index, max_tokens=64)
+                  for l in range(args.decode_layers)]
+
+        def step():
+            x = torch.randn((T, 2048), generator=g, device=dev).to(torch.bfloat16)
+            x[:, 0] = 1.0
+            for b in blocks:
+                b.forward(x)
+    else:
+        L = args.paging_layers
+        layers = []
+        store = torch.empty((L, cfg["experts"], paging.page_bytes(cfg)), dtype=torch.uint8,
+                            pin_memory=True)
+        for l in range(L):
+            w = synthetic.make_block_weights_torch(cfg, seed=9000 + l, device=dev)
+            paging.pack_layer(store[l], w)
+            layers.append(w)
+        stack = paging.PagedMoEStack(layers, store, int(args.paging_cache_gb * 1e9),
+                                     device=dev.index)
+
+        def step():
+            x = torch.randn((T, 2048), generator=g, device=dev).to(torch.bfloat16)
+            x[:, 0] = 1.0
+            for l in range(L):
+                stack.forward(l, x)
+    for _ in range(args.warmup + args.steps):
+        step()
+    torch.cuda.synchronize()
+
+
 EXPERT_BYTES = 1769472  # one routed expert: gate + up + down, int4 g64 with bf16 scales/biases
 
 
@@ -487,6 +536,9 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.profile and args.profile_workload != "prefill":
+        run_profile_workload(args, dev)
+        return
     if world > 1:
         from datetime import timedelta
 
