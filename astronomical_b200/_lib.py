@@ -119,6 +119,13 @@ SIGNATURES = {
     "astro_moe_ep_dispatch": ([_P, _I32, _P, _I64, _P, _P], ctypes.c_int),
     "astro_moe_ep_experts": ([_P, _I32, _P, _P, _I32, _I64, _P, _I64, _P], ctypes.c_int),
     "astro_moe_ep_combine": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
+    "astro_moe_ep_exchange_create": ([_P, _I32, _I32, _I32, _I64, _I64, _P], ctypes.c_int),
+    "astro_moe_ep_exchange_connect": ([_P, _P], ctypes.c_int),
+    "astro_moe_ep_exchange_buffers": ([_P, ctypes.POINTER(ctypes.c_void_p),
+                                       ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
+    "astro_moe_ep_route": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
+    "astro_moe_ep_push": ([_P, _I32, _P, _I64, _P, _P], ctypes.c_int),
+    "astro_moe_ep_experts_push": ([_P, _I32, _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
     "astro_moe_page_bytes": ([_I32, _I32, _I32, _I32], ctypes.c_int64),
     "astro_moe_pager_create": ([_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64,
                                 ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),

@@ -137,6 +137,15 @@ struct astro_moe_ctx {
   DevBuf ep_disp, ep_exp, ep_shared;
   int ep_layer = -1;
   int64_t ep_tokens = -1;
+  // peer-memory exchange: this rank's receive / return buffers and every rank's
+  // mapping of them (index = rank)
+  int xr_world = 0, xr_rank = -1;
+  void* xr_recv = nullptr;
+  void* xr_ret = nullptr;
+  int64_t xr_recv_rows = 0, xr_ret_rows = 0;
+  void* xr_peer_recv[astro::kMaxPeers] = {};
+  void* xr_peer_ret[astro::kMaxPeers] = {};
+  bool xr_connected = false;
 };
 
 // Expert page cache: pinned host pages, HBM slots, LRU over slots (host side).
@@ -1045,6 +1054,16 @@ int astro_moe_ctx_destroy(astro_moe_ctx* ctx) {
   for (auto e : ctx->event_pool) cudaEventDestroy(e);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->io) cudaFree(ctx->io);
+  if (ctx->ep_disp.p) cudaFree(ctx->ep_disp.p);
+  if (ctx->ep_exp.p) cudaFree(ctx->ep_exp.p);
+  if (ctx->ep_shared.p) cudaFree(ctx->ep_shared.p);
+  for (int r = 0; r < ctx->xr_world; ++r) {
+    if (r == ctx->xr_rank) continue;
+    if (ctx->xr_peer_recv[r]) cudaIpcCloseMemHandle(ctx->xr_peer_recv[r]);
+    if (ctx->xr_peer_ret[r]) cudaIpcCloseMemHandle(ctx->xr_peer_ret[r]);
+  }
+  if (ctx->xr_recv) cudaFree(ctx->xr_recv);
+  if (ctx->xr_ret) cudaFree(ctx->xr_ret);
   delete ctx;
   return ASTRO_MOE_OK;
 }
@@ -1256,10 +1275,11 @@ int astro_moe_ep_dispatch(astro_moe_ctx* ctx, int32_t layer, const void* x, int6
   return ASTRO_MOE_OK;
 }
 
-int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_rows,
-                         const uint32_t* recv_counts, int32_t world, int64_t recv_total,
-                         const void* x, int64_t T, void* out_rows) {
-  const char* op = "expert-parallel experts";
+// Expert side of an expert-parallel layer up to the expert-major outputs (in
+// ctx->ep_exp: yrows, dest) and the shared-expert rows (ctx->ep_shared).
+static int ep_experts_compute(astro_moe_ctx* ctx, int32_t layer, const char* op,
+                              const void* recv_rows, const uint32_t* recv_counts, int32_t world,
+                              int64_t recv_total, const void* x, int64_t T) {
   LayerState* Lp = nullptr;
   if (int rc = ep_layer(ctx, layer, op, &Lp)) return rc;
   LayerState& L = *Lp;
@@ -1269,7 +1289,7 @@ int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_row
     return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: world * local experts must be <= 2048", op);
   if (recv_total < 0 || T < 0 || recv_total + T > 0x7fffffffLL)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid row counts", op);
-  if (!recv_counts || (recv_total > 0 && (!recv_rows || !out_rows)) || (T > 0 && !x))
+  if (!recv_counts || (recv_total > 0 && !recv_rows) || (T > 0 && !x))
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
   DeviceGuard g(ctx->device);
   cudaStream_t st = ctx->stream;
@@ -1336,12 +1356,29 @@ int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_row
     }
     ctx->launches += 2;
   }
-  CK(astro::launch_take_rows(e.yrows, rows, e.dest, recv_total, H, out_rows, ctx->status, st),
-     "received order");
   if (shared_rows > 0)
     CK(cudaMemcpyAsync(ctx->ep_shared.p, e.yrows + recv_total * H, sizeof(uint16_t) * shared_rows * H,
                        cudaMemcpyDeviceToDevice, st),
        "shared-expert rows");
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_rows,
+                         const uint32_t* recv_counts, int32_t world, int64_t recv_total,
+                         const void* x, int64_t T, void* out_rows) {
+  const char* op = "expert-parallel experts";
+  if (recv_total > 0 && !out_rows) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  if (int rc = ep_experts_compute(ctx, layer, op, recv_rows, recv_counts, world, recv_total, x, T))
+    return rc;
+  const astro_moe_layer_weights& w = ctx->layers[layer].w;
+  const int64_t rows = recv_total + (w.shared_intermediate > 0 ? T : 0);
+  EpExperts e{};
+  plan_ep_experts(rows, recv_total, w.hidden, w.intermediate, world * w.experts, w.experts, &e,
+                  (char*)ctx->ep_exp.p);
+  DeviceGuard g(ctx->device);
+  CK(astro::launch_take_rows(e.yrows, rows, e.dest, recv_total, w.hidden, out_rows, ctx->status,
+                             ctx->stream),
+     "received order");
   ctx->launches += 1;
   return ASTRO_MOE_OK;
 }
@@ -1357,6 +1394,7 @@ int astro_moe_ep_combine(astro_moe_ctx* ctx, int32_t layer, const void* returned
                 "%s: layer %d with %lld tokens does not match the dispatch in flight", op, layer,
                 (long long)T);
   if (T == 0) return ASTRO_MOE_OK;
+  if (!returned_rows) returned_rows = ctx->xr_ret;  // rows returned by the peer exchange
   if (!returned_rows || !out) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
   const int H = w.hidden, E = Lp->ep_total, K = w.top_k;
   const bool has_shared = w.shared_intermediate > 0;
@@ -1542,6 +1580,163 @@ int astro_moe_paged_block_forward(astro_moe_ctx* ctx, int32_t layer, const void*
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: hidden states must be 16-byte aligned", op);
   DeviceGuard g(ctx->device);
   return run_paged_block(ctx, it->second, layer, x, T, out);
+}
+
+
+// --- peer-memory exchange -------------------------------------------------
+int astro_moe_ep_exchange_create(astro_moe_ctx* ctx, int32_t world, int32_t rank, int32_t hidden,
+                                 int64_t recv_rows, int64_t return_rows, void* handles_out) {
+  const char* op = "expert-parallel exchange create";
+  if (!ctx || !handles_out) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null argument", op);
+  if (world < 2 || world > astro::kMaxPeers || rank < 0 || rank >= world)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: 2 <= world <= %d", op, astro::kMaxPeers);
+  if (hidden <= 0 || hidden % 8 || recv_rows <= 0 || return_rows <= 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid sizes", op);
+  if (ctx->xr_recv) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: already created", op);
+  DeviceGuard g(ctx->device);
+  CK(cudaMalloc(&ctx->xr_recv, sizeof(uint16_t) * (size_t)recv_rows * hidden), "cudaMalloc(receive buffer)");
+  CK(cudaMalloc(&ctx->xr_ret, sizeof(uint16_t) * (size_t)return_rows * hidden), "cudaMalloc(return buffer)");
+  cudaIpcMemHandle_t h[2];
+  CK(cudaIpcGetMemHandle(&h[0], ctx->xr_recv), "cudaIpcGetMemHandle");
+  CK(cudaIpcGetMemHandle(&h[1], ctx->xr_ret), "cudaIpcGetMemHandle");
+  std::memcpy(handles_out, h, sizeof(h));
+  ctx->xr_world = world;
+  ctx->xr_rank = rank;
+  ctx->xr_recv_rows = recv_rows;
+  ctx->xr_ret_rows = return_rows;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_exchange_connect(astro_moe_ctx* ctx, const void* all_handles) {
+  const char* op = "expert-parallel exchange connect";
+  if (!ctx || !all_handles) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null argument", op);
+  if (!ctx->xr_recv) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: create the exchange first", op);
+  if (ctx->xr_connected) return ASTRO_MOE_OK;
+  DeviceGuard g(ctx->device);
+  const auto* h = static_cast<const cudaIpcMemHandle_t*>(all_handles);
+  for (int r = 0; r < ctx->xr_world; ++r) {
+    if (r == ctx->xr_rank) {
+      ctx->xr_peer_recv[r] = ctx->xr_recv;
+      ctx->xr_peer_ret[r] = ctx->xr_ret;
+      continue;
+    }
+    CK(cudaIpcOpenMemHandle(&ctx->xr_peer_recv[r], h[2 * r], cudaIpcMemLazyEnablePeerAccess),
+       "cudaIpcOpenMemHandle(receive buffer)");
+    CK(cudaIpcOpenMemHandle(&ctx->xr_peer_ret[r], h[2 * r + 1], cudaIpcMemLazyEnablePeerAccess),
+       "cudaIpcOpenMemHandle(return buffer)");
+  }
+  ctx->xr_connected = true;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_route(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T,
+                       uint32_t* expert_offsets) {
+  // the dispatch without its gather: rows go out with astro_moe_ep_push
+  const char* op = "expert-parallel route";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_layer(ctx, layer, op, &Lp)) return rc;
+  LayerState& L = *Lp;
+  const astro_moe_layer_weights& w = L.w;
+  const int H = w.hidden, E = L.ep_total, K = w.top_k;
+  if (T < 0 || T * (int64_t)K > 0x7fffffffLL)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid token count", op);
+  if (T > 0 && (!x || !expert_offsets)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: hidden states must be 16-byte aligned", op);
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = ctx->stream;
+  const bool has_shared = w.shared_intermediate > 0;
+  EpDispatch d{};
+  if (int rc = devbuf_ensure(ctx, ctx->ep_disp, plan_ep_dispatch(T > 0 ? T : 1, E, K, nullptr, nullptr)))
+    return rc;
+  plan_ep_dispatch(T > 0 ? T : 1, E, K, &d, (char*)ctx->ep_disp.p);
+  ctx->ep_layer = layer;
+  ctx->ep_tokens = T;
+  if (T == 0) {
+    CK(cudaMemsetAsync(expert_offsets, 0, sizeof(uint32_t) * (E + 1), st), op);
+    return ASTRO_MOE_OK;
+  }
+  if (T <= kRouterGemvTokens && L.router_gemv_ok) {
+    CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, d.logits, st), "router projection");
+  } else if (astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores)) {
+    CK(astro::moe_gemm_router(L.gemm, x, T, d.logits, nullptr, ctx->status, st), "router projection");
+  } else {
+    CK(astro::launch_dense_nt_simt(x, w.router_weight, T, E, H, d.logits, E, st), "router projection");
+  }
+  CK(astro::launch_route_experts(d.logits, ASTRO_MOE_DTYPE_BF16, T, E, K, w.normalize_top_k, d.ids,
+                                 d.scores, x, has_shared ? w.shared_expert_gate : nullptr, H,
+                                 has_shared ? d.gate_logit : nullptr, st),
+     "route experts");
+  CK(astro::launch_sort_assignments(d.ids, T, K, E, 0, d.order, d.inverse, d.sids, d.stok,
+                                    expert_offsets, ctx->status, d.sort_scratch, st),
+     "sort expert assignments");
+  ctx->launches += 2 + astro::sort_launch_count(T * K);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_push(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T,
+                      const int64_t* send_starts, const int64_t* dest_offsets) {
+  const char* op = "expert-parallel push";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_layer(ctx, layer, op, &Lp)) return rc;
+  if (!ctx->xr_connected) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: exchange not connected", op);
+  if (ctx->ep_layer != layer || ctx->ep_tokens != T)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: does not match the routing in flight", op);
+  if (T == 0) return ASTRO_MOE_OK;
+  if (!x || !send_starts || !dest_offsets) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  const astro_moe_layer_weights& w = Lp->w;
+  const int E = Lp->ep_total, K = w.top_k, El = w.experts;
+  DeviceGuard g(ctx->device);
+  EpDispatch d{};
+  plan_ep_dispatch(T, E, K, &d, (char*)ctx->ep_disp.p);
+  int64_t caps[astro::kMaxPeers];
+  for (int r = 0; r < ctx->xr_world; ++r) caps[r] = ctx->xr_recv_rows;
+  CK(astro::launch_ep_push_rows(x, T, d.stok, d.sids, T * K, El, ctx->xr_world, w.hidden,
+                                ctx->xr_peer_recv, caps, dest_offsets, send_starts, ctx->status,
+                                ctx->stream),
+     op);
+  ctx->launches += 1;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_experts_push(astro_moe_ctx* ctx, int32_t layer, const uint32_t* recv_counts,
+                              int64_t recv_total, const void* x, int64_t T,
+                              const int64_t* recv_starts, const int64_t* return_offsets) {
+  const char* op = "expert-parallel experts (peer return)";
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null ctx", op);
+  if (!ctx->xr_connected) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: exchange not connected", op);
+  if (recv_total > ctx->xr_recv_rows)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: %lld received rows exceed the receive buffer", op,
+                (long long)recv_total);
+  if (!recv_starts || !return_offsets) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  // the expert arithmetic reads the receive buffer; outputs land in ep_exp.yrows
+  // in expert-major order, then travel back by the peer return kernel
+  if (int rc = ep_experts_compute(ctx, layer, op, ctx->xr_recv, recv_counts, ctx->xr_world,
+                                  recv_total, x, T))
+    return rc;
+  LayerState* Lp = nullptr;
+  ep_layer(ctx, layer, op, &Lp);
+  const astro_moe_layer_weights& w = Lp->w;
+  EpExperts e{};
+  const int64_t rows = recv_total + (w.shared_intermediate > 0 ? T : 0);
+  plan_ep_experts(rows, recv_total, w.hidden, w.intermediate, ctx->xr_world * w.experts, w.experts,
+                  &e, (char*)ctx->ep_exp.p);
+  int64_t caps[astro::kMaxPeers];
+  for (int r = 0; r < ctx->xr_world; ++r) caps[r] = ctx->xr_ret_rows;
+  DeviceGuard g(ctx->device);
+  CK(astro::launch_ep_return_rows(e.yrows, rows, e.dest, recv_total, ctx->xr_world, w.hidden,
+                                  ctx->xr_peer_ret, caps, return_offsets, recv_starts, ctx->status,
+                                  ctx->stream),
+     op);
+  ctx->launches += 1;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_exchange_buffers(astro_moe_ctx* ctx, void** recv, void** ret) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "exchange buffers: null ctx");
+  if (recv) *recv = ctx->xr_recv;
+  if (ret) *ret = ctx->xr_ret;
+  return ASTRO_MOE_OK;
 }
 
 }  // extern "C"

@@ -120,3 +120,121 @@ cudaError_t launch_ep_permutation(const uint32_t* counts, int world, int El, int
 }
 
 }  // namespace astro
+
+// ===========================================================================
+// Peer-memory exchange.  Each rank's receive and return buffers are mapped into
+// every peer (CUDA IPC), so the dispatch gather stores a token row straight into
+// the destination rank's receive buffer over NVLink, and the expert side stores
+// each output row straight into its source rank's return buffer: the all-to-all
+// is fused into the kernels that produce the rows.  No kernel waits on another
+// GPU; the host orders the phases with stream-ordered collectives.  Every remote
+// store is checked against the destination buffer's capacity (a bad row is
+// recorded in the status word and skipped).
+namespace astro {
+namespace {
+
+struct PeerTable {
+  uint4* base[kMaxPeers];
+  int64_t cap_rows[kMaxPeers];
+  int64_t off[kMaxPeers];    // first row written in that peer's buffer
+  int64_t start[kMaxPeers];  // first local row (sorted position or received row) for that peer
+};
+
+// row p (sorted position) of this rank's assignments: destination rank d =
+// sorted_ids[p] / El, copied from x[sorted_tokens[p]] to peer d's receive row
+// off[d] + p - start[d]
+__global__ void ep_push_rows_kernel(const uint4* __restrict__ x, const uint32_t* __restrict__ stok,
+                                   const uint32_t* __restrict__ sids, int64_t n, int El, int world,
+                                   int chunks, int64_t x_rows, const __grid_constant__ PeerTable t,
+                                   uint32_t* __restrict__ status) {
+  const int64_t total = n * chunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = i / chunks;
+    const int c = (int)(i - p * chunks);
+    const uint32_t d = sids[p] / (uint32_t)El;
+    const uint32_t tok = stok[p];
+    if (d >= (uint32_t)world || tok >= (uint64_t)x_rows) {
+      record_status(status, kDevBadShape);
+      continue;
+    }
+    const int64_t row = t.off[d] + (p - t.start[d]);
+    if (row < 0 || row >= t.cap_rows[d]) {
+      record_status(status, kDevBadShape);
+      continue;
+    }
+    t.base[d][row * chunks + c] = x[(int64_t)tok * chunks + c];
+  }
+}
+
+// received row q (source-major) of source s (start[s] <= q < start[s+1]) holds
+// expert-major row dest[q] of yrows; stored to source s's return row
+// off[s] + q - start[s]
+__global__ void ep_return_rows_kernel(const uint4* __restrict__ yrows,
+                                     const uint32_t* __restrict__ dest, int64_t n, int world,
+                                     int chunks, int64_t y_rows,
+                                     const __grid_constant__ PeerTable t,
+                                     uint32_t* __restrict__ status) {
+  const int64_t total = n * chunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = i / chunks;
+    const int c = (int)(i - q * chunks);
+    int s = 0;
+    while (s + 1 < world && q >= t.start[s + 1]) ++s;
+    const uint32_t src = dest[q];
+    const int64_t row = t.off[s] + (q - t.start[s]);
+    if (src >= (uint64_t)y_rows || row < 0 || row >= t.cap_rows[s]) {
+      record_status(status, kDevBadShape);
+      continue;
+    }
+    t.base[s][row * chunks + c] = yrows[(int64_t)src * chunks + c];
+  }
+}
+
+PeerTable make_table(void* const* bases, const int64_t* caps, const int64_t* offs,
+                     const int64_t* starts, int world) {
+  PeerTable t{};
+  for (int i = 0; i < world && i < kMaxPeers; ++i) {
+    t.base[i] = reinterpret_cast<uint4*>(bases[i]);
+    t.cap_rows[i] = caps[i];
+    t.off[i] = offs[i];
+    t.start[i] = starts[i];
+  }
+  return t;
+}
+
+int grid_rows(int64_t n, int chunks) {
+  const int64_t threads = 256, total = n * chunks;
+  int64_t b = (total + threads - 1) / threads;
+  return (int)(b < 1 ? 1 : (b > 148 * 16 ? 148 * 16 : b));
+}
+
+}  // namespace
+
+cudaError_t launch_ep_push_rows(const void* x, int64_t x_rows, const uint32_t* stok,
+                                const uint32_t* sids, int64_t n, int El, int world, int H,
+                                void* const* peer_bases, const int64_t* peer_cap_rows,
+                                const int64_t* peer_offs, const int64_t* starts, uint32_t* status,
+                                cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  if (world < 1 || world > kMaxPeers || H % 8) return cudaErrorInvalidValue;
+  const PeerTable t = make_table(peer_bases, peer_cap_rows, peer_offs, starts, world);
+  ep_push_rows_kernel<<<grid_rows(n, H / 8), 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(x), stok, sids, n, El, world, H / 8, x_rows, t, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return_rows(const void* yrows, int64_t y_rows, const uint32_t* dest,
+                                  int64_t n, int world, int H, void* const* peer_bases,
+                                  const int64_t* peer_cap_rows, const int64_t* peer_offs,
+                                  const int64_t* starts, uint32_t* status, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  if (world < 1 || world > kMaxPeers || H % 8) return cudaErrorInvalidValue;
+  const PeerTable t = make_table(peer_bases, peer_cap_rows, peer_offs, starts, world);
+  ep_return_rows_kernel<<<grid_rows(n, H / 8), 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(yrows), dest, n, world, H / 8, y_rows, t, status);
+  return cudaGetLastError();
+}
+
+}  // namespace astro

@@ -146,6 +146,21 @@ cudaError_t launch_ep_permutation(const uint32_t* counts, int world, int El, int
                                   uint32_t* src_start, uint32_t* exp_start, uint32_t* offsets,
                                   uint32_t* dest, uint32_t* src_of, cudaStream_t st);
 
+// Peer-memory exchange (ep.cu).  Up to kMaxPeers ranks.  push: sorted row p goes
+// to rank d = sorted_ids[p] / El, row peer_offs[d] + p - starts[d] of its receive
+// buffer.  return: received row q of source s (starts[s] <= q < starts[s+1])
+// takes yrows[dest[q]] to row peer_offs[s] + q - starts[s] of s's return buffer.
+constexpr int kMaxPeers = 8;
+cudaError_t launch_ep_push_rows(const void* x, int64_t x_rows, const uint32_t* stok,
+                                const uint32_t* sids, int64_t n, int El, int world, int H,
+                                void* const* peer_bases, const int64_t* peer_cap_rows,
+                                const int64_t* peer_offs, const int64_t* starts, uint32_t* status,
+                                cudaStream_t st);
+cudaError_t launch_ep_return_rows(const void* yrows, int64_t y_rows, const uint32_t* dest,
+                                  int64_t n, int world, int H, void* const* peer_bases,
+                                  const int64_t* peer_cap_rows, const int64_t* peer_offs,
+                                  const int64_t* starts, uint32_t* status, cudaStream_t st);
+
 // Sets the calling thread's astro_moe_last_error() message and returns `status`
 // (for entry points defined outside api.cu).
 int set_last_error(int status, const char* message);

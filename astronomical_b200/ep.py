@@ -143,11 +143,50 @@ class CudaExpertShard:
                                               _ptr(out)))
         return out
 
-    def combine(self, layer: int, returned: torch.Tensor, T: int) -> torch.Tensor:
-        out = torch.empty((T, self.cfg["hidden"]), dtype=torch.bfloat16, device=returned.device)
+    def combine(self, layer: int, returned: Optional[torch.Tensor], T: int) -> torch.Tensor:
+        """returned=None: the rows the peer exchange stored in this rank's return buffer."""
+        out = torch.empty((T, self.cfg["hidden"]), dtype=torch.bfloat16, device=self.device)
         self._bind()
         check(_lib.lib().astro_moe_ep_combine(self.ctx, layer, _ptr(returned), T, _ptr(out)))
         return out
+
+    # -- peer-memory exchange ------------------------------------------------------
+    def connect_exchange(self, max_tokens: int, group=None) -> None:
+        """Allocates this rank's receive / return buffers, trades IPC handles with
+        the other ranks (all-gather) and maps theirs."""
+        K, H = self.cfg["top_k"], self.cfg["hidden"]
+        handles = (ctypes.c_ubyte * 128)()
+        check(_lib.lib().astro_moe_ep_exchange_create(self.ctx, self.world, self.rank, H,
+                                                      self.world * max_tokens * K, max_tokens * K,
+                                                      ctypes.byref(handles)))
+        mine = torch.tensor(bytearray(handles), dtype=torch.uint8, device=self.device)
+        everyone = torch.empty((self.world, 128), dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(everyone, mine, group=group)
+        buf = bytes(everyone.cpu().numpy().tobytes())
+        arr = (ctypes.c_ubyte * len(buf)).from_buffer_copy(buf)
+        check(_lib.lib().astro_moe_ep_exchange_connect(self.ctx, ctypes.byref(arr)))
+
+    def route(self, layer: int, x: torch.Tensor) -> torch.Tensor:
+        offsets = torch.empty(self.E + 1, dtype=torch.int32, device=x.device)
+        self._bind()
+        check(_lib.lib().astro_moe_ep_route(self.ctx, layer, _ptr(x), x.shape[0], _ptr(offsets)))
+        return offsets
+
+    @staticmethod
+    def _i64(vals):
+        return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+
+    def push(self, layer: int, x: torch.Tensor, send_starts, dest_offsets) -> None:
+        self._bind()
+        check(_lib.lib().astro_moe_ep_push(self.ctx, layer, _ptr(x), x.shape[0],
+                                           self._i64(send_starts), self._i64(dest_offsets)))
+
+    def experts_push(self, layer: int, recv_counts: torch.Tensor, recv_total: int, x: torch.Tensor,
+                     recv_starts, return_offsets) -> None:
+        self._bind()
+        check(_lib.lib().astro_moe_ep_experts_push(self.ctx, layer, _ptr(recv_counts), recv_total,
+                                                   _ptr(x), x.shape[0], self._i64(recv_starts),
+                                                   self._i64(return_offsets)))
 
     def kernel_launches(self, reset: bool = True) -> int:
         a = _lib.Attribution()
@@ -172,11 +211,17 @@ class ExpertParallelBlock:
     ``shard`` provides dispatch/experts/combine for this rank; ``group`` is the
     process group of the `world` ranks (default: the world group)."""
 
-    def __init__(self, shard, rank: int, world: int, experts: int, group=None):
+    def __init__(self, shard, rank: int, world: int, experts: int, group=None,
+                 exchange: str = "nccl"):
+        """exchange: "nccl" (all-to-all-v of rows through torch.distributed) or
+        "peer" (rows stored into the peers' buffers by the dispatch and expert
+        kernels; needs ``shard.connect_exchange`` first)."""
         self.shard, self.rank, self.world, self.E = shard, rank, world, experts
         self.El = expert_range(rank, world, experts)[1]
         self.group = group
+        self.exchange = exchange if world > 1 else "nccl"
         self.last_splits: Optional[Tuple[List[int], List[int]]] = None
+        self._flag = None
 
     def plan(self, offsets: torch.Tensor):
         """Per-expert counts out, per-source counts in; returns host splits and the
@@ -193,10 +238,46 @@ class ExpertParallelBlock:
         recv_splits = [int(v) for v in rc_h.view(self.world, self.El).sum(1)]
         return send_splits, recv_splits, recv_counts
 
+    def _barrier(self, device):
+        # stream-ordered: no rank passes until every rank's prior kernels finished
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=device)
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _forward_peer(self, layer: int, x: torch.Tensor, mark) -> torch.Tensor:
+        T, W, me = x.shape[0], self.world, self.rank
+        offsets = self.shard.route(layer, x)
+        mark("dispatch")
+        counts = (offsets[1:] - offsets[:-1]).to(torch.int32).contiguous()
+        recv_counts = torch.empty(W * self.El, dtype=torch.int32, device=x.device)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        per_dest = counts.view(W, self.El).sum(1).to(torch.int32)
+        M = torch.empty((W, W), dtype=torch.int32, device=x.device)
+        dist.all_gather_into_tensor(M, per_dest, group=self.group)
+        Mh = M.cpu().tolist()  # Mh[s][d]: rows rank s sends to rank d
+        send_starts = [sum(Mh[me][:d]) for d in range(W)]
+        dest_offsets = [sum(Mh[s][d] for s in range(me)) for d in range(W)]
+        recv_starts = [sum(Mh[s][me] for s in range(q)) for q in range(W)]
+        return_offsets = [sum(Mh[s][:me]) for s in range(W)]
+        recv_total = sum(Mh[s][me] for s in range(W))
+        self.last_splits = ([Mh[me][d] for d in range(W)], [Mh[s][me] for s in range(W)])
+        self.shard.push(layer, x, send_starts, dest_offsets)
+        self._barrier(x.device)
+        mark("exchange_out")
+        self.shard.experts_push(layer, recv_counts, recv_total, x, recv_starts, return_offsets)
+        mark("experts")
+        self._barrier(x.device)
+        mark("exchange_back")
+        y = self.shard.combine(layer, None, T)
+        mark("combine")
+        return y
+
     def forward(self, layer: int, x: torch.Tensor, marks=None) -> torch.Tensor:
         """``marks``: optional callable recording a named point (stage timing)."""
         T = x.shape[0]
         mark = marks or (lambda name: None)
+        if self.exchange == "peer":
+            return self._forward_peer(layer, x, mark)
         send, offsets = self.shard.dispatch(layer, x)
         mark("dispatch")
         send_splits, recv_splits, recv_counts = self.plan(offsets)

@@ -51,6 +51,8 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode sweep")
     ap.add_argument("--no-stack", action="store_true", help="skip the config-3 40-layer stack")
     ap.add_argument("--no-paging", action="store_true", help="skip the config-4 paged decode")
+    ap.add_argument("--ep-exchange", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: rows stored into peer buffers by our kernels, or NCCL all-to-all-v")
     ap.add_argument("--paging-layers", type=int, default=40)
     ap.add_argument("--paging-cache-gb", type=float, default=6.0)
     ap.add_argument("--stack-layers", type=int, default=40)
@@ -319,7 +321,9 @@ def run_ep(args, rank, world, local, dev):
     shard = CudaExpertShard([w], rank, world, device=local, max_tokens=T)
     del w
     torch.cuda.empty_cache()
-    block = ExpertParallelBlock(shard, rank, world, E)
+    if args.ep_exchange == "peer":
+        shard.connect_exchange(T)
+    block = ExpertParallelBlock(shard, rank, world, E, exchange=args.ep_exchange)
     g = torch.Generator(device=dev)
     g.manual_seed(99 + rank)
     x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
@@ -331,11 +335,17 @@ def run_ep(args, rank, world, local, dev):
 
     for _ in range(args.warmup):
         block.forward(0, x)
+    torch.cuda.synchronize()
+    # load pre-roll of ~1 s for the clock sampler: the same number of steps on every
+    # rank (each step holds collectives, so ranks must agree on the count)
+    t0 = time.perf_counter()
+    block.forward(0, x)
+    torch.cuda.synchronize()
+    pre = int(max_over_ranks(min(1000.0, 1.0 / max(time.perf_counter() - t0, 1e-4))))
     shard.kernel_launches(reset=True)
     clocks = ClockSampler(local)
     clocks.start()
-    t_end = time.time() + 1.0
-    while time.time() < t_end:
+    for _ in range(pre):
         block.forward(0, x)
     dist.barrier()
     torch.cuda.synchronize()
@@ -389,7 +399,11 @@ def run_ep(args, rank, world, local, dev):
                    "tokens_per_gpu": T, "tokens": T * world, "hidden": H, "experts": E,
                    "experts_per_gpu": E // world, "top_k": K, "intermediate": I,
                    "shared_intermediate": Is, "quant": "affine int4 g64",
-                   "parallelism": f"ep{world}", "exchange": "NCCL all-to-all-v (torch.distributed)",
+                   "parallelism": f"ep{world}",
+                   "exchange": ("rows stored into peer buffers by the dispatch and expert kernels "
+                                "(CUDA IPC over NVLink), NCCL for counts and ordering"
+                                if args.ep_exchange == "peer" else
+                                "NCCL all-to-all-v (torch.distributed)"),
                    "l2": "inputs larger than L2 (expert weights read per step exceed 126 MB "
                          "per GPU for N <= 2; L2 not flushed)"},
         "roofline": {"bound": "nvlink" if t_link > t_tensor else "tensor",
@@ -403,6 +417,8 @@ def run_ep(args, rank, world, local, dev):
                 "h2d_bytes_per_step": T * H * 2 * world, "d2h_bytes_per_step": T * H * 2 * world},
         "gpu_launches": launches,
     }
+    torch.cuda.synchronize()
+    dist.barrier()  # no peer still uses this rank's exchange buffers
     shard.close()
     del block, shard
     torch.cuda.empty_cache()
@@ -432,7 +448,9 @@ def measure_stack(args, rank, world, local, dev, max_over_ranks):
     shard = CudaExpertShard(layers, rank, world, device=local, max_tokens=T)
     del layers
     torch.cuda.empty_cache()
-    block = ExpertParallelBlock(shard, rank, world, E)
+    if world > 1 and args.ep_exchange == "peer":
+        shard.connect_exchange(T)
+    block = ExpertParallelBlock(shard, rank, world, E, exchange=args.ep_exchange)
     g = torch.Generator(device=dev)
     g.manual_seed(500 + rank)
     x = torch.randn((T, H), generator=g, device=dev).to(torch.bfloat16)
@@ -450,6 +468,8 @@ def measure_stack(args, rank, world, local, dev, max_over_ranks):
     e.record()
     torch.cuda.synchronize()
     ms = max_over_ranks(s.elapsed_time(e) / steps)
+    if world > 1:
+        dist.barrier()  # no peer still uses this rank's exchange buffers
     shard.close()
     del block, shard
     torch.cuda.empty_cache()
@@ -542,7 +562,7 @@ def run_ours(args):
     if world > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=60))
         line = run_ep(args, rank, world, local, dev)
 
         def mor(v):

@@ -297,10 +297,45 @@ int astro_moe_ep_experts(astro_moe_ctx* ctx, int32_t layer, const void* recv_row
                          const void* hidden_states, int64_t tokens, void* out_rows);
 
 /* returned_rows bf16 [tokens*top_k, H]: the expert outputs of send_rows, in
- * send order.  out bf16 [tokens, H] = router-weighted sum + gated shared expert,
- * the same arithmetic as astro_moe_block_forward. */
+ * send order (NULL: the peer exchange's return buffer).  out bf16 [tokens, H] =
+ * router-weighted sum + gated shared expert, the same arithmetic as
+ * astro_moe_block_forward. */
 int astro_moe_ep_combine(astro_moe_ctx* ctx, int32_t layer, const void* returned_rows,
                          int64_t tokens, void* out);
+
+/* Peer-memory exchange (world <= 8 GPUs of one node with peer access): the
+ * dispatch gather stores rows straight into the destination rank's receive
+ * buffer, and the expert side stores outputs straight into the source rank's
+ * return buffer, over NVLink.  No kernel waits on another GPU: between push and
+ * experts, and between experts and combine, the caller orders all ranks with a
+ * stream-ordered collective (e.g. a one-element NCCL all-reduce).
+ *
+ * create: allocates this rank's receive buffer (recv_rows rows of H bf16; size
+ * it for the most rows any rank can receive, world * tokens * top_k) and return
+ * buffer (return_rows >= tokens * top_k) and writes their two IPC handles (2 x 64
+ * bytes) to handles_out.  connect: all_handles = every rank's handles, in rank
+ * order (world x 2 x 64 bytes); opens the peers' buffers. */
+int astro_moe_ep_exchange_create(astro_moe_ctx* ctx, int32_t world, int32_t rank, int32_t hidden,
+                                 int64_t recv_rows, int64_t return_rows, void* handles_out);
+int astro_moe_ep_exchange_connect(astro_moe_ctx* ctx, const void* all_handles);
+int astro_moe_ep_exchange_buffers(astro_moe_ctx* ctx, void** recv_buffer, void** return_buffer);
+
+/* astro_moe_ep_dispatch without the gather: router, routing and sort. */
+int astro_moe_ep_route(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                       int64_t tokens, uint32_t* expert_offsets);
+
+/* Gathers the sorted rows and stores the rows for rank d into d's receive buffer
+ * from row dest_offsets[d]; this rank's rows for d start at sorted position
+ * send_starts[d] (HOST arrays of world entries). */
+int astro_moe_ep_push(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                      int64_t tokens, const int64_t* send_starts, const int64_t* dest_offsets);
+
+/* astro_moe_ep_experts on this rank's receive buffer (recv_total rows; source
+ * s's rows start at received row recv_starts[s]); the outputs of source s are
+ * stored into s's return buffer from row return_offsets[s] (HOST arrays). */
+int astro_moe_ep_experts_push(astro_moe_ctx* ctx, int32_t layer, const uint32_t* recv_counts,
+                              int64_t recv_total, const void* hidden_states, int64_t tokens,
+                              const int64_t* recv_starts, const int64_t* return_offsets);
 
 /* ------------------------------------------------------------------------ */
 /* Expert paging (config 4): Qwen3_5ExpertPager and the paged branch of        */

@@ -24,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, T, outdir, zipf):
+def _rank(rank, world, port, T, outdir, zipf, exchange):
     import torch.distributed as dist
 
     from astronomical_b200 import moe, synthetic
@@ -43,7 +43,9 @@ def _rank(rank, world, port, T, outdir, zipf):
     if zipf:
         x[:, 0] = 1.0
     shard = CudaExpertShard(layers, rank, world, device=rank, max_tokens=T)
-    block = ExpertParallelBlock(shard, rank, world, cfg["experts"])
+    if exchange == "peer":
+        shard.connect_exchange(T)
+    block = ExpertParallelBlock(shard, rank, world, cfg["experts"], exchange=exchange)
     for l in range(2):
         y = block.forward(l, x)
         ref = moe.Qwen3_5MoEBlock(layers[l], device=rank, max_tokens=T)
@@ -53,12 +55,14 @@ def _rank(rank, world, port, T, outdir, zipf):
         np.save(os.path.join(outdir, f"r_{rank}_{l}.npy"), y_ref.view(torch.int16).cpu().numpy())
         ref.close()
     torch.cuda.synchronize()
+    dist.barrier()  # no peer still uses this rank's exchange buffers
     shard.close()
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.parametrize("T,zipf", [(512, False), (96, True)])
-def test_expert_parallel_matches_single_gpu_block(T, zipf):
+def test_expert_parallel_matches_single_gpu_block(T, zipf, exchange):
     import torch.multiprocessing as mp
 
     from tests.helpers import assert_block_close
@@ -67,7 +71,8 @@ def test_expert_parallel_matches_single_gpu_block(T, zipf):
     with tempfile.TemporaryDirectory() as d:
         ctx = mp.get_context("spawn")
         port = _free_port()
-        procs = [ctx.Process(target=_rank, args=(r, world, port, T, d, zipf)) for r in range(world)]
+        procs = [ctx.Process(target=_rank, args=(r, world, port, T, d, zipf, exchange))
+                 for r in range(world)]
         for p in procs:
             p.start()
         for p in procs:
