@@ -126,6 +126,10 @@ SIGNATURES = {
     "astro_moe_ep_route": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
     "astro_moe_ep_push": ([_P, _I32, _P, _I64, _P, _P], ctypes.c_int),
     "astro_moe_ep_experts_push": ([_P, _I32, _P, _I64, _P, _I64, _P, _P], ctypes.c_int),
+    "astro_moe_ep_post_counts": ([_P, _I32, _P], ctypes.c_int),
+    "astro_moe_ep_push_dev": ([_P, _I32, _P, _I64], ctypes.c_int),
+    "astro_moe_ep_experts_dev": ([_P, _I32, _P, _I64], ctypes.c_int),
+    "astro_moe_ep_exchange_counts": ([_P, _P], ctypes.c_int),
     "astro_moe_page_bytes": ([_I32, _I32, _I32, _I32], ctypes.c_int64),
     "astro_moe_pager_create": ([_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64,
                                 ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),

@@ -145,6 +145,10 @@ struct astro_moe_ctx {
   int64_t xr_recv_rows = 0, xr_ret_rows = 0;
   void* xr_peer_recv[astro::kMaxPeers] = {};
   void* xr_peer_ret[astro::kMaxPeers] = {};
+  // count mailbox: uint32 [world][kMailboxExperts] received per-expert counts, then
+  // the [world][world] send matrix
+  void* xr_mbox = nullptr;
+  void* xr_peer_mbox[astro::kMaxPeers] = {};
   bool xr_connected = false;
 };
 
@@ -339,6 +343,9 @@ int copy_taps(astro_moe_ctx* ctx, const BlockWorkspace& b, int64_t T, int E, int
   }
   return ASTRO_MOE_OK;
 }
+
+// experts per rank a count mailbox holds
+constexpr int kMailboxExperts = 1024;
 
 // batches up to this many tokens take the decode GEMVs unless the options say otherwise
 constexpr int64_t kDefaultDecodeTokens = 8;
@@ -1061,9 +1068,11 @@ int astro_moe_ctx_destroy(astro_moe_ctx* ctx) {
     if (r == ctx->xr_rank) continue;
     if (ctx->xr_peer_recv[r]) cudaIpcCloseMemHandle(ctx->xr_peer_recv[r]);
     if (ctx->xr_peer_ret[r]) cudaIpcCloseMemHandle(ctx->xr_peer_ret[r]);
+    if (ctx->xr_peer_mbox[r]) cudaIpcCloseMemHandle(ctx->xr_peer_mbox[r]);
   }
   if (ctx->xr_recv) cudaFree(ctx->xr_recv);
   if (ctx->xr_ret) cudaFree(ctx->xr_ret);
+  if (ctx->xr_mbox) cudaFree(ctx->xr_mbox);
   delete ctx;
   return ASTRO_MOE_OK;
 }
@@ -1596,9 +1605,12 @@ int astro_moe_ep_exchange_create(astro_moe_ctx* ctx, int32_t world, int32_t rank
   DeviceGuard g(ctx->device);
   CK(cudaMalloc(&ctx->xr_recv, sizeof(uint16_t) * (size_t)recv_rows * hidden), "cudaMalloc(receive buffer)");
   CK(cudaMalloc(&ctx->xr_ret, sizeof(uint16_t) * (size_t)return_rows * hidden), "cudaMalloc(return buffer)");
-  cudaIpcMemHandle_t h[2];
+  CK(cudaMalloc(&ctx->xr_mbox, sizeof(uint32_t) * (size_t)world * (kMailboxExperts + world)),
+     "cudaMalloc(count mailbox)");
+  cudaIpcMemHandle_t h[3];
   CK(cudaIpcGetMemHandle(&h[0], ctx->xr_recv), "cudaIpcGetMemHandle");
   CK(cudaIpcGetMemHandle(&h[1], ctx->xr_ret), "cudaIpcGetMemHandle");
+  CK(cudaIpcGetMemHandle(&h[2], ctx->xr_mbox), "cudaIpcGetMemHandle");
   std::memcpy(handles_out, h, sizeof(h));
   ctx->xr_world = world;
   ctx->xr_rank = rank;
@@ -1618,12 +1630,15 @@ int astro_moe_ep_exchange_connect(astro_moe_ctx* ctx, const void* all_handles) {
     if (r == ctx->xr_rank) {
       ctx->xr_peer_recv[r] = ctx->xr_recv;
       ctx->xr_peer_ret[r] = ctx->xr_ret;
+      ctx->xr_peer_mbox[r] = ctx->xr_mbox;
       continue;
     }
-    CK(cudaIpcOpenMemHandle(&ctx->xr_peer_recv[r], h[2 * r], cudaIpcMemLazyEnablePeerAccess),
+    CK(cudaIpcOpenMemHandle(&ctx->xr_peer_recv[r], h[3 * r], cudaIpcMemLazyEnablePeerAccess),
        "cudaIpcOpenMemHandle(receive buffer)");
-    CK(cudaIpcOpenMemHandle(&ctx->xr_peer_ret[r], h[2 * r + 1], cudaIpcMemLazyEnablePeerAccess),
+    CK(cudaIpcOpenMemHandle(&ctx->xr_peer_ret[r], h[3 * r + 1], cudaIpcMemLazyEnablePeerAccess),
        "cudaIpcOpenMemHandle(return buffer)");
+    CK(cudaIpcOpenMemHandle(&ctx->xr_peer_mbox[r], h[3 * r + 2], cudaIpcMemLazyEnablePeerAccess),
+       "cudaIpcOpenMemHandle(count mailbox)");
   }
   ctx->xr_connected = true;
   return ASTRO_MOE_OK;
@@ -1736,6 +1751,148 @@ int astro_moe_ep_exchange_buffers(astro_moe_ctx* ctx, void** recv, void** ret) {
   if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "exchange buffers: null ctx");
   if (recv) *recv = ctx->xr_recv;
   if (ret) *ret = ctx->xr_ret;
+  return ASTRO_MOE_OK;
+}
+
+
+// --- device-planned peer exchange (no host synchronisation) -----------------
+static int ep_dev_check(astro_moe_ctx* ctx, int32_t layer, const char* op, LayerState** Lp) {
+  if (int rc = ep_layer(ctx, layer, op, Lp)) return rc;
+  if (!ctx->xr_connected) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: exchange not connected", op);
+  if ((*Lp)->w.experts > kMailboxExperts)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: more than %d experts per rank", op, kMailboxExperts);
+  return ASTRO_MOE_OK;
+}
+
+static const uint32_t* mailbox_matrix(astro_moe_ctx* ctx) {
+  return static_cast<const uint32_t*>(ctx->xr_mbox) + (size_t)ctx->xr_world * kMailboxExperts;
+}
+
+int astro_moe_ep_post_counts(astro_moe_ctx* ctx, int32_t layer, const uint32_t* expert_offsets) {
+  const char* op = "expert-parallel post counts";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_dev_check(ctx, layer, op, &Lp)) return rc;
+  if (!expert_offsets) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null offsets", op);
+  DeviceGuard g(ctx->device);
+  // mailbox rows are [world][kMailboxExperts]; the send matrix follows them
+  const int El = Lp->w.experts;
+  void* boxes[astro::kMaxPeers];
+  for (int r = 0; r < ctx->xr_world; ++r) boxes[r] = ctx->xr_peer_mbox[r];
+  CK(astro::launch_ep_post_counts(expert_offsets, El, ctx->xr_world, ctx->xr_rank, boxes,
+                                  kMailboxExperts, ctx->stream),
+     op);
+  ctx->launches += 1;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_push_dev(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T) {
+  const char* op = "expert-parallel push (device-planned)";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_dev_check(ctx, layer, op, &Lp)) return rc;
+  if (ctx->ep_layer != layer || ctx->ep_tokens != T)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: does not match the routing in flight", op);
+  if (T == 0) return ASTRO_MOE_OK;
+  const astro_moe_layer_weights& w = Lp->w;
+  const int E = Lp->ep_total, K = w.top_k;
+  DeviceGuard g(ctx->device);
+  EpDispatch d{};
+  plan_ep_dispatch(T, E, K, &d, (char*)ctx->ep_disp.p);
+  CK(astro::launch_ep_push_rows_dev(x, T, d.stok, d.sids, T * K, w.experts, ctx->xr_world,
+                                    ctx->xr_rank, w.hidden, mailbox_matrix(ctx), ctx->xr_peer_recv,
+                                    ctx->xr_recv_rows, ctx->status, ctx->stream),
+     op);
+  ctx->launches += 1;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_experts_dev(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T) {
+  const char* op = "expert-parallel experts (device-planned)";
+  LayerState* Lp = nullptr;
+  if (int rc = ep_dev_check(ctx, layer, op, &Lp)) return rc;
+  LayerState& L = *Lp;
+  const astro_moe_layer_weights& w = L.w;
+  const int H = w.hidden, El = w.experts, I = w.intermediate, K = w.top_k, W = ctx->xr_world;
+  const bool has_shared = w.shared_intermediate > 0;
+  if (T < 0 || (T > 0 && !x)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid tokens", op);
+  const int64_t n_cap = ctx->xr_recv_rows;  // every row this rank can receive
+  const int64_t shared_rows = has_shared ? T : 0;
+  const int64_t rows_cap = n_cap + shared_rows;
+  DeviceGuard g(ctx->device);
+  cudaStream_t st = ctx->stream;
+  EpExperts e{};
+  if (int rc = devbuf_ensure(ctx, ctx->ep_exp, plan_ep_experts(rows_cap, n_cap, H, I, W * El, El,
+                                                               nullptr, nullptr)))
+    return rc;
+  plan_ep_experts(rows_cap, n_cap, H, I, W * El, El, &e, (char*)ctx->ep_exp.p);
+  if (has_shared)
+    if (int rc = devbuf_ensure(ctx, ctx->ep_shared, sizeof(uint16_t) * (size_t)(T > 0 ? T : 1) * H))
+      return rc;
+  const uint32_t* counts = static_cast<const uint32_t*>(ctx->xr_mbox);  // [W][kMailboxExperts]
+  CK(astro::launch_ep_permutation_strided(counts, kMailboxExperts, W, El, (int)shared_rows, n_cap,
+                                          e.src_start, e.exp_start, e.offsets, e.dest, e.src_of, st),
+     "expert-major permutation");
+  CK(astro::launch_ep_gather_states(ctx->xr_recv, e.src_of, x, shared_rows, W, ctx->xr_rank, H,
+                                    mailbox_matrix(ctx), n_cap, e.states, ctx->status, st),
+     "expert-major rows");
+  if (astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores)) {
+    CK(astro::moe_gemm_gate_up(L.gemm, e.states, rows_cap, e.offsets, e.act, e.gemm_scratch,
+                               ctx->status, st),
+       "gate/up projection");
+    CK(astro::moe_gemm_down(L.gemm, e.act, rows_cap, e.offsets, e.yrows, e.gemm_scratch, ctx->status,
+                            st),
+       "down projection");
+  } else {
+    astro::GroupedGemvDesc dsc;
+    dsc.x = e.states;
+    dsc.x_limit = rows_cap;
+    dsc.in_features = H;
+    dsc.seg_offsets = e.offsets;
+    dsc.nseg = El + (has_shared ? 1 : 0);
+    dsc.shared_seg = has_shared ? El : -1;
+    dsc.rows_total = rows_cap;
+    astro::AffineRef down[2];
+    fill_projections(w, dsc.wa, dsc.wb, down);
+    dsc.out_features = I;
+    dsc.group = w.group_size;
+    dsc.bits = w.bits;
+    dsc.swiglu = true;
+    dsc.y = e.act;
+    dsc.y_limit = rows_cap;
+    dsc.ldy = I;
+    dsc.status = ctx->status;
+    CK(astro::launch_grouped_gemv(dsc, st), "gate/up projection");
+    astro::GroupedGemvDesc dd = dsc;
+    dd.x = e.act;
+    dd.in_features = I;
+    dd.wa[0] = down[0];
+    dd.wa[1] = down[1];
+    dd.wb[0] = dd.wb[1] = astro::AffineRef{};
+    dd.out_features = H;
+    dd.swiglu = false;
+    dd.y = e.yrows;
+    dd.ldy = H;
+    CK(astro::launch_grouped_gemv(dd, st), "down projection");
+  }
+  CK(astro::launch_ep_return_rows_dev(e.yrows, rows_cap, e.dest, W, ctx->xr_rank, H,
+                                      mailbox_matrix(ctx), ctx->xr_peer_ret, ctx->xr_ret_rows,
+                                      ctx->status, st),
+     "return rows");
+  if (has_shared)
+    CK(astro::launch_ep_copy_shared_rows(e.yrows, rows_cap, W, ctx->xr_rank, T, H,
+                                         mailbox_matrix(ctx), ctx->ep_shared.p, st),
+       "shared-expert rows");
+  ctx->launches += 7;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_ep_exchange_counts(astro_moe_ctx* ctx, uint32_t* host_matrix) {
+  if (!ctx || !host_matrix || !ctx->xr_mbox)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "exchange counts: no exchange");
+  DeviceGuard g(ctx->device);
+  CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  CK(cudaMemcpy(host_matrix, mailbox_matrix(ctx), sizeof(uint32_t) * ctx->xr_world * ctx->xr_world,
+                cudaMemcpyDeviceToHost),
+     "read count matrix");
   return ASTRO_MOE_OK;
 }
 

@@ -54,7 +54,7 @@ ASTRO_DEVINL uint32_t block_exclusive_scan(uint32_t& v, uint32_t* warp_tot) {
 }
 
 __global__ void __launch_bounds__(kSegThreads) ep_segments_kernel(
-    const uint32_t* __restrict__ counts, int world, int El, int shared_rows,
+    const uint32_t* __restrict__ counts, int cstride, int world, int El, int shared_rows,
     uint32_t* __restrict__ src_start, uint32_t* __restrict__ exp_start,
     uint32_t* __restrict__ offsets) {
   __shared__ uint32_t warp_tot[33];
@@ -64,7 +64,8 @@ __global__ void __launch_bounds__(kSegThreads) ep_segments_kernel(
   // source-major order: run index i = s * El + e
   {
     const int i0 = 2 * threadIdx.x, i1 = i0 + 1;
-    const uint32_t c0 = i0 < runs ? counts[i0] : 0u, c1 = i1 < runs ? counts[i1] : 0u;
+    auto cnt = [&](int i) { return counts[(i / El) * cstride + i % El]; };  // run i = s*El + e
+    const uint32_t c0 = i0 < runs ? cnt(i0) : 0u, c1 = i1 < runs ? cnt(i1) : 0u;
     uint32_t v = c0 + c1;
     block_exclusive_scan(v, warp_tot);
     if (i0 < runs) src_start[i0] = v;
@@ -74,8 +75,9 @@ __global__ void __launch_bounds__(kSegThreads) ep_segments_kernel(
   {
     const int j0 = 2 * threadIdx.x, j1 = j0 + 1;
     auto run_of = [&](int j) { return (j % world) * El + j / world; };
-    const uint32_t c0 = j0 < runs ? counts[run_of(j0)] : 0u;
-    const uint32_t c1 = j1 < runs ? counts[run_of(j1)] : 0u;
+    auto cnt = [&](int i) { return counts[(i / El) * cstride + i % El]; };
+    const uint32_t c0 = j0 < runs ? cnt(run_of(j0)) : 0u;
+    const uint32_t c1 = j1 < runs ? cnt(run_of(j1)) : 0u;
     uint32_t v = c0 + c1;
     const uint32_t total = block_exclusive_scan(v, warp_tot);
     if (j0 < runs) {
@@ -95,12 +97,14 @@ __global__ void __launch_bounds__(kSegThreads) ep_segments_kernel(
   }
 }
 
-__global__ void ep_perm_kernel(const uint32_t* __restrict__ counts,
+__global__ void ep_perm_kernel(const uint32_t* __restrict__ counts, int cstride, int El,
                                const uint32_t* __restrict__ src_start,
-                               const uint32_t* __restrict__ exp_start, uint32_t* __restrict__ dest,
-                               uint32_t* __restrict__ src_of) {
+                               const uint32_t* __restrict__ exp_start, int64_t cap,
+                               uint32_t* __restrict__ dest, uint32_t* __restrict__ src_of) {
   const int run = blockIdx.x;
-  const uint32_t n = counts[run], q0 = src_start[run], d0 = exp_start[run];
+  const uint32_t n = counts[(run / El) * cstride + run % El], q0 = src_start[run],
+                 d0 = exp_start[run];
+  if ((int64_t)q0 + n > cap || (int64_t)d0 + n > cap) return;  // inconsistent counts
   for (uint32_t r = threadIdx.x; r < n; r += blockDim.x) {
     dest[q0 + r] = d0 + r;
     src_of[d0 + r] = q0 + r;
@@ -109,14 +113,24 @@ __global__ void ep_perm_kernel(const uint32_t* __restrict__ counts,
 
 }  // namespace
 
+cudaError_t launch_ep_permutation_strided(const uint32_t* counts, int cstride, int world, int El,
+                                          int shared_rows, int64_t cap, uint32_t* src_start,
+                                          uint32_t* exp_start, uint32_t* offsets, uint32_t* dest,
+                                          uint32_t* src_of, cudaStream_t st) {
+  if (world < 1 || El < 1 || world * El > kMaxRuns || cstride < El) return cudaErrorInvalidValue;
+  ep_segments_kernel<<<1, kSegThreads, 0, st>>>(counts, cstride, world, El, shared_rows, src_start,
+                                                exp_start, offsets);
+  ep_perm_kernel<<<world * El, 128, 0, st>>>(counts, cstride, El, src_start, exp_start, cap, dest,
+                                             src_of);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_ep_permutation(const uint32_t* counts, int world, int El, int shared_rows,
                                   uint32_t* src_start, uint32_t* exp_start, uint32_t* offsets,
                                   uint32_t* dest, uint32_t* src_of, cudaStream_t st) {
-  if (world < 1 || El < 1 || world * El > kMaxRuns) return cudaErrorInvalidValue;
-  ep_segments_kernel<<<1, kSegThreads, 0, st>>>(counts, world, El, shared_rows, src_start,
-                                                exp_start, offsets);
-  ep_perm_kernel<<<world * El, 128, 0, st>>>(counts, src_start, exp_start, dest, src_of);
-  return cudaGetLastError();
+  // counts from this process's own all-to-all: the receive buffers were sized from them
+  return launch_ep_permutation_strided(counts, El, world, El, shared_rows, INT64_MAX, src_start,
+                                       exp_start, offsets, dest, src_of, st);
 }
 
 }  // namespace astro
@@ -237,4 +251,235 @@ cudaError_t launch_ep_return_rows(const void* yrows, int64_t y_rows, const uint3
   return cudaGetLastError();
 }
 
+}  // namespace astro
+
+// ===========================================================================
+// Device-planned peer exchange: counts travel through per-rank mailboxes
+// (uint32 [world][El] per-expert counts received, then [world][world] rows each
+// rank sends each rank), so every placement below is computed on the device and
+// a layer needs no host synchronisation.
+namespace astro {
+namespace {
+
+struct PeerPtrs {
+  void* p[kMaxPeers];
+};
+
+// this rank's counts into every rank's mailbox: per-expert counts of rank d's
+// experts into d's slot [me][*]; per-destination totals into row me of every
+// rank's matrix
+__global__ void ep_post_counts_kernel(const uint32_t* __restrict__ offsets, int El, int world,
+                                      int me, int stride, const __grid_constant__ PeerPtrs mbox) {
+  for (int i = threadIdx.x; i < world * El; i += blockDim.x) {
+    const int d = i / El, e = i - d * El;
+    const uint32_t c = offsets[d * El + e + 1] - offsets[d * El + e];
+    reinterpret_cast<uint32_t*>(mbox.p[d])[me * stride + e] = c;
+  }
+  for (int i = threadIdx.x; i < world * world; i += blockDim.x) {
+    const int r = i / world, d = i - r * world;  // to rank r: my total for d
+    const uint32_t c = offsets[(d + 1) * El] - offsets[d * El];
+    reinterpret_cast<uint32_t*>(mbox.p[r])[world * stride + me * world + d] = c;
+  }
+}
+
+// prefix sums of the send matrix M[s][d] (this rank's mailbox) needed by a block
+struct Placement {
+  int64_t send_start[kMaxPeers];   // my rows for d start at this sorted position
+  int64_t dest_off[kMaxPeers];     // ... and land from this row of d's receive buffer
+  int64_t recv_start[kMaxPeers];   // rows from s start at this received row
+  int64_t ret_off[kMaxPeers];      // ... and return to this row of s's return buffer
+  int64_t recv_total;
+};
+
+ASTRO_DEVINL void load_placement(const uint32_t* __restrict__ M, int world, int me, Placement* P) {
+  __shared__ uint32_t m[kMaxPeers * kMaxPeers];
+  if (threadIdx.x < world * world) m[threadIdx.x] = __ldcg(M + threadIdx.x);  // one round trip
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int64_t a = 0, t = 0;
+    for (int d = 0; d < world; ++d) {
+      P->send_start[d] = a;
+      a += m[me * world + d];
+      int64_t o = 0;
+      for (int s = 0; s < me; ++s) o += m[s * world + d];
+      P->dest_off[d] = o;
+    }
+    for (int s = 0; s < world; ++s) {
+      P->recv_start[s] = t;
+      t += m[s * world + me];
+      int64_t o = 0;
+      for (int d = 0; d < me; ++d) o += m[s * world + d];
+      P->ret_off[s] = o;
+    }
+    P->recv_total = t;
+  }
+  __syncthreads();
+}
+
+__global__ void ep_push_rows_dev_kernel(const uint4* __restrict__ x, const uint32_t* __restrict__ stok,
+                                       const uint32_t* __restrict__ sids, int64_t n, int El,
+                                       int world, int me, int chunks, int64_t x_rows,
+                                       const uint32_t* __restrict__ M,
+                                       const __grid_constant__ PeerPtrs recv, int64_t cap_rows,
+                                       uint32_t* __restrict__ status) {
+  __shared__ Placement P;
+  load_placement(M, world, me, &P);
+  const int64_t total = n * chunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = i / chunks;
+    const int c = (int)(i - p * chunks);
+    const uint32_t d = sids[p] / (uint32_t)El;
+    const uint32_t tok = stok[p];
+    if (d >= (uint32_t)world || tok >= (uint64_t)x_rows) {
+      record_status(status, kDevBadShape);
+      continue;
+    }
+    const int64_t row = P.dest_off[d] + (p - P.send_start[d]);
+    if (row < 0 || row >= cap_rows) {
+      record_status(status, kDevBadShape);
+      continue;
+    }
+    reinterpret_cast<uint4*>(recv.p[d])[row * chunks + c] = x[(int64_t)tok * chunks + c];
+  }
+}
+
+// received rows -> expert-major states (src_of), then this rank's own tokens
+// appended as the shared expert's rows after the routed ones
+__global__ void ep_gather_states_kernel(const uint4* __restrict__ recv,
+                                        const uint32_t* __restrict__ src_of,
+                                        const uint4* __restrict__ x, int64_t T, int world, int me,
+                                        int chunks, const uint32_t* __restrict__ M,
+                                        int64_t cap_rows, uint4* __restrict__ states,
+                                        uint32_t* __restrict__ status) {
+  __shared__ Placement P;
+  load_placement(M, world, me, &P);
+  const int64_t n = P.recv_total;
+  if (n > cap_rows) {  // counts inconsistent with the receive buffer: touch nothing
+    if (threadIdx.x == 0) record_status(status, kDevBadShape);
+    return;
+  }
+  const int64_t total = (n + T) * chunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = i / chunks;
+    const int c = (int)(i - q * chunks);
+    if (q < n) {
+      const uint32_t s = src_of[q];
+      if (s >= (uint64_t)n) {
+        record_status(status, kDevBadShape);
+        continue;
+      }
+      states[q * chunks + c] = recv[(int64_t)s * chunks + c];
+    } else {
+      states[q * chunks + c] = x[(q - n) * chunks + c];
+    }
+  }
+}
+
+__global__ void ep_return_rows_dev_kernel(const uint4* __restrict__ yrows,
+                                          const uint32_t* __restrict__ dest, int world, int me,
+                                          int chunks, int64_t y_rows,
+                                          const uint32_t* __restrict__ M,
+                                          const __grid_constant__ PeerPtrs ret, int64_t cap_rows,
+                                          uint32_t* __restrict__ status) {
+  __shared__ Placement P;
+  load_placement(M, world, me, &P);
+  if (P.recv_total > y_rows) {
+    if (threadIdx.x == 0) record_status(status, kDevBadShape);
+    return;
+  }
+  const int64_t total = P.recv_total * chunks;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t q = i / chunks;
+    const int c = (int)(i - q * chunks);
+    int s = 0;
+    while (s + 1 < world && q >= P.recv_start[s + 1]) ++s;
+    const uint32_t src = dest[q];
+    const int64_t row = P.ret_off[s] + (q - P.recv_start[s]);
+    if (src >= (uint64_t)y_rows || row < 0 || row >= cap_rows) {
+      record_status(status, kDevBadShape);
+      continue;
+    }
+    reinterpret_cast<uint4*>(ret.p[s])[row * chunks + c] = yrows[(int64_t)src * chunks + c];
+  }
+}
+
+PeerPtrs make_ptrs(void* const* p, int world) {
+  PeerPtrs t{};
+  for (int i = 0; i < world && i < kMaxPeers; ++i) t.p[i] = p[i];
+  return t;
+}
+
+}  // namespace
+
+cudaError_t launch_ep_post_counts(const uint32_t* offsets, int El, int world, int me,
+                                  void* const* mailboxes, int stride, cudaStream_t st) {
+  if (world < 1 || world > kMaxPeers || stride < El) return cudaErrorInvalidValue;
+  ep_post_counts_kernel<<<1, 256, 0, st>>>(offsets, El, world, me, stride,
+                                           make_ptrs(mailboxes, world));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_push_rows_dev(const void* x, int64_t x_rows, const uint32_t* stok,
+                                    const uint32_t* sids, int64_t n, int El, int world, int me,
+                                    int H, const uint32_t* M, void* const* peer_recv,
+                                    int64_t cap_rows, uint32_t* status, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  if (world < 1 || world > kMaxPeers || H % 8) return cudaErrorInvalidValue;
+  ep_push_rows_dev_kernel<<<grid_rows(n, H / 8), 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(x), stok, sids, n, El, world, me, H / 8, x_rows, M,
+      make_ptrs(peer_recv, world), cap_rows, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_gather_states(const void* recv, const uint32_t* src_of, const void* x,
+                                    int64_t T, int world, int me, int H, const uint32_t* M,
+                                    int64_t cap_rows, void* states, uint32_t* status,
+                                    cudaStream_t st) {
+  if (world < 1 || world > kMaxPeers || H % 8) return cudaErrorInvalidValue;
+  ep_gather_states_kernel<<<148 * 8, 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(recv), src_of, reinterpret_cast<const uint4*>(x), T, world,
+      me, H / 8, M, cap_rows, reinterpret_cast<uint4*>(states), status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return_rows_dev(const void* yrows, int64_t y_rows, const uint32_t* dest,
+                                      int world, int me, int H, const uint32_t* M,
+                                      void* const* peer_ret, int64_t cap_rows, uint32_t* status,
+                                      cudaStream_t st) {
+  if (world < 1 || world > kMaxPeers || H % 8) return cudaErrorInvalidValue;
+  ep_return_rows_dev_kernel<<<148 * 8, 256, 0, st>>>(
+      reinterpret_cast<const uint4*>(yrows), dest, world, me, H / 8, y_rows, M,
+      make_ptrs(peer_ret, world), cap_rows, status);
+  return cudaGetLastError();
+}
+
+}  // namespace astro
+
+namespace astro {
+namespace {
+__global__ void ep_copy_shared_rows_kernel(const uint4* __restrict__ yrows, int world, int me,
+                                           int64_t T, int chunks, const uint32_t* __restrict__ M,
+                                           int64_t y_rows, uint4* __restrict__ out) {
+  __shared__ Placement P;
+  load_placement(M, world, me, &P);
+  const int64_t base = P.recv_total;
+  if (base + T > y_rows) return;  // inconsistent counts (the gather recorded it)
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < T * chunks;
+       i += (int64_t)gridDim.x * blockDim.x)
+    out[i] = yrows[base * chunks + i];
+}
+}  // namespace
+
+cudaError_t launch_ep_copy_shared_rows(const void* yrows, int64_t y_rows, int world, int me,
+                                       int64_t T, int H, const uint32_t* M, void* out,
+                                       cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  ep_copy_shared_rows_kernel<<<148 * 2, 256, 0, st>>>(reinterpret_cast<const uint4*>(yrows), world,
+                                                      me, T, H / 8, M, y_rows,
+                                                      reinterpret_cast<uint4*>(out));
+  return cudaGetLastError();
+}
 }  // namespace astro

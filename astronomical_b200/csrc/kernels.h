@@ -161,6 +161,32 @@ cudaError_t launch_ep_return_rows(const void* yrows, int64_t y_rows, const uint3
                                   const int64_t* peer_cap_rows, const int64_t* peer_offs,
                                   const int64_t* starts, uint32_t* status, cudaStream_t st);
 
+// Device-planned peer exchange (ep.cu).  Mailbox of every rank: uint32
+// [world][El] per-expert counts it receives, then the [world][world] send matrix.
+cudaError_t launch_ep_post_counts(const uint32_t* offsets, int El, int world, int me,
+                                  void* const* mailboxes, int stride, cudaStream_t st);
+// counts [world][cstride] (the first El of each row used)
+cudaError_t launch_ep_permutation_strided(const uint32_t* counts, int cstride, int world, int El,
+                                          int shared_rows, int64_t cap, uint32_t* src_start,
+                                          uint32_t* exp_start, uint32_t* offsets, uint32_t* dest,
+                                          uint32_t* src_of, cudaStream_t st);
+cudaError_t launch_ep_push_rows_dev(const void* x, int64_t x_rows, const uint32_t* stok,
+                                    const uint32_t* sids, int64_t n, int El, int world, int me,
+                                    int H, const uint32_t* M, void* const* peer_recv,
+                                    int64_t cap_rows, uint32_t* status, cudaStream_t st);
+cudaError_t launch_ep_gather_states(const void* recv, const uint32_t* src_of, const void* x,
+                                    int64_t T, int world, int me, int H, const uint32_t* M,
+                                    int64_t cap_rows, void* states, uint32_t* status,
+                                    cudaStream_t st);
+cudaError_t launch_ep_return_rows_dev(const void* yrows, int64_t y_rows, const uint32_t* dest,
+                                      int world, int me, int H, const uint32_t* M,
+                                      void* const* peer_ret, int64_t cap_rows, uint32_t* status,
+                                      cudaStream_t st);
+
+cudaError_t launch_ep_copy_shared_rows(const void* yrows, int64_t y_rows, int world, int me,
+                                       int64_t T, int H, const uint32_t* M, void* out,
+                                       cudaStream_t st);
+
 // Sets the calling thread's astro_moe_last_error() message and returns `status`
 // (for entry points defined outside api.cu).
 int set_last_error(int status, const char* message);

@@ -155,12 +155,12 @@ class CudaExpertShard:
         """Allocates this rank's receive / return buffers, trades IPC handles with
         the other ranks (all-gather) and maps theirs."""
         K, H = self.cfg["top_k"], self.cfg["hidden"]
-        handles = (ctypes.c_ubyte * 128)()
+        handles = (ctypes.c_ubyte * 192)()
         check(_lib.lib().astro_moe_ep_exchange_create(self.ctx, self.world, self.rank, H,
                                                       self.world * max_tokens * K, max_tokens * K,
                                                       ctypes.byref(handles)))
         mine = torch.tensor(bytearray(handles), dtype=torch.uint8, device=self.device)
-        everyone = torch.empty((self.world, 128), dtype=torch.uint8, device=self.device)
+        everyone = torch.empty((self.world, 192), dtype=torch.uint8, device=self.device)
         dist.all_gather_into_tensor(everyone, mine, group=group)
         buf = bytes(everyone.cpu().numpy().tobytes())
         arr = (ctypes.c_ubyte * len(buf)).from_buffer_copy(buf)
@@ -188,6 +188,24 @@ class CudaExpertShard:
                                                    _ptr(x), x.shape[0], self._i64(recv_starts),
                                                    self._i64(return_offsets)))
 
+    def post_counts(self, layer: int, offsets: torch.Tensor) -> None:
+        self._bind()
+        check(_lib.lib().astro_moe_ep_post_counts(self.ctx, layer, _ptr(offsets)))
+
+    def push_dev(self, layer: int, x: torch.Tensor) -> None:
+        self._bind()
+        check(_lib.lib().astro_moe_ep_push_dev(self.ctx, layer, _ptr(x), x.shape[0]))
+
+    def experts_dev(self, layer: int, x: torch.Tensor) -> None:
+        self._bind()
+        check(_lib.lib().astro_moe_ep_experts_dev(self.ctx, layer, _ptr(x), x.shape[0]))
+
+    def exchange_counts(self):
+        """[world][world] rows rank s sent rank d in the last layer (synchronises)."""
+        m = (ctypes.c_uint32 * (self.world * self.world))()
+        check(_lib.lib().astro_moe_ep_exchange_counts(self.ctx, m))
+        return [[m[s * self.world + d] for d in range(self.world)] for s in range(self.world)]
+
     def kernel_launches(self, reset: bool = True) -> int:
         a = _lib.Attribution()
         check(_lib.lib().astro_moe_ctx_read_attribution(self.ctx, ctypes.byref(a), int(reset)))
@@ -213,9 +231,12 @@ class ExpertParallelBlock:
 
     def __init__(self, shard, rank: int, world: int, experts: int, group=None,
                  exchange: str = "nccl"):
-        """exchange: "nccl" (all-to-all-v of rows through torch.distributed) or
+        """exchange: "nccl" (all-to-all-v of rows through torch.distributed),
         "peer" (rows stored into the peers' buffers by the dispatch and expert
-        kernels; needs ``shard.connect_exchange`` first)."""
+        kernels, placements computed on the device from count mailboxes: no host
+        synchronisation), or "peer_host" (the same stores, placements computed on
+        the host after reading the counts back).  The peer modes need
+        ``shard.connect_exchange`` first."""
         self.shard, self.rank, self.world, self.E = shard, rank, world, experts
         self.El = expert_range(rank, world, experts)[1]
         self.group = group
@@ -272,11 +293,37 @@ class ExpertParallelBlock:
         mark("combine")
         return y
 
+    def _forward_peer_dev(self, layer: int, x: torch.Tensor, mark) -> torch.Tensor:
+        offsets = self.shard.route(layer, x)
+        self.shard.post_counts(layer, offsets)
+        mark("dispatch")
+        self._barrier(x.device)
+        self.shard.push_dev(layer, x)
+        self._barrier(x.device)
+        mark("exchange_out")
+        self.shard.experts_dev(layer, x)
+        mark("experts")
+        self._barrier(x.device)
+        mark("exchange_back")
+        y = self.shard.combine(layer, None, x.shape[0])
+        mark("combine")
+        return y
+
+    def splits(self):
+        """(rows this rank sent each rank, rows it received from each rank) of the last layer."""
+        if self.exchange == "peer":
+            M = self.shard.exchange_counts()
+            return ([M[self.rank][d] for d in range(self.world)],
+                    [M[s][self.rank] for s in range(self.world)])
+        return self.last_splits
+
     def forward(self, layer: int, x: torch.Tensor, marks=None) -> torch.Tensor:
         """``marks``: optional callable recording a named point (stage timing)."""
         T = x.shape[0]
         mark = marks or (lambda name: None)
         if self.exchange == "peer":
+            return self._forward_peer_dev(layer, x, mark)
+        if self.exchange == "peer_host":
             return self._forward_peer(layer, x, mark)
         send, offsets = self.shard.dispatch(layer, x)
         mark("dispatch")

@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--no-decode", action="store_true", help="skip the config-2 decode sweep")
     ap.add_argument("--no-stack", action="store_true", help="skip the config-3 40-layer stack")
     ap.add_argument("--no-paging", action="store_true", help="skip the config-4 paged decode")
-    ap.add_argument("--ep-exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--ep-exchange", default="peer", choices=["peer", "peer_host", "nccl"],
                     help="N > 1: rows stored into peer buffers by our kernels, or NCCL all-to-all-v")
     ap.add_argument("--paging-layers", type=int, default=40)
     ap.add_argument("--paging-cache-gb", type=float, default=6.0)
@@ -321,7 +321,7 @@ def run_ep(args, rank, world, local, dev):
     shard = CudaExpertShard([w], rank, world, device=local, max_tokens=T)
     del w
     torch.cuda.empty_cache()
-    if args.ep_exchange == "peer":
+    if args.ep_exchange != "nccl":
         shard.connect_exchange(T)
     block = ExpertParallelBlock(shard, rank, world, E, exchange=args.ep_exchange)
     g = torch.Generator(device=dev)
@@ -361,7 +361,7 @@ def run_ep(args, rank, world, local, dev):
     launches = shard.kernel_launches(reset=True)
     ms = max_over_ranks(start.elapsed_time(end) / args.steps)
     value = T * world / (ms / 1e3)
-    sent_remote = sum(v for r, v in enumerate(block.last_splits[0]) if r != rank)
+    sent_remote = sum(v for r, v in enumerate(block.splits()[0]) if r != rank)
     nvlink_bytes = max_over_ranks(2.0 * sent_remote * H * 2)  # rows out and back, per rank
     # stage attribution (events on the launching stream), a separate pass
     m = stage_marker(dev)
@@ -448,7 +448,7 @@ def measure_stack(args, rank, world, local, dev, max_over_ranks):
     shard = CudaExpertShard(layers, rank, world, device=local, max_tokens=T)
     del layers
     torch.cuda.empty_cache()
-    if world > 1 and args.ep_exchange == "peer":
+    if world > 1 and args.ep_exchange != "nccl":
         shard.connect_exchange(T)
     block = ExpertParallelBlock(shard, rank, world, E, exchange=args.ep_exchange)
     g = torch.Generator(device=dev)

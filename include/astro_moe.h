@@ -311,10 +311,10 @@ int astro_moe_ep_combine(astro_moe_ctx* ctx, int32_t layer, const void* returned
  * stream-ordered collective (e.g. a one-element NCCL all-reduce).
  *
  * create: allocates this rank's receive buffer (recv_rows rows of H bf16; size
- * it for the most rows any rank can receive, world * tokens * top_k) and return
- * buffer (return_rows >= tokens * top_k) and writes their two IPC handles (2 x 64
- * bytes) to handles_out.  connect: all_handles = every rank's handles, in rank
- * order (world x 2 x 64 bytes); opens the peers' buffers. */
+ * it for the most rows any rank can receive, world * tokens * top_k), return
+ * buffer (return_rows >= tokens * top_k) and count mailbox, and writes their
+ * three IPC handles (3 x 64 bytes) to handles_out.  connect: all_handles = every
+ * rank's handles, in rank order (world x 3 x 64 bytes); opens the peers' buffers. */
 int astro_moe_ep_exchange_create(astro_moe_ctx* ctx, int32_t world, int32_t rank, int32_t hidden,
                                  int64_t recv_rows, int64_t return_rows, void* handles_out);
 int astro_moe_ep_exchange_connect(astro_moe_ctx* ctx, const void* all_handles);
@@ -336,6 +336,22 @@ int astro_moe_ep_push(astro_moe_ctx* ctx, int32_t layer, const void* hidden_stat
 int astro_moe_ep_experts_push(astro_moe_ctx* ctx, int32_t layer, const uint32_t* recv_counts,
                               int64_t recv_total, const void* hidden_states, int64_t tokens,
                               const int64_t* recv_starts, const int64_t* return_offsets);
+
+/* Device-planned variant (no host synchronisation in a layer): after
+ * astro_moe_ep_route, post_counts stores this rank's per-expert counts and
+ * per-rank totals into every rank's count mailbox; after an all-rank ordering
+ * collective, push_dev stores the rows (placements computed on the device from
+ * the mailbox), and after another, experts_dev runs the experts over this rank's
+ * whole receive buffer capacity (bounds read on the device) and stores the
+ * outputs back; after a third, astro_moe_ep_combine(returned_rows = NULL). */
+int astro_moe_ep_post_counts(astro_moe_ctx* ctx, int32_t layer, const uint32_t* expert_offsets);
+int astro_moe_ep_push_dev(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                          int64_t tokens);
+int astro_moe_ep_experts_dev(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
+                             int64_t tokens);
+/* The last layer's [world][world] send matrix (rows rank s sent rank d);
+ * synchronises the context stream. */
+int astro_moe_ep_exchange_counts(astro_moe_ctx* ctx, uint32_t* host_matrix);
 
 /* ------------------------------------------------------------------------ */
 /* Expert paging (config 4): Qwen3_5ExpertPager and the paged branch of        */

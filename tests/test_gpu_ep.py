@@ -43,7 +43,7 @@ def _rank(rank, world, port, T, outdir, zipf, exchange):
     if zipf:
         x[:, 0] = 1.0
     shard = CudaExpertShard(layers, rank, world, device=rank, max_tokens=T)
-    if exchange == "peer":
+    if exchange != "nccl":
         shard.connect_exchange(T)
     block = ExpertParallelBlock(shard, rank, world, cfg["experts"], exchange=exchange)
     for l in range(2):
@@ -60,7 +60,7 @@ def _rank(rank, world, port, T, outdir, zipf, exchange):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+@pytest.mark.parametrize("exchange", ["nccl", "peer_host", "peer"])
 @pytest.mark.parametrize("T,zipf", [(512, False), (96, True)])
 def test_expert_parallel_matches_single_gpu_block(T, zipf, exchange):
     import torch.multiprocessing as mp
