@@ -44,11 +44,11 @@ def _rank_main(rank, world, port, T, layers, outdir, skew):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T,skew", [(40, None), (3, None), (24, 1.1)])
-def test_expert_parallel_exchange_matches_single_process_oracle(T, skew):
+@pytest.mark.parametrize("T,skew,world", [(40, None, 2), (3, None, 2), (24, 1.1, 2), (16, 1.1, 4)])
+def test_expert_parallel_exchange_matches_single_process_oracle(T, skew, world):
     from oracle import oracle as O
 
-    world, layers = 2, 2
+    layers = 2
     with tempfile.TemporaryDirectory() as d:
         ctx = mp.get_context("spawn")
         port = _free_port()
@@ -70,5 +70,7 @@ def test_expert_parallel_exchange_matches_single_process_oracle(T, skew):
                                    for r in range(world)])
             assert np.array_equal(got, want)
         # rows sent by rank a to rank b are the rows rank b received from rank a
-        s0, s1 = (np.load(os.path.join(d, f"splits_{r}.npy")) for r in range(world))
-        assert s0[0][1] == s1[1][0] and s1[0][0] == s0[1][1]
+        sp = [np.load(os.path.join(d, f"splits_{r}.npy")) for r in range(world)]
+        for a in range(world):
+            for b in range(world):
+                assert sp[a][0][b] == sp[b][1][a]

@@ -60,14 +60,16 @@ def _rank(rank, world, port, T, outdir, zipf, exchange):
     dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("world", [2, 4])
 @pytest.mark.parametrize("exchange", ["nccl", "peer_host", "peer"])
 @pytest.mark.parametrize("T,zipf", [(512, False), (96, True)])
-def test_expert_parallel_matches_single_gpu_block(T, zipf, exchange):
+def test_expert_parallel_matches_single_gpu_block(T, zipf, exchange, world):
     import torch.multiprocessing as mp
 
     from tests.helpers import assert_block_close
 
-    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     with tempfile.TemporaryDirectory() as d:
         ctx = mp.get_context("spawn")
         port = _free_port()
