@@ -112,6 +112,8 @@ SIGNATURES = {
     "astro_moe_block_forward_taps": ([_P, _I32, _P, _I64, _P, ctypes.POINTER(BlockTaps)],
                                      ctypes.c_int),
     "astro_moe_block_forward_host": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
+    "astro_moe_block_forward_host_async": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
+    "astro_moe_host_synchronize": ([_P], ctypes.c_int),
     "astro_moe_ctx_set_attribution": ([_P, _I32], ctypes.c_int),
     "astro_moe_ctx_read_attribution": ([_P, ctypes.POINTER(Attribution), _I32], ctypes.c_int),
     "astro_moe_ep_register_layer": ([_P, _I32, ctypes.POINTER(LayerWeights), _I32, _I32],

@@ -127,6 +127,14 @@ struct astro_moe_ctx {
   size_t ws_bytes = 0;
   void* io = nullptr;  // device staging for the host-buffer entry point
   size_t io_bytes = 0;
+  // asynchronous host-buffer calls: two staging slots (input + output each), an
+  // upload and a download stream, and per slot the events that order them
+  void* aio[2] = {nullptr, nullptr};
+  size_t aio_bytes = 0;
+  cudaStream_t up = nullptr, down = nullptr;
+  cudaEvent_t ev_in[2] = {}, ev_done[2] = {}, ev_out[2] = {};
+  bool ev_out_used[2] = {false, false}, ev_done_used[2] = {false, false};
+  int aio_next = 0;
   // stage attribution
   bool attribution = false;
   std::vector<cudaEvent_t> event_pool;
@@ -1061,6 +1069,16 @@ int astro_moe_ctx_destroy(astro_moe_ctx* ctx) {
   for (auto e : ctx->event_pool) cudaEventDestroy(e);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->io) cudaFree(ctx->io);
+  if (ctx->up) cudaStreamSynchronize(ctx->up);
+  if (ctx->down) cudaStreamSynchronize(ctx->down);
+  for (int i = 0; i < 2; ++i) {
+    if (ctx->aio[i]) cudaFree(ctx->aio[i]);
+    if (ctx->ev_in[i]) cudaEventDestroy(ctx->ev_in[i]);
+    if (ctx->ev_done[i]) cudaEventDestroy(ctx->ev_done[i]);
+    if (ctx->ev_out[i]) cudaEventDestroy(ctx->ev_out[i]);
+  }
+  if (ctx->up) cudaStreamDestroy(ctx->up);
+  if (ctx->down) cudaStreamDestroy(ctx->down);
   if (ctx->ep_disp.p) cudaFree(ctx->ep_disp.p);
   if (ctx->ep_exp.p) cudaFree(ctx->ep_exp.p);
   if (ctx->ep_shared.p) cudaFree(ctx->ep_shared.p);
@@ -1894,6 +1912,72 @@ int astro_moe_ep_exchange_counts(astro_moe_ctx* ctx, uint32_t* host_matrix) {
                 cudaMemcpyDeviceToHost),
      "read count matrix");
   return ASTRO_MOE_OK;
+}
+
+
+// --- asynchronous host-buffer calls ------------------------------------------
+int astro_moe_block_forward_host_async(astro_moe_ctx* ctx, int32_t layer, const void* host_x,
+                                       int64_t T, void* host_out) {
+  const char* op = "block forward (host, async)";
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null ctx", op);
+  auto it = ctx->layers.find(layer);
+  if (it == ctx->layers.end() || !it->second.registered)
+    return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "%s: layer %d is not registered", op, layer);
+  if (it->second.ep || it->second.pager)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: layer %d is expert-parallel or paged", op, layer);
+  if (T < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: negative tokens", op);
+  if (T == 0) return ASTRO_MOE_OK;
+  if (!host_x || !host_out) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null buffer", op);
+  DeviceGuard g(ctx->device);
+  const size_t bytes = sizeof(uint16_t) * (size_t)T * it->second.w.hidden;
+  if (!ctx->up) {
+    CK(cudaStreamCreateWithFlags(&ctx->up, cudaStreamNonBlocking), "cudaStreamCreate");
+    CK(cudaStreamCreateWithFlags(&ctx->down, cudaStreamNonBlocking), "cudaStreamCreate");
+    for (int i = 0; i < 2; ++i) {
+      CK(cudaEventCreateWithFlags(&ctx->ev_in[i], cudaEventDisableTiming), "cudaEventCreate");
+      CK(cudaEventCreateWithFlags(&ctx->ev_done[i], cudaEventDisableTiming), "cudaEventCreate");
+      CK(cudaEventCreateWithFlags(&ctx->ev_out[i], cudaEventDisableTiming), "cudaEventCreate");
+    }
+  }
+  if (ctx->aio_bytes < 2 * bytes) {
+    CK(cudaStreamSynchronize(ctx->up), "sync");
+    CK(cudaStreamSynchronize(ctx->down), "sync");
+    CK(cudaStreamSynchronize(ctx->stream), "sync");
+    for (int i = 0; i < 2; ++i) {
+      if (ctx->aio[i]) cudaFree(ctx->aio[i]);
+      ctx->aio[i] = nullptr;
+    }
+    ctx->aio_bytes = 0;
+    for (int i = 0; i < 2; ++i) CK(cudaMalloc(&ctx->aio[i], 2 * bytes), "cudaMalloc(async staging)");
+    ctx->aio_bytes = 2 * bytes;
+  }
+  const int slot = ctx->aio_next;
+  ctx->aio_next ^= 1;
+  char* dx = (char*)ctx->aio[slot];
+  char* dy = dx + bytes;
+  // the slot's input may be overwritten once the block two calls ago read it
+  if (ctx->ev_done_used[slot]) CK(cudaStreamWaitEvent(ctx->up, ctx->ev_done[slot], 0), op);
+  CK(cudaMemcpyAsync(dx, host_x, bytes, cudaMemcpyHostToDevice, ctx->up), "copy hidden states in");
+  CK(cudaEventRecord(ctx->ev_in[slot], ctx->up), op);
+  CK(cudaStreamWaitEvent(ctx->stream, ctx->ev_in[slot], 0), op);
+  // ... and its output once the download two calls ago finished
+  if (ctx->ev_out_used[slot]) CK(cudaStreamWaitEvent(ctx->stream, ctx->ev_out[slot], 0), op);
+  if (int rc = run_block(ctx, it->second, dx, T, dy, nullptr)) return rc;
+  CK(cudaEventRecord(ctx->ev_done[slot], ctx->stream), op);
+  ctx->ev_done_used[slot] = true;
+  CK(cudaStreamWaitEvent(ctx->down, ctx->ev_done[slot], 0), op);
+  CK(cudaMemcpyAsync(host_out, dy, bytes, cudaMemcpyDeviceToHost, ctx->down), "copy output out");
+  CK(cudaEventRecord(ctx->ev_out[slot], ctx->down), op);
+  ctx->ev_out_used[slot] = true;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_host_synchronize(astro_moe_ctx* ctx) {
+  if (!ctx) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "synchronize: null ctx");
+  DeviceGuard g(ctx->device);
+  if (ctx->up) CK(cudaStreamSynchronize(ctx->up), "cudaStreamSynchronize");
+  if (ctx->down) CK(cudaStreamSynchronize(ctx->down), "cudaStreamSynchronize");
+  return astro_moe_ctx_synchronize(ctx);
 }
 
 }  // extern "C"

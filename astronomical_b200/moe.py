@@ -399,6 +399,17 @@ class Qwen3_5MoEBlock:
         check(_lib.lib().astro_moe_block_forward_host(self.ctx, self.layer, _ptr(host_hidden), T,
                                                       _ptr(host_out)))
 
+    def forward_host_async(self, host_hidden: torch.Tensor, host_out: torch.Tensor) -> None:
+        """Host buffers in and out without synchronising (call synchronize_host);
+        consecutive calls overlap their copies with each other's compute."""
+        T = host_hidden.numel() // self.cfg["hidden"]
+        self._bind_stream()
+        check(_lib.lib().astro_moe_block_forward_host_async(self.ctx, self.layer,
+                                                            _ptr(host_hidden), T, _ptr(host_out)))
+
+    def synchronize_host(self) -> None:
+        check(_lib.lib().astro_moe_host_synchronize(self.ctx))
+
     def set_attribution(self, enabled: bool) -> None:
         check(_lib.lib().astro_moe_ctx_set_attribution(self.ctx, int(enabled)))
 

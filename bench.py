@@ -664,18 +664,20 @@ def run_ours(args):
     # e2e through the host-buffer entry point
     hx = x.cpu().pin_memory()
     hy = torch.empty_like(hx).pin_memory()
+    # end to end through the asynchronous host-buffer entry point: every step
+    # uploads its input from pinned host memory and downloads its output; steps
+    # overlap one another's copies and compute (timed on the host clock, from the
+    # first upload to the last download)
     for _ in range(max(1, args.warmup)):
-        blk.forward_host(hx, hy)
+        blk.forward_host_async(hx, hy)
+    blk.synchronize_host()
     barrier()
-    torch.cuda.synchronize()
-    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
+    t0 = time.perf_counter()
     for _ in range(args.steps):
-        blk.forward_host(hx, hy)
-    e2.record()
-    torch.cuda.synchronize()
+        blk.forward_host_async(hx, hy)
+    blk.synchronize_host()
+    e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps)
     barrier()
-    e2e_ms = max_over_ranks(s2.elapsed_time(e2) / args.steps)
     e2e_value = T * world / (e2e_ms / 1e3)
 
     line = {

@@ -259,6 +259,16 @@ int astro_moe_ctx_read_attribution(astro_moe_ctx* ctx, astro_moe_attribution* ou
 int astro_moe_block_forward_host(astro_moe_ctx* ctx, int32_t layer, const void* host_hidden,
                                  int64_t tokens, void* host_out);
 
+/* Same with HOST buffers (pinned for overlap), without synchronising: the input
+ * goes up on an upload stream, the block runs on the context stream, the output
+ * comes down on a download stream, through two staging slots that alternate
+ * between calls, so call i's download and call i+1's upload overlap call i+1's
+ * block.  host_out is written when astro_moe_host_synchronize returns; the
+ * caller keeps both host buffers of a call untouched until then. */
+int astro_moe_block_forward_host_async(astro_moe_ctx* ctx, int32_t layer, const void* host_hidden,
+                                       int64_t tokens, void* host_out);
+int astro_moe_host_synchronize(astro_moe_ctx* ctx);
+
 /* ------------------------------------------------------------------------ */
 /* Expert parallelism over the GPUs of one node.  No counterpart in the       */
 /* reference (MLX runs the block on one device); it splits the same block      */

@@ -157,3 +157,22 @@ def test_block_host_entry_matches_device_entry():
     torch.cuda.synchronize()
     assert torch.equal(y.cpu(), hy)
     blk.close()
+
+
+def test_block_host_async_calls_match_device_entry():
+    """Four overlapping asynchronous host-buffer calls (the staging slots are
+    reused twice) each equal the device entry point on their own input."""
+    cfg = small_cfg()
+    w = synthetic.make_block_weights(cfg, seed=14)
+    blk = moe.Qwen3_5MoEBlock(w, max_tokens=384)
+    xs = [bf16_tensor(synthetic.make_hidden_states(384, cfg["hidden"], seed=20 + i)) for i in range(4)]
+    want = [blk.forward(x) for x in xs]
+    torch.cuda.synchronize()
+    hin = [x.cpu().pin_memory() for x in xs]
+    hout = [torch.empty_like(h).pin_memory() for h in hin]
+    for i in range(4):
+        blk.forward_host_async(hin[i], hout[i])
+    blk.synchronize_host()
+    for h, y in zip(hout, want):
+        assert torch.equal(h, y.cpu())
+    blk.close()
