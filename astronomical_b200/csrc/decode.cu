@@ -411,18 +411,154 @@ int grid_for(int64_t items_upper) {
 //   2. every block routes all T tokens and sorts the T*K assignments in its own
 //      shared memory (identical inputs give identical results in every block, so
 //      no barrier follows); block 0 publishes ids, scores and offsets;
-//   3. gate/up + SwiGLU over (active segment, 16 features) items -> act rows;
+//   3. gate/up + SwiGLU over (active segment, 32 features) items -> act rows;
 //   -- grid barrier --
 //   4. down over (active segment, 64 output rows) items -> expert rows;
+//      phases 3 and 4 run on warp tensor-core tiles (mma.sync m16n8k16, bf16
+//      operands, fp32 accumulation): a decode batch is at most 16 tokens wide, so
+//      each warp keeps one 16-row weight tile in registers, with no shared-memory
+//      or tensor-memory hand-off of the A operand, and the CUDA cores only
+//      dequantise; each block takes a contiguous share of the items;
 //   -- grid barrier --
 //   5. weighted combine with the gated shared expert -> out.
 // Launch gaps and the per-kernel dependency chains of the multi-kernel path
-// disappear; the arithmetic of every phase is the multi-kernel path's (same
-// routing, sort order, dequantisation, fp32 accumulation and combine), so the
-// two paths agree to the block tolerance and routing is bit-identical.
+// disappear.  Routing, sort order, dequantised weights and the combine are the
+// multi-kernel path's; the projections add the same fp32 products in another
+// order (tensor-core tiles, four K quarters summed in a fixed order), so the two
+// paths agree to the block tolerance and routing is bit-identical.
 constexpr int kFusedMaxTokens = 16;
 constexpr int kFusedMaxExperts = 256;
 constexpr int kFusedMaxAssign = 512;
+
+// Block b's share [lo, hi) of n items: contiguous, sizes differ by at most one,
+// so a block's consecutive items mostly share a segment and neighbouring rows.
+ASTRO_DEVINL void block_range(int n, int& lo, int& hi) {
+  lo = (int)((int64_t)n * blockIdx.x / gridDim.x);
+  hi = (int)((int64_t)n * (blockIdx.x + 1) / gridDim.x);
+}
+
+// ---- warp tensor-core tiles for the fused decode projections ----
+// mma.sync m16n8k16: A (16 x 16, bf16) = 16 weight rows, B (16 x 8, bf16) = 8
+// token rows, D (16 x 8) fp32 += A B.  Lane l holds A rows l/4 and l/4 + 8 and
+// B column l/4, at K positions 2(l%4) + {0, 1} and + 8.  A packed int4 word
+// dequantises most cheaply into the pairs (element i, element i + 4), so every
+// 8-element chunk of K is taken in the order (0,4,1,5,2,6,3,7): lane l%4 = c
+// reads words 2c and 2c + 1 of each 64-wide group (elements 16c .. 16c + 15),
+// and the token rows are staged with each 16-byte chunk pair-interleaved the
+// same way.  Both operands see one permutation of K, so the products and the
+// fp32 sum are those of the natural order up to the order of addition.
+ASTRO_DEVINL void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                 uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// (element i, element i + 4) of a packed word as bf16 s * q + b (i = 0 .. 3)
+ASTRO_DEVINL uint32_t dq_pair(uint32_t v, int i, __nv_bfloat162 s2, __nv_bfloat162 b2) {
+  const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
+  const uint32_t tq = ((v >> (4 * i)) & 0x000f000fu) | 0x43004300u;  // bf16 (128 + q)
+  const __nv_bfloat162 q = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&tq), k128);
+  const __nv_bfloat162 w = __hfma2(q, s2, b2);
+  return *reinterpret_cast<const uint32_t*>(&w);
+}
+
+// 8 natural-order bf16 -> the pairs (0,4) (1,5) (2,6) (3,7)
+ASTRO_DEVINL uint4 pair_interleave(const uint4& v) {
+  return make_uint4(__byte_perm(v.x, v.z, 0x5410), __byte_perm(v.x, v.z, 0x7632),
+                    __byte_perm(v.y, v.w, 0x5410), __byte_perm(v.y, v.w, 0x7632));
+}
+
+ASTRO_DEVINL uint2 ld_stream2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
+// One lane's share of a 16-row tile over KG groups of K: rows r and r + 8
+// (codes words 2c, 2c + 1 of each group; scale | bias << 16 per group).
+template <int KG> struct TileRegs {
+  uint2 qa[KG], qb[KG];
+  uint32_t sa[KG], sb[KG];
+};
+template <int KG>
+ASTRO_DEVINL void load_tile(TileRegs<KG>& R, const AffineRef& W, int64_t e, int64_t r, int K,
+                            int g0, int c) {
+  const int words = K / 8, groups = K / 64;
+  const uint32_t* qa = reinterpret_cast<const uint32_t*>(W.q) + q_row(W, e, r) * words + g0 * 8 + 2 * c;
+  const uint32_t* qb = qa + (int64_t)8 * words;
+  const uint16_t* s = reinterpret_cast<const uint16_t*>(W.s);
+  const uint16_t* b = reinterpret_cast<const uint16_t*>(W.b);
+  const int64_t ra = sb_row(W, e, r) * groups + g0, rb = ra + (int64_t)8 * groups;
+#pragma unroll
+  for (int G = 0; G < KG; ++G) {
+    R.qa[G] = ld_stream2(qa + G * 8);
+    R.qb[G] = ld_stream2(qb + G * 8);
+  }
+#pragma unroll
+  for (int G = 0; G < KG; ++G) {
+    R.sa[G] = (uint32_t)__ldg(s + ra + G) | ((uint32_t)__ldg(b + ra + G) << 16);
+    R.sb[G] = (uint32_t)__ldg(s + rb + G) | ((uint32_t)__ldg(b + rb + G) << 16);
+  }
+}
+
+// D0 (+ D1) += tile x token rows over the tile's KG groups.  x0 / x1: this
+// lane's B rows (pair-interleaved, at the tile's first group + 32 c bytes).
+template <int KG>
+ASTRO_DEVINL void tile_mma(const TileRegs<KG>& R, const uint8_t* x0, const uint8_t* x1, bool two,
+                           float (&d0)[4], float (&d1)[4]) {
+#pragma unroll
+  for (int G = 0; G < KG; ++G) {
+    const __nv_bfloat162 sa = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)R.sa[G]),
+                                                 __ushort_as_bfloat16((uint16_t)R.sa[G]));
+    const __nv_bfloat162 ba = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)(R.sa[G] >> 16)),
+                                                 __ushort_as_bfloat16((uint16_t)(R.sa[G] >> 16)));
+    const __nv_bfloat162 sb = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)R.sb[G]),
+                                                 __ushort_as_bfloat16((uint16_t)R.sb[G]));
+    const __nv_bfloat162 bb = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)(R.sb[G] >> 16)),
+                                                 __ushort_as_bfloat16((uint16_t)(R.sb[G] >> 16)));
+    const uint4 u0 = *reinterpret_cast<const uint4*>(x0 + G * 128);
+    const uint4 u1 = *reinterpret_cast<const uint4*>(x0 + G * 128 + 16);
+    uint4 v0 = u0, v1 = u1;
+    if (two) {
+      v0 = *reinterpret_cast<const uint4*>(x1 + G * 128);
+      v1 = *reinterpret_cast<const uint4*>(x1 + G * 128 + 16);
+    }
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const uint32_t wa = s < 2 ? R.qa[G].x : R.qa[G].y;
+      const uint32_t wb = s < 2 ? R.qb[G].x : R.qb[G].y;
+      const int i0 = 2 * (s & 1);
+      const uint32_t a0 = dq_pair(wa, i0, sa, ba), a2 = dq_pair(wa, i0 + 1, sa, ba);
+      const uint32_t a1 = dq_pair(wb, i0, sb, bb), a3 = dq_pair(wb, i0 + 1, sb, bb);
+      const uint4& xu = s < 2 ? u0 : u1;
+      mma_bf16_16816(d0, a0, a1, a2, a3, (s & 1) ? xu.z : xu.x, (s & 1) ? xu.w : xu.y);
+      if (two) {
+        const uint4& xv = s < 2 ? v0 : v1;
+        mma_bf16_16816(d1, a0, a1, a2, a3, (s & 1) ? xv.z : xv.x, (s & 1) ? xv.w : xv.y);
+      }
+    }
+  }
+}
+
+constexpr int kStageRows = kFusedMaxTokens;  // activation rows staged per down pass
+constexpr int kRedFloats = 4 * 4 * 2 * 4 * 32;
+
+// fp32 partial sums of the four K quarters: [quarter][tile][chunk][reg][lane]
+ASTRO_DEVINL int red_at(int quarter, int tile, int chunk, int reg, int lane) {
+  return (((quarter * 4 + tile) * 2 + chunk) * 4 + reg) * 32 + lane;
+}
+// the quarters' sum, in a fixed order, of output (row r of tile, token column j)
+ASTRO_DEVINL float red_sum(const float* red, int tile, int r, int j) {
+  const int ch = j >> 3, c = j & 7;
+  const int ln = (r & 7) * 4 + (c >> 1), rg = (r >> 3) * 2 + (c & 1);
+  float v = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) v = __fadd_rn(v, red[red_at(q, tile, ch, rg, ln)]);
+  return v;
+}
 
 struct FusedDecodeParams {
   const __nv_bfloat16* x;  // [T, H]
@@ -466,41 +602,37 @@ struct FusedDecodeParams {
   __nv_bfloat16* act;         // [T * K + T, I]
   __nv_bfloat16* yrows;       // [T * K + T, H]
   __nv_bfloat16* out;         // [T, H]
-  uint32_t* barrier;          // {count, generation}; count is zero between launches
+  uint32_t* barrier;          // {arrivals, exits}; both zero between launches
   uint32_t* status;
 };
 
-// Grid-wide barrier for a cooperative launch: the last block to arrive resets
-// the count and advances the generation (release); the others poll the
-// generation with acquire loads and a short back-off.  The wait is bounded
+// Grid-wide barrier number `nth` (1, 2, 3) of a cooperative launch: every block
+// adds one to the arrival word with a release reduction (no round trip) and
+// polls it with acquire loads until nth * gridDim arrivals are in, so the last
+// arrival releases everyone after one trip through L2.  The wait is bounded
 // (2 s): on timeout it records kDevWaitTimeout and returns false, and the
-// caller skips the rest of the kernel.
-ASTRO_DEVINL bool grid_barrier(uint32_t* bar, uint32_t* status, int* flag) {
+// caller skips the rest of the kernel.  grid_exit() zeroes the words again once
+// every block has passed the last barrier.
+ASTRO_DEVINL bool grid_barrier(uint32_t* bar, uint32_t nth, uint32_t* status, int* flag) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    uint32_t gen, old, v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(gen) : "l"(bar + 1) : "memory");
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(bar) : "memory");
+    const uint32_t target = nth * gridDim.x;
+    uint32_t v;
     int ok = 1;
-    if (old == gridDim.x - 1) {
-      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
-      asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar + 1) : "memory");
-    } else {
-      uint64_t t0;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-      uint32_t spins = 0;
-      while (true) {
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar + 1) : "memory");
-        if (v != gen) break;
-        __nanosleep(32);
-        if ((++spins & 255u) == 0) {
-          uint64_t t1;
-          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-          if (t1 - t0 > 2000000000ull) {
-            record_status(status, kDevWaitTimeout);
-            ok = 0;
-            break;
-          }
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(bar) : "memory");
+    uint64_t t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    uint32_t spins = 0;
+    while (true) {
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+      if (v >= target) break;
+      if ((++spins & 255u) == 0) {
+        uint64_t t1;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+        if (t1 - t0 > 2000000000ull) {
+          record_status(status, kDevWaitTimeout);
+          ok = 0;
+          break;
         }
       }
     }
@@ -508,6 +640,20 @@ ASTRO_DEVINL bool grid_barrier(uint32_t* bar, uint32_t* status, int* flag) {
   }
   __syncthreads();
   return *flag != 0;
+}
+
+// After the last barrier: the last block to get here zeroes both words for the
+// next launch (no block polls the arrival word any more).
+ASTRO_DEVINL void grid_exit(uint32_t* bar) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(bar + 1) : "memory");
+    if (old == gridDim.x - 1) {
+      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar) : "memory");
+      asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(bar + 1) : "memory");
+    }
+  }
 }
 
 // prefetch one 128-byte line into L2
@@ -519,13 +665,13 @@ template <int H, int I>
 __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDecodeParams P) {
   constexpr int kVecs = H / 8;            // uint4 per x row
   constexpr int J = H / 256;              // router: uint4 per lane per row
-  constexpr int SGU = H / 1024, SD = I / 512;
-  constexpr int kWordsGU = H / 8, kGroupsGU = H / 64, kWordsD = I / 8, kGroupsD = I / 64;
-  constexpr int kDVecs = I / 8;
+  constexpr int kXpStride = H * 2 + 16, kApStride = I * 2 + 16;  // padded: no bank conflicts
   extern __shared__ uint4 smem[];
-  uint4* xs = smem;                                   // [T][kVecs], swizzled
-  uint4* ys = xs + kFusedMaxTokens * kVecs;           // [kRowChunk][kDVecs], swizzled
-  __nv_bfloat16* s_logits = reinterpret_cast<__nv_bfloat16*>(ys + kRowChunk * kDVecs);  // [T][E]
+  uint4* xs = smem;                                                 // [T][kVecs], swizzled
+  uint8_t* xp = reinterpret_cast<uint8_t*>(xs + kFusedMaxTokens * kVecs);  // [T] pair-interleaved
+  float* red = reinterpret_cast<float*>(xp + kFusedMaxTokens * kXpStride);  // quarter partials
+  uint8_t* ap = reinterpret_cast<uint8_t*>(red + kRedFloats);      // [kStageRows] act rows
+  __nv_bfloat16* s_logits = reinterpret_cast<__nv_bfloat16*>(ap + kStageRows * kApStride);  // [T][E]
   __shared__ uint32_t s_ids[kFusedMaxAssign];
   __shared__ __nv_bfloat16 s_sc16[kFusedMaxAssign];
   __shared__ float s_score[kFusedMaxAssign];
@@ -541,15 +687,30 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
 
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int T = P.T, E = P.E, K = P.K, N = T * K;
-  const int gwarp = blockIdx.x * kGemvWarps + w, nwarps = gridDim.x * kGemvWarps;
+  const int nwarps = gridDim.x * kGemvWarps;
   const int gtid = blockIdx.x * kGemvThreads + threadIdx.x, nthreads = gridDim.x * kGemvThreads;
 
   // ---- phase 1: router logits (+ shared gate logit) ----
   {
+    const int tgroups = (T + kRouterTokens - 1) / kRouterTokens;
+    const int rows = E + (P.has_shared ? 1 : 0);
+    // unit u runs on block u % grid (warp u / grid): the rows are spread over all SMs
+    const int gw_spread = w * gridDim.x + blockIdx.x;
+    uint4 wv[J];
+    auto load_w = [&](int u) {
+      const int r = u / tgroups;
+      const uint4* wrow = reinterpret_cast<const uint4*>(r < E ? P.wr + (int64_t)r * H : P.wg);
+#pragma unroll
+      for (int j = 0; j < J; ++j) wv[j] = ld_stream(wrow + j * 32 + lane);
+    };
+    // the first router row is in flight while x is staged
+    if (gw_spread < rows * tgroups) load_w(gw_spread);
     const uint4* xsrc = reinterpret_cast<const uint4*>(P.x);
     for (int i = threadIdx.x; i < T * kVecs; i += kGemvThreads) {
       const int t = i / kVecs, q = i - t * kVecs;
-      xs[t * kVecs + swz(q)] = ld_cached(xsrc + (int64_t)t * kVecs + q);
+      const uint4 v = ld_cached(xsrc + (int64_t)t * kVecs + q);
+      xs[t * kVecs + swz(q)] = v;
+      *reinterpret_cast<uint4*>(xp + t * kXpStride + q * 16) = pair_interleave(v);
     }
     if (P.has_shared) {
       // the shared expert is always used: start pulling its weights into L2
@@ -570,17 +731,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       }
     }
     __syncthreads();
-    const int tgroups = (T + kRouterTokens - 1) / kRouterTokens;
-    const int rows = E + (P.has_shared ? 1 : 0);
-    // unit u runs on block u % grid (warp u / grid): the rows are spread over all SMs
-    const int gw_spread = w * gridDim.x + blockIdx.x;
     for (int u = gw_spread; u < rows * tgroups; u += nwarps) {
       const int r = u / tgroups, t0 = (u - r * tgroups) * kRouterTokens;
       const int nt = T - t0 < kRouterTokens ? T - t0 : kRouterTokens;
-      const uint4* wrow = reinterpret_cast<const uint4*>(r < E ? P.wr + (int64_t)r * H : P.wg);
-      uint4 wv[J];
-#pragma unroll
-      for (int j = 0; j < J; ++j) wv[j] = ld_stream(wrow + j * 32 + lane);
+      if (u != gw_spread) load_w(u);
       float acc[kRouterTokens];
 #pragma unroll
       for (int t = 0; t < kRouterTokens; ++t) acc[t] = 0.f;
@@ -610,7 +764,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       }
     }
   }
-  if (!grid_barrier(P.barrier, P.status, &s_flag)) return;
+  if (!grid_barrier(P.barrier, 1, P.status, &s_flag)) return;
 
   // ---- phase 2: route + sort, redundantly in every block ----
   for (int i = threadIdx.x; i < T * E; i += kGemvThreads)
@@ -697,25 +851,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   const uint32_t rows_total = s_offs[E + 1];
   {
     // the experts are known: pull this block's gate/up and down weight rows into
-    // L2 now, so the loads of phases 3 and 4 do not each wait a full HBM trip
-    const int per_gu = I / kGemvWarps, per_d = H / (4 * kGemvWarps);
-    const int items_gu = n_act * per_gu, items_d = n_act * per_d;
-    constexpr int kLinesGU = kGemvWarps * (H / 2) / 128;       // 16 rows of packed codes
-    constexpr int kLinesGUs = (kGemvWarps * (H / 64) * 2 + 127) / 128;
-    constexpr int kLinesD = 4 * kGemvWarps * (I / 2) / 128;    // 64 rows of packed codes
-    constexpr int kLinesDs = (4 * kGemvWarps * (I / 64) * 2 + 127) / 128;
-    constexpr int kPerGU = 2 * (kLinesGU + 2 * kLinesGUs), kPerD = kLinesD + 2 * kLinesDs;
-    const int n_gu = (items_gu - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int n_d = (items_d - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    // L2 now, so the loads of phases 3 and 4 do not each wait a full HBM trip.
+    // Gate/up item: 32 consecutive rows of gate and of up; down item: 64 rows.
+    constexpr int kLinesGU = 32 * (H / 2) / 128, kLinesGUs = (32 * (H / 64) * 2 + 127) / 128;
+    constexpr int kLinesD = 64 * (I / 2) / 128, kLinesDs = (64 * (I / 64) * 2 + 127) / 128;
+    constexpr int kMatGU = kLinesGU + 2 * kLinesGUs;
+    constexpr int kPerGU = 2 * kMatGU, kPerD = kLinesD + 2 * kLinesDs;
+    const int per_gu = I / 32, per_d = H / 64;
+    int lo_gu, hi_gu, lo_d, hi_d;
+    block_range(n_act * per_gu, lo_gu, hi_gu);
+    block_range(n_act * per_d, lo_d, hi_d);
+    const int n_gu = hi_gu - lo_gu, n_d = hi_d - lo_d;
     for (int i = threadIdx.x; i < n_gu * kPerGU + n_d * kPerD; i += kGemvThreads) {
       const char* line;
       if (i < n_gu * kPerGU) {
         const int k = i / kPerGU, l = i - k * kPerGU;
-        const int it = (int)blockIdx.x + k * (int)gridDim.x;
+        const int it = lo_gu + k;
         const int seg = s_list[it / per_gu];
-        const int f0 = (it % per_gu) * kGemvWarps;
+        const int f0 = (it % per_gu) * 32;
         const int sh = seg == E ? 1 : 0;
-        const int which = l / (kLinesGU + 2 * kLinesGUs), ll = l - which * (kLinesGU + 2 * kLinesGUs);
+        const int which = l / kMatGU, ll = l - which * kMatGU;
         const AffineRef W = which ? (sh ? P.up[1] : P.up[0]) : (sh ? P.gate[1] : P.gate[0]);
         const int64_t ex = sh ? 0 : (int64_t)seg;
         const int64_t row = q_row(W, ex, f0), srow = sb_row(W, ex, f0);
@@ -729,9 +884,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       } else {
         const int i2 = i - n_gu * kPerGU;
         const int k = i2 / kPerD, l = i2 - k * kPerD;
-        const int it = (int)blockIdx.x + k * (int)gridDim.x;
+        const int it = lo_d + k;
         const int seg = s_list[it / per_d];
-        const int r0 = (it % per_d) * 4 * kGemvWarps;
+        const int r0 = (it % per_d) * 64;
         const int sh = seg == E ? 1 : 0;
         const AffineRef W = sh ? P.down[1] : P.down[0];
         const int64_t ex = sh ? 0 : (int64_t)seg;
@@ -749,118 +904,112 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   }
 
   // ---- phase 3: gate/up + SwiGLU ----
+  // Item = (active segment, 32 features): their 32 gate and 32 up rows against
+  // every token row of the segment.  Warp w takes tile w & 3 (gate rows of
+  // features 0-15, 16-31, then up rows of the same) over K quarter w >> 2 on
+  // warp tensor-core tiles; the quarters' partials are added in shared memory.
   {
-    const int per_seg = I / kGemvWarps;
-    const int items = n_act * per_seg;
-    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    constexpr int kGQ = H / 256;  // 64-wide groups per K quarter
+    const int g8 = lane >> 2, c4 = lane & 3;
+    const int tile = w & 3, quarter = w >> 2;
+    const int per_seg = I / 32;
+    int lo, hi;
+    block_range(n_act * per_seg, lo, hi);
+    for (int it = lo; it < hi; ++it) {
       const int seg = s_list[it / per_seg];
-      const int f = (it % per_seg) * kGemvWarps + w;
+      const int fi = (it % per_seg) * 32;
       const int sh = seg == E ? 1 : 0;
-      const AffineRef A = sh ? P.gate[1] : P.gate[0];
-      const AffineRef B = sh ? P.up[1] : P.up[0];
-      const int64_t e = sh ? 0 : seg;
-      RowRegs<SGU> ga, ua;
-      load_row<SGU>(ga, A, e, f, kWordsGU, kGroupsGU, lane * 4, lane / 2, 128, 16);
-      load_row<SGU>(ua, B, e, f, kWordsGU, kGroupsGU, lane * 4, lane / 2, 128, 16);
+      const AffineRef W = tile < 2 ? (sh ? P.gate[1] : P.gate[0]) : (sh ? P.up[1] : P.up[0]);
+      TileRegs<kGQ> R;
+      load_tile<kGQ>(R, W, sh ? 0 : seg, fi + (tile & 1) * 16 + g8, H, quarter * kGQ, c4);
       const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
-      for (uint32_t p = p0; p < p1; p += kRowChunkGU) {
-        const int n = (int)(p1 - p < (uint32_t)kRowChunkGU ? p1 - p : (uint32_t)kRowChunkGU);
-        float g[kRowChunkGU], u[kRowChunkGU];
+      for (uint32_t pb = p0; pb < p1; pb += 16) {
+        const int n = (int)(p1 - pb < 16u ? p1 - pb : 16u);
+        // B column g8 of chunk 0 / 1: sorted rows pb + g8 / pb + 8 + g8 (a valid
+        // row stands in past n; its columns are not stored)
+        const int j0 = g8 < n ? g8 : 0, j1 = g8 + 8 < n ? g8 + 8 : 0;
+        const int off = quarter * kGQ * 128 + c4 * 32;
+        const uint8_t* x0 = xp + (int)s_stok[pb + j0] * kXpStride + off;
+        const uint8_t* x1 = xp + (int)s_stok[pb + j1] * kXpStride + off;
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        tile_mma<kGQ>(R, x0, x1, n > 8, d0, d1);
+        __syncthreads();  // the previous epilogue is done with red
 #pragma unroll
-        for (int j = 0; j < kRowChunkGU; ++j) g[j] = u[j] = 0.f;
-#pragma unroll
-        for (int st = 0; st < SGU; ++st) {
-          uint32_t wg[16], wu[16];
-          dequant32(ga.q[st], (uint16_t)ga.sb[st], (uint16_t)(ga.sb[st] >> 16), wg);
-          dequant32(ua.q[st], (uint16_t)ua.sb[st], (uint16_t)(ua.sb[st] >> 16), wu);
-#pragma unroll
-          for (int j = 0; j < kRowChunkGU; ++j) {
-            if (j < n) {
-              const int t = (int)s_stok[p + j];
-#pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                float xf[8];
-                bf16x8_to_f32(xs[t * kVecs + swz(st * 128 + lane * 4 + c)], xf);
-                g[j] = dot8(wg, c, xf, g[j]);
-                u[j] = dot8(wu, c, xf, u[j]);
-              }
-            }
-          }
+        for (int r = 0; r < 4; ++r) {
+          red[red_at(quarter, tile, 0, r, lane)] = d0[r];
+          red[red_at(quarter, tile, 1, r, lane)] = d1[r];
         }
-#pragma unroll
-        for (int j = 0; j < kRowChunkGU; ++j) {
-          if (j < n) {
-            const float gs = warp_sum(g[j]), us = warp_sum(u[j]);
-            if (lane == 0)
-              P.act[(int64_t)(p + j) * I + f] =
-                  __float2bfloat16_rn(swiglu_bf16(round_bf16(gs), round_bf16(us)));
-          }
+        __syncthreads();
+        const int fl = threadIdx.x & 31, j = threadIdx.x >> 5;  // 32 features x 16 rows
+        if (j < n) {
+          const float g = red_sum(red, fl >> 4, fl & 15, j);
+          const float u = red_sum(red, 2 + (fl >> 4), fl & 15, j);
+          P.act[(int64_t)(pb + j) * I + fi + fl] =
+              __float2bfloat16_rn(swiglu_bf16(round_bf16(g), round_bf16(u)));
         }
       }
     }
   }
-  if (!grid_barrier(P.barrier, P.status, &s_flag)) return;
+  if (!grid_barrier(P.barrier, 2, P.status, &s_flag)) return;
 
   // ---- phase 4: down ----
+  // Item = (active segment, 64 output rows); warp w: tile w & 3 (16 rows) over K
+  // quarter w >> 2 of the intermediate width.  B = the segment's activation
+  // rows, staged (pair-interleaved) once for all of the block's items on it.
   {
-    const int half = lane >> 4, li = lane & 15;
-    constexpr int kRowsPerHalf = 2;
-    constexpr int kRowsPerItem = 2 * kRowsPerHalf * kGemvWarps;  // 64
-    const int per_seg = H / kRowsPerItem;
-    const int items = n_act * per_seg;
+    constexpr int kGQ = I / 256;
+    constexpr int kAVecs = I / 8;
+    const int g8 = lane >> 2, c4 = lane & 3;
+    const int tile = w & 3, quarter = w >> 2;
+    const int per_seg = H / 64;
+    int lo, hi;
+    block_range(n_act * per_seg, lo, hi);
     const uint4* asrc = reinterpret_cast<const uint4*>(P.act);
-    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    int staged_seg = -1;  // segment whose rows from staged_p sit in ap
+    uint32_t staged_p = 0;
+    for (int it = lo; it < hi; ++it) {
       const int seg = s_list[it / per_seg];
-      const int r0 = (it % per_seg) * kRowsPerItem + w * 2 * kRowsPerHalf + half * kRowsPerHalf;
+      const int r0 = (it % per_seg) * 64;
       const int sh = seg == E ? 1 : 0;
-      const AffineRef A = sh ? P.down[1] : P.down[0];
-      const int64_t e = sh ? 0 : seg;
-      RowRegs<SD> rr[kRowsPerHalf];
-#pragma unroll
-      for (int r = 0; r < kRowsPerHalf; ++r)
-        load_row<SD>(rr[r], A, e, r0 + r, kWordsD, kGroupsD, li * 4, li / 2, 64, 8);
+      const AffineRef W = sh ? P.down[1] : P.down[0];
+      TileRegs<kGQ> R;
+      load_tile<kGQ>(R, W, sh ? 0 : seg, r0 + tile * 16 + g8, I, quarter * kGQ, c4);
       const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
-      for (uint32_t p = p0; p < p1; p += kRowChunk) {
-        const int n = (int)(p1 - p < (uint32_t)kRowChunk ? p1 - p : (uint32_t)kRowChunk);
-        __syncthreads();
-        for (int i = threadIdx.x; i < n * kDVecs; i += kGemvThreads) {
-          const int j = i / kDVecs, q = i - j * kDVecs;
-          ys[j * kDVecs + swz(q)] = __ldcg(asrc + (int64_t)(p + j) * kDVecs + q);
+      for (uint32_t pb = p0; pb < p1; pb += kStageRows) {
+        const int n = (int)(p1 - pb < (uint32_t)kStageRows ? p1 - pb : (uint32_t)kStageRows);
+        __syncthreads();  // the previous epilogue is done with red (and ap)
+        if (seg != staged_seg || pb != staged_p) {
+          for (int i = threadIdx.x; i < n * kAVecs; i += kGemvThreads) {
+            const int j = i / kAVecs, q = i - j * kAVecs;
+            *reinterpret_cast<uint4*>(ap + j * kApStride + q * 16) =
+                pair_interleave(__ldcg(asrc + (int64_t)(pb + j) * kAVecs + q));
+          }
+          staged_seg = seg;
+          staged_p = pb;
+          __syncthreads();
+        }
+        const int j0 = g8 < n ? g8 : 0, j1 = g8 + 8 < n ? g8 + 8 : 0;
+        const int off = quarter * kGQ * 128 + c4 * 32;
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        tile_mma<kGQ>(R, ap + j0 * kApStride + off, ap + j1 * kApStride + off, n > 8, d0, d1);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          red[red_at(quarter, tile, 0, r, lane)] = d0[r];
+          red[red_at(quarter, tile, 1, r, lane)] = d1[r];
         }
         __syncthreads();
+        const int rl = threadIdx.x & 63, jb = threadIdx.x >> 6;  // 64 rows x 8 (+8) tokens
 #pragma unroll
-        for (int r = 0; r < kRowsPerHalf; ++r) {
-          float a[kRowChunk];
-#pragma unroll
-          for (int j = 0; j < kRowChunk; ++j) a[j] = 0.f;
-#pragma unroll
-          for (int st = 0; st < SD; ++st) {
-            uint32_t wd[16];
-            dequant32(rr[r].q[st], (uint16_t)rr[r].sb[st], (uint16_t)(rr[r].sb[st] >> 16), wd);
-#pragma unroll
-            for (int j = 0; j < kRowChunk; ++j) {
-              if (j < n) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                  float xf[8];
-                  bf16x8_to_f32(ys[j * kDVecs + swz(st * 64 + li * 4 + c)], xf);
-                  a[j] = dot8(wd, c, xf, a[j]);
-                }
-              }
-            }
-          }
-#pragma unroll
-          for (int j = 0; j < kRowChunk; ++j) {
-            if (j < n) {
-              const float v = half_warp_sum(a[j]);
-              if (li == 0) P.yrows[(int64_t)(p + j) * H + r0 + r] = __float2bfloat16_rn(v);
-            }
-          }
+        for (int h = 0; h < 2; ++h) {
+          const int j = jb + 8 * h;
+          if (j < n)
+            P.yrows[(int64_t)(pb + j) * H + r0 + rl] =
+                __float2bfloat16_rn(red_sum(red, rl >> 4, rl & 15, j));
         }
       }
     }
   }
-  if (!grid_barrier(P.barrier, P.status, &s_flag)) return;
+  if (!grid_barrier(P.barrier, 3, P.status, &s_flag)) return;
 
   // ---- phase 5: weighted combine + gated shared expert ----
   {
@@ -873,6 +1022,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
     }
   }
   (void)rows_total;
+  grid_exit(P.barrier);
 }
 
 }  // namespace
@@ -956,7 +1106,8 @@ namespace {
 template <int H, int I>
 cudaError_t launch_fused_t(const FusedDecodeParams& p, cudaStream_t st) {
   auto kern = decode_fused_kernel<H, I>;
-  const size_t smem = (size_t)(kFusedMaxTokens * (H / 8) + kRowChunk * (I / 8)) * 16 +
+  const size_t smem = (size_t)kFusedMaxTokens * (H * 2) + (size_t)kFusedMaxTokens * (H * 2 + 16) +
+                      (size_t)kRedFloats * 4 + (size_t)kStageRows * (I * 2 + 16) +
                       (size_t)kFusedMaxTokens * kFusedMaxExperts * 2;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
