@@ -102,6 +102,7 @@ struct LayerState {
   bool registered = false;
   astro::MoeGemmPlan gemm{};  // tensor-core plan (TMA descriptors), when eligible
   bool decode_ok = false;     // the small-batch GEMVs cover this layer's geometry
+  bool fused_ok = false;      // ... and scale / bias rows suit the fused decode kernel's vector loads
   bool router_gemv_ok = false;
   // expert-parallel layer: w.experts counts the local stacks, ep_total all experts
   bool ep = false;
@@ -355,7 +356,10 @@ int copy_taps(astro_moe_ctx* ctx, const BlockWorkspace& b, int64_t T, int E, int
 // experts per rank a count mailbox holds
 constexpr int kMailboxExperts = 1024;
 
-// batches up to this many tokens take the decode GEMVs unless the options say otherwise
+// batches up to this many tokens take the decode path unless the options say
+// otherwise: the fused decode kernel where its shapes apply, else the separate
+// decode GEMVs
+constexpr int64_t kDefaultFusedTokens = 16;
 constexpr int64_t kDefaultDecodeTokens = 8;
 // batches up to this many tokens compute router logits with the router GEMV
 constexpr int64_t kRouterGemvTokens = 64;
@@ -381,17 +385,19 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   marks.mark();
   // a1: router projection
   const bool x_aligned = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
-  const int64_t decode_max = ctx->opt.decode_max_tokens == 0 ? kDefaultDecodeTokens
-                                                             : ctx->opt.decode_max_tokens;
+  const bool fused_shape = ctx->opt.decode_fused >= 0 && L.fused_ok &&
+                           astro::decode_fused_supported((int)T, H, E, K, I) &&
+                           w.shared_intermediate == (has_shared ? I : 0);
+  const int64_t decode_max =
+      ctx->opt.decode_max_tokens != 0 ? ctx->opt.decode_max_tokens
+                                      : (fused_shape ? kDefaultFusedTokens : kDefaultDecodeTokens);
   // small batches: GEMVs over the active experts (HBM-bound); otherwise the
   // tcgen05 grouped GEMMs, or the CUDA-core grouped GEMV when those are off
   const bool use_decode = decode_max > 0 && T <= decode_max && x_aligned && L.decode_ok;
   const bool use_tc = !use_decode && astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores) &&
                       x_aligned;
   const bool router_gemv = T <= kRouterGemvTokens && x_aligned && L.router_gemv_ok;
-  const bool try_fused = use_decode && ctx->opt.decode_fused >= 0 &&
-                         astro::decode_fused_supported((int)T, H, E, K, I) &&
-                         w.shared_intermediate == (has_shared ? I : 0);
+  const bool try_fused = use_decode && fused_shape;
   if (try_fused) {
     astro::DecodeFusedArgs a;
     a.x = x;
@@ -1137,6 +1143,16 @@ int astro_moe_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_moe_
   L.decode_ok = weights_aligned &&
                 astro::decode_gemv_supported(w->hidden, w->intermediate, w->group_size, w->bits);
   L.router_gemv_ok = aligned16(w->router_weight) && astro::router_gemv_supported(w->hidden);
+  // the fused decode kernel reads each row's scales and biases of a K quarter as
+  // one vector of up to 16 bytes
+  bool sb_aligned = aligned16(w->gate.scales) && aligned16(w->gate.biases) &&
+                    aligned16(w->down.scales) && aligned16(w->down.biases) &&
+                    (w->gate_up_fused || (aligned16(w->up.scales) && aligned16(w->up.biases)));
+  if (w->shared_intermediate > 0)
+    sb_aligned = sb_aligned && aligned16(w->shared_gate.scales) && aligned16(w->shared_gate.biases) &&
+                 aligned16(w->shared_up.scales) && aligned16(w->shared_up.biases) &&
+                 aligned16(w->shared_down.scales) && aligned16(w->shared_down.biases);
+  L.fused_ok = L.decode_ok && sb_aligned;
   return ASTRO_MOE_OK;
 }
 
@@ -1247,6 +1263,7 @@ int astro_moe_ep_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_m
   L.ep_total = w->experts;
   L.registered = true;
   L.decode_ok = false;
+  L.fused_ok = false;
   if (int st = astro::moe_gemm_plan(local, &L.gemm, w->experts)) {
     L.registered = false;
     return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);

@@ -477,12 +477,35 @@ ASTRO_DEVINL uint2 ld_stream2(const void* p) {
   return v;
 }
 
+// KG consecutive bf16 (a row's scales or biases over the tile's groups) in
+// (KG + 1) / 2 words, loaded as one vector; nothing waits on it until use.
+template <int KG> struct Bf16Vec {
+  uint32_t w[(KG + 1) / 2];
+  ASTRO_DEVINL void load(const uint16_t* p) {
+    if constexpr (KG == 8) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(p));
+      w[0] = v.x; w[1] = v.y; w[2] = v.z; w[3] = v.w;
+    } else if constexpr (KG == 4) {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+      w[0] = v.x; w[1] = v.y;
+    } else {
+      static_assert(KG == 2, "2, 4 or 8 groups per K quarter");
+      w[0] = __ldg(reinterpret_cast<const unsigned int*>(p));
+    }
+  }
+  ASTRO_DEVINL __nv_bfloat162 pair(int G) const {  // value G in both halves
+    const uint16_t h = (uint16_t)(w[G >> 1] >> (16 * (G & 1)));
+    return __halves2bfloat162(__ushort_as_bfloat16(h), __ushort_as_bfloat16(h));
+  }
+};
+
 // One lane's share of a 16-row tile over KG groups of K: rows r and r + 8
-// (codes words 2c, 2c + 1 of each group; scale | bias << 16 per group).
+// (codes: words 2c, 2c + 1 of each group; the groups' scales and biases).
 template <int KG> struct TileRegs {
   uint2 qa[KG], qb[KG];
-  uint32_t sa[KG], sb[KG];
+  Bf16Vec<KG> sa, ba, sb, bb;
 };
+// Issues the tile's loads (the scale and bias rows must be 2*KG-byte aligned).
 template <int KG>
 ASTRO_DEVINL void load_tile(TileRegs<KG>& R, const AffineRef& W, int64_t e, int64_t r, int K,
                             int g0, int c) {
@@ -497,11 +520,10 @@ ASTRO_DEVINL void load_tile(TileRegs<KG>& R, const AffineRef& W, int64_t e, int6
     R.qa[G] = ld_stream2(qa + G * 8);
     R.qb[G] = ld_stream2(qb + G * 8);
   }
-#pragma unroll
-  for (int G = 0; G < KG; ++G) {
-    R.sa[G] = (uint32_t)__ldg(s + ra + G) | ((uint32_t)__ldg(b + ra + G) << 16);
-    R.sb[G] = (uint32_t)__ldg(s + rb + G) | ((uint32_t)__ldg(b + rb + G) << 16);
-  }
+  R.sa.load(s + ra);
+  R.ba.load(b + ra);
+  R.sb.load(s + rb);
+  R.bb.load(b + rb);
 }
 
 // D0 (+ D1) += tile x token rows over the tile's KG groups.  x0 / x1: this
@@ -511,14 +533,8 @@ ASTRO_DEVINL void tile_mma(const TileRegs<KG>& R, const uint8_t* x0, const uint8
                            float (&d0)[4], float (&d1)[4]) {
 #pragma unroll
   for (int G = 0; G < KG; ++G) {
-    const __nv_bfloat162 sa = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)R.sa[G]),
-                                                 __ushort_as_bfloat16((uint16_t)R.sa[G]));
-    const __nv_bfloat162 ba = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)(R.sa[G] >> 16)),
-                                                 __ushort_as_bfloat16((uint16_t)(R.sa[G] >> 16)));
-    const __nv_bfloat162 sb = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)R.sb[G]),
-                                                 __ushort_as_bfloat16((uint16_t)R.sb[G]));
-    const __nv_bfloat162 bb = __halves2bfloat162(__ushort_as_bfloat16((uint16_t)(R.sb[G] >> 16)),
-                                                 __ushort_as_bfloat16((uint16_t)(R.sb[G] >> 16)));
+    const __nv_bfloat162 sa = R.sa.pair(G), ba = R.ba.pair(G);
+    const __nv_bfloat162 sb = R.sb.pair(G), bb = R.bb.pair(G);
     const uint4 u0 = *reinterpret_cast<const uint4*>(x0 + G * 128);
     const uint4 u1 = *reinterpret_cast<const uint4*>(x0 + G * 128 + 16);
     uint4 v0 = u0, v1 = u1;
@@ -656,15 +672,24 @@ ASTRO_DEVINL void grid_exit(uint32_t* bar) {
   }
 }
 
-// prefetch one 128-byte line into L2
-ASTRO_DEVINL void prefetch_l2(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+// one bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a
+// multiple of 16; callers keep pieces at or below 32 KB)
+ASTRO_DEVINL void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// the grid's share of [p, p + bytes): 16 KB pieces, block b taking pieces b,
+// b + grid, ... (issued by the calling thread)
+ASTRO_DEVINL void prefetch_l2_grid(const void* p, int64_t bytes) {
+  constexpr int64_t kPiece = 16384;
+  const char* c = reinterpret_cast<const char*>(p);
+  for (int64_t off = (int64_t)blockIdx.x * kPiece; off < bytes; off += (int64_t)gridDim.x * kPiece)
+    prefetch_l2_bulk(c + off, (uint32_t)(bytes - off < kPiece ? bytes - off : kPiece));
 }
 
 template <int H, int I>
 __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDecodeParams P) {
   constexpr int kVecs = H / 8;            // uint4 per x row
-  constexpr int J = H / 256;              // router: uint4 per lane per row
   constexpr int kXpStride = H * 2 + 16, kApStride = I * 2 + 16;  // padded: no bank conflicts
   extern __shared__ uint4 smem[];
   uint4* xs = smem;                                                 // [T][kVecs], swizzled
@@ -677,34 +702,34 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   __shared__ float s_score[kFusedMaxAssign];
   __shared__ uint32_t s_inv[kFusedMaxAssign];
   __shared__ uint32_t s_stok[kFusedMaxAssign + kFusedMaxTokens];
-  __shared__ int s_cnt[kFusedMaxExperts + 1];
+  __shared__ uint8_t s_wcnt[kFusedMaxAssign / 32][kFusedMaxExperts];  // ids per warp of assignments
   __shared__ uint32_t s_offs[kFusedMaxExperts + 2];
   __shared__ uint16_t s_list[kFusedMaxExperts + 1];
   __shared__ float s_sg[kFusedMaxTokens];
-  __shared__ int s_warp[kGemvWarps];
   __shared__ int s_flag;
   __shared__ int s_nact;
 
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int T = P.T, E = P.E, K = P.K, N = T * K;
-  const int nwarps = gridDim.x * kGemvWarps;
   const int gtid = blockIdx.x * kGemvThreads + threadIdx.x, nthreads = gridDim.x * kGemvThreads;
 
   // ---- phase 1: router logits (+ shared gate logit) ----
+  // Block b computes router rows b, b + grid, ...: two rows per pass, each split
+  // into eight K slices of H / 8 (warp w: row w >> 3 of the pass, slice w & 7);
+  // a warp's slice sums go through shared memory and the eight slices are added
+  // in order.  Each warp's weight vector is requested before x is staged.
   {
-    const int tgroups = (T + kRouterTokens - 1) / kRouterTokens;
+    constexpr int kSliceVecs = kVecs / 8;  // uint4 per slice: 32 (H = 2048) or 16
     const int rows = E + (P.has_shared ? 1 : 0);
-    // unit u runs on block u % grid (warp u / grid): the rows are spread over all SMs
-    const int gw_spread = w * gridDim.x + blockIdx.x;
-    uint4 wv[J];
-    auto load_w = [&](int u) {
-      const int r = u / tgroups;
-      const uint4* wrow = reinterpret_cast<const uint4*>(r < E ? P.wr + (int64_t)r * H : P.wg);
-#pragma unroll
-      for (int j = 0; j < J; ++j) wv[j] = ld_stream(wrow + j * 32 + lane);
+    const int rs = w >> 3, sl = w & 7;
+    const bool vlane = lane < kSliceVecs;
+    auto row_ptr = [&](int r) {
+      return reinterpret_cast<const uint4*>(r < E ? P.wr + (int64_t)r * H : P.wg) + sl * kSliceVecs +
+             lane;
     };
-    // the first router row is in flight while x is staged
-    if (gw_spread < rows * tgroups) load_w(gw_spread);
+    int r = (int)blockIdx.x + rs * (int)gridDim.x;
+    uint4 wv = make_uint4(0u, 0u, 0u, 0u);
+    if (r < rows && vlane) wv = ld_stream(row_ptr(r));
     const uint4* xsrc = reinterpret_cast<const uint4*>(P.x);
     for (int i = threadIdx.x; i < T * kVecs; i += kGemvThreads) {
       const int t = i / kVecs, q = i - t * kVecs;
@@ -712,54 +737,58 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       xs[t * kVecs + swz(q)] = v;
       *reinterpret_cast<uint4*>(xp + t * kXpStride + q * 16) = pair_interleave(v);
     }
-    if (P.has_shared) {
+    if (P.has_shared && threadIdx.x == 0) {
       // the shared expert is always used: start pulling its weights into L2
-      const AffineRef* sw[3] = {&P.gate[1], &P.up[1], &P.down[1]};
+      const AffineRef sw[3] = {P.gate[1], P.up[1], P.down[1]};
       const int64_t qbytes[3] = {(int64_t)I * H / 2, (int64_t)I * H / 2, (int64_t)H * I / 2};
       const int64_t sbytes[3] = {(int64_t)I * (H / 64) * 2, (int64_t)I * (H / 64) * 2,
                                  (int64_t)H * (I / 64) * 2};
 #pragma unroll
       for (int m = 0; m < 3; ++m) {
-        const char* q = reinterpret_cast<const char*>(sw[m]->q);
-        for (int64_t l = gtid; l * 128 < qbytes[m]; l += nthreads) prefetch_l2(q + l * 128);
-        const char* sc = reinterpret_cast<const char*>(sw[m]->s);
-        const char* bi = reinterpret_cast<const char*>(sw[m]->b);
-        for (int64_t l = gtid; l * 128 < sbytes[m]; l += nthreads) {
-          prefetch_l2(sc + l * 128);
-          prefetch_l2(bi + l * 128);
-        }
+        prefetch_l2_grid(sw[m].q, qbytes[m]);
+        prefetch_l2_grid(sw[m].s, sbytes[m]);
+        prefetch_l2_grid(sw[m].b, sbytes[m]);
       }
     }
-    __syncthreads();
-    for (int u = gw_spread; u < rows * tgroups; u += nwarps) {
-      const int r = u / tgroups, t0 = (u - r * tgroups) * kRouterTokens;
-      const int nt = T - t0 < kRouterTokens ? T - t0 : kRouterTokens;
-      if (u != gw_spread) load_w(u);
-      float acc[kRouterTokens];
-#pragma unroll
-      for (int t = 0; t < kRouterTokens; ++t) acc[t] = 0.f;
-#pragma unroll
-      for (int j = 0; j < J; ++j) {
+    float* s_part = red;  // [2 rows][8 slices][kFusedMaxTokens]
+    for (int pass = 0; pass * 2 * (int)gridDim.x < rows; ++pass) {
+      if (pass > 0) {
+        r = (int)blockIdx.x + (2 * pass + rs) * (int)gridDim.x;
+        if (r < rows && vlane) wv = ld_stream(row_ptr(r));
+      }
+      __syncthreads();  // x staged; the previous pass is done with s_part
+      if (r < rows) {
         float wf[8];
-        bf16x8_to_f32(wv[j], wf);
+        bf16x8_to_f32(wv, wf);
+        float acc[kFusedMaxTokens];
 #pragma unroll
-        for (int t = 0; t < kRouterTokens; ++t) {
-          if (t < nt) {
+        for (int t = 0; t < kFusedMaxTokens; ++t) {
+          acc[t] = 0.f;
+          if (t < T && vlane) {
             float xf[8];
-            bf16x8_to_f32(xs[(t0 + t) * kVecs + swz(j * 32 + lane)], xf);
+            bf16x8_to_f32(xs[t * kVecs + swz(sl * kSliceVecs + lane)], xf);
 #pragma unroll
             for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(wf[i], xf[i], acc[t]);
           }
         }
-      }
 #pragma unroll
-      for (int t = 0; t < kRouterTokens; ++t) {
-        if (t < nt) {
-          const float v = warp_sum(acc[t]);
-          if (lane == 0) {
-            if (r < E) P.logits[(int64_t)(t0 + t) * E + r] = __float2bfloat16_rn(v);
-            else P.gate_logit[t0 + t] = __float2bfloat16_rn(v);
+        for (int t = 0; t < kFusedMaxTokens; ++t) {
+          if (t < T) {
+            const float v = warp_sum(acc[t]);
+            if (lane == 0) s_part[(rs * 8 + sl) * kFusedMaxTokens + t] = v;
           }
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x < 2 * T) {
+        const int k = threadIdx.x / T, t = threadIdx.x - k * T;
+        const int rr = (int)blockIdx.x + (2 * pass + k) * (int)gridDim.x;
+        if (rr < rows) {
+          float v = 0.f;
+#pragma unroll
+          for (int s = 0; s < 8; ++s) v = __fadd_rn(v, s_part[(k * 8 + s) * kFusedMaxTokens + t]);
+          if (rr < E) P.logits[(int64_t)t * E + rr] = __float2bfloat16_rn(v);
+          else P.gate_logit[t] = __float2bfloat16_rn(v);
         }
       }
     }
@@ -769,7 +798,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   // ---- phase 2: route + sort, redundantly in every block ----
   for (int i = threadIdx.x; i < T * E; i += kGemvThreads)
     s_logits[i] = __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(P.logits) + i));
-  for (int e = threadIdx.x; e <= E; e += kGemvThreads) s_cnt[e] = 0;
+  const int nw_assign = (N + 31) >> 5;  // warps holding assignments
+  for (int i = threadIdx.x; i < nw_assign * kFusedMaxExperts / 4; i += kGemvThreads)
+    reinterpret_cast<uint32_t*>(&s_wcnt[0][0])[i] = 0u;
   if (threadIdx.x < T)
     s_sg[threadIdx.x] =
         P.has_shared
@@ -778,46 +809,73 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   __syncthreads();
   if (w < T) route_token<__nv_bfloat16, 8>(s_logits + w * E, E, K, P.normalize, s_ids + w * K, s_sc16 + w * K);
   __syncthreads();
+  // stable counting sort of the N assignments by expert: the rank of an
+  // assignment among equal ids is its rank inside its warp (match_any) plus the
+  // count of that id in earlier warps (per-warp counts, no atomics)
   int rank = 0;
   uint32_t my_id = 0xffffffffu;
-  if (threadIdx.x < N) {
-    s_inv[threadIdx.x] = 0;  // an id >= E keeps slot row 0 (recorded, never used for output)
-    my_id = s_ids[threadIdx.x];
-    s_score[threadIdx.x] = __bfloat162float(s_sc16[threadIdx.x]);
-    if (my_id < (uint32_t)E) {
-      for (int j = 0; j < (int)threadIdx.x; ++j) rank += s_ids[j] == my_id ? 1 : 0;
-      atomicAdd(&s_cnt[my_id], 1);
-    } else {
-      record_status(P.status, kDevBadExpertId);
+  if (w < nw_assign) {
+    if (threadIdx.x < N) {
+      s_inv[threadIdx.x] = 0;  // an id >= E keeps slot row 0 (recorded, never used for output)
+      my_id = s_ids[threadIdx.x];
+      s_score[threadIdx.x] = __bfloat162float(s_sc16[threadIdx.x]);
+      if (my_id >= (uint32_t)E) record_status(P.status, kDevBadExpertId);
+      if (blockIdx.x == 0) {
+        P.ids[threadIdx.x] = my_id;
+        P.scores[threadIdx.x] = s_sc16[threadIdx.x];
+      }
     }
-    if (blockIdx.x == 0) {
-      P.ids[threadIdx.x] = my_id;
-      P.scores[threadIdx.x] = s_sc16[threadIdx.x];
-    }
+    const uint32_t m = __match_any_sync(0xffffffffu, my_id);
+    rank = __popc(m & lanemask_lt());
+    if (my_id < (uint32_t)E && rank == 0) s_wcnt[w][my_id] = (uint8_t)__popc(m);
   }
   __syncthreads();
+  if (my_id < (uint32_t)E)
+    for (int v = 0; v < w; ++v) rank += s_wcnt[v][my_id];
   if (w == 0) {
-    // exclusive scan of the E counts: lane l owns experts [l*C, l*C + C)
+    // exclusive scans of the E counts and of the non-empty experts: lane l owns
+    // experts [l*C, l*C + C); the active list follows expert order, then the
+    // shared expert
+    constexpr int kCMax = kFusedMaxExperts / 32;
     const int C = (E + 31) / 32;
-    int part = 0;
-    for (int i = 0; i < C; ++i) part += (lane * C + i < E) ? s_cnt[lane * C + i] : 0;
-    int incl = part;
+    int cnt[kCMax];
+    int part = 0, npart = 0;
 #pragma unroll
-    for (int m = 1; m < 32; m <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, m);
-      if (lane >= m) incl += o;
-    }
-    int run = incl - part;
-    for (int i = 0; i < C; ++i) {
+    for (int i = 0; i < kCMax; ++i) {
       const int e = lane * C + i;
-      if (e < E) {
+      int c = 0;
+      if (i < C && e < E)
+        for (int v = 0; v < nw_assign; ++v) c += s_wcnt[v][e];
+      cnt[i] = c;
+      part += c;
+      npart += c > 0 ? 1 : 0;
+    }
+    int incl = part, nincl = npart;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      const int no = __shfl_up_sync(0xffffffffu, nincl, d);
+      if (lane >= d) {
+        incl += o;
+        nincl += no;
+      }
+    }
+    int run = incl - part, nrun = nincl - npart;
+#pragma unroll
+    for (int i = 0; i < kCMax; ++i) {
+      const int e = lane * C + i;
+      if (i < C && e < E) {
         s_offs[e] = (uint32_t)run;
-        run += s_cnt[e];
+        run += cnt[i];
+        if (cnt[i] > 0) s_list[nrun++] = (uint16_t)e;
       }
     }
     if (lane == 31) {
       s_offs[E] = (uint32_t)incl;
       s_offs[E + 1] = (uint32_t)(incl + (P.has_shared ? T : 0));
+      int na = nincl;
+      if (P.has_shared && T > 0) s_list[na++] = (uint16_t)E;
+      s_nact = na;
     }
   }
   __syncthreads();
@@ -830,150 +888,128 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   if (blockIdx.x == 0)
     for (int e = threadIdx.x; e < E + 2; e += kGemvThreads) P.offsets[e] = s_offs[e];
   __syncthreads();
-  {
-    const int nseg = E + (P.has_shared ? 1 : 0);
-    const int s = threadIdx.x;
-    const bool ne = s < nseg && s_offs[s + 1] > s_offs[s];
-    const uint32_t bal = __ballot_sync(0xffffffffu, ne);
-    if (lane == 0) s_warp[w] = __popc(bal);
-    __syncthreads();
-    int before = 0, total = 0;
-#pragma unroll
-    for (int i = 0; i < kGemvWarps; ++i) {
-      before += i < w ? s_warp[i] : 0;
-      total += s_warp[i];
-    }
-    if (ne) s_list[before + __popc(bal & lanemask_lt())] = (uint16_t)s;
-    if (threadIdx.x == 0) s_nact = total;
-    __syncthreads();
-  }
   const int n_act = s_nact;
-  const uint32_t rows_total = s_offs[E + 1];
-  {
-    // the experts are known: pull this block's gate/up and down weight rows into
-    // L2 now, so the loads of phases 3 and 4 do not each wait a full HBM trip.
-    // Gate/up item: 32 consecutive rows of gate and of up; down item: 64 rows.
-    constexpr int kLinesGU = 32 * (H / 2) / 128, kLinesGUs = (32 * (H / 64) * 2 + 127) / 128;
-    constexpr int kLinesD = 64 * (I / 2) / 128, kLinesDs = (64 * (I / 64) * 2 + 127) / 128;
-    constexpr int kMatGU = kLinesGU + 2 * kLinesGUs;
-    constexpr int kPerGU = 2 * kMatGU, kPerD = kLinesD + 2 * kLinesDs;
-    const int per_gu = I / 32, per_d = H / 64;
-    int lo_gu, hi_gu, lo_d, hi_d;
-    block_range(n_act * per_gu, lo_gu, hi_gu);
-    block_range(n_act * per_d, lo_d, hi_d);
-    const int n_gu = hi_gu - lo_gu, n_d = hi_d - lo_d;
-    for (int i = threadIdx.x; i < n_gu * kPerGU + n_d * kPerD; i += kGemvThreads) {
-      const char* line;
-      if (i < n_gu * kPerGU) {
-        const int k = i / kPerGU, l = i - k * kPerGU;
-        const int it = lo_gu + k;
-        const int seg = s_list[it / per_gu];
-        const int f0 = (it % per_gu) * 32;
-        const int sh = seg == E ? 1 : 0;
-        const int which = l / kMatGU, ll = l - which * kMatGU;
-        const AffineRef W = which ? (sh ? P.up[1] : P.up[0]) : (sh ? P.gate[1] : P.gate[0]);
-        const int64_t ex = sh ? 0 : (int64_t)seg;
-        const int64_t row = q_row(W, ex, f0), srow = sb_row(W, ex, f0);
-        if (ll < kLinesGU)
-          line = reinterpret_cast<const char*>(W.q) + row * (H / 2) + (int64_t)ll * 128;
-        else if (ll < kLinesGU + kLinesGUs)
-          line = reinterpret_cast<const char*>(W.s) + srow * (H / 64) * 2 + (int64_t)(ll - kLinesGU) * 128;
-        else
-          line = reinterpret_cast<const char*>(W.b) + srow * (H / 64) * 2 +
-                 (int64_t)(ll - kLinesGU - kLinesGUs) * 128;
+  // ---- phases 3 and 4: items and weight tiles ----
+  // Gate/up item = (active segment, 32 features): their 32 gate and 32 up rows
+  // against every token row of the segment; down item = (active segment, 64
+  // output rows).  Warp w takes tile w & 3 (gate/up: gate rows of features
+  // 0-15, 16-31, then up rows of the same) over K quarter w >> 2 on warp
+  // tensor-core tiles; the quarters' partials are added in shared memory.  Each
+  // block takes a contiguous share of the items; an item's weight rows are
+  // requested before the previous item's epilogue (the first gate/up item's
+  // before the L2 prefetch below, the first down item's before barrier 2).
+  constexpr int kGQ3 = H / 256, kGQ4 = I / 256;  // 64-wide groups per K quarter
+  const int g8 = lane >> 2, c4 = lane & 3;
+  const int tile = w & 3, quarter = w >> 2;
+  const int per_gu = I / 32, per_d = H / 64;
+  int lo3, hi3, lo4, hi4;
+  block_range(n_act * per_gu, lo3, hi3);
+  block_range(n_act * per_d, lo4, hi4);
+  TileRegs<kGQ3> R3;
+  auto load3 = [&](int it) {
+    const int seg = s_list[it / per_gu];
+    const int sh = seg == E ? 1 : 0;
+    const AffineRef W = tile < 2 ? (sh ? P.gate[1] : P.gate[0]) : (sh ? P.up[1] : P.up[0]);
+    load_tile<kGQ3>(R3, W, sh ? 0 : seg, (it % per_gu) * 32 + (tile & 1) * 16 + g8, H,
+                    quarter * kGQ3, c4);
+  };
+  if (lo3 < hi3) load3(lo3);
+  // the experts are known: pull the rest of this block's gate/up rows (now) and
+  // its down rows (once the first gate/up tile's own loads are served, after
+  // its MMAs) into L2, one bulk prefetch per contiguous range (an item's codes,
+  // scales or biases), so the loads of phases 3 and 4 do not each wait a full
+  // HBM trip
+  auto prefetch_items = [&](bool gate_up, bool down_rows) {
+    const int n_gu = gate_up && hi3 - lo3 > 1 ? hi3 - lo3 - 1 : 0, n_d = down_rows ? hi4 - lo4 : 0;
+    for (int i = threadIdx.x; i < n_gu * 6 + n_d * 3; i += kGemvThreads) {
+      int seg, row0, rows, K, range;
+      bool up = false, down = false;
+      if (i < n_gu * 6) {
+        const int it = lo3 + 1 + i / 6, m = i % 6;
+        seg = s_list[it / per_gu];
+        row0 = (it % per_gu) * 32;
+        rows = 32;
+        K = H;
+        up = m >= 3;
+        range = m % 3;
       } else {
-        const int i2 = i - n_gu * kPerGU;
-        const int k = i2 / kPerD, l = i2 - k * kPerD;
-        const int it = lo_d + k;
-        const int seg = s_list[it / per_d];
-        const int r0 = (it % per_d) * 64;
-        const int sh = seg == E ? 1 : 0;
-        const AffineRef W = sh ? P.down[1] : P.down[0];
-        const int64_t ex = sh ? 0 : (int64_t)seg;
-        const int64_t row = q_row(W, ex, r0), srow = sb_row(W, ex, r0);
-        if (l < kLinesD)
-          line = reinterpret_cast<const char*>(W.q) + row * (I / 2) + (int64_t)l * 128;
-        else if (l < kLinesD + kLinesDs)
-          line = reinterpret_cast<const char*>(W.s) + srow * (I / 64) * 2 + (int64_t)(l - kLinesD) * 128;
-        else
-          line = reinterpret_cast<const char*>(W.b) + srow * (I / 64) * 2 +
-                 (int64_t)(l - kLinesD - kLinesDs) * 128;
+        const int i2 = i - n_gu * 6;
+        const int it = lo4 + i2 / 3;
+        seg = s_list[it / per_d];
+        row0 = (it % per_d) * 64;
+        rows = 64;
+        K = I;
+        down = true;
+        range = i2 % 3;
       }
-      prefetch_l2(line);
+      const int sh = seg == E ? 1 : 0;
+      const AffineRef W = down ? (sh ? P.down[1] : P.down[0])
+                               : (up ? (sh ? P.up[1] : P.up[0]) : (sh ? P.gate[1] : P.gate[0]));
+      const int64_t ex = sh ? 0 : (int64_t)seg;
+      if (range == 0)
+        prefetch_l2_bulk(reinterpret_cast<const char*>(W.q) + q_row(W, ex, row0) * (K / 2),
+                         (uint32_t)(rows * (K / 2)));
+      else
+        prefetch_l2_bulk(reinterpret_cast<const char*>(range == 1 ? W.s : W.b) +
+                             sb_row(W, ex, row0) * (K / 64) * 2,
+                         (uint32_t)(rows * (K / 64) * 2));
     }
-  }
+  };
+  prefetch_items(true, lo3 >= hi3);
 
   // ---- phase 3: gate/up + SwiGLU ----
-  // Item = (active segment, 32 features): their 32 gate and 32 up rows against
-  // every token row of the segment.  Warp w takes tile w & 3 (gate rows of
-  // features 0-15, 16-31, then up rows of the same) over K quarter w >> 2 on
-  // warp tensor-core tiles; the quarters' partials are added in shared memory.
-  {
-    constexpr int kGQ = H / 256;  // 64-wide groups per K quarter
-    const int g8 = lane >> 2, c4 = lane & 3;
-    const int tile = w & 3, quarter = w >> 2;
-    const int per_seg = I / 32;
-    int lo, hi;
-    block_range(n_act * per_seg, lo, hi);
-    for (int it = lo; it < hi; ++it) {
-      const int seg = s_list[it / per_seg];
-      const int fi = (it % per_seg) * 32;
-      const int sh = seg == E ? 1 : 0;
-      const AffineRef W = tile < 2 ? (sh ? P.gate[1] : P.gate[0]) : (sh ? P.up[1] : P.up[0]);
-      TileRegs<kGQ> R;
-      load_tile<kGQ>(R, W, sh ? 0 : seg, fi + (tile & 1) * 16 + g8, H, quarter * kGQ, c4);
-      const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
-      for (uint32_t pb = p0; pb < p1; pb += 16) {
-        const int n = (int)(p1 - pb < 16u ? p1 - pb : 16u);
-        // B column g8 of chunk 0 / 1: sorted rows pb + g8 / pb + 8 + g8 (a valid
-        // row stands in past n; its columns are not stored)
-        const int j0 = g8 < n ? g8 : 0, j1 = g8 + 8 < n ? g8 + 8 : 0;
-        const int off = quarter * kGQ * 128 + c4 * 32;
-        const uint8_t* x0 = xp + (int)s_stok[pb + j0] * kXpStride + off;
-        const uint8_t* x1 = xp + (int)s_stok[pb + j1] * kXpStride + off;
-        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-        tile_mma<kGQ>(R, x0, x1, n > 8, d0, d1);
-        __syncthreads();  // the previous epilogue is done with red
+  for (int it = lo3; it < hi3; ++it) {
+    const int seg = s_list[it / per_gu];
+    const int fi = (it % per_gu) * 32;
+    const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
+    for (uint32_t pb = p0; pb < p1; pb += 16) {
+      const int n = (int)(p1 - pb < 16u ? p1 - pb : 16u);
+      // B column g8 of chunk 0 / 1: sorted rows pb + g8 / pb + 8 + g8 (a valid row
+      // stands in past n; its columns are not stored)
+      const int j0 = g8 < n ? g8 : 0, j1 = g8 + 8 < n ? g8 + 8 : 0;
+      const int off = quarter * kGQ3 * 128 + c4 * 32;
+      float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+      tile_mma<kGQ3>(R3, xp + (int)s_stok[pb + j0] * kXpStride + off,
+                     xp + (int)s_stok[pb + j1] * kXpStride + off, n > 8, d0, d1);
+      if (it == lo3 && pb == p0) prefetch_items(false, true);
+      if (pb + 16 >= p1 && it + 1 < hi3) load3(it + 1);
+      __syncthreads();  // the previous epilogue is done with red
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          red[red_at(quarter, tile, 0, r, lane)] = d0[r];
-          red[red_at(quarter, tile, 1, r, lane)] = d1[r];
-        }
-        __syncthreads();
-        const int fl = threadIdx.x & 31, j = threadIdx.x >> 5;  // 32 features x 16 rows
-        if (j < n) {
-          const float g = red_sum(red, fl >> 4, fl & 15, j);
-          const float u = red_sum(red, 2 + (fl >> 4), fl & 15, j);
-          P.act[(int64_t)(pb + j) * I + fi + fl] =
-              __float2bfloat16_rn(swiglu_bf16(round_bf16(g), round_bf16(u)));
-        }
+      for (int r = 0; r < 4; ++r) {
+        red[red_at(quarter, tile, 0, r, lane)] = d0[r];
+        red[red_at(quarter, tile, 1, r, lane)] = d1[r];
+      }
+      __syncthreads();
+      const int fl = threadIdx.x & 31, j = threadIdx.x >> 5;  // 32 features x 16 rows
+      if (j < n) {
+        const float g = red_sum(red, fl >> 4, fl & 15, j);
+        const float u = red_sum(red, 2 + (fl >> 4), fl & 15, j);
+        P.act[(int64_t)(pb + j) * I + fi + fl] =
+            __float2bfloat16_rn(swiglu_bf16(round_bf16(g), round_bf16(u)));
       }
     }
   }
+  TileRegs<kGQ4> R4;
+  auto load4 = [&](int it) {
+    const int seg = s_list[it / per_d];
+    const int sh = seg == E ? 1 : 0;
+    load_tile<kGQ4>(R4, sh ? P.down[1] : P.down[0], sh ? 0 : seg,
+                    (it % per_d) * 64 + tile * 16 + g8, I, quarter * kGQ4, c4);
+  };
+  if (lo4 < hi4) load4(lo4);
   if (!grid_barrier(P.barrier, 2, P.status, &s_flag)) return;
 
   // ---- phase 4: down ----
-  // Item = (active segment, 64 output rows); warp w: tile w & 3 (16 rows) over K
-  // quarter w >> 2 of the intermediate width.  B = the segment's activation
-  // rows, staged (pair-interleaved) once for all of the block's items on it.
+  // B = the segment's activation rows, staged (pair-interleaved) once for all
+  // of the block's items on it.
   {
-    constexpr int kGQ = I / 256;
     constexpr int kAVecs = I / 8;
-    const int g8 = lane >> 2, c4 = lane & 3;
-    const int tile = w & 3, quarter = w >> 2;
-    const int per_seg = H / 64;
-    int lo, hi;
-    block_range(n_act * per_seg, lo, hi);
     const uint4* asrc = reinterpret_cast<const uint4*>(P.act);
     int staged_seg = -1;  // segment whose rows from staged_p sit in ap
     uint32_t staged_p = 0;
-    for (int it = lo; it < hi; ++it) {
-      const int seg = s_list[it / per_seg];
-      const int r0 = (it % per_seg) * 64;
-      const int sh = seg == E ? 1 : 0;
-      const AffineRef W = sh ? P.down[1] : P.down[0];
-      TileRegs<kGQ> R;
-      load_tile<kGQ>(R, W, sh ? 0 : seg, r0 + tile * 16 + g8, I, quarter * kGQ, c4);
+    for (int it = lo4; it < hi4; ++it) {
+      const int seg = s_list[it / per_d];
+      const int r0 = (it % per_d) * 64;
       const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
       for (uint32_t pb = p0; pb < p1; pb += kStageRows) {
         const int n = (int)(p1 - pb < (uint32_t)kStageRows ? p1 - pb : (uint32_t)kStageRows);
@@ -989,9 +1025,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
           __syncthreads();
         }
         const int j0 = g8 < n ? g8 : 0, j1 = g8 + 8 < n ? g8 + 8 : 0;
-        const int off = quarter * kGQ * 128 + c4 * 32;
+        const int off = quarter * kGQ4 * 128 + c4 * 32;
         float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-        tile_mma<kGQ>(R, ap + j0 * kApStride + off, ap + j1 * kApStride + off, n > 8, d0, d1);
+        tile_mma<kGQ4>(R4, ap + j0 * kApStride + off, ap + j1 * kApStride + off, n > 8, d0, d1);
+        if (pb + kStageRows >= p1 && it + 1 < hi4) load4(it + 1);
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
           red[red_at(quarter, tile, 0, r, lane)] = d0[r];
@@ -1021,7 +1058,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
                              P.sorted != 0, P.has_shared ? (int64_t)(s_offs[E] + t) : -1, s_sg[t]);
     }
   }
-  (void)rows_total;
   grid_exit(P.barrier);
 }
 
