@@ -357,8 +357,9 @@ int copy_taps(astro_moe_ctx* ctx, const BlockWorkspace& b, int64_t T, int E, int
 constexpr int kMailboxExperts = 1024;
 
 // batches up to this many tokens take the decode path unless the options say
-// otherwise: the fused decode kernel where its shapes apply, else the separate
-// decode GEMVs
+// otherwise: the fused decode kernel where its shapes apply (it takes up to 64
+// tokens when asked; above 16 it restages and re-dequantises per 16 token rows
+// of a segment and loses to the grouped GEMMs), else the separate decode GEMVs
 constexpr int64_t kDefaultFusedTokens = 16;
 constexpr int64_t kDefaultDecodeTokens = 8;
 // batches up to this many tokens compute router logits with the router GEMV

@@ -149,34 +149,49 @@ __global__ void __launch_bounds__(kThreads) router_gemv_kernel(
   __syncthreads();
   const int e = blockIdx.x * kWarps + w;
   if (e >= E) return;
-  uint4 wv[J];
+  // eight K slices of H / 8: a slice's lane products are summed per lane, then
+  // across the warp, and the slice sums are added in order -- the fused decode
+  // kernel's order, so both paths give the same logits
+  constexpr int kSliceVecs = kRowVec / 8, kPerLane = (kSliceVecs + 31) / 32;
+  uint4 wv[8][kPerLane];
   const uint4* wrow = reinterpret_cast<const uint4*>(wr + (int64_t)e * H);
 #pragma unroll
-  for (int j = 0; j < J; ++j) wv[j] = ld_stream(wrow + j * 32 + lane);
+  for (int s = 0; s < 8; ++s)
+#pragma unroll
+    for (int k = 0; k < kPerLane; ++k)
+      wv[s][k] = (k * 32 + lane < kSliceVecs) ? ld_stream(wrow + s * kSliceVecs + k * 32 + lane)
+                                              : make_uint4(0u, 0u, 0u, 0u);
   float acc[kRouterTokens];
 #pragma unroll
   for (int t = 0; t < kRouterTokens; ++t) acc[t] = 0.0f;
 #pragma unroll
-  for (int j = 0; j < J; ++j) {
-    float wf[8];
-    bf16x8_to_f32(wv[j], wf);
+  for (int s = 0; s < 8; ++s) {
+    float part[kRouterTokens];
 #pragma unroll
-    for (int t = 0; t < kRouterTokens; ++t) {
-      if (t < nt) {
-        float xf[8];
-        bf16x8_to_f32(xs[t * kRowVec + j * 32 + lane], xf);
+    for (int t = 0; t < kRouterTokens; ++t) part[t] = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(wf[i], xf[i], acc[t]);
+    for (int k = 0; k < kPerLane; ++k) {
+      if (k * 32 + lane < kSliceVecs) {
+        float wf[8];
+        bf16x8_to_f32(wv[s][k], wf);
+#pragma unroll
+        for (int t = 0; t < kRouterTokens; ++t) {
+          if (t < nt) {
+            float xf[8];
+            bf16x8_to_f32(xs[t * kRowVec + s * kSliceVecs + k * 32 + lane], xf);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) part[t] = __fmaf_rn(wf[i], xf[i], part[t]);
+          }
+        }
       }
     }
+#pragma unroll
+    for (int t = 0; t < kRouterTokens; ++t)
+      if (t < nt) acc[t] = __fadd_rn(acc[t], warp_sum(part[t]));
   }
 #pragma unroll
-  for (int t = 0; t < kRouterTokens; ++t) {
-    if (t < nt) {
-      const float v = warp_sum(acc[t]);
-      if (lane == 0) logits[(t0 + t) * E + e] = __float2bfloat16_rn(v);
-    }
-  }
+  for (int t = 0; t < kRouterTokens; ++t)
+    if (t < nt && lane == 0) logits[(t0 + t) * E + e] = __float2bfloat16_rn(acc[t]);
 }
 
 // ---------------------------------------------------------------------------
@@ -426,7 +441,8 @@ int grid_for(int64_t items_upper) {
 // multi-kernel path's; the projections add the same fp32 products in another
 // order (tensor-core tiles, four K quarters summed in a fixed order), so the two
 // paths agree to the block tolerance and routing is bit-identical.
-constexpr int kFusedMaxTokens = 16;
+constexpr int kFusedMaxTokens = 64;
+constexpr int kStageTokens = 16;  // token rows staged (pair-interleaved) at a time
 constexpr int kFusedMaxExperts = 256;
 constexpr int kFusedMaxAssign = 512;
 
@@ -559,8 +575,17 @@ ASTRO_DEVINL void tile_mma(const TileRegs<KG>& R, const uint8_t* x0, const uint8
   }
 }
 
-constexpr int kStageRows = kFusedMaxTokens;  // activation rows staged per down pass
+constexpr int kStageRows = 16;  // activation rows staged per down pass
 constexpr int kRedFloats = 4 * 4 * 2 * 4 * 32;
+// bytes of the phase-1 / phase-2 / phase-4 union at the start of shared memory
+template <int H, int I> constexpr int kUnionBytes() {
+  constexpr int a = kStageTokens * H * 2, b = kFusedMaxTokens * kFusedMaxExperts * 2,
+                c = kStageRows * (I * 2 + 16);
+  return a > b ? (a > c ? a : c) : (b > c ? b : c);
+}
+template <int H, int I> constexpr int fused_smem_bytes() {
+  return kUnionBytes<H, I>() + kStageTokens * (H * 2 + 16) + kRedFloats * 4;
+}
 
 // fp32 partial sums of the four K quarters: [quarter][tile][chunk][reg][lane]
 ASTRO_DEVINL int red_at(int quarter, int tile, int chunk, int reg, int lane) {
@@ -691,12 +716,14 @@ template <int H, int I>
 __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDecodeParams P) {
   constexpr int kVecs = H / 8;            // uint4 per x row
   constexpr int kXpStride = H * 2 + 16, kApStride = I * 2 + 16;  // padded: no bank conflicts
+  // dynamic shared memory: [union: x rows (phase 1) | logits (phase 2) | act rows
+  // (phase 4)] [token rows, pair-interleaved] [partial sums]
   extern __shared__ uint4 smem[];
-  uint4* xs = smem;                                                 // [T][kVecs], swizzled
-  uint8_t* xp = reinterpret_cast<uint8_t*>(xs + kFusedMaxTokens * kVecs);  // [T] pair-interleaved
-  float* red = reinterpret_cast<float*>(xp + kFusedMaxTokens * kXpStride);  // quarter partials
-  uint8_t* ap = reinterpret_cast<uint8_t*>(red + kRedFloats);      // [kStageRows] act rows
-  __nv_bfloat16* s_logits = reinterpret_cast<__nv_bfloat16*>(ap + kStageRows * kApStride);  // [T][E]
+  uint4* xs = smem;  // phase 1, T <= kStageTokens: [T][kVecs], swizzled
+  __nv_bfloat16* s_logits = reinterpret_cast<__nv_bfloat16*>(smem);  // phase 2: [T][E]
+  uint8_t* ap = reinterpret_cast<uint8_t*>(smem);                      // phase 4: [kStageRows]
+  uint8_t* xp = reinterpret_cast<uint8_t*>(smem) + kUnionBytes<H, I>();  // [kStageTokens] rows
+  float* red = reinterpret_cast<float*>(xp + kStageTokens * kXpStride);  // partial sums
   __shared__ uint32_t s_ids[kFusedMaxAssign];
   __shared__ __nv_bfloat16 s_sc16[kFusedMaxAssign];
   __shared__ float s_score[kFusedMaxAssign];
@@ -717,7 +744,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   // Block b computes router rows b, b + grid, ...: two rows per pass, each split
   // into eight K slices of H / 8 (warp w: row w >> 3 of the pass, slice w & 7);
   // a warp's slice sums go through shared memory and the eight slices are added
-  // in order.  Each warp's weight vector is requested before x is staged.
+  // in order.  Each warp's weight vector is requested before x is staged.  Up to
+  // kStageTokens tokens, x is staged in shared memory (and pair-interleaved for
+  // phase 3); above, warps read their x slices from L2 and phase 3 stages the
+  // token rows of each segment.
+  const bool stage_all = T <= kStageTokens;
   {
     constexpr int kSliceVecs = kVecs / 8;  // uint4 per slice: 32 (H = 2048) or 16
     const int rows = E + (P.has_shared ? 1 : 0);
@@ -731,12 +762,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
     uint4 wv = make_uint4(0u, 0u, 0u, 0u);
     if (r < rows && vlane) wv = ld_stream(row_ptr(r));
     const uint4* xsrc = reinterpret_cast<const uint4*>(P.x);
-    for (int i = threadIdx.x; i < T * kVecs; i += kGemvThreads) {
-      const int t = i / kVecs, q = i - t * kVecs;
-      const uint4 v = ld_cached(xsrc + (int64_t)t * kVecs + q);
-      xs[t * kVecs + swz(q)] = v;
-      *reinterpret_cast<uint4*>(xp + t * kXpStride + q * 16) = pair_interleave(v);
-    }
+    if (stage_all)
+      for (int i = threadIdx.x; i < T * kVecs; i += kGemvThreads) {
+        const int t = i / kVecs, q = i - t * kVecs;
+        const uint4 v = ld_cached(xsrc + (int64_t)t * kVecs + q);
+        xs[t * kVecs + swz(q)] = v;
+        *reinterpret_cast<uint4*>(xp + t * kXpStride + q * 16) = pair_interleave(v);
+      }
     if (P.has_shared && threadIdx.x == 0) {
       // the shared expert is always used: start pulling its weights into L2
       const AffineRef sw[3] = {P.gate[1], P.up[1], P.down[1]};
@@ -751,6 +783,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       }
     }
     float* s_part = red;  // [2 rows][8 slices][kFusedMaxTokens]
+    const int xq = sl * kSliceVecs + lane;  // this lane's x vector of the slice
     for (int pass = 0; pass * 2 * (int)gridDim.x < rows; ++pass) {
       if (pass > 0) {
         r = (int)blockIdx.x + (2 * pass + rs) * (int)gridDim.x;
@@ -760,22 +793,25 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       if (r < rows) {
         float wf[8];
         bf16x8_to_f32(wv, wf);
-        float acc[kFusedMaxTokens];
+        for (int t0 = 0; t0 < T; t0 += kStageTokens) {  // 16 tokens' sums at a time
+          float acc[kStageTokens];
 #pragma unroll
-        for (int t = 0; t < kFusedMaxTokens; ++t) {
-          acc[t] = 0.f;
-          if (t < T && vlane) {
-            float xf[8];
-            bf16x8_to_f32(xs[t * kVecs + swz(sl * kSliceVecs + lane)], xf);
+          for (int t = 0; t < kStageTokens; ++t) {
+            acc[t] = 0.f;
+            if (t0 + t < T && vlane) {
+              float xf[8];
+              bf16x8_to_f32(stage_all ? xs[t * kVecs + swz(xq)]
+                                      : ld_cached(xsrc + (int64_t)(t0 + t) * kVecs + xq), xf);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(wf[i], xf[i], acc[t]);
+              for (int i = 0; i < 8; ++i) acc[t] = __fmaf_rn(wf[i], xf[i], acc[t]);
+            }
           }
-        }
 #pragma unroll
-        for (int t = 0; t < kFusedMaxTokens; ++t) {
-          if (t < T) {
-            const float v = warp_sum(acc[t]);
-            if (lane == 0) s_part[(rs * 8 + sl) * kFusedMaxTokens + t] = v;
+          for (int t = 0; t < kStageTokens; ++t) {
+            if (t0 + t < T) {
+              const float v = warp_sum(acc[t]);
+              if (lane == 0) s_part[(rs * 8 + sl) * kFusedMaxTokens + t0 + t] = v;
+            }
           }
         }
       }
@@ -807,7 +843,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
             ? round_bf16(sigmoid_mlx(bf16_to_f32(__ldcg(reinterpret_cast<const unsigned short*>(P.gate_logit) + threadIdx.x))))
             : 0.f;
   __syncthreads();
-  if (w < T) route_token<__nv_bfloat16, 8>(s_logits + w * E, E, K, P.normalize, s_ids + w * K, s_sc16 + w * K);
+  for (int tk = w; tk < T; tk += kGemvWarps)
+    route_token<__nv_bfloat16, 8>(s_logits + tk * E, E, K, P.normalize, s_ids + tk * K, s_sc16 + tk * K);
   __syncthreads();
   // stable counting sort of the N assignments by expert: the rank of an
   // assignment among equal ids is its rank inside its warp (match_any) plus the
@@ -958,21 +995,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   prefetch_items(true, lo3 >= hi3);
 
   // ---- phase 3: gate/up + SwiGLU ----
+  int xp_seg = -1;  // (T > kStageTokens) segment whose rows from xp_p sit in xp
+  uint32_t xp_p = 0;
+  const uint4* xsrc = reinterpret_cast<const uint4*>(P.x);
   for (int it = lo3; it < hi3; ++it) {
     const int seg = s_list[it / per_gu];
     const int fi = (it % per_gu) * 32;
     const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
-    for (uint32_t pb = p0; pb < p1; pb += 16) {
-      const int n = (int)(p1 - pb < 16u ? p1 - pb : 16u);
+    for (uint32_t pb = p0; pb < p1; pb += kStageTokens) {
+      const int n = (int)(p1 - pb < (uint32_t)kStageTokens ? p1 - pb : (uint32_t)kStageTokens);
+      if (!stage_all && (seg != xp_seg || pb != xp_p)) {
+        // every warp finished its previous MMAs before the last epilogue's barrier
+        for (int i = threadIdx.x; i < n * kVecs; i += kGemvThreads) {
+          const int j = i / kVecs, q = i - j * kVecs;
+          *reinterpret_cast<uint4*>(xp + j * kXpStride + q * 16) =
+              pair_interleave(ld_cached(xsrc + (int64_t)s_stok[pb + j] * kVecs + q));
+        }
+        xp_seg = seg;
+        xp_p = pb;
+        __syncthreads();
+      }
       // B column g8 of chunk 0 / 1: sorted rows pb + g8 / pb + 8 + g8 (a valid row
       // stands in past n; its columns are not stored)
       const int j0 = g8 < n ? g8 : 0, j1 = g8 + 8 < n ? g8 + 8 : 0;
+      const int b0 = stage_all ? (int)s_stok[pb + j0] : j0, b1 = stage_all ? (int)s_stok[pb + j1] : j1;
       const int off = quarter * kGQ3 * 128 + c4 * 32;
       float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-      tile_mma<kGQ3>(R3, xp + (int)s_stok[pb + j0] * kXpStride + off,
-                     xp + (int)s_stok[pb + j1] * kXpStride + off, n > 8, d0, d1);
+      tile_mma<kGQ3>(R3, xp + b0 * kXpStride + off, xp + b1 * kXpStride + off, n > 8, d0, d1);
       if (it == lo3 && pb == p0) prefetch_items(false, true);
-      if (pb + 16 >= p1 && it + 1 < hi3) load3(it + 1);
+      if (pb + kStageTokens >= p1 && it + 1 < hi3) load3(it + 1);
       __syncthreads();  // the previous epilogue is done with red
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
@@ -980,7 +1031,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
         red[red_at(quarter, tile, 1, r, lane)] = d1[r];
       }
       __syncthreads();
-      const int fl = threadIdx.x & 31, j = threadIdx.x >> 5;  // 32 features x 16 rows
+      const int fl = threadIdx.x & 31, j = threadIdx.x >> 5;  // 32 features x kStageTokens rows
       if (j < n) {
         const float g = red_sum(red, fl >> 4, fl & 15, j);
         const float u = red_sum(red, 2 + (fl >> 4), fl & 15, j);
@@ -1142,9 +1193,7 @@ namespace {
 template <int H, int I>
 cudaError_t launch_fused_t(const FusedDecodeParams& p, cudaStream_t st) {
   auto kern = decode_fused_kernel<H, I>;
-  const size_t smem = (size_t)kFusedMaxTokens * (H * 2) + (size_t)kFusedMaxTokens * (H * 2 + 16) +
-                      (size_t)kRedFloats * 4 + (size_t)kStageRows * (I * 2 + 16) +
-                      (size_t)kFusedMaxTokens * kFusedMaxExperts * 2;
+  const size_t smem = (size_t)fused_smem_bytes<H, I>();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int dev = 0, sms = 0, per_sm = 0;

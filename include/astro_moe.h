@@ -184,7 +184,7 @@ typedef struct {
   int64_t decode_max_tokens; /* batches of at most this many tokens take the decode
                                 path (4-bit g64 layers); 0 = 16 where the fused
                                 decode kernel applies, else 8; -1 = never */
-  int64_t decode_fused;      /* decode batches of <= 16 tokens run as one cooperative
+  int64_t decode_fused;      /* decode batches of <= 64 tokens run as one cooperative
                                 kernel; 0 = auto, -1 = never (separate kernels) */
   int64_t reserved[4];
 } astro_moe_options;

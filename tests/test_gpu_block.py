@@ -63,7 +63,7 @@ def run_and_compare(cfg, T, seed=0, subset=None, fuse=False, path=(0, 0, 0)):
 # path = (use_tensor_cores, decode_max_tokens, decode_fused): the tcgen05 grouped
 # GEMMs, the CUDA-core grouped GEMV, the separate decode kernels (taken here up
 # to 1024 tokens so that segments of many rows are covered too), and the fused
-# decode kernel (T <= 16; larger T falls through to the separate decode kernels)
+# decode kernel (T <= 64; larger T falls through to the separate decode kernels)
 PATHS = [pytest.param((1, -1, -1), id="tcgen05"), pytest.param((-1, -1, -1), id="cudacore"),
          pytest.param((0, 1024, -1), id="decode"), pytest.param((0, 1024, 0), id="fused")]
 
