@@ -188,6 +188,13 @@ struct astro_moe_pager {
 
 namespace {
 
+// fused decode synchronisation words at workspace offset 0: the grid barrier's
+// two words, then (from word 64) one completion counter per expert segment
+constexpr size_t kFusedSyncBytes = 2048;
+constexpr int kFusedSegDoneWord = 64;
+static_assert((kFusedSyncBytes / 4 - kFusedSegDoneWord) >= 257,
+              "a counter per segment of the fused decode kernel (<= 256 experts + shared)");
+
 struct BlockWorkspace {
   uint32_t* barrier;  // fused decode grid barrier; first in the workspace (fixed address)
   uint16_t* logits;
@@ -221,7 +228,7 @@ size_t plan_workspace(const astro_moe_layer_weights& w, int64_t T, BlockWorkspac
     return p;
   };
   BlockWorkspace b{};
-  b.barrier = (uint32_t*)take(2 * sizeof(uint32_t));
+  b.barrier = (uint32_t*)take(kFusedSyncBytes);
   b.logits = (uint16_t*)take(sizeof(uint16_t) * T * E);
   b.ids = (uint32_t*)take(sizeof(uint32_t) * N);
   b.scores = (uint16_t*)take(sizeof(uint16_t) * N);
@@ -250,8 +257,9 @@ int ensure_ws(astro_moe_ctx* ctx, size_t bytes) {
   }
   CK(cudaMalloc(&ctx->ws, bytes), "cudaMalloc(workspace)");
   ctx->ws_bytes = bytes;
-  // the fused decode kernel's barrier words (workspace offset 0) start at zero
-  CK(cudaMemset(ctx->ws, 0, 256), "cudaMemset(workspace barrier)");
+  // the fused decode kernel's barrier words and segment counters (workspace
+  // offset 0) start at zero; the kernel leaves them zero
+  CK(cudaMemset(ctx->ws, 0, kFusedSyncBytes), "cudaMemset(workspace barrier)");
   return ASTRO_MOE_OK;
 }
 
@@ -422,6 +430,7 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     a.yrows = b.yrows;
     a.out = out;
     a.barrier = b.barrier;
+    a.seg_done = b.barrier + kFusedSegDoneWord;
     a.status = ctx->status;
     // one kernel: its whole time is reported under gate_up_ms
     marks.mark();

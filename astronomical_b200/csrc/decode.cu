@@ -427,8 +427,11 @@ int grid_for(int64_t items_upper) {
 //      shared memory (identical inputs give identical results in every block, so
 //      no barrier follows); block 0 publishes ids, scores and offsets;
 //   3. gate/up + SwiGLU over (active segment, 32 features) items -> act rows;
-//   -- grid barrier --
-//   4. down over (active segment, 64 output rows) items -> expert rows;
+//      each finished item adds one to its segment's completion counter;
+//   4. down over (active segment, 64 output rows) items -> expert rows; a
+//      block starts a segment's down items once all of that segment's gate/up
+//      items are counted (no grid barrier: early blocks go on while late ones
+//      finish gate/up);
 //      phases 3 and 4 run on warp tensor-core tiles (mma.sync m16n8k16, bf16
 //      operands, fp32 accumulation): a decode batch is at most 16 tokens wide, so
 //      each warp keeps one 16-row weight tile in registers, with no shared-memory
@@ -628,6 +631,7 @@ struct FusedDecodeParams {
     p.yrows = reinterpret_cast<__nv_bfloat16*>(a.yrows);
     p.out = reinterpret_cast<__nv_bfloat16*>(a.out);
     p.barrier = a.barrier;
+    p.seg_done = a.seg_done;
     p.status = a.status;
     return p;
   }
@@ -644,6 +648,7 @@ struct FusedDecodeParams {
   __nv_bfloat16* yrows;       // [T * K + T, H]
   __nv_bfloat16* out;         // [T, H]
   uint32_t* barrier;          // {arrivals, exits}; both zero between launches
+  uint32_t* seg_done;         // [E + 1] gate/up items finished per segment; zero between launches
   uint32_t* status;
 };
 
@@ -697,6 +702,27 @@ ASTRO_DEVINL void grid_exit(uint32_t* bar) {
   }
 }
 
+// Waits (acquire, bounded at 2 s) until *c >= target; on timeout records
+// kDevWaitTimeout and returns 0.
+ASTRO_DEVINL int wait_count(const uint32_t* c, uint32_t target, uint32_t* status) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  uint32_t spins = 0;
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+    if (v >= target) return 1;
+    if ((++spins & 255u) == 0) {
+      uint64_t t1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+      if (t1 - t0 > 2000000000ull) {
+        record_status(status, kDevWaitTimeout);
+        return 0;
+      }
+    }
+  }
+}
+
 // one bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a
 // multiple of 16; callers keep pieces at or below 32 KB)
 ASTRO_DEVINL void prefetch_l2_bulk(const void* p, uint32_t bytes) {
@@ -734,6 +760,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   __shared__ uint16_t s_list[kFusedMaxExperts + 1];
   __shared__ float s_sg[kFusedMaxTokens];
   __shared__ int s_flag;
+  __shared__ int s_ready;
   __shared__ int s_nact;
 
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -1038,6 +1065,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
         P.act[(int64_t)(pb + j) * I + fi + fl] =
             __float2bfloat16_rn(swiglu_bf16(round_bf16(g), round_bf16(u)));
       }
+      if (pb + kStageTokens >= p1) {
+        // the item's act columns are stored: count it for its segment (release)
+        __syncthreads();
+        if (threadIdx.x == 0)
+          asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(P.seg_done + seg) : "memory");
+      }
     }
   }
   TileRegs<kGQ4> R4;
@@ -1048,7 +1081,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
                     (it % per_d) * 64 + tile * 16 + g8, I, quarter * kGQ4, c4);
   };
   if (lo4 < hi4) load4(lo4);
-  if (!grid_barrier(P.barrier, 2, P.status, &s_flag)) return;
 
   // ---- phase 4: down ----
   // B = the segment's activation rows, staged (pair-interleaved) once for all
@@ -1058,14 +1090,22 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
     const uint4* asrc = reinterpret_cast<const uint4*>(P.act);
     int staged_seg = -1;  // segment whose rows from staged_p sit in ap
     uint32_t staged_p = 0;
+    int ready_seg = -1;   // segment whose gate/up items are all counted
     for (int it = lo4; it < hi4; ++it) {
       const int seg = s_list[it / per_d];
       const int r0 = (it % per_d) * 64;
       const uint32_t p0 = s_offs[seg], p1 = s_offs[seg + 1];
       for (uint32_t pb = p0; pb < p1; pb += kStageRows) {
         const int n = (int)(p1 - pb < (uint32_t)kStageRows ? p1 - pb : (uint32_t)kStageRows);
-        __syncthreads();  // the previous epilogue is done with red (and ap)
-        if (seg != staged_seg || pb != staged_p) {
+        const bool restage = seg != staged_seg || pb != staged_p;
+        if (restage && seg != ready_seg && threadIdx.x == 0)
+          s_ready = wait_count(P.seg_done + seg, (uint32_t)per_gu, P.status);
+        __syncthreads();  // the previous epilogue is done with red (and ap); the segment is ready
+        if (restage && seg != ready_seg) {
+          if (!s_ready) return;
+          ready_seg = seg;
+        }
+        if (restage) {
           for (int i = threadIdx.x; i < n * kAVecs; i += kGemvThreads) {
             const int j = i / kAVecs, q = i - j * kAVecs;
             *reinterpret_cast<uint4*>(ap + j * kApStride + q * 16) =
@@ -1097,7 +1137,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
       }
     }
   }
-  if (!grid_barrier(P.barrier, 3, P.status, &s_flag)) return;
+  if (!grid_barrier(P.barrier, 2, P.status, &s_flag)) return;
+  // every block is past its counter waits: zero the counters for the next launch
+  for (int i = gtid; i <= E; i += nthreads) P.seg_done[i] = 0;
 
   // ---- phase 5: weighted combine + gated shared expert ----
   {

@@ -109,10 +109,12 @@ cudaError_t launch_decode_gate_up(const GroupedGemvDesc& d, int64_t max_active, 
 cudaError_t launch_decode_down(const GroupedGemvDesc& d, int64_t max_active, cudaStream_t st);
 
 // Fused decode block (decode.cu): router, route, sort, gate/up, down and
-// combine of T <= 16 tokens in one cooperative launch (one block per SM, grid
-// barriers between dependent phases).  `barrier` is two words that must be zero
-// before the first launch; the kernel leaves them reusable.  Returns
-// cudaErrorCooperativeLaunchTooLarge when the device cannot hold the grid.
+// combine of T <= 64 tokens in one cooperative launch (one block per SM; grid
+// barriers after the router and the down projection, per-segment completion
+// counters between gate/up and down).  `barrier` (two words) and `seg_done`
+// (E + 1 words) must be zero before the first launch; the kernel leaves them
+// zero.  Returns cudaErrorCooperativeLaunchTooLarge when the device cannot hold
+// the grid.
 struct DecodeFusedArgs {
   const void* x = nullptr;  // bf16 [T, H]
   int T = 0, H = 0, E = 0, K = 0, I = 0, normalize = 1, sorted = 0, has_shared = 0;
@@ -128,6 +130,7 @@ struct DecodeFusedArgs {
   void* yrows = nullptr;
   void* out = nullptr;
   uint32_t* barrier = nullptr;
+  uint32_t* seg_done = nullptr;  // [E + 1] gate/up items done per segment, zero between launches
   uint32_t* status = nullptr;
 };
 bool decode_fused_supported(int T, int H, int E, int K, int I);
