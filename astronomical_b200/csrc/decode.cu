@@ -449,11 +449,37 @@ constexpr int kStageTokens = 16;  // token rows staged (pair-interleaved) at a t
 constexpr int kFusedMaxExperts = 256;
 constexpr int kFusedMaxAssign = 512;
 
-// Block b's share [lo, hi) of n items: contiguous, sizes differ by at most one,
-// so a block's consecutive items mostly share a segment and neighbouring rows.
-ASTRO_DEVINL void block_range(int n, int& lo, int& hi) {
-  lo = (int)((int64_t)n * blockIdx.x / gridDim.x);
-  hi = (int)((int64_t)n * (blockIdx.x + 1) / gridDim.x);
+// Items of the active segments, m per segment, each costing its segment's
+// 16-row passes P (cum[i] = passes of the segments before list entry i,
+// cum[na] = all): the first item whose cost starts at or after `target`.
+ASTRO_DEVINL int item_at_cost(const int* cum, const uint16_t* list, const uint32_t* offs, int na,
+                              int m, int64_t target) {
+  int lo = 0, hi = na - 1;  // largest i with m * cum[i] <= target
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if ((int64_t)m * cum[mid] <= target) lo = mid;
+    else hi = mid - 1;
+  }
+  const int seg = list[lo];
+  const int64_t P = (offs[seg + 1] - offs[seg] + 15) / 16;
+  const int64_t k = (target - (int64_t)m * cum[lo] + P - 1) / P;
+  return lo * m + (int)(k < m ? k : m);
+}
+
+// Block b's share [lo, hi) of those items: contiguous (a block's consecutive
+// items mostly share a segment and neighbouring rows) and of near-equal cost,
+// so the shared expert's many-row items do not pile up on a few blocks.
+ASTRO_DEVINL void block_range(const int* cum, const uint16_t* list, const uint32_t* offs, int na,
+                              int m, bool single_pass, int& lo, int& hi) {
+  if (single_pass || na == 0) {  // every item costs one pass
+    lo = (int)((int64_t)na * m * blockIdx.x / gridDim.x);
+    hi = (int)((int64_t)na * m * (blockIdx.x + 1) / gridDim.x);
+    return;
+  }
+  const int64_t C = (int64_t)m * cum[na];
+  lo = item_at_cost(cum, list, offs, na, m, C * blockIdx.x / gridDim.x);
+  hi = blockIdx.x + 1 == gridDim.x ? na * m
+                                   : item_at_cost(cum, list, offs, na, m, C * (blockIdx.x + 1) / gridDim.x);
 }
 
 // ---- warp tensor-core tiles for the fused decode projections ----
@@ -758,6 +784,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   __shared__ uint8_t s_wcnt[kFusedMaxAssign / 32][kFusedMaxExperts];  // ids per warp of assignments
   __shared__ uint32_t s_offs[kFusedMaxExperts + 2];
   __shared__ uint16_t s_list[kFusedMaxExperts + 1];
+  __shared__ int s_cum[kFusedMaxExperts + 2];  // 16-row passes before each active segment
   __shared__ float s_sg[kFusedMaxTokens];
   __shared__ int s_flag;
   __shared__ int s_ready;
@@ -943,6 +970,35 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
     }
   }
   __syncthreads();
+  if (w == 0 && T > kStageTokens) {
+    // pass counts of the active segments, exclusive scan (block ranges by cost;
+    // up to 16 tokens every segment is one pass)
+    const int na = s_nact, C2 = (na + 31) / 32;
+    int part = 0;
+    for (int i = 0; i < C2; ++i) {
+      const int idx = lane * C2 + i;
+      if (idx < na) {
+        const int sg = s_list[idx];
+        part += (int)((s_offs[sg + 1] - s_offs[sg] + 15) / 16);
+      }
+    }
+    int incl = part;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
+    }
+    int run = incl - part;
+    for (int i = 0; i < C2; ++i) {
+      const int idx = lane * C2 + i;
+      if (idx < na) {
+        const int sg = s_list[idx];
+        s_cum[idx] = run;
+        run += (int)((s_offs[sg + 1] - s_offs[sg] + 15) / 16);
+      }
+    }
+    if (lane == 31) s_cum[na] = incl;
+  }
   if (threadIdx.x < N && my_id < (uint32_t)E) {
     const uint32_t pos = s_offs[my_id] + (uint32_t)rank;
     s_stok[pos] = threadIdx.x / K;
@@ -967,8 +1023,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   const int tile = w & 3, quarter = w >> 2;
   const int per_gu = I / 32, per_d = H / 64;
   int lo3, hi3, lo4, hi4;
-  block_range(n_act * per_gu, lo3, hi3);
-  block_range(n_act * per_d, lo4, hi4);
+  block_range(s_cum, s_list, s_offs, n_act, per_gu, stage_all, lo3, hi3);
+  block_range(s_cum, s_list, s_offs, n_act, per_d, stage_all, lo4, hi4);
   TileRegs<kGQ3> R3;
   auto load3 = [&](int it) {
     const int seg = s_list[it / per_gu];

@@ -239,7 +239,7 @@ def measure_decode(args, dev, rank, hbm_peak, max_over_ranks):
                                                                      device=dev),
                                   device=dev.index, max_tokens=64) for l in range(L)]
     out = {"workload": "config2_decode_zipf1.1", "layers_in_graph": L,
-           "path": "fused decode kernel for T<=16, tcgen05 grouped GEMMs above", "sweep": {}}
+           "path": "fused decode kernel for T<=32, tcgen05 grouped GEMMs above", "sweep": {}}
     for T in (1, 4, 16, 64):
         g = torch.Generator(device=dev)
         g.manual_seed(700 + T)
