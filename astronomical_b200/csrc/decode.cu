@@ -448,6 +448,7 @@ constexpr int kFusedMaxTokens = 64;
 constexpr int kStageTokens = 16;  // token rows staged (pair-interleaved) at a time
 constexpr int kFusedMaxExperts = 256;
 constexpr int kFusedMaxAssign = 512;
+static_assert(kFusedMaxExperts <= kGemvThreads, "one thread per expert in the count scan");
 
 // Items of the active segments, m per segment, each costing its segment's
 // 16-row passes P (cum[i] = passes of the segments before list entry i,
@@ -786,6 +787,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   __shared__ uint16_t s_list[kFusedMaxExperts + 1];
   __shared__ int s_cum[kFusedMaxExperts + 2];  // 16-row passes before each active segment
   __shared__ float s_sg[kFusedMaxTokens];
+  __shared__ int s_wsum[kGemvWarps], s_wnz[kGemvWarps];  // per-warp scan totals
   __shared__ int s_flag;
   __shared__ int s_ready;
   __shared__ int s_nact;
@@ -923,48 +925,46 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
   __syncthreads();
   if (my_id < (uint32_t)E)
     for (int v = 0; v < w; ++v) rank += s_wcnt[v][my_id];
-  if (w == 0) {
-    // exclusive scans of the E counts and of the non-empty experts: lane l owns
-    // experts [l*C, l*C + C); the active list follows expert order, then the
+  {
+    // exclusive scans, over the block, of the E counts (thread e: expert e) and of
+    // the non-empty experts; the active list follows expert order, then the
     // shared expert
-    constexpr int kCMax = kFusedMaxExperts / 32;
-    const int C = (E + 31) / 32;
-    int cnt[kCMax];
-    int part = 0, npart = 0;
-#pragma unroll
-    for (int i = 0; i < kCMax; ++i) {
-      const int e = lane * C + i;
-      int c = 0;
-      if (i < C && e < E)
-        for (int v = 0; v < nw_assign; ++v) c += s_wcnt[v][e];
-      cnt[i] = c;
-      part += c;
-      npart += c > 0 ? 1 : 0;
-    }
-    int incl = part, nincl = npart;
+    int c = 0;
+    if ((int)threadIdx.x < E)
+      for (int v = 0; v < nw_assign; ++v) c += s_wcnt[v][threadIdx.x];
+    const int nz = c > 0 ? 1 : 0;
+    int ic = c, inz = nz;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, d);
-      const int no = __shfl_up_sync(0xffffffffu, nincl, d);
+      const int o = __shfl_up_sync(0xffffffffu, ic, d);
+      const int no = __shfl_up_sync(0xffffffffu, inz, d);
       if (lane >= d) {
-        incl += o;
-        nincl += no;
-      }
-    }
-    int run = incl - part, nrun = nincl - npart;
-#pragma unroll
-    for (int i = 0; i < kCMax; ++i) {
-      const int e = lane * C + i;
-      if (i < C && e < E) {
-        s_offs[e] = (uint32_t)run;
-        run += cnt[i];
-        if (cnt[i] > 0) s_list[nrun++] = (uint16_t)e;
+        ic += o;
+        inz += no;
       }
     }
     if (lane == 31) {
-      s_offs[E] = (uint32_t)incl;
-      s_offs[E + 1] = (uint32_t)(incl + (P.has_shared ? T : 0));
-      int na = nincl;
+      s_wsum[w] = ic;
+      s_wnz[w] = inz;
+    }
+    __syncthreads();
+    int base = 0, nbase = 0, tot = 0, ntot = 0;
+#pragma unroll
+    for (int i = 0; i < kGemvWarps; ++i) {
+      const int s = s_wsum[i], z = s_wnz[i];
+      base += i < w ? s : 0;
+      nbase += i < w ? z : 0;
+      tot += s;
+      ntot += z;
+    }
+    if ((int)threadIdx.x < E) {
+      s_offs[threadIdx.x] = (uint32_t)(base + ic - c);
+      if (nz) s_list[nbase + inz - 1] = (uint16_t)threadIdx.x;
+    }
+    if (threadIdx.x == 0) {
+      s_offs[E] = (uint32_t)tot;
+      s_offs[E + 1] = (uint32_t)(tot + (P.has_shared ? T : 0));
+      int na = ntot;
       if (P.has_shared && T > 0) s_list[na++] = (uint16_t)E;
       s_nact = na;
     }
