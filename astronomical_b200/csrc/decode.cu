@@ -421,7 +421,8 @@ int grid_for(int64_t items_upper) {
 // Fused decode block: the whole MoE block for T <= kFusedMaxTokens tokens in one
 // cooperative launch (one 16-warp block per SM).  Phases:
 //   1. router logits and the shared-expert gate logit (x staged in shared
-//      memory); idle lanes prefetch the shared expert's weights into L2;
+//      memory up to 16 tokens); one thread per block issues bulk L2 prefetches
+//      of the shared expert's weights;
 //   -- grid barrier --
 //   2. every block routes all T tokens and sorts the T*K assignments in its own
 //      shared memory (identical inputs give identical results in every block, so
@@ -433,7 +434,7 @@ int grid_for(int64_t items_upper) {
 //      items are counted (no grid barrier: early blocks go on while late ones
 //      finish gate/up);
 //      phases 3 and 4 run on warp tensor-core tiles (mma.sync m16n8k16, bf16
-//      operands, fp32 accumulation): a decode batch is at most 16 tokens wide, so
+//      operands, fp32 accumulation): a pass covers at most 16 token rows, so
 //      each warp keeps one 16-row weight tile in registers, with no shared-memory
 //      or tensor-memory hand-off of the A operand, and the CUDA cores only
 //      dequantise; each block takes a contiguous share of the items;
