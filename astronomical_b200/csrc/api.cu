@@ -180,8 +180,12 @@ struct astro_moe_pager {
   cudaStream_t copy = nullptr;
   cudaEvent_t ready = nullptr;
   uint32_t* h_offsets = nullptr;  // pinned [E + 2]
-  uint32_t* h_table = nullptr;    // pinned [E]
-  uint32_t* d_table = nullptr;    // device [E]
+  // slot tables of the two launches of a paged layer: [0, E) the experts whose
+  // pages were resident (computed while the missing pages copy), [E, 2E) the
+  // experts whose pages were copied in; kSlotElsewhere marks the other launch's
+  uint32_t* h_table = nullptr;    // pinned [2E]
+  uint32_t* d_table = nullptr;    // device [2E]
+  std::vector<uint8_t> missed;    // [E] this call copied the expert's page
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending, spare;
   astro_moe_pager_stats st{};
 };
@@ -694,6 +698,7 @@ int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs) {
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   for (int e = 0; e < pg->E; ++e) {
     pg->h_table[e] = 0;
+    pg->missed[e] = 0;
     if (offs[e + 1] <= offs[e]) continue;
     const int64_t page = (int64_t)layer * pg->E + e;
     pg->st.lookups += 1;
@@ -735,9 +740,17 @@ int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs) {
                       (size_t)pg->page_bytes, cudaMemcpyHostToDevice, pg->copy);
       pg->st.bytes_h2d += pg->page_bytes;
       copies += 1;
+      pg->missed[e] = 1;
     }
     pg->last_call[slot] = pg->call;
     pg->h_table[e] = (uint32_t)slot;
+  }
+  // a slot that this call touched is never evicted by it, so the resident
+  // experts' slots stay valid while the copies land
+  for (int e = 0; e < pg->E; ++e) {
+    const uint32_t slot = pg->h_table[e];
+    pg->h_table[pg->E + e] = pg->missed[e] ? slot : astro::kSlotElsewhere;
+    if (pg->missed[e]) pg->h_table[e] = astro::kSlotElsewhere;
   }
   if (copies) {
     cudaEventRecord(e1, pg->copy);
@@ -778,11 +791,13 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
   CK(cudaMemcpyAsync(pg->h_offsets, b.offsets, sizeof(uint32_t) * (E + 2), cudaMemcpyDeviceToHost, st),
      "read back expert offsets");
   CK(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-  admit_pages(pg, layer, pg->h_offsets);
-  CK(cudaMemcpyAsync(pg->d_table, pg->h_table, sizeof(uint32_t) * E, cudaMemcpyHostToDevice, pg->copy),
-     "slot table");
-  CK(cudaEventRecord(pg->ready, pg->copy), op);
-  CK(cudaStreamWaitEvent(st, pg->ready, 0), op);
+  const int64_t copies = admit_pages(pg, layer, pg->h_offsets);
+  // the slot tables travel on the compute stream (the next layer's read-back
+  // sync covers them before the host rewrites the pinned copy); the experts whose
+  // pages are resident are computed while the missing pages copy
+  CK(cudaMemcpyAsync(pg->d_table, pg->h_table, sizeof(uint32_t) * 2 * E, cudaMemcpyHostToDevice, st),
+     "slot tables");
+  if (copies) CK(cudaEventRecord(pg->ready, pg->copy), op);
   astro::GroupedGemvDesc d;
   d.x = x;
   d.x_rows = b.stok;
@@ -808,7 +823,6 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
   d.status = ctx->status;
   d.slot_of = pg->d_table;
   const int64_t max_active = (N < E ? N : E) + (has_shared ? 1 : 0);
-  CK(astro::launch_decode_gate_up(d, max_active, st), "gate/up projection");
   astro::GroupedGemvDesc dd = d;
   dd.x = b.act;
   dd.x_rows = nullptr;
@@ -821,11 +835,20 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
   dd.swiglu = false;
   dd.y = b.yrows;
   dd.ldy = H;
+  // resident experts and the shared expert, then (after the copies) the rest
+  CK(astro::launch_decode_gate_up(d, max_active, st), "gate/up projection");
   CK(astro::launch_decode_down(dd, max_active, st), "down projection");
+  if (copies) {
+    CK(cudaStreamWaitEvent(st, pg->ready, 0), op);
+    d.slot_of = dd.slot_of = pg->d_table + E;
+    d.skip_shared = dd.skip_shared = true;
+    CK(astro::launch_decode_gate_up(d, max_active, st), "gate/up projection (copied pages)");
+    CK(astro::launch_decode_down(dd, max_active, st), "down projection (copied pages)");
+  }
   CK(astro::launch_block_combine(b.yrows, b.inverse, b.scores, has_shared ? b.gate_logit : nullptr,
                                  N, T, K, H, N >= threshold ? 1 : 0, out, st),
      "weighted combine");
-  ctx->launches += 6 + astro::sort_launch_count(N);
+  ctx->launches += 6 + (copies ? 2 : 0) + astro::sort_launch_count(N);
   return ASTRO_MOE_OK;
 }
 
@@ -1520,6 +1543,7 @@ int astro_moe_pager_create(astro_moe_ctx* ctx, int32_t layers, int32_t experts, 
   pg->slot_of_page.assign((size_t)layers * experts, -1);
   pg->page_of_slot.assign((size_t)slots, -1);
   pg->last_call.assign((size_t)slots, -1);
+  pg->missed.assign((size_t)experts, 0);
   pg->lru_pos.resize((size_t)slots);
   pg->st.capacity_pages = slots;
   auto cleanup = [&](cudaError_t e, const char* what) {
@@ -1534,8 +1558,8 @@ int astro_moe_pager_create(astro_moe_ctx* ctx, int32_t layers, int32_t experts, 
   };
   cudaError_t e;
   if ((e = cudaMalloc(&pg->pool, (size_t)(slots * page))) != cudaSuccess) return cleanup(e, "cudaMalloc(page cache)");
-  if ((e = cudaMalloc(&pg->d_table, sizeof(uint32_t) * experts)) != cudaSuccess) return cleanup(e, "cudaMalloc(slot table)");
-  if ((e = cudaHostAlloc(&pg->h_table, sizeof(uint32_t) * experts, cudaHostAllocDefault)) != cudaSuccess)
+  if ((e = cudaMalloc(&pg->d_table, sizeof(uint32_t) * 2 * experts)) != cudaSuccess) return cleanup(e, "cudaMalloc(slot table)");
+  if ((e = cudaHostAlloc(&pg->h_table, sizeof(uint32_t) * 2 * experts, cudaHostAllocDefault)) != cudaSuccess)
     return cleanup(e, "cudaHostAlloc(slot table)");
   if ((e = cudaHostAlloc(&pg->h_offsets, sizeof(uint32_t) * (experts + 2), cudaHostAllocDefault)) != cudaSuccess)
     return cleanup(e, "cudaHostAlloc(offsets)");

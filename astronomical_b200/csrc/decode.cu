@@ -104,16 +104,20 @@ ASTRO_DEVINL float half_warp_sum(float v) {
   return v;
 }
 
-// Compacts the non-empty segments of offsets[0..nseg] (ascending) into `list`;
-// returns their count.  Called by every thread of the block.
+// Compacts the non-empty segments of offsets[0..nseg] (ascending) into `list`,
+// leaving out routed segments whose slot is kSlotElsewhere and, with
+// skip_shared, the shared segment; returns their count.  Called by every thread
+// of the block.
 template <int NT>
 ASTRO_DEVINL int active_segments(const uint32_t* __restrict__ offsets, int nseg, uint16_t* list,
-                                 int* warp_cnt) {
+                                 int* warp_cnt, const uint32_t* slot_of, int shared_seg,
+                                 bool skip_shared) {
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   int base = 0;
   for (int s0 = 0; s0 < nseg; s0 += NT) {
     const int s = s0 + threadIdx.x;
-    const bool ne = s < nseg && offsets[s + 1] > offsets[s];
+    bool ne = s < nseg && offsets[s + 1] > offsets[s];
+    if (ne) ne = s == shared_seg ? !skip_shared : !(slot_of && slot_of[s] == kSlotElsewhere);
     const uint32_t bal = __ballot_sync(0xffffffffu, ne);
     if (lane == 0) warp_cnt[w] = __popc(bal);
     __syncthreads();
@@ -259,7 +263,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_gate_up_kernel(Grouped
   extern __shared__ uint4 xs[];  // [kRowChunkGU][H / 8]
   __shared__ uint16_t list[kMaxSegs];
   __shared__ int warp_cnt[kGemvWarps];
-  const int n_act = active_segments<kGemvThreads>(d.seg_offsets, d.nseg, list, warp_cnt);
+  const int n_act = active_segments<kGemvThreads>(d.seg_offsets, d.nseg, list, warp_cnt, d.slot_of,
+                                                  d.shared_seg, d.skip_shared);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   constexpr int H = 1024 * STEPS;
   constexpr int kVecs = H / 8, kWords = H / 8, kGroups = H / 64;
@@ -339,7 +344,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_down_kernel(GroupedGem
   extern __shared__ uint4 xs[];  // [kRowChunk][K / 8]
   __shared__ uint16_t list[kMaxSegs];
   __shared__ int warp_cnt[kGemvWarps];
-  const int n_act = active_segments<kGemvThreads>(d.seg_offsets, d.nseg, list, warp_cnt);
+  const int n_act = active_segments<kGemvThreads>(d.seg_offsets, d.nseg, list, warp_cnt, d.slot_of,
+                                                  d.shared_seg, d.skip_shared);
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int half = lane >> 4, li = lane & 15;
   constexpr int K = 512 * STEPS;

@@ -89,9 +89,12 @@ struct GroupedGemvDesc {
   int64_t ldy = 0;
   uint32_t* status = nullptr;
   // decode GEMVs only: routed segment e reads expert slot slot_of[e] of wa/wb
-  // (expert paging); nullptr = slot e
+  // (expert paging); nullptr = slot e.  A slot of kSlotElsewhere leaves the
+  // segment to another launch, and skip_shared leaves the shared expert to one.
   const uint32_t* slot_of = nullptr;
+  bool skip_shared = false;
 };
+constexpr uint32_t kSlotElsewhere = 0xffffffffu;
 
 cudaError_t launch_grouped_gemv(const GroupedGemvDesc& d, cudaStream_t st);
 
