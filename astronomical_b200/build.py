@@ -42,16 +42,38 @@ def needs_build() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compiles every .cu to an object in parallel, then links the shared library."""
     if not force and not needs_build():
         return LIB
     env = dict(os.environ)
     # nvcc's host compiler: the system gcc (an environment CC may point elsewhere)
     ccbin = ["-ccbin", "/usr/bin/g++"] if os.path.exists("/usr/bin/g++") else []
+    objdir = os.path.join(HERE, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+    jobs = []
+    for src in sources():
+        obj = os.path.join(objdir, os.path.basename(src)[:-3] + ".o")
+        cmd = [nvcc(), *compile_flags, *ccbin, "-I", os.path.join(ROOT, "include"), "-c", "-o",
+               obj, src]
+        if verbose:
+            print(" ".join(cmd), file=sys.stderr)
+        jobs.append((cmd, obj))
+    from concurrent.futures import ThreadPoolExecutor
+
+    with ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
+        results = list(ex.map(lambda j: subprocess.run(j[0], env=env, capture_output=True,
+                                                       text=True), jobs))
+    for (cmd, _), r in zip(jobs, results):
+        if r.returncode != 0:
+            sys.stderr.write(r.stdout + r.stderr)
+            raise subprocess.CalledProcessError(r.returncode, cmd)
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, *ccbin, "-I", os.path.join(ROOT, "include"), "-o", tmp, *sources()]
+    link = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", *ccbin, "-o", tmp,
+            *[o for _, o in jobs]]
     if verbose:
-        print(" ".join(cmd), file=sys.stderr)
-    subprocess.run(cmd, check=True, env=env)
+        print(" ".join(link), file=sys.stderr)
+    subprocess.run(link, check=True, env=env)
     os.replace(tmp, LIB)
     return LIB
 
