@@ -134,6 +134,164 @@ float ao_sigmoidf(float x) {
 }
 
 /* ------------------------------------------------------------------------ */
+/* accumulation arithmetic of a dot product                                  */
+/* ------------------------------------------------------------------------ */
+
+static inline int f_exp(float v) { return (int)((f2u(v) >> 23) & 0xffu) - 127; }
+
+/* 2^e for -1022 <= e <= 1023 */
+static inline double pow2d(int e) {
+  const uint64_t u = (uint64_t)(e + 1023) << 52;
+  double d;
+  memcpy(&d, &u, 8);
+  return d;
+}
+
+/* Tensor-core step (see the header): exact products truncated toward zero at
+ * 2^(emax - 25), exact sum, the sum rounded toward zero to 24 bits.  Every term
+ * is an integer multiple of the quantum below 2^27 of it, so the double sum of
+ * the 17 terms is exact; clearing the low 29 of the sum's 52 stored mantissa
+ * bits keeps its 24 leading bits (rounding toward zero).  idx (NULL: 0..15)
+ * lists the 16 element positions the step takes. */
+static float tc_step_idx(float c, const float* a, const float* b, const int* idx) {
+  int emax = -100000;
+  for (int i = 0; i < 16; ++i) {
+    const int k = idx ? idx[i] : i;
+    const int e = (a[k] != 0.0f && b[k] != 0.0f) ? f_exp(a[k]) + f_exp(b[k]) : -100000;
+    emax = e > emax ? e : emax;
+  }
+  if (c != 0.0f && f_exp(c) > emax) emax = f_exp(c);
+  if (emax == -100000) return 0.0f;
+  const double up = pow2d(25 - emax);
+  double sum = 0.0;
+  for (int i = 0; i < 16; ++i) {
+    const int k = idx ? idx[i] : i;
+    sum += trunc((double)a[k] * (double)b[k] * up); /* zero products add 0 */
+  }
+  if (c != 0.0f) sum += trunc((double)c * up);
+  uint64_t u;
+  memcpy(&u, &sum, 8);
+  u &= ~(((uint64_t)1 << 29) - 1u);
+  memcpy(&sum, &u, 8);
+  return (float)(sum * pow2d(emax - 25));
+}
+
+float ao_tc_step(float c, const float* a, const float* b) { return tc_step_idx(c, a, b, NULL); }
+
+void ao_tc_chain_batch(const float* a, const float* b, const float* c, int64_t count, int64_t n,
+                       float* out) {
+#pragma omp parallel for schedule(static)
+  for (int64_t i = 0; i < count; ++i) {
+    float acc = c ? c[i] : 0.0f;
+    for (int64_t k = 0; k + 16 <= n; k += 16)
+      acc = tc_step_idx(acc, a + i * n + k, b + i * n + k, NULL);
+    out[i] = acc;
+  }
+}
+
+/* partial[0] after a butterfly over L lanes (partial[l] + partial[l ^ m]). */
+static float butterfly(float* part, int L) {
+  for (int m = L / 2; m >= 1; m >>= 1) {
+    float nxt[32];
+    for (int l = 0; l < L; ++l) nxt[l] = part[l] + part[l ^ m];
+    for (int l = 0; l < L; ++l) part[l] = nxt[l];
+  }
+  return part[0];
+}
+
+float ao_dot(const float* a, const float* b, int64_t n, int mode) {
+  switch (mode) {
+    case AO_DOT_TC: {
+      float acc = 0.0f;
+      for (int64_t k = 0; k + 16 <= n; k += 16) acc = tc_step_idx(acc, a + k, b + k, NULL);
+      return acc;
+    }
+    case AO_DOT_TC_QUARTERS: {
+      static const int kSet[4][16] = {
+          {0, 1, 4, 5, 16, 17, 20, 21, 32, 33, 36, 37, 48, 49, 52, 53},
+          {2, 3, 6, 7, 18, 19, 22, 23, 34, 35, 38, 39, 50, 51, 54, 55},
+          {8, 9, 12, 13, 24, 25, 28, 29, 40, 41, 44, 45, 56, 57, 60, 61},
+          {10, 11, 14, 15, 26, 27, 30, 31, 42, 43, 46, 47, 58, 59, 62, 63}};
+      const int64_t ql = n / 4;
+      float v = 0.0f;
+      for (int q = 0; q < 4; ++q) {
+        float acc = 0.0f;
+        for (int64_t g0 = q * ql; g0 < (q + 1) * ql; g0 += 64)
+          for (int s = 0; s < 4; ++s) acc = tc_step_idx(acc, a + g0, b + g0, kSet[s]);
+        v = v + acc;
+      }
+      return v;
+    }
+    case AO_DOT_SLICES8: {
+      const int64_t slen = n / 8, svecs = slen / 8, per_lane = (svecs + 31) / 32;
+      float v = 0.0f;
+      for (int sl = 0; sl < 8; ++sl) {
+        float part[32];
+        for (int l = 0; l < 32; ++l) {
+          float p = 0.0f;
+          for (int64_t kk = 0; kk < per_lane; ++kk) {
+            const int64_t vi = kk * 32 + l;
+            if (vi >= svecs) continue;
+            const int64_t base = sl * slen + vi * 8;
+            for (int i = 0; i < 8; ++i) p = fmaf(a[base + i], b[base + i], p);
+          }
+          part[l] = p;
+        }
+        v = v + butterfly(part, 32);
+      }
+      return v;
+    }
+    case AO_DOT_LANES8: {
+      float part[32];
+      for (int l = 0; l < 32; ++l) {
+        float p = 0.0f;
+        for (int64_t c = l; c < n / 8; c += 32)
+          for (int i = 0; i < 8; ++i) p = fmaf(a[c * 8 + i], b[c * 8 + i], p);
+        part[l] = p;
+      }
+      return butterfly(part, 32);
+    }
+    case AO_DOT_DECODE32:
+    case AO_DOT_DECODE16: {
+      const int L = mode == AO_DOT_DECODE32 ? 32 : 16;
+      const int64_t step = 32 * (int64_t)L;
+      float part[32];
+      for (int l = 0; l < L; ++l) {
+        float p = 0.0f;
+        for (int64_t s0 = 0; s0 + step <= n; s0 += step)
+          for (int c = 0; c < 4; ++c) {
+            const int64_t base = s0 + 32 * l + 8 * c;
+            for (int i = 0; i < 4; ++i) {
+              p = fmaf(a[base + i], b[base + i], p);
+              p = fmaf(a[base + i + 4], b[base + i + 4], p);
+            }
+          }
+        part[l] = p;
+      }
+      return butterfly(part, L);
+    }
+    case AO_DOT_CHUNK32: {
+      const int64_t chunks = n / 32;
+      int L = 32;
+      while (L > chunks && L > 1) L >>= 1;
+      float part[32];
+      for (int l = 0; l < L; ++l) {
+        float p = 0.0f;
+        for (int64_t c = l; c < chunks; c += L)
+          for (int j = 0; j < 32; ++j) p = fmaf(a[c * 32 + j], b[c * 32 + j], p);
+        part[l] = p;
+      }
+      return butterfly(part, L);
+    }
+    default: {
+      float acc = 0.0f;
+      for (int64_t k = 0; k < n; ++k) acc = fmaf(a[k], b[k], acc);
+      return acc;
+    }
+  }
+}
+
+/* ------------------------------------------------------------------------ */
 /* a1: dense bf16 projection                                                 */
 /* ------------------------------------------------------------------------ */
 
@@ -150,6 +308,28 @@ void ao_matmul_bf16_nt(const uint16_t* x, const uint16_t* w, int64_t rows, int64
       out[r * cols + c] = ao_f32_to_bf16(acc);
     }
   }
+}
+
+void ao_matmul_bf16_nt_mode(const uint16_t* x, const uint16_t* w, int64_t rows, int64_t cols,
+                            int64_t depth, int mode, uint16_t* out) {
+  if (mode == AO_DOT_SEQ) {
+    ao_matmul_bf16_nt(x, w, rows, cols, depth, out);
+    return;
+  }
+  float* wf = (float*)malloc(sizeof(float) * (size_t)(cols > 0 ? cols : 1) * (size_t)depth);
+  for (int64_t i = 0; i < cols * depth; ++i) wf[i] = ao_bf16_to_f32(w[i]);
+#pragma omp parallel
+  {
+    float* xf = (float*)malloc(sizeof(float) * (size_t)(depth > 0 ? depth : 1));
+#pragma omp for schedule(static)
+    for (int64_t r = 0; r < rows; ++r) {
+      for (int64_t k = 0; k < depth; ++k) xf[k] = ao_bf16_to_f32(x[r * depth + k]);
+      for (int64_t c = 0; c < cols; ++c)
+        out[r * cols + c] = ao_f32_to_bf16(ao_dot(wf + c * depth, xf, depth, mode));
+    }
+    free(xf);
+  }
+  free(wf);
 }
 
 /* ------------------------------------------------------------------------ */
@@ -481,6 +661,67 @@ void ao_combine_sparse_and_shared(const void* sparse, const void* shared, const 
 /* a9: whole block                                                           */
 /* ------------------------------------------------------------------------ */
 
+typedef struct {
+  const uint32_t* q;
+  const uint16_t* s;
+  const uint16_t* b;
+  int bits, group;
+} proj_t;
+
+/* projection `which` (0 gate, 1 up, 2 down, 3 shared gate, 4 shared up, 5 shared
+ * down) with its own quantisation (qwen3_5/model/decoder_layer_weights.rs:15-26) */
+static proj_t proj_of(const ao_block_weights* w, int which) {
+  proj_t p;
+  switch (which) {
+    case 0: p.q = w->gate_q; p.s = w->gate_s; p.b = w->gate_b; break;
+    case 1: p.q = w->up_q; p.s = w->up_s; p.b = w->up_b; break;
+    case 2: p.q = w->down_q; p.s = w->down_s; p.b = w->down_b; break;
+    case 3: p.q = w->sgate_q; p.s = w->sgate_s; p.b = w->sgate_b; break;
+    case 4: p.q = w->sup_q; p.s = w->sup_s; p.b = w->sup_b; break;
+    default: p.q = w->sdown_q; p.s = w->sdown_s; p.b = w->sdown_b; break;
+  }
+  p.bits = w->proj_bits[which] > 0 ? w->proj_bits[which] : w->bits;
+  p.group = w->proj_group[which] > 0 ? w->proj_group[which] : w->group;
+  return p;
+}
+
+/* y[r] = bf16(x_row(r) . dequant(W[e])^T) for n rows of one expert, in `mode`. */
+static void expert_rows(const proj_t* P, int e, int out_features, int in_features,
+                        const uint16_t* const* xrows, int64_t n, int mode, uint16_t* y,
+                        int64_t ldy) {
+  if (n == 0) return;
+  if (mode == AO_DOT_SEQ) {
+    float* acc = (float*)malloc(sizeof(float) * (size_t)out_features);
+    float* wt = dequant_expert_transposed(P->q, P->s, P->b, e, out_features, in_features,
+                                          P->group, P->bits);
+    for (int64_t r = 0; r < n; ++r) rows_times_wt(xrows[r], wt, in_features, out_features, acc, y + r * ldy);
+    free(wt);
+    free(acc);
+    return;
+  }
+  float* wf = (float*)malloc(sizeof(float) * (size_t)out_features * in_features);
+  float* xf = (float*)malloc(sizeof(float) * (size_t)in_features);
+  dequant_rows_f32(P->q, P->s, P->b, (int64_t)e * out_features, out_features, in_features,
+                   P->group, P->bits, wf);
+  for (int64_t r = 0; r < n; ++r) {
+    for (int k = 0; k < in_features; ++k) xf[k] = ao_bf16_to_f32(xrows[r][k]);
+    for (int o = 0; o < out_features; ++o)
+      y[r * ldy + o] = ao_f32_to_bf16(ao_dot(wf + (int64_t)o * in_features, xf, in_features, mode));
+  }
+  free(xf);
+  free(wf);
+}
+
+/* bf16 [rows, in] weight of a dense-or-affine projection (the affine one
+ * dequantised: the weight MLX's quantized matmul multiplies); caller frees. */
+static uint16_t* dense_or_affine(const uint16_t* dense, const uint32_t* q, const uint16_t* sc,
+                                 const uint16_t* bi, int bits, int group, int64_t rows, int in) {
+  uint16_t* out = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)rows * in);
+  if (bits > 0) ao_dequantize_affine(q, sc, bi, rows, in, group, bits, out);
+  else memcpy(out, dense, sizeof(uint16_t) * (size_t)rows * in);
+  return out;
+}
+
 int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t tokens,
                          const int64_t* token_subset, int64_t n_subset,
                          const uint16_t* logits_override, uint16_t* out,
@@ -495,10 +736,20 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
                                uint32_t* out_ids, uint16_t* out_scores, uint16_t* out_sparse,
                                uint16_t* out_shared_gated, int num_threads) {
   const int H = w->hidden, E = w->experts, K = w->top_k, I = w->intermediate;
-  const int Is = w->shared_intermediate, G = w->group, B = w->bits;
+  const int Is = w->shared_intermediate;
   if (tokens < 0 || H <= 0 || E <= 0 || K <= 0 || K > E || I <= 0 || Is < 0)
     return AO_ERR_INVALID_ARGUMENT;
-  if (!valid_affine(H, G, B) || !valid_affine(I, G, B) || (Is > 0 && !valid_affine(Is, G, B)))
+  proj_t P[6];
+  for (int i = 0; i < 6; ++i) P[i] = proj_of(w, i);
+  if (!valid_affine(H, P[0].group, P[0].bits) || !valid_affine(H, P[1].group, P[1].bits) ||
+      !valid_affine(I, P[2].group, P[2].bits))
+    return AO_ERR_INVALID_ARGUMENT;
+  if (Is > 0 && (!valid_affine(H, P[3].group, P[3].bits) || !valid_affine(H, P[4].group, P[4].bits) ||
+                 !valid_affine(Is, P[5].group, P[5].bits)))
+    return AO_ERR_INVALID_ARGUMENT;
+  if (w->router_bits > 0 && !valid_affine(H, w->router_group, w->router_bits))
+    return AO_ERR_INVALID_ARGUMENT;
+  if (Is > 0 && w->shared_gate_bits > 0 && !valid_affine(H, w->shared_gate_group, w->shared_gate_bits))
     return AO_ERR_INVALID_ARGUMENT;
 #ifdef _OPENMP
   if (num_threads > 0) omp_set_num_threads(num_threads);
@@ -508,6 +759,8 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
   const int64_t nt = token_subset ? n_subset : tokens;
   /* routing.rs:13 / resident_execution.rs:86-96: sorted iff T*K >= 64 */
   const int sorted = tokens * (int64_t)K >= 64;
+  const int m_router = w->arith[0], m_glogit = w->arith[1], m_gu = w->arith[2],
+            m_down = w->arith[3], m_sgu = w->arith[4], m_sdown = w->arith[5];
 
   uint16_t* xs = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * H);
   uint16_t* logits = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * E);
@@ -516,8 +769,14 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
     memcpy(xs + i * H, x + t * H, sizeof(uint16_t) * H);
     if (logits_override) memcpy(logits + i * E, logits_override + t * E, sizeof(uint16_t) * E);
   }
-  /* a1: router projection (forward.rs:52-93) */
-  if (!logits_override) ao_matmul_bf16_nt(xs, w->router_w, nt, E, H, logits);
+  /* a1: router projection (forward.rs:52-93; an affine router goes through
+   * quantized_linear, :53-58) */
+  if (!logits_override) {
+    uint16_t* wr = dense_or_affine(w->router_w, w->router_q, w->router_s, w->router_b,
+                                   w->router_bits, w->router_group, E, H);
+    ao_matmul_bf16_nt_mode(xs, wr, nt, E, H, m_router, logits);
+    free(wr);
+  }
   /* a2: route (routing.rs:16-49) */
   uint32_t* ids = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(nt > 0 ? nt : 1) * K);
   uint16_t* scores = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * K);
@@ -536,23 +795,22 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
   uint16_t* yrows = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(n > 0 ? n : 1) * H);
 #pragma omp parallel for schedule(dynamic, 1)
   for (int e = 0; e < E; ++e) {
-    const int64_t r0 = offs[e], r1 = offs[e + 1];
-    if (r1 == r0) continue;
-    float* wg = dequant_expert_transposed(w->gate_q, w->gate_s, w->gate_b, e, I, H, G, B);
-    float* wu = dequant_expert_transposed(w->up_q, w->up_s, w->up_b, e, I, H, G, B);
-    float* wd = dequant_expert_transposed(w->down_q, w->down_s, w->down_b, e, H, I, G, B);
-    float* acc = (float*)malloc(sizeof(float) * (size_t)(H > I ? H : I));
-    uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)I);
-    uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)I);
-    uint16_t* a = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)I);
-    for (int64_t r = r0; r < r1; ++r) {
-      const uint16_t* xr = xs + (int64_t)stok[r] * H;
-      rows_times_wt(xr, wg, H, I, acc, g);
-      rows_times_wt(xr, wu, H, I, acc, u);
-      ao_swiglu(g, u, I, a);
-      rows_times_wt(a, wd, I, H, acc, yrows + r * H);
+    const int64_t r0 = offs[e], r1 = offs[e + 1], m = r1 - r0;
+    if (m == 0) continue;
+    const uint16_t** xr = (const uint16_t**)malloc(sizeof(uint16_t*) * (size_t)m);
+    const uint16_t** ar = (const uint16_t**)malloc(sizeof(uint16_t*) * (size_t)m);
+    uint16_t* g = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)m * I);
+    uint16_t* u = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)m * I);
+    uint16_t* a = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)m * I);
+    for (int64_t r = 0; r < m; ++r) {
+      xr[r] = xs + (int64_t)stok[r0 + r] * H;
+      ar[r] = a + r * I;
     }
-    free(a); free(u); free(g); free(acc); free(wd); free(wu); free(wg);
+    expert_rows(&P[0], e, I, H, xr, m, m_gu, g, I);
+    expert_rows(&P[1], e, I, H, xr, m, m_gu, u, I);
+    ao_swiglu(g, u, m * I, a);
+    expert_rows(&P[2], e, H, I, ar, m, m_down, yrows + r0 * H, H);
+    free(a); free(u); free(g); free(ar); free(xr);
   }
 
   /* a7: weighted sum (sorted kernel, or unsorted multiply+sum for N < 64) */
@@ -573,16 +831,30 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
 
   /* a8: shared expert + sigmoid gate (resident_execution.rs:352-400) */
   if (Is > 0) {
-    uint16_t* sg = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * Is);
-    uint16_t* su = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * Is);
-    uint16_t* sa = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * Is);
-    uint16_t* so = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * H);
-    uint16_t* gl = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1));
-    ao_gather_qmm(xs, NULL, NULL, nt, H, w->sgate_q, w->sgate_s, w->sgate_b, 1, Is, G, B, sg);
-    ao_gather_qmm(xs, NULL, NULL, nt, H, w->sup_q, w->sup_s, w->sup_b, 1, Is, G, B, su);
-    ao_swiglu(sg, su, nt * Is, sa);
-    ao_gather_qmm(sa, NULL, NULL, nt, Is, w->sdown_q, w->sdown_s, w->sdown_b, 1, H, G, B, so);
-    ao_matmul_bf16_nt(xs, w->shared_gate_w, nt, 1, H, gl);
+    const int64_t nn = nt > 0 ? nt : 1;
+    uint16_t* sg = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)nn * Is);
+    uint16_t* su = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)nn * Is);
+    uint16_t* sa = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)nn * Is);
+    uint16_t* so = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)nn * H);
+    uint16_t* gl = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)nn);
+#pragma omp parallel for schedule(dynamic, 1)
+    for (int64_t t0 = 0; t0 < nt; t0 += 64) {
+      const int64_t m = (nt - t0 < 64) ? nt - t0 : 64;
+      const uint16_t* xr[64];
+      const uint16_t* ar[64];
+      for (int64_t r = 0; r < m; ++r) {
+        xr[r] = xs + (t0 + r) * H;
+        ar[r] = sa + (t0 + r) * Is;
+      }
+      expert_rows(&P[3], 0, Is, H, xr, m, m_sgu, sg + t0 * Is, Is);
+      expert_rows(&P[4], 0, Is, H, xr, m, m_sgu, su + t0 * Is, Is);
+      ao_swiglu(sg + t0 * Is, su + t0 * Is, m * Is, sa + t0 * Is);
+      expert_rows(&P[5], 0, H, Is, ar, m, m_sdown, so + t0 * H, H);
+    }
+    uint16_t* wg = dense_or_affine(w->shared_gate_w, w->shared_gate_q, w->shared_gate_s,
+                                   w->shared_gate_b, w->shared_gate_bits, w->shared_gate_group, 1, H);
+    ao_matmul_bf16_nt_mode(xs, wg, nt, 1, H, m_glogit, gl);
+    free(wg);
     ao_combine_sparse_and_shared(sparse, so, gl, AO_BF16, nt, H, out);
     if (out_shared_gated) {
       for (int64_t t = 0; t < nt; ++t) {

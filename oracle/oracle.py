@@ -71,6 +71,11 @@ def _declare(l: ctypes.CDLL) -> None:
     l.ao_moe_block_forward.restype = I
     l.ao_moe_block_forward_terms.argtypes = [P, P, I64, P, I64, P, P, P, P, P, P, I]
     l.ao_moe_block_forward_terms.restype = I
+    l.ao_tc_step.argtypes, l.ao_tc_step.restype = [ctypes.c_float, P, P], ctypes.c_float
+    l.ao_dot.argtypes, l.ao_dot.restype = [P, P, I64, I], ctypes.c_float
+    l.ao_tc_chain_batch.argtypes, l.ao_tc_chain_batch.restype = [P, P, P, I64, I64, P], None
+    l.ao_matmul_bf16_nt_mode.argtypes = [P, P, I64, I64, I64, I, P]
+    l.ao_matmul_bf16_nt_mode.restype = None
 
 
 class BlockWeights(ctypes.Structure):
@@ -80,7 +85,54 @@ class BlockWeights(ctypes.Structure):
             "router_w",
             "gate_q", "gate_s", "gate_b", "up_q", "up_s", "up_b", "down_q", "down_s", "down_b",
             "sgate_q", "sgate_s", "sgate_b", "sup_q", "sup_s", "sup_b", "sdown_q", "sdown_s",
-            "sdown_b", "shared_gate_w")]
+            "sdown_b", "shared_gate_w")] + [
+        ("proj_bits", ctypes.c_int * 6), ("proj_group", ctypes.c_int * 6),
+        ("router_q", ctypes.c_void_p), ("router_s", ctypes.c_void_p), ("router_b", ctypes.c_void_p),
+        ("router_bits", ctypes.c_int), ("router_group", ctypes.c_int),
+        ("shared_gate_q", ctypes.c_void_p), ("shared_gate_s", ctypes.c_void_p),
+        ("shared_gate_b", ctypes.c_void_p), ("shared_gate_bits", ctypes.c_int),
+        ("shared_gate_group", ctypes.c_int), ("arith", ctypes.c_int * 6)]
+
+
+# accumulation modes of a dot product (AO_DOT_* in astro_oracle.h)
+DOT = dict(seq=0, tc=1, tc_quarters=2, slices8=3, lanes8=4, decode32=5, decode16=6, chunk32=7)
+# the order of the six modes a block takes
+ARITH_STAGES = ("router", "gate_logit", "gate_up", "down", "shared_gate_up", "shared_down")
+PROJ_NAMES = ("gate", "up", "down", "sgate", "sup", "sdown")
+
+# Accumulation arithmetic of each kernel of libastro_moe, as AO_DOT_* modes: the
+# parity tests ask the library which kernels a block call ran
+# (astro_moe_ctx_last_block_path) and run the oracle with the same arithmetic,
+# so every stage compares bit for bit.
+_ROUTER_ARITH = {"tcgen05_gemm": "tc", "fused_decode": "slices8", "router_gemv": "slices8",
+                 "simt_gemm": "seq"}
+_GATE_LOGIT_ARITH = {"fused_decode": "slices8", "route": "lanes8", "none": "seq"}
+_EXPERT_ARITH = {"tcgen05_gemm": ("tc", "tc"), "fused_decode": ("tc_quarters", "tc_quarters"),
+                 "decode_gemv": ("decode32", "decode16"), "grouped_gemv": ("chunk32", "chunk32"),
+                 "none": ("seq", "seq")}
+
+
+def arith_for_kernels(path: dict) -> dict:
+    """Oracle accumulation modes for a block call's kernels (router, gate_logit,
+    experts, shared_expert names as the library reports them)."""
+    gu, dn = _EXPERT_ARITH[path["experts"]]
+    sgu, sdn = _EXPERT_ARITH[path["shared_expert"]]
+    return dict(router=_ROUTER_ARITH[path["router"]], gate_logit=_GATE_LOGIT_ARITH[path["gate_logit"]],
+                gate_up=gu, down=dn, shared_gate_up=sgu, shared_down=sdn)
+
+
+def arith_codes(arith) -> list:
+    """arith: None (all canonical), a dict stage -> mode name, or a 6-sequence."""
+    if arith is None:
+        return [0] * 6
+    if isinstance(arith, dict):
+        unknown = set(arith) - set(ARITH_STAGES)
+        if unknown:
+            raise ValueError(f"unknown stages {sorted(unknown)}")
+        vals = [arith.get(k, "seq") for k in ARITH_STAGES]
+    else:
+        vals = list(arith)
+    return [DOT[a] if isinstance(a, str) else int(a) for a in vals]
 
 
 def _p(a):
@@ -123,11 +175,40 @@ def expf(x) -> np.ndarray:
     return out
 
 
-def matmul_bf16_nt(x, w) -> np.ndarray:
+def _mode(mode) -> int:
+    return DOT[mode] if isinstance(mode, str) else int(mode)
+
+
+def matmul_bf16_nt(x, w, mode="seq") -> np.ndarray:
+    """bf16(x . w^T) with the accumulation `mode` (a DOT name)."""
     x, w = _c(x, np.uint16), _c(w, np.uint16)
     out = np.empty((x.shape[0], w.shape[0]), np.uint16)
-    lib().ao_matmul_bf16_nt(_p(x), _p(w), x.shape[0], w.shape[0], x.shape[1], _p(out))
+    lib().ao_matmul_bf16_nt_mode(_p(x), _p(w), x.shape[0], w.shape[0], x.shape[1], _mode(mode),
+                                 _p(out))
     return out
+
+
+def tc_step(c: float, a, b) -> float:
+    """One tensor-core accumulation step over 16 bf16-valued products."""
+    a, b = _c(a, np.float32), _c(b, np.float32)
+    assert a.size == 16 and b.size == 16
+    return float(np.float32(lib().ao_tc_step(float(np.float32(c)), _p(a), _p(b))))
+
+
+def tc_chain(a, b, c=None) -> np.ndarray:
+    """a, b float32 [count, n] (bf16 values): the tensor-core step chain per row,
+    from c [count] (None: zero)."""
+    a, b = _c(a, np.float32), _c(b, np.float32)
+    count, n = a.shape
+    cc = None if c is None else _c(c, np.float32)
+    out = np.empty(count, np.float32)
+    lib().ao_tc_chain_batch(_p(a), _p(b), _p(cc), count, n, _p(out))
+    return out
+
+
+def dot(a, b, mode="seq") -> float:
+    a, b = _c(a, np.float32), _c(b, np.float32)
+    return float(np.float32(lib().ao_dot(_p(a), _p(b), a.size, _mode(mode))))
 
 
 def route_experts(logits, top_k: int, normalize: bool = True, bf16: bool = True):
@@ -238,10 +319,15 @@ def combine_sparse_and_shared(sparse, shared, gate_logits, bf16=True):
 
 
 def moe_block_forward(weights: dict, x, token_subset=None, logits_override=None,
-                      num_threads: int = 0, terms: bool = False):
+                      num_threads: int = 0, terms: bool = False, arith=None):
     """Whole block on CPU.  weights: dict from astronomical_b200.synthetic (MLX layout).
     Returns (y bf16 [n, H], ids [n, K], scores bf16 [n, K]) for the listed tokens, plus
-    (sparse, gated_shared) -- the bf16 terms of the final addition -- when terms=True."""
+    (sparse, gated_shared) -- the bf16 terms of the final addition -- when terms=True.
+    arith: accumulation modes per stage (see arith_codes); None = canonical order.
+    Optional weight keys: "<proj>_bits" / "<proj>_group" per projection
+    (gate, up, down, sgate, sup, sdown), an affine router ("router_q", "router_s",
+    "router_b", "router_bits", "router_group") and an affine shared-expert gate
+    ("shared_gate_q", .._s, .._b, .._bits, .._group)."""
     cfg = weights["config"]
     x = _c(x, np.uint16)
     T, H = x.shape
@@ -270,7 +356,17 @@ def moe_block_forward(weights: dict, x, token_subset=None, logits_override=None,
         sup_q=arr("sup_q", np.uint32), sup_s=arr("sup_s", np.uint16), sup_b=arr("sup_b", np.uint16),
         sdown_q=arr("sdown_q", np.uint32), sdown_s=arr("sdown_s", np.uint16),
         sdown_b=arr("sdown_b", np.uint16),
-        shared_gate_w=arr("shared_gate_w", np.uint16))
+        shared_gate_w=arr("shared_gate_w", np.uint16),
+        proj_bits=(ctypes.c_int * 6)(*[int(weights.get(f"{n}_bits", 0)) for n in PROJ_NAMES]),
+        proj_group=(ctypes.c_int * 6)(*[int(weights.get(f"{n}_group", 0)) for n in PROJ_NAMES]),
+        router_q=arr("router_q", np.uint32), router_s=arr("router_s", np.uint16),
+        router_b=arr("router_b", np.uint16), router_bits=int(weights.get("router_bits", 0)),
+        router_group=int(weights.get("router_group", 0)),
+        shared_gate_q=arr("shared_gate_q", np.uint32), shared_gate_s=arr("shared_gate_s", np.uint16),
+        shared_gate_b=arr("shared_gate_b", np.uint16),
+        shared_gate_bits=int(weights.get("shared_gate_bits", 0)),
+        shared_gate_group=int(weights.get("shared_gate_group", 0)),
+        arith=(ctypes.c_int * 6)(*arith_codes(arith)))
     sub = None if token_subset is None else _c(token_subset, np.int64)
     n = T if sub is None else sub.size
     K = cfg["top_k"]
