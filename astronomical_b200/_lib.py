@@ -57,6 +57,19 @@ class BlockTaps(ctypes.Structure):
                 ("selected_scores", ctypes.c_void_p), ("expert_offsets", ctypes.c_void_p)]
 
 
+# kernels a block call ran (ASTRO_MOE_KERNEL_*)
+KERNEL_NAMES = {0: "none", 1: "tcgen05_gemm", 2: "fused_decode", 3: "decode_gemv",
+                4: "grouped_gemv", 5: "router_gemv", 6: "simt_gemm", 7: "route"}
+
+
+class BlockPath(ctypes.Structure):
+    _fields_ = [("router", ctypes.c_int32), ("gate_logit", ctypes.c_int32),
+                ("experts", ctypes.c_int32), ("shared_expert", ctypes.c_int32)]
+
+    def as_dict(self):
+        return {n: KERNEL_NAMES.get(getattr(self, n), str(getattr(self, n))) for n, _ in self._fields_}
+
+
 class PagerStats(ctypes.Structure):
     _fields_ = [("lookups", ctypes.c_int64), ("hits", ctypes.c_int64), ("misses", ctypes.c_int64),
                 ("evictions", ctypes.c_int64), ("bytes_h2d", ctypes.c_int64),
@@ -85,6 +98,8 @@ SIGNATURES = {
     "astro_moe_last_error": ([], ctypes.c_char_p),
     "astro_moe_abi_version": ([], ctypes.c_int),
     "astro_moe_device_status": ([_I32, _P, _I32], ctypes.c_int),
+    "astro_moe_tensor_core_probe": ([_I32, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _P],
+                                    ctypes.c_int),
     "astro_moe_route_experts": ([_P, _I32, _I64, _I32, _I32, _I32, _P, _P, _P], ctypes.c_int),
     "astro_moe_sort_expert_assignments": ([_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P],
                                           ctypes.c_int),
@@ -114,6 +129,7 @@ SIGNATURES = {
     "astro_moe_block_forward_host": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
     "astro_moe_block_forward_host_async": ([_P, _I32, _P, _I64, _P], ctypes.c_int),
     "astro_moe_host_synchronize": ([_P], ctypes.c_int),
+    "astro_moe_ctx_last_block_path": ([_P, ctypes.POINTER(BlockPath)], ctypes.c_int),
     "astro_moe_ctx_set_attribution": ([_P, _I32], ctypes.c_int),
     "astro_moe_ctx_read_attribution": ([_P, ctypes.POINTER(Attribution), _I32], ctypes.c_int),
     "astro_moe_ep_register_layer": ([_P, _I32, ctypes.POINTER(LayerWeights), _I32, _I32],

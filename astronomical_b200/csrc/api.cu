@@ -142,6 +142,7 @@ struct astro_moe_ctx {
   std::vector<std::vector<cudaEvent_t>> pending;  // 6 events per measured call
   astro_moe_attribution acc{};
   int64_t launches = 0;
+  astro_moe_block_path last_path{};
   // expert-parallel block in flight (dispatch -> experts -> combine)
   DevBuf ep_disp, ep_exp, ep_shared;
   int ep_layer = -1;
@@ -443,6 +444,10 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     const cudaError_t e = astro::launch_decode_fused(a, st);
     if (e == cudaSuccess) {
       ctx->launches += 1;
+      ctx->last_path.router = ASTRO_MOE_KERNEL_FUSED_DECODE;
+      ctx->last_path.gate_logit = has_shared ? ASTRO_MOE_KERNEL_FUSED_DECODE : ASTRO_MOE_KERNEL_NONE;
+      ctx->last_path.experts = ASTRO_MOE_KERNEL_FUSED_DECODE;
+      ctx->last_path.shared_expert = has_shared ? ASTRO_MOE_KERNEL_FUSED_DECODE : ASTRO_MOE_KERNEL_NONE;
       marks.mark();
       marks.mark();
       marks.mark();
@@ -457,6 +462,15 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     marks.drop(2);
   }
   ctx->launches += 3 + astro::sort_launch_count(N) + (use_tc ? 3 : 2);
+  {
+    const int ek = use_tc ? ASTRO_MOE_KERNEL_TCGEN05_GEMM
+                          : (use_decode ? ASTRO_MOE_KERNEL_DECODE_GEMV : ASTRO_MOE_KERNEL_GROUPED_GEMV);
+    ctx->last_path.router = router_gemv ? ASTRO_MOE_KERNEL_ROUTER_GEMV
+                                        : (use_tc ? ASTRO_MOE_KERNEL_TCGEN05_GEMM : ASTRO_MOE_KERNEL_SIMT_GEMM);
+    ctx->last_path.gate_logit = has_shared ? ASTRO_MOE_KERNEL_ROUTE : ASTRO_MOE_KERNEL_NONE;
+    ctx->last_path.experts = ek;
+    ctx->last_path.shared_expert = has_shared ? ek : ASTRO_MOE_KERNEL_NONE;
+  }
   if (router_gemv) {
     CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, b.logits, st), "router projection");
   } else if (use_tc) {
@@ -775,6 +789,10 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
   const int64_t N = T * K;
   const int64_t rows = N + (has_shared ? T : 0);
   const int threshold = ctx->opt.sorted_threshold > 0 ? ctx->opt.sorted_threshold : 64;
+  ctx->last_path.router = L.router_gemv_ok ? ASTRO_MOE_KERNEL_ROUTER_GEMV : ASTRO_MOE_KERNEL_SIMT_GEMM;
+  ctx->last_path.gate_logit = has_shared ? ASTRO_MOE_KERNEL_ROUTE : ASTRO_MOE_KERNEL_NONE;
+  ctx->last_path.experts = ASTRO_MOE_KERNEL_DECODE_GEMV;
+  ctx->last_path.shared_expert = has_shared ? ASTRO_MOE_KERNEL_DECODE_GEMV : ASTRO_MOE_KERNEL_NONE;
   if (L.router_gemv_ok) {
     CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, b.logits, st), "router projection");
   } else {
@@ -1212,6 +1230,12 @@ int astro_moe_block_forward_taps(astro_moe_ctx* ctx, int32_t layer, const void* 
 
 int astro_moe_block_forward(astro_moe_ctx* ctx, int32_t layer, const void* x, int64_t T, void* out) {
   return astro_moe_block_forward_taps(ctx, layer, x, T, out, nullptr);
+}
+
+int astro_moe_ctx_last_block_path(astro_moe_ctx* ctx, astro_moe_block_path* out) {
+  if (!ctx || !out) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "last block path: null argument");
+  *out = ctx->last_path;
+  return ASTRO_MOE_OK;
 }
 
 int astro_moe_ctx_set_attribution(astro_moe_ctx* ctx, int32_t enabled) {

@@ -410,6 +410,13 @@ class Qwen3_5MoEBlock:
     def synchronize_host(self) -> None:
         check(_lib.lib().astro_moe_host_synchronize(self.ctx))
 
+    def last_path(self) -> dict:
+        """Kernels the last block call ran, per stage (router, gate_logit, experts,
+        shared_expert), by name."""
+        p = _lib.BlockPath()
+        check(_lib.lib().astro_moe_ctx_last_block_path(self.ctx, ctypes.byref(p)))
+        return p.as_dict()
+
     def set_attribution(self, enabled: bool) -> None:
         check(_lib.lib().astro_moe_ctx_set_attribution(self.ctx, int(enabled)))
 

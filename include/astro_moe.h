@@ -55,6 +55,21 @@ enum {
   ASTRO_MOE_DEVICE_BAD_SHAPE = 4
 };
 
+/* No counterpart in the reference.  One tensor-core accumulation on given
+ * operands, for checking the arithmetic the CPU restatement models (not on any
+ * hot path): d = c + a . b^T in fp32 with bf16 a and b, per problem.
+ *   instruction 0: tcgen05.mma kind::f16 (M = 128, N = n in {16, 32}, K = 16*k16,
+ *     k16 <= 16); a bf16 [problems][128][K], b bf16 [problems][n][K], c and d fp32
+ *     [problems][128][n]; accumulate = 0 starts from zero (c unused);
+ *     device_status (required) receives ASTRO_MOE_DEVICE_WAIT_TIMEOUT if the MMAs
+ *     do not complete within 1 s.
+ *   instruction 1: mma.sync m16n8k16 (n = 8, K = 16*k16, k16 <= 64); a [problems][16][K],
+ *     b [problems][8][K], c and d [problems][16][8]; always starts from c.
+ * K steps are issued in order, 16 at a time. */
+int astro_moe_tensor_core_probe(int32_t instruction, const void* a, const void* b, const float* c,
+                                float* d, int64_t problems, int32_t n, int32_t k16,
+                                int32_t accumulate, uint32_t* device_status, void* stream);
+
 /* Thread-local message of the last failed call; replaces the handler installed
  * by crates/runtime-integration/src/mlx_runtime/error_handling.rs:10-44. */
 const char* astro_moe_last_error(void);
@@ -251,6 +266,28 @@ typedef struct {
   double down_ms;                    /* GatheredExpertExecution: down projection */
   double weighted_reduction_ms;      /* ExpertWeightedReduction, fused with the shared expert */
 } astro_moe_attribution;
+
+/* Kernels that the last block call of a context ran, stage by stage (no
+ * counterpart in the reference, whose MLX graph hides its kernels).  A stage's
+ * accumulation order follows from its kernel, which is what the parity tests
+ * use to pick the matching arithmetic of the CPU restatement. */
+enum {
+  ASTRO_MOE_KERNEL_NONE = 0,
+  ASTRO_MOE_KERNEL_TCGEN05_GEMM = 1,  /* tcgen05 grouped GEMM / router GEMM */
+  ASTRO_MOE_KERNEL_FUSED_DECODE = 2,  /* the cooperative decode kernel (mma.sync tiles) */
+  ASTRO_MOE_KERNEL_DECODE_GEMV = 3,   /* the separate decode GEMVs */
+  ASTRO_MOE_KERNEL_GROUPED_GEMV = 4,  /* the CUDA-core grouped GEMV (every bits / group) */
+  ASTRO_MOE_KERNEL_ROUTER_GEMV = 5,   /* the router GEMV (small batches) */
+  ASTRO_MOE_KERNEL_SIMT_GEMM = 6,     /* the CUDA-core dense GEMM */
+  ASTRO_MOE_KERNEL_ROUTE = 7          /* the routing kernel (shared-expert gate dot) */
+};
+typedef struct {
+  int32_t router;         /* router logits */
+  int32_t gate_logit;     /* shared-expert gate logit (NONE without a shared expert) */
+  int32_t experts;        /* routed gate/up + SwiGLU and down projections */
+  int32_t shared_expert;  /* shared expert's projections (NONE without one) */
+} astro_moe_block_path;
+int astro_moe_ctx_last_block_path(astro_moe_ctx* ctx, astro_moe_block_path* out);
 
 int astro_moe_ctx_set_attribution(astro_moe_ctx* ctx, int32_t enabled);
 /* Synchronises, adds up the pending measurements and optionally resets them. */
