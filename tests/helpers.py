@@ -87,6 +87,40 @@ def assert_block_close(got_bits, ref_bits, terms=None):
     return max_abs, scaled, rel_l2
 
 
-__all__ = ["to_np_bf16", "to_np_u32", "bf16_tensor", "u32_tensor", "assert_bf16_ulps",
+# the oracle's accumulation arithmetic for the kernels of one block call
+from oracle.oracle import arith_for_kernels as oracle_arith  # noqa: E402
+
+
+def reference_metrics(got_bits, ref_bits):
+    """The reference's comparison convention (assert_f32_close,
+    crates/model-serving/tests/direct_mlx/sparse_expert_projection.rs:32-44):
+    |got - expected| <= tol * max(|expected|, 1).  Returns raw max-abs, the
+    largest scaled error, relative L2, the count of elements beyond 2e-2 and the
+    count of elements that differ at all."""
+    g = bf16_to_f32(got_bits).astype(np.float64)
+    r = bf16_to_f32(ref_bits).astype(np.float64)
+    if not g.size:
+        return dict(raw_max_abs=0.0, scaled_max_abs=0.0, rel_l2=0.0, n_beyond=0, n_differ=0, n=0)
+    d = np.abs(g - r)
+    scaled = d / np.maximum(np.abs(r), 1.0)
+    return dict(raw_max_abs=float(d.max()), scaled_max_abs=float(scaled.max()),
+                rel_l2=float(np.linalg.norm(g - r) / max(np.linalg.norm(r), 1e-30)),
+                n_beyond=int((scaled > MAX_ABS).sum()), n_differ=int((d > 0).sum()), n=int(d.size))
+
+
+def record_parity(case: str, **fields) -> None:
+    """Appends one JSON line to $ASTRO_PARITY_LOG (when set): the figures behind
+    the committed parity summary."""
+    import json
+    import os
+
+    path = os.environ.get("ASTRO_PARITY_LOG")
+    if not path:
+        return
+    with open(path, "a") as f:
+        f.write(json.dumps(dict(case=case, **fields)) + "\n")
+
+
+__all__ = ["oracle_arith", "reference_metrics", "record_parity", "to_np_bf16", "to_np_u32", "bf16_tensor", "u32_tensor", "assert_bf16_ulps",
            "block_metrics", "assert_block_close", "bf16_to_f32", "f32_to_bf16", "MAX_ABS",
            "REL_L2"]

@@ -68,3 +68,16 @@ def test_invert_assignment_order_on_host():
     oor = np.array([0, 2], np.uint32)
     assert L.astro_moe_invert_assignment_order(oor.ctypes.data, 2, inv.ctypes.data) == \
         _lib.ERR_OUT_OF_RANGE_SLOT
+
+
+def test_tensor_core_probe_rejects_bad_shapes_on_the_host():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(256)  # never dereferenced: rejected before any CUDA call
+    assert L.astro_moe_tensor_core_probe(0, fake, fake, fake, fake, 1, 24, 1, 0, fake, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert L.astro_moe_tensor_core_probe(0, fake, fake, fake, fake, 1, 16, 1, 0, None, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert L.astro_moe_tensor_core_probe(1, fake, fake, fake, fake, 1, 8, 65, 1, None, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert L.astro_moe_tensor_core_probe(2, fake, fake, fake, fake, 1, 8, 1, 1, None, None) == \
+        _lib.ERR_INVALID_ARGUMENT

@@ -1,15 +1,15 @@
 """Decode-path properties beyond oracle parity (which test_gpu_block covers):
 the fused decode kernel routes bit-identically to the separate decode kernels
-(up to 64 tokens) and both hold the block tolerance against the oracle, and a
-stack of block calls captured in a CUDA graph replays bit-identically to eager
-calls."""
+(up to 64 tokens) and each equals the oracle run with its own accumulation
+arithmetic bit for bit, and a stack of block calls captured in a CUDA graph
+replays bit-identically to eager calls."""
 import pytest
 
 torch = pytest.importorskip("torch")
 
 from oracle import oracle as O  # noqa: E402
 from astronomical_b200 import moe, synthetic  # noqa: E402
-from tests.helpers import assert_block_close, bf16_tensor, to_np_bf16  # noqa: E402
+from tests.helpers import bf16_tensor, oracle_arith, to_np_bf16  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 
@@ -29,8 +29,11 @@ def test_fused_decode_matches_separate_kernels(T):
     x_np = synthetic.make_hidden_states(T, 2048, seed=40 + T, zipf=True)
     x = bf16_tensor(x_np)
     ya, ta = fused.forward(x, taps=True)
+    path_a = fused.last_path()
     yb, tb = split.forward(x, taps=True)
+    path_b = split.last_path()
     torch.cuda.synchronize()
+    assert path_a["experts"] == "fused_decode" and path_b["experts"] == "decode_gemv"
     assert fused.read_attribution()["kernel_launches"] == 1
     # the two router GEMVs add in the same order: identical logits, so routing
     # and sort are bit-identical
@@ -39,12 +42,12 @@ def test_fused_decode_matches_separate_kernels(T):
     assert torch.equal(ta["selected_scores"], tb["selected_scores"])
     assert torch.equal(ta["expert_offsets"], tb["expert_offsets"])
     # the projections add their products in different orders (tensor-core tiles
-    # against fma chains): each path is held to the block tolerance against the
-    # oracle on the same logits
-    logits = to_np_bf16(ta["router_logits"])
-    y_ref, _, _, sp, sg = O.moe_block_forward(w, x_np, logits_override=logits, terms=True)
-    assert_block_close(to_np_bf16(ya), y_ref, terms=(sp, sg))
-    assert_block_close(to_np_bf16(yb), y_ref, terms=(sp, sg))
+    # against fma chains): each path equals the oracle, from x, run with its own
+    # kernels' arithmetic
+    for path, y in ((path_a, ya), (path_b, yb)):
+        arith = oracle_arith(path)
+        y_ref, _, _ = O.moe_block_forward(w, x_np, arith=arith)
+        assert (to_np_bf16(y) == y_ref).all(), arith
     fused.close()
     split.close()
 
