@@ -40,7 +40,8 @@ class Options(ctypes.Structure):
 
 class Affine(ctypes.Structure):
     _fields_ = [("packed", ctypes.c_void_p), ("scales", ctypes.c_void_p),
-                ("biases", ctypes.c_void_p)]
+                ("biases", ctypes.c_void_p), ("bits", ctypes.c_int32),
+                ("group_size", ctypes.c_int32)]
 
 
 class LayerWeights(ctypes.Structure):
@@ -49,7 +50,8 @@ class LayerWeights(ctypes.Structure):
         "bits", "normalize_top_k", "gate_up_fused")] + [
         ("router_weight", ctypes.c_void_p), ("gate", Affine), ("up", Affine), ("down", Affine),
         ("shared_gate", Affine), ("shared_up", Affine), ("shared_down", Affine),
-        ("shared_expert_gate", ctypes.c_void_p)]
+        ("shared_expert_gate", ctypes.c_void_p), ("router_affine", Affine),
+        ("shared_expert_gate_affine", Affine)]
 
 
 class BlockTaps(ctypes.Structure):
@@ -110,6 +112,7 @@ SIGNATURES = {
                               _I32, _P, _P], ctypes.c_int),
     "astro_moe_quantized_matmul": ([_P, _I64, _I32, _P, _P, _P, _I32, _I32, _I32, _P, _P],
                                    ctypes.c_int),
+    "astro_moe_dequantize_affine": ([_P, _P, _P, _I64, _I32, _I32, _I32, _P, _P], ctypes.c_int),
     "astro_moe_swiglu": ([_P, _P, _I64, _P, _P], ctypes.c_int),
     "astro_moe_sorted_expert_weighted_sum": ([_P, _I32, _P, _P, _I32, _I64, _I32, _I64, _P, _P],
                                              ctypes.c_int),

@@ -109,7 +109,21 @@ struct LayerState {
   int ep_first = 0, ep_total = 0;
   // paged layer: routed experts come from the pager's pages of this layer
   astro_moe_pager* pager = nullptr;
+  // quantisation {bits, group} of gate, up, down, shared gate, shared up, shared down
+  int qbits[6] = {}, qgroup[6] = {};
+  // shared expert quantised unlike the routed experts: it runs as its own launches
+  bool shared_separate = false;
+  // bf16 copies of an affine router / shared-expert gate, dequantised at registration
+  void* router_dense = nullptr;
+  void* sgate_dense = nullptr;
 };
+
+void release_layer(LayerState& L) {
+  astro::moe_gemm_release(L.gemm);
+  if (L.router_dense) cudaFree(L.router_dense);
+  if (L.sgate_dense) cudaFree(L.sgate_dense);
+  L.router_dense = L.sgate_dense = nullptr;
+}
 
 // Grow-only device buffer (synchronises the stream before replacing memory).
 struct DevBuf {
@@ -469,8 +483,10 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
                                         : (use_tc ? ASTRO_MOE_KERNEL_TCGEN05_GEMM : ASTRO_MOE_KERNEL_SIMT_GEMM);
     ctx->last_path.gate_logit = has_shared ? ASTRO_MOE_KERNEL_ROUTE : ASTRO_MOE_KERNEL_NONE;
     ctx->last_path.experts = ek;
-    ctx->last_path.shared_expert = has_shared ? ek : ASTRO_MOE_KERNEL_NONE;
+    ctx->last_path.shared_expert =
+        has_shared ? (L.shared_separate ? ASTRO_MOE_KERNEL_GROUPED_GEMV : ek) : ASTRO_MOE_KERNEL_NONE;
   }
+  if (L.shared_separate) ctx->launches += 2;
   if (router_gemv) {
     CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, b.logits, st), "router projection");
   } else if (use_tc) {
@@ -511,8 +527,8 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     d.x_limit = T;
     d.in_features = H;
     d.seg_offsets = b.offsets;
-    d.nseg = E + (has_shared ? 1 : 0);
-    d.shared_seg = has_shared ? E : -1;
+    d.nseg = E + (has_shared && !L.shared_separate ? 1 : 0);
+    d.shared_seg = has_shared && !L.shared_separate ? E : -1;
     d.rows_total = rows;
     if (w.gate_up_fused) {
       d.wa[0] = astro::AffineRef{w.gate.packed, w.gate.scales, w.gate.biases, 2LL * I, 0};
@@ -526,8 +542,8 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
       d.wb[1] = astro::AffineRef{w.shared_up.packed, w.shared_up.scales, w.shared_up.biases, Is, 0};
     }
     d.out_features = I;
-    d.group = w.group_size;
-    d.bits = w.bits;
+    d.group = L.qgroup[0];
+    d.bits = L.qbits[0];
     d.swiglu = true;
     d.y = b.act;
     d.y_limit = rows;
@@ -550,6 +566,8 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
       dd.wa[1] = astro::AffineRef{w.shared_down.packed, w.shared_down.scales, w.shared_down.biases, H, 0};
     dd.wb[0] = dd.wb[1] = astro::AffineRef{};
     dd.out_features = H;
+    dd.group = L.qgroup[2];
+    dd.bits = L.qbits[2];
     dd.swiglu = false;
     dd.y = b.yrows;
     dd.ldy = H;
@@ -558,6 +576,44 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     } else {
       CK(astro::launch_grouped_gemv(dd, st), "down projection");
     }
+  }
+  if (L.shared_separate) {
+    // a shared expert quantised unlike the routed experts: its own grouped-GEMV
+    // launches over its rows [N, N + T) (segment E of the sort), same outputs
+    astro::GroupedGemvDesc d;
+    d.x = x;
+    d.x_rows = b.stok;
+    d.x_limit = T;
+    d.in_features = H;
+    d.seg_offsets = b.offsets + E;
+    d.nseg = 1;
+    d.shared_seg = 0;
+    d.rows_total = rows;
+    d.wa[1] = astro::AffineRef{w.shared_gate.packed, w.shared_gate.scales, w.shared_gate.biases, Is, 0};
+    d.wb[1] = astro::AffineRef{w.shared_up.packed, w.shared_up.scales, w.shared_up.biases, Is, 0};
+    d.out_features = I;
+    d.group = L.qgroup[3];
+    d.bits = L.qbits[3];
+    d.swiglu = true;
+    d.y = b.act;
+    d.y_limit = rows;
+    d.ldy = I;
+    d.status = ctx->status;
+    CK(astro::launch_grouped_gemv(d, st), "shared expert gate/up projection");
+    astro::GroupedGemvDesc dd = d;
+    dd.x = b.act;
+    dd.x_rows = nullptr;
+    dd.x_limit = rows;
+    dd.in_features = I;
+    dd.wa[1] = astro::AffineRef{w.shared_down.packed, w.shared_down.scales, w.shared_down.biases, H, 0};
+    dd.wb[1] = astro::AffineRef{};
+    dd.out_features = H;
+    dd.group = L.qgroup[5];
+    dd.bits = L.qbits[5];
+    dd.swiglu = false;
+    dd.y = b.yrows;
+    dd.ldy = H;
+    CK(astro::launch_grouped_gemv(dd, st), "shared expert down projection");
   }
   marks.mark();
   // a7 + a8: weighted sum fused with the shared expert and its gate
@@ -572,32 +628,139 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
 
 // geometry and pointer checks of one layer's weights (register_layer and the
 // expert-parallel registration)
-int validate_layer(const char* op, const astro_moe_layer_weights* w) {
+// {bits, group} of a projection: its own when set, else the layer's
+void eff_quant(const astro_moe_affine& a, const astro_moe_layer_weights& w, int* bits, int* group) {
+  *bits = a.bits > 0 ? a.bits : w.bits;
+  *group = a.group_size > 0 ? a.group_size : w.group_size;
+}
+
+// quantisation of gate, up, down, shared gate, shared up, shared down
+void layer_quant(const astro_moe_layer_weights& w, int (&bits)[6], int (&group)[6]) {
+  eff_quant(w.gate, w, &bits[0], &group[0]);
+  if (w.gate_up_fused) {
+    bits[1] = bits[0];
+    group[1] = group[0];
+  } else {
+    eff_quant(w.up, w, &bits[1], &group[1]);
+  }
+  eff_quant(w.down, w, &bits[2], &group[2]);
+  eff_quant(w.shared_gate, w, &bits[3], &group[3]);
+  eff_quant(w.shared_up, w, &bits[4], &group[4]);
+  eff_quant(w.shared_down, w, &bits[5], &group[5]);
+}
+
+// geometry and pointer checks of one layer's weights (register_layer and the
+// expert-parallel registration); routed_stacks = false skips the routed expert
+// stacks (a paged layer's come from its pages)
+int validate_layer(const char* op, const astro_moe_layer_weights* w, bool routed_stacks = true) {
   if (w->hidden <= 0 || w->experts <= 0 || w->top_k <= 0 || w->top_k > w->experts ||
       w->intermediate <= 0 || w->shared_intermediate < 0)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid geometry", op);
   if (w->top_k > 32 || w->experts > 1024)
     return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: top_k <= 32 and experts <= 1024 are supported", op);
   if (w->hidden % 8 != 0) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: hidden must be a multiple of 8", op);
-  if (int rc = check_affine(op, w->hidden, w->group_size, w->bits)) return rc;
-  if (int rc = check_affine(op, w->intermediate, w->group_size, w->bits)) return rc;
-  if (w->shared_intermediate > 0)
-    if (int rc = check_affine(op, w->shared_intermediate, w->group_size, w->bits)) return rc;
+  int qb[6], qg[6];
+  layer_quant(*w, qb, qg);
+  if (routed_stacks) {
+    if (int rc = check_affine(op, w->hidden, qg[0], qb[0])) return rc;
+    if (int rc = check_affine(op, w->hidden, qg[1], qb[1])) return rc;
+    if (int rc = check_affine(op, w->intermediate, qg[2], qb[2])) return rc;
+    if (qb[0] != qb[1] || qg[0] != qg[1])
+      return fail(ASTRO_MOE_ERR_UNSUPPORTED,
+                  "%s: the gate and up projections must share their bits and group size", op);
+  }
+  const bool has_shared = w->shared_intermediate > 0;
+  if (has_shared) {
+    if (int rc = check_affine(op, w->hidden, qg[3], qb[3])) return rc;
+    if (int rc = check_affine(op, w->hidden, qg[4], qb[4])) return rc;
+    if (int rc = check_affine(op, w->shared_intermediate, qg[5], qb[5])) return rc;
+    if (qb[3] != qb[4] || qg[3] != qg[4])
+      return fail(ASTRO_MOE_ERR_UNSUPPORTED,
+                  "%s: the shared gate and shared up projections must share their bits and group size", op);
+  }
   if (w->shared_intermediate != 0 && w->shared_intermediate != w->intermediate)
     return fail(ASTRO_MOE_ERR_UNSUPPORTED,
                 "%s: the shared expert must have the routed intermediate width (or be absent)", op);
-  if (!w->router_weight) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight", op);
-  if (int rc = validate_affine_tensor("gate", w->gate)) return rc;
-  if (!w->gate_up_fused)
-    if (int rc = validate_affine_tensor("up", w->up)) return rc;
-  if (int rc = validate_affine_tensor("down", w->down)) return rc;
-  if (w->shared_intermediate > 0) {
+  if (!w->router_weight) {
+    if (!w->router_affine.packed)
+      return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight (bf16 or affine)", op);
+    if (int rc = validate_affine_tensor("affine router", w->router_affine)) return rc;
+    int rb, rg;
+    eff_quant(w->router_affine, *w, &rb, &rg);
+    if (int rc = check_affine(op, w->hidden, rg, rb)) return rc;
+  }
+  if (routed_stacks) {
+    if (int rc = validate_affine_tensor("gate", w->gate)) return rc;
+    if (!w->gate_up_fused)
+      if (int rc = validate_affine_tensor("up", w->up)) return rc;
+    if (int rc = validate_affine_tensor("down", w->down)) return rc;
+  }
+  if (has_shared) {
     if (int rc = validate_affine_tensor("shared gate", w->shared_gate)) return rc;
     if (int rc = validate_affine_tensor("shared up", w->shared_up)) return rc;
     if (int rc = validate_affine_tensor("shared down", w->shared_down)) return rc;
-    if (!w->shared_expert_gate) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate", op);
+    if (!w->shared_expert_gate) {
+      if (!w->shared_expert_gate_affine.packed)
+        return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate (bf16 or affine)", op);
+      if (int rc = validate_affine_tensor("affine shared expert gate", w->shared_expert_gate_affine))
+        return rc;
+      int gb, gg;
+      eff_quant(w->shared_expert_gate_affine, *w, &gb, &gg);
+      if (int rc = check_affine(op, w->hidden, gg, gb)) return rc;
+    }
   }
   return ASTRO_MOE_OK;
+}
+
+// Takes a validated layer into L: per-projection quantisation, bf16 copies of an
+// affine router / shared-expert gate (router_rows rows of the router), and the
+// weights the kernels read (L.w: dense router and gate pointers, bits / group of
+// the routed gate/up).  Synchronises the context stream after any dequantisation.
+int resolve_layer(astro_moe_ctx* ctx, const astro_moe_layer_weights* in, int router_rows,
+                  LayerState& L) {
+  release_layer(L);
+  L.w = *in;
+  layer_quant(*in, L.qbits, L.qgroup);
+  L.w.bits = L.qbits[0];
+  L.w.group_size = L.qgroup[0];
+  const bool has_shared = in->shared_intermediate > 0;
+  L.shared_separate = has_shared && (L.qbits[3] != L.qbits[0] || L.qgroup[3] != L.qgroup[0] ||
+                                     L.qbits[5] != L.qbits[2] || L.qgroup[5] != L.qgroup[2]);
+  bool sync = false;
+  if (!in->router_weight) {
+    int rb, rg;
+    eff_quant(in->router_affine, *in, &rb, &rg);
+    CK(cudaMalloc(&L.router_dense, sizeof(uint16_t) * (size_t)router_rows * in->hidden),
+       "cudaMalloc(dequantised router)");
+    CK(astro::launch_dequantize_affine(in->router_affine.packed, in->router_affine.scales,
+                                       in->router_affine.biases, router_rows, in->hidden, rg, rb,
+                                       L.router_dense, ctx->stream),
+       "dequantise router");
+    L.w.router_weight = L.router_dense;
+    sync = true;
+  }
+  if (has_shared && !in->shared_expert_gate) {
+    int gb, gg;
+    eff_quant(in->shared_expert_gate_affine, *in, &gb, &gg);
+    CK(cudaMalloc(&L.sgate_dense, sizeof(uint16_t) * (size_t)in->hidden),
+       "cudaMalloc(dequantised shared expert gate)");
+    CK(astro::launch_dequantize_affine(in->shared_expert_gate_affine.packed,
+                                       in->shared_expert_gate_affine.scales,
+                                       in->shared_expert_gate_affine.biases, 1, in->hidden, gg, gb,
+                                       L.sgate_dense, ctx->stream),
+       "dequantise shared expert gate");
+    L.w.shared_expert_gate = L.sgate_dense;
+    sync = true;
+  }
+  if (sync) CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+  return ASTRO_MOE_OK;
+}
+
+// every projection in [first, last] is 4-bit, group 64 (the tcgen05 / decode kernels)
+bool q4g64(const LayerState& L, int first, int last) {
+  for (int i = first; i <= last; ++i)
+    if (L.qbits[i] != 4 || L.qgroup[i] != 64) return false;
+  return true;
 }
 
 int devbuf_ensure(astro_moe_ctx* ctx, DevBuf& b, size_t bytes) {
@@ -1029,6 +1192,20 @@ int astro_moe_quantized_matmul(const void* x, int64_t rows, int32_t in_features,
                               1, out_features, group, bits, 1, out, stream);
 }
 
+int astro_moe_dequantize_affine(const uint32_t* packed, const void* scales, const void* biases,
+                                int64_t rows, int32_t in_features, int32_t group_size,
+                                int32_t bits, void* out, void* stream) {
+  const char* op = "dequantize affine";
+  if (rows < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: negative row count", op);
+  if (int rc = check_affine(op, in_features, group_size, bits)) return rc;
+  if (rows > 0 && (!packed || !scales || !biases || !out))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  CK(astro::launch_dequantize_affine(packed, scales, biases, rows, in_features, group_size, bits, out,
+                                     S(stream)),
+     op);
+  return ASTRO_MOE_OK;
+}
+
 int astro_moe_swiglu(const void* gate, const void* up, int64_t n, void* out, void* stream) {
   if (n < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "apply a compiled MLX SwiGLU graph: negative size");
   CK(astro::launch_swiglu(gate, up, n, out, S(stream)), "apply a compiled MLX SwiGLU graph");
@@ -1121,7 +1298,7 @@ int astro_moe_ctx_destroy(astro_moe_ctx* ctx) {
   if (!ctx) return ASTRO_MOE_OK;
   DeviceGuard g(ctx->device);
   cudaStreamSynchronize(ctx->stream);
-  for (auto& kv : ctx->layers) astro::moe_gemm_release(kv.second.gemm);
+  for (auto& kv : ctx->layers) release_layer(kv.second);
   for (auto& ev : ctx->pending)
     for (auto e : ev) cudaEventDestroy(e);
   for (auto e : ctx->event_pool) cudaEventDestroy(e);
@@ -1179,28 +1356,36 @@ int astro_moe_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_moe_
   if (int rc = validate_layer(op, w)) return rc;
   DeviceGuard g(ctx->device);
   LayerState& L = ctx->layers[layer];
-  astro::moe_gemm_release(L.gemm);
-  L.w = *w;
-  L.registered = true;
-  if (int st = astro::moe_gemm_plan(*w, &L.gemm)) {
-    L.registered = false;
-    return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);
+  L.registered = false;
+  if (int rc = resolve_layer(ctx, w, w->experts, L)) return rc;
+  const bool has_shared = w->shared_intermediate > 0;
+  // the tcgen05 kernels: routed experts 4-bit g64 (and the shared expert too, or
+  // it runs separately); the plan covers the shared expert only when it is a
+  // segment of the same launches
+  const bool routed_q4 = q4g64(L, 0, 2);
+  const bool shared_q4 = !has_shared || q4g64(L, 3, 5);
+  if (routed_q4 && (shared_q4 || L.shared_separate)) {
+    astro_moe_layer_weights view = L.w;
+    if (L.shared_separate) view.shared_intermediate = 0;
+    if (int st = astro::moe_gemm_plan(view, &L.gemm))
+      return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);
   }
+  L.registered = true;
   auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   bool weights_aligned = aligned16(w->gate.packed) && aligned16(w->down.packed) &&
                          (w->gate_up_fused || aligned16(w->up.packed));
-  if (w->shared_intermediate > 0)
+  if (has_shared)
     weights_aligned = weights_aligned && aligned16(w->shared_gate.packed) &&
                       aligned16(w->shared_up.packed) && aligned16(w->shared_down.packed);
-  L.decode_ok = weights_aligned &&
-                astro::decode_gemv_supported(w->hidden, w->intermediate, w->group_size, w->bits);
-  L.router_gemv_ok = aligned16(w->router_weight) && astro::router_gemv_supported(w->hidden);
+  L.decode_ok = weights_aligned && routed_q4 && shared_q4 && !L.shared_separate &&
+                astro::decode_gemv_supported(w->hidden, w->intermediate, 64, 4);
+  L.router_gemv_ok = aligned16(L.w.router_weight) && astro::router_gemv_supported(w->hidden);
   // the fused decode kernel reads each row's scales and biases of a K quarter as
   // one vector of up to 16 bytes
   bool sb_aligned = aligned16(w->gate.scales) && aligned16(w->gate.biases) &&
                     aligned16(w->down.scales) && aligned16(w->down.biases) &&
                     (w->gate_up_fused || (aligned16(w->up.scales) && aligned16(w->up.biases)));
-  if (w->shared_intermediate > 0)
+  if (has_shared)
     sb_aligned = sb_aligned && aligned16(w->shared_gate.scales) && aligned16(w->shared_gate.biases) &&
                  aligned16(w->shared_up.scales) && aligned16(w->shared_up.biases) &&
                  aligned16(w->shared_down.scales) && aligned16(w->shared_down.biases);
@@ -1312,21 +1497,22 @@ int astro_moe_ep_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_m
                 expert_first, expert_first + expert_count, w->experts);
   DeviceGuard g(ctx->device);
   LayerState& L = ctx->layers[layer];
-  astro::moe_gemm_release(L.gemm);
-  astro_moe_layer_weights local = *w;
-  local.experts = expert_count;
-  L.w = local;
+  L.registered = false;
+  if (int rc = resolve_layer(ctx, w, w->experts, L)) return rc;
+  if (L.shared_separate)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED,
+                "%s: the shared expert must share the routed experts' quantisation here", op);
+  L.w.experts = expert_count;
   L.ep = true;
   L.ep_first = expert_first;
   L.ep_total = w->experts;
-  L.registered = true;
   L.decode_ok = false;
   L.fused_ok = false;
-  if (int st = astro::moe_gemm_plan(local, &L.gemm, w->experts)) {
-    L.registered = false;
-    return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);
-  }
-  L.router_gemv_ok = (reinterpret_cast<uintptr_t>(w->router_weight) & 15u) == 0 &&
+  if (q4g64(L, 0, 2) && (w->shared_intermediate == 0 || q4g64(L, 3, 5)))
+    if (int st = astro::moe_gemm_plan(L.w, &L.gemm, w->experts))
+      return fail(ASTRO_MOE_ERR_CUDA, "%s: tensor-core plan failed (%d)", op, st);
+  L.registered = true;
+  L.router_gemv_ok = (reinterpret_cast<uintptr_t>(L.w.router_weight) & 15u) == 0 &&
                      astro::router_gemv_supported(w->hidden);
   return ASTRO_MOE_OK;
 }
@@ -1436,8 +1622,8 @@ static int ep_experts_compute(astro_moe_ctx* ctx, int32_t layer, const char* op,
       astro::AffineRef down[2];
       fill_projections(w, d.wa, d.wb, down);
       d.out_features = I;
-      d.group = w.group_size;
-      d.bits = w.bits;
+      d.group = L.qgroup[0];
+      d.bits = L.qbits[0];
       d.swiglu = true;
       d.y = e.act;
       d.y_limit = rows;
@@ -1451,6 +1637,8 @@ static int ep_experts_compute(astro_moe_ctx* ctx, int32_t layer, const char* op,
       dd.wa[1] = down[1];
       dd.wb[0] = dd.wb[1] = astro::AffineRef{};
       dd.out_features = H;
+      dd.group = L.qgroup[2];
+      dd.bits = L.qbits[2];
       dd.swiglu = false;
       dd.y = e.yrows;
       dd.ldy = H;
@@ -1645,27 +1833,22 @@ int astro_moe_register_paged_layer(astro_moe_ctx* ctx, int32_t layer, const astr
   if (w->experts != pg->E || w->hidden != pg->H || w->intermediate != pg->I ||
       w->group_size != pg->group || w->bits != pg->bits)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: layer geometry differs from the pager's pages", op);
-  if (w->top_k <= 0 || w->top_k > w->experts || w->top_k > 32)
-    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid top_k", op);
-  if (w->shared_intermediate != 0 && w->shared_intermediate != w->intermediate)
-    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: the shared expert must have the routed width", op);
-  if (!w->router_weight) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight", op);
-  if (w->shared_intermediate > 0) {
-    if (int rc = validate_affine_tensor("shared gate", w->shared_gate)) return rc;
-    if (int rc = validate_affine_tensor("shared up", w->shared_up)) return rc;
-    if (int rc = validate_affine_tensor("shared down", w->shared_down)) return rc;
-    if (!w->shared_expert_gate) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate", op);
-  }
+  if (int rc = validate_layer(op, w, /*routed_stacks=*/false)) return rc;
   DeviceGuard g(ctx->device);
   LayerState& L = ctx->layers[layer];
-  astro::moe_gemm_release(L.gemm);
+  release_layer(L);
   L = LayerState{};
-  L.w = *w;
-  L.w.gate = L.w.up = L.w.down = astro_moe_affine{};
-  L.w.gate_up_fused = 0;
+  astro_moe_layer_weights pw = *w;
+  pw.gate = pw.up = pw.down = astro_moe_affine{};  // the routed experts are the pages
+  pw.gate_up_fused = 0;
+  if (int rc = resolve_layer(ctx, &pw, w->experts, L)) return rc;
+  if (w->shared_intermediate > 0 && !q4g64(L, 3, 5))
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED,
+                "%s: a paged layer's shared expert must be 4-bit with group 64 (the decode kernels)", op);
+  L.shared_separate = false;
   L.registered = true;
   L.pager = pg;
-  L.router_gemv_ok = (reinterpret_cast<uintptr_t>(w->router_weight) & 15u) == 0 &&
+  L.router_gemv_ok = (reinterpret_cast<uintptr_t>(L.w.router_weight) & 15u) == 0 &&
                      astro::router_gemv_supported(w->hidden);
   return ASTRO_MOE_OK;
 }
@@ -1947,8 +2130,8 @@ int astro_moe_ep_experts_dev(astro_moe_ctx* ctx, int32_t layer, const void* x, i
     astro::AffineRef down[2];
     fill_projections(w, dsc.wa, dsc.wb, down);
     dsc.out_features = I;
-    dsc.group = w.group_size;
-    dsc.bits = w.bits;
+    dsc.group = L.qgroup[0];
+    dsc.bits = L.qbits[0];
     dsc.swiglu = true;
     dsc.y = e.act;
     dsc.y_limit = rows_cap;
@@ -1962,6 +2145,8 @@ int astro_moe_ep_experts_dev(astro_moe_ctx* ctx, int32_t layer, const void* x, i
     dd.wa[1] = down[1];
     dd.wb[0] = dd.wb[1] = astro::AffineRef{};
     dd.out_features = H;
+    dd.group = L.qgroup[2];
+    dd.bits = L.qbits[2];
     dd.swiglu = false;
     dd.y = e.yrows;
     dd.ldy = H;

@@ -141,6 +141,9 @@ cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t st);
 
 cudaError_t launch_offsets_from_sorted(const uint32_t* ids, int64_t n, int E, uint32_t* offsets,
                                        uint32_t* status, cudaStream_t st);
+cudaError_t launch_dequantize_affine(const uint32_t* packed, const void* scales,
+                                     const void* biases, int64_t rows, int in_features, int group,
+                                     int bits, void* out, cudaStream_t st);
 cudaError_t launch_compose_rows(const uint32_t* lhs, const uint32_t* order, int64_t n,
                                 uint32_t* rows_out, cudaStream_t st);
 

@@ -31,8 +31,8 @@ from typing import List, Optional, Sequence, Tuple
 import torch
 import torch.distributed as dist
 
-from . import _lib
-from .moe import _ptr, _to_dev, check
+from . import _lib, moe
+from .moe import _ptr, check
 
 __all__ = ["expert_range", "local_expert_weights", "CudaExpertShard", "ExpertParallelBlock",
            "ExpertParallelStack"]
@@ -93,29 +93,9 @@ class CudaExpertShard:
 
     def _register(self, layer: int, w: dict):
         dev = self.device
-        t = {k: _to_dev(v, dev, bf16=k.endswith("_s") or k.endswith("_b") or
-                        k in ("router_w", "shared_gate_w"))
-             for k, v in w.items() if k != "config" and v is not None}
+        t = moe.device_weights(w, dev)
         self._keep.append(t)
-        cfg = self.cfg
-
-        def aff(prefix):
-            if prefix + "_q" not in t:
-                return _lib.Affine()
-            return _lib.Affine(t[prefix + "_q"].data_ptr(), t[prefix + "_s"].data_ptr(),
-                               t[prefix + "_b"].data_ptr())
-
-        lw = _lib.LayerWeights()
-        lw.hidden, lw.experts, lw.top_k = cfg["hidden"], self.E, cfg["top_k"]
-        lw.intermediate = cfg["intermediate"]
-        lw.shared_intermediate = cfg.get("shared_intermediate", 0)
-        lw.group_size, lw.bits = cfg["group"], cfg["bits"]
-        lw.normalize_top_k = int(cfg.get("normalize", True))
-        lw.gate_up_fused = 0
-        lw.router_weight = t["router_w"].data_ptr()
-        lw.gate, lw.up, lw.down = aff("gate"), aff("up"), aff("down")
-        lw.shared_gate, lw.shared_up, lw.shared_down = aff("sgate"), aff("sup"), aff("sdown")
-        lw.shared_expert_gate = t["shared_gate_w"].data_ptr() if "shared_gate_w" in t else None
+        lw = moe.layer_weights_struct(t, self.cfg, self.E)
         check(_lib.lib().astro_moe_ep_register_layer(self.ctx, layer, ctypes.byref(lw),
                                                      self.first, self.count))
 

@@ -269,6 +269,56 @@ def qwen3_5_moe_combine_experts(selected_expert_outputs, selected_scores, shared
     return out
 
 
+# weight-dict keys holding bf16 arrays (everything else is packed uint32 codes)
+def _is_bf16_key(k: str) -> bool:
+    return k.endswith("_s") or k.endswith("_b") or k in ("router_w", "shared_gate_w")
+
+
+def device_weights(weights: dict, device, keys=None) -> dict:
+    """The array entries of a weight dict (MLX layout) on `device`; integer
+    entries (per-projection "<name>_bits" / "<name>_group") are kept as they are."""
+    out = {}
+    for k, v in weights.items():
+        if k == "config" or v is None or (keys is not None and k not in keys):
+            continue
+        out[k] = int(v) if isinstance(v, (int, np.integer)) else _to_dev(v, device, _is_bf16_key(k))
+    return out
+
+
+def layer_weights_struct(t: dict, cfg: dict, experts: int, fuse_gate_up: bool = False,
+                         routed: bool = True) -> "_lib.LayerWeights":
+    """astro_moe_layer_weights over device tensors `t` (keys of
+    synthetic.make_block_weights): projections gate/up/down/sgate/sup/sdown with
+    optional "<name>_bits" / "<name>_group", a bf16 router ("router_w") or an
+    affine one ("router_q/_s/_b" + "router_bits/_group"), a bf16 shared-expert
+    gate ("shared_gate_w") or an affine one ("shared_gate_q/_s/_b" + bits/group).
+    routed=False leaves the routed stacks empty (a paged layer)."""
+    def aff(prefix):
+        if prefix + "_q" not in t:
+            return _lib.Affine()
+        return _lib.Affine(t[prefix + "_q"].data_ptr(), t[prefix + "_s"].data_ptr(),
+                           t[prefix + "_b"].data_ptr(), int(t.get(prefix + "_bits", 0)),
+                           int(t.get(prefix + "_group", 0)))
+
+    lw = _lib.LayerWeights()
+    lw.hidden, lw.experts, lw.top_k = cfg["hidden"], experts, cfg["top_k"]
+    lw.intermediate = cfg["intermediate"]
+    lw.shared_intermediate = cfg.get("shared_intermediate", 0)
+    lw.group_size, lw.bits = cfg["group"], cfg["bits"]
+    lw.normalize_top_k = int(cfg.get("normalize", True))
+    lw.gate_up_fused = int(fuse_gate_up and routed)
+    lw.router_weight = t["router_w"].data_ptr() if "router_w" in t else None
+    lw.router_affine = aff("router")
+    if routed:
+        lw.gate = aff("gate")
+        lw.up = aff("up") if not fuse_gate_up else _lib.Affine()
+        lw.down = aff("down")
+    lw.shared_gate, lw.shared_up, lw.shared_down = aff("sgate"), aff("sup"), aff("sdown")
+    lw.shared_expert_gate = t["shared_gate_w"].data_ptr() if "shared_gate_w" in t else None
+    lw.shared_expert_gate_affine = aff("shared_gate")
+    return lw
+
+
 def _to_dev(a, device, bf16=False):
     if isinstance(a, torch.Tensor):
         t = a.to(device)
@@ -300,12 +350,7 @@ class Qwen3_5MoEBlock:
         self.device = torch.device("cuda", device)
         self.layer = layer
         dev = self.device
-        t = {}
-        for k, v in weights.items():
-            if k == "config" or v is None:
-                continue
-            t[k] = _to_dev(v, dev, bf16=k.endswith("_s") or k.endswith("_b") or k in (
-                "router_w", "shared_gate_w"))
+        t = device_weights(weights, dev)
         if fuse_gate_up:
             # resident_gate_up_fusion.rs:221-260: concatenate along the output axis
             t["gate_q"] = torch.cat([t["gate_q"], t.pop("up_q")], 1).contiguous()
@@ -325,30 +370,7 @@ class Qwen3_5MoEBlock:
                 torch.cuda.current_stream(dev).cuda_stream), ctypes.byref(opts), ctypes.byref(ctx)))
         self.ctx = ctx
 
-        def aff(prefix):
-            if prefix + "_q" not in t:
-                return _lib.Affine()
-            return _lib.Affine(t[prefix + "_q"].data_ptr(), t[prefix + "_s"].data_ptr(),
-                               t[prefix + "_b"].data_ptr())
-
-        lw = _lib.LayerWeights()
-        lw.hidden = cfg["hidden"]
-        lw.experts = cfg["experts"]
-        lw.top_k = cfg["top_k"]
-        lw.intermediate = cfg["intermediate"]
-        lw.shared_intermediate = cfg.get("shared_intermediate", 0)
-        lw.group_size = cfg["group"]
-        lw.bits = cfg["bits"]
-        lw.normalize_top_k = int(cfg.get("normalize", True))
-        lw.gate_up_fused = int(fuse_gate_up)
-        lw.router_weight = t["router_w"].data_ptr()
-        lw.gate = aff("gate")
-        lw.up = aff("up") if not fuse_gate_up else _lib.Affine()
-        lw.down = aff("down")
-        lw.shared_gate = aff("sgate")
-        lw.shared_up = aff("sup")
-        lw.shared_down = aff("sdown")
-        lw.shared_expert_gate = t["shared_gate_w"].data_ptr() if "shared_gate_w" in t else None
+        lw = layer_weights_struct(t, cfg, cfg["experts"], fuse_gate_up=fuse_gate_up)
         self._lw = lw
         check(_lib.lib().astro_moe_register_layer(self.ctx, layer, ctypes.byref(lw)))
 

@@ -18,7 +18,7 @@ from typing import Sequence
 import numpy as np
 import torch
 
-from . import _lib
+from . import _lib, moe
 from .moe import _ptr, _to_dev, check
 
 __all__ = ["page_bytes", "pack_layer", "pack_expert_pages", "PagedMoEStack"]
@@ -85,27 +85,10 @@ class PagedMoEStack:
         self.pager = pg
         self._keep = []
         for li, w in enumerate(layers):
-            t = {k: _to_dev(w[k], self.device, bf16=k.endswith("_s") or k.endswith("_b") or
-                            k in ("router_w", "shared_gate_w"))
-                 for k in ("router_w", "shared_gate_w", "sgate_q", "sgate_s", "sgate_b", "sup_q",
-                           "sup_s", "sup_b", "sdown_q", "sdown_s", "sdown_b") if w.get(k) is not None}
+            t = moe.device_weights(w, self.device, keys=[k for k in w if not k.startswith(
+                ("gate_", "up_", "down_"))])
             self._keep.append(t)
-
-            def aff(prefix):
-                if prefix + "_q" not in t:
-                    return _lib.Affine()
-                return _lib.Affine(t[prefix + "_q"].data_ptr(), t[prefix + "_s"].data_ptr(),
-                                   t[prefix + "_b"].data_ptr())
-
-            lw = _lib.LayerWeights()
-            lw.hidden, lw.experts, lw.top_k = cfg["hidden"], cfg["experts"], cfg["top_k"]
-            lw.intermediate = cfg["intermediate"]
-            lw.shared_intermediate = cfg.get("shared_intermediate", 0)
-            lw.group_size, lw.bits = cfg["group"], cfg["bits"]
-            lw.normalize_top_k = int(cfg.get("normalize", True))
-            lw.router_weight = t["router_w"].data_ptr()
-            lw.shared_gate, lw.shared_up, lw.shared_down = aff("sgate"), aff("sup"), aff("sdown")
-            lw.shared_expert_gate = t["shared_gate_w"].data_ptr() if "shared_gate_w" in t else None
+            lw = moe.layer_weights_struct(t, cfg, cfg["experts"], routed=False)
             check(_lib.lib().astro_moe_register_paged_layer(self.ctx, li, ctypes.byref(lw),
                                                             self.pager))
 

@@ -77,16 +77,40 @@ def unpack_affine(packed: np.ndarray, bits: int = 4) -> np.ndarray:
 
 
 def _affine(rng, shape_rows, in_f, group, bits):
-    """Random q (uniform 0..2^bits-1), |N(0,0.01)| scales, -8*scale biases."""
+    """Random q (uniform 0..2^bits-1), |N(0,0.01 * 16/2^bits)| scales and
+    -2^(bits-1)*scale biases (for 4 bits: |N(0,0.01)| and -8*scale), so every bit
+    width spans about the same weight range."""
     words = in_f * bits // 32
     if bits in (2, 4, 8):
         # uniformly random words have independent uniform fields
         q = rng.integers(0, 2**32, size=shape_rows + (words,), dtype=np.uint64).astype(np.uint32)
     else:
         q = pack_affine(rng.integers(0, 2**bits, size=shape_rows + (in_f,)), bits)
-    s = f32_to_bf16(np.abs(rng.normal(0.0, 0.01, size=shape_rows + (in_f // group,))))
-    b = f32_to_bf16(-8.0 * bf16_to_f32(s))
+    s = f32_to_bf16(np.abs(rng.normal(0.0, 0.01 * 16.0 / 2**bits,
+                                      size=shape_rows + (in_f // group,))))
+    b = f32_to_bf16(-float(2 ** (bits - 1)) * bf16_to_f32(s))
     return q, s, b
+
+
+def quantize_affine(w, bits: int, group: int):
+    """MLX-style affine quantisation of float rows [..., in]: per group of
+    `group` elements scale = (max - min) / (2^bits - 1), bias = min (both bf16),
+    q = round((w - bias) / scale) clipped to the code range.  Returns (packed
+    uint32, scales bf16 bits, biases bf16 bits)."""
+    w = np.asarray(w, np.float32)
+    rows = w.shape[:-1]
+    in_f = w.shape[-1]
+    g = w.reshape(rows + (in_f // group, group))
+    lo, hi = g.min(-1), g.max(-1)
+    scale = f32_to_bf16(np.maximum(hi - lo, 1e-8) / (2 ** bits - 1))
+    bias = f32_to_bf16(lo)
+    sf, bf = bf16_to_f32(scale)[..., None], bf16_to_f32(bias)[..., None]
+    q = np.clip(np.rint((g - bf) / sf), 0, 2 ** bits - 1).astype(np.uint32)
+    return pack_affine(q.reshape(rows + (in_f,)), bits), scale, bias
+
+
+# projections whose quantisation make_block_weights can override
+QUANT_NAMES = ("gate", "up", "down", "sgate", "sup", "sdown", "router", "shared_gate")
 
 
 def zipf_router_bias(experts: int, s: float, rng) -> np.ndarray:
@@ -97,8 +121,14 @@ def zipf_router_bias(experts: int, s: float, rng) -> np.ndarray:
     return np.log(p[perm])  # b_e = ln p(pi(e))
 
 
-def make_block_weights(cfg: dict, seed: int = 0) -> dict:
-    """Router, routed experts (separate gate/up, MLX layout) and optional shared expert."""
+def make_block_weights(cfg: dict, seed: int = 0, quant: dict | None = None) -> dict:
+    """Router, routed experts (separate gate/up, MLX layout) and optional shared expert.
+
+    quant maps a projection (QUANT_NAMES) to its own (bits, group): the routed and
+    shared projections are then drawn with that profile and carry "<name>_bits" /
+    "<name>_group" keys, and "router" / "shared_gate" replace the bf16 router or
+    shared-expert gate by an MLX-style affine quantisation of the same values
+    ("<name>_q/_s/_b", as the reference's Qwen3_5MoERouterGateWeights::Affine)."""
     rng = np.random.default_rng(seed)
     H, E, I = cfg["hidden"], cfg["experts"], cfg["intermediate"]
     Is, G, B = cfg.get("shared_intermediate", 0), cfg["group"], cfg["bits"]
@@ -115,6 +145,23 @@ def make_block_weights(cfg: dict, seed: int = 0) -> dict:
         w["sup_q"], w["sup_s"], w["sup_b"] = _affine(rng, (Is,), H, G, B)
         w["sdown_q"], w["sdown_s"], w["sdown_b"] = _affine(rng, (H,), Is, G, B)
         w["shared_gate_w"] = f32_to_bf16(rng.normal(0.0, 0.02, size=(1, H)))
+    for name, (bits, group) in (quant or {}).items():
+        if name not in QUANT_NAMES:
+            raise ValueError(f"unknown projection {name}")
+        if name == "shared_gate" and not Is:
+            continue
+        if name in ("router", "shared_gate"):
+            dense = w.pop("router_w" if name == "router" else "shared_gate_w")
+            w[name + "_q"], w[name + "_s"], w[name + "_b"] = quantize_affine(
+                bf16_to_f32(dense), bits, group)
+        else:
+            if name in ("sgate", "sup", "sdown") and not Is:
+                continue
+            qrng = np.random.default_rng([seed, QUANT_NAMES.index(name), bits, group])
+            rows, in_f = {"gate": ((E, I), H), "up": ((E, I), H), "down": ((E, H), I),
+                          "sgate": ((Is,), H), "sup": ((Is,), H), "sdown": ((H,), Is)}[name]
+            w[name + "_q"], w[name + "_s"], w[name + "_b"] = _affine(qrng, rows, in_f, group, bits)
+        w[name + "_bits"], w[name + "_group"] = int(bits), int(group)
     return w
 
 

@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define ASTRO_MOE_ABI_VERSION 1
+#define ASTRO_MOE_ABI_VERSION 2
 
 enum {
   ASTRO_MOE_OK = 0,
@@ -153,6 +153,13 @@ int astro_moe_quantized_matmul(const void* activations, int64_t rows, int32_t in
                                int32_t out_features, int32_t group_size, int32_t bits, void* out,
                                void* stream);
 
+/* MLX affine dequantize, crates/runtime-integration/src/mlx_quantized_operations.rs:5-47:
+ * out[r, j] = bf16(scale[r, j/group] * q[r, j] + bias[r, j/group]) for `rows`
+ * rows of in_features elements (MLX layout, any supported bits / group). */
+int astro_moe_dequantize_affine(const uint32_t* packed, const void* scales, const void* biases,
+                                int64_t rows, int32_t in_features, int32_t group_size,
+                                int32_t bits, void* out, void* stream);
+
 /* MlxRuntime::apply_compiled_swiglu, crates/runtime-integration/src/mlx_compiled_swiglu.rs:32-89:
  * out = gate * sigmoid(gate) * up, bf16, n elements. */
 int astro_moe_swiglu(const void* gate, const void* up, int64_t n, void* out, void* stream);
@@ -205,17 +212,35 @@ typedef struct {
 } astro_moe_options;
 
 /* One stacked affine projection in MLX layout (Qwen3_5AffineWeights::Quantized,
- * qwen3_5/model/decoder_layer_weights.rs:15-26). */
+ * qwen3_5/model/decoder_layer_weights.rs:15-26), with its own bit width and
+ * group size as each reference module carries them (0 = the layer's). */
 typedef struct {
   const uint32_t* packed;
   const void* scales;  /* bf16 */
   const void* biases;  /* bf16 */
+  int32_t bits;        /* 2, 3, 4, 5, 6 or 8; 0 = astro_moe_layer_weights.bits */
+  int32_t group_size;  /* 32, 64 or 128; 0 = astro_moe_layer_weights.group_size */
 } astro_moe_affine;
 
 /* Qwen3_5MoEFeedForwardWeights (qwen3_5_moe/model/feed_forward_weights.rs:16-24)
  * plus the resident expert stacks (expert_residency).  With gate_up_fused the
  * `gate` tensor is the [E, 2I, .] concatenation of resident_gate_up_fusion.rs:221-260
- * (gate rows first) and `up` is ignored.  shared_intermediate == 0: no shared expert. */
+ * (gate rows first) and `up` is ignored.  shared_intermediate == 0: no shared expert.
+ *
+ * Quantisation: `bits` / `group_size` are the defaults; each astro_moe_affine may
+ * carry its own.  gate and up must share theirs, and so must the shared gate and
+ * shared up.  The tcgen05 and decode kernels serve 4-bit group-64 experts; other
+ * profiles run on the CUDA-core grouped GEMV.  A shared expert quantised unlike
+ * the routed experts runs as its own launches.
+ *
+ * Router (Qwen3_5MoERouterGateWeights, feed_forward_weights.rs:10-14): a bf16
+ * `router_weight`, or NULL with `router_affine` set (the Affine variant, which the
+ * reference runs through quantized_linear, forward.rs:53-58).  The shared-expert
+ * output gate likewise: bf16 `shared_expert_gate`, or NULL with
+ * `shared_expert_gate_affine`.  An affine router or gate is dequantised once at
+ * registration into a bf16 copy the context owns (w = bf16(scale * q + bias), the
+ * weight MLX's quantized matmul multiplies; 2*E*H bytes for the router); every
+ * call then runs the dense router kernels on it. */
 typedef struct {
   int32_t hidden, experts, top_k, intermediate, shared_intermediate;
   int32_t group_size, bits, normalize_top_k, gate_up_fused;
@@ -225,6 +250,8 @@ typedef struct {
   astro_moe_affine shared_gate, shared_up; /* [Is, H*bits/32] */
   astro_moe_affine shared_down;    /* [H, Is*bits/32] */
   const void* shared_expert_gate;  /* bf16 [1, H] */
+  astro_moe_affine router_affine;            /* [E, H*bits/32] when router_weight is NULL */
+  astro_moe_affine shared_expert_gate_affine; /* [1, H*bits/32] when shared_expert_gate is NULL */
 } astro_moe_layer_weights;
 
 /* Optional device outputs of one block call, for parity checks. */

@@ -33,7 +33,38 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_abi_version():
-    assert _lib.lib().astro_moe_abi_version() == 1
+    assert _lib.lib().astro_moe_abi_version() == 2
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors of the ABI's structs have the C compiler's sizes and
+    field offsets (a mismatch would misread every weight pointer)."""
+    import shutil
+    import subprocess
+
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    structs = {"astro_moe_affine": _lib.Affine, "astro_moe_layer_weights": _lib.LayerWeights,
+               "astro_moe_options": _lib.Options, "astro_moe_block_taps": _lib.BlockTaps,
+               "astro_moe_block_path": _lib.BlockPath, "astro_moe_pager_stats": _lib.PagerStats,
+               "astro_moe_attribution": _lib.Attribution}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "astro_moe.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f, _ in py._fields_:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("  return 0;\n}")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run([cc, "-I", os.path.join(ROOT, "include"), "-o", str(exe), str(src)], check=True)
+    got = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    c_side = {tuple(l.split()[:2]): int(l.split()[2]) for l in got if l.strip()}
+    for cname, py in structs.items():
+        assert c_side[(cname, "size")] == ctypes.sizeof(py), cname
+        for f, _ in py._fields_:
+            assert c_side[(cname, f)] == getattr(py, f).offset, (cname, f)
 
 
 def test_host_validation_rejects_bad_geometry():

@@ -212,3 +212,39 @@ def test_block_host_async_calls_match_device_entry():
     for h, y in zip(hout, want):
         assert torch.equal(h, y.cpu())
     blk.close()
+
+
+# Each reference projection carries its own quantisation (Qwen3_5AffineWeights,
+# qwen3_5/model/decoder_layer_weights.rs:15-26) and the router and shared-expert
+# gate may be affine (feed_forward_weights.rs:10-14): the block must equal the
+# oracle bit for bit in every mix, whichever kernels each mix selects.
+QUANTS = [
+    pytest.param({"router": (8, 64), "shared_gate": (8, 64)}, id="affine-router-and-gate-8bit"),
+    pytest.param({"router": (4, 64)}, id="affine-router-4bit"),
+    pytest.param({"down": (8, 64), "sdown": (8, 64)}, id="down-8bit"),
+    pytest.param({"sgate": (8, 64), "sup": (8, 64), "sdown": (8, 64)}, id="shared-8bit-separate"),
+    pytest.param({"gate": (8, 128), "up": (8, 128), "down": (3, 32), "sgate": (6, 64),
+                  "sup": (6, 64), "sdown": (2, 32), "router": (5, 32), "shared_gate": (6, 128)},
+                 id="every-projection-its-own"),
+]
+
+
+@pytest.mark.parametrize("quant", QUANTS)
+@pytest.mark.parametrize("T", [5, 64, 300])
+def test_block_per_projection_quantisation(quant, T):
+    cfg = small_cfg()
+    w = synthetic.make_block_weights(cfg, seed=40 + T, quant=quant)
+    f = run_and_compare(cfg, T, seed=40 + T, weights=w, case="per_projection_quant")
+    kernels = f["kernels"]
+    separate = "sgate" in quant and "gate" not in quant
+    if separate:
+        assert kernels["shared_expert"] == "grouped_gemv"
+    if "gate" in quant or "down" in quant:
+        assert kernels["experts"] == "grouped_gemv"
+
+
+def test_gate_and_up_must_share_their_quantisation():
+    cfg = small_cfg()
+    w = synthetic.make_block_weights(cfg, seed=3, quant={"gate": (8, 64)})
+    with pytest.raises(moe.AstroMoeError, match="gate and up"):
+        moe.Qwen3_5MoEBlock(w, max_tokens=8)
