@@ -76,7 +76,8 @@ class PagerStats(ctypes.Structure):
     _fields_ = [("lookups", ctypes.c_int64), ("hits", ctypes.c_int64), ("misses", ctypes.c_int64),
                 ("evictions", ctypes.c_int64), ("bytes_h2d", ctypes.c_int64),
                 ("copy_ms", ctypes.c_double), ("resident_pages", ctypes.c_int64),
-                ("capacity_pages", ctypes.c_int64)]
+                ("capacity_pages", ctypes.c_int64), ("calls", ctypes.c_int64),
+                ("split_calls", ctypes.c_int64)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}

@@ -1030,6 +1030,8 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
                                  N, T, K, H, N >= threshold ? 1 : 0, out, st),
      "weighted combine");
   ctx->launches += 6 + (copies ? 2 : 0) + astro::sort_launch_count(N);
+  pg->st.calls += 1;
+  if (copies) pg->st.split_calls += 1;
   return ASTRO_MOE_OK;
 }
 

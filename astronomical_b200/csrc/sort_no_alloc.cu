@@ -25,14 +25,20 @@
 // (unordered streams, or several host threads on one device) race on the array
 // and produce wrong results; order such calls on one stream.
 //
-// Set-up: the first call on each device, with that device current, looks up
-// the array's device address with cudaGetSymbolAddress (the host-side symbol is
-// only a stand-in and must never reach a kernel) and caches it.  That first
-// call should come before any stream capture on that device.
+// Set-up: the first call in each CUDA context -- normally a device's primary
+// context, with that device current -- looks up the array's device address with
+// cudaGetSymbolAddress (the host-side symbol is only a stand-in and must never
+// reach a kernel) and keeps it for that context, keyed by the context's unique
+// id (cuCtxGetId), so a kept address never outlives its context: after a
+// cudaDeviceReset, or in another context the caller makes current, the next
+// call looks it up again.  The first call in a context should come before any
+// stream capture on it.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
 #include <cstdio>
+#include <map>
 #include <mutex>
 
 #include "astro_moe.h"
@@ -41,12 +47,11 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = ASTRO_MOE_NO_ALLOC_SCRATCH_BYTES;
-constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_sort_scratch[kNoAllocScratchBytes];
 
 std::mutex g_mu;
-void* g_scratch_addr[kMaxDevices] = {};
+std::map<unsigned long long, void*> g_scratch_addr;  // context id -> address of g_sort_scratch
 
 int failf(int status, const char* fmt, ...) __attribute__((format(printf, 2, 3)));
 int failf(int status, const char* fmt, ...) {
@@ -62,23 +67,55 @@ int cuda_failf(cudaError_t e, const char* what) {
   return failf(ASTRO_MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
 }
 
-// Device address of g_sort_scratch on the current device (looked up once).
-int scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return cuda_failf(e, "cudaGetDevice");
-  if (dev < 0 || dev >= kMaxDevices)
-    return failf(ASTRO_MOE_ERR_UNSUPPORTED, "no-alloc sort: device %d is beyond the %d supported",
-                 dev, kMaxDevices);
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!g_scratch_addr[dev]) {
+// Unique id of the current CUDA context, or 0 when none is current or the
+// driver does not report ids.
+unsigned long long current_context_id() {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_sort_scratch);
-    if (e != cudaSuccess) return cuda_failf(e, "cudaGetSymbolAddress(no-alloc sort scratch)");
-    if (!p) return failf(ASTRO_MOE_ERR_CUDA, "cudaGetSymbolAddress returned a null address");
-    g_scratch_addr[dev] = p;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(p);
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
+  if (!get_current || !get_id) return 0;
+  CUcontext c = nullptr;
+  unsigned long long id = 0;
+  if (get_current(&c) != CUDA_SUCCESS || !c || get_id(c, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
+
+// Device address of g_sort_scratch in the current context: kept per context
+// (looked up with cudaGetSymbolAddress on the first call in a context, which
+// also makes the device's primary context current if none is); looked up on
+// every call when the context cannot be identified.
+int scratch_address(void** out) {
+  const unsigned long long id = current_context_id();
+  if (id != 0) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_scratch_addr.find(id);
+    if (it != g_scratch_addr.end()) {
+      *out = it->second;
+      return ASTRO_MOE_OK;
+    }
   }
-  *out = g_scratch_addr[dev];
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_sort_scratch);
+  if (e != cudaSuccess) return cuda_failf(e, "cudaGetSymbolAddress(no-alloc sort scratch)");
+  if (!p) return failf(ASTRO_MOE_ERR_CUDA, "cudaGetSymbolAddress returned a null address");
+  const unsigned long long id2 = current_context_id();
+  if (id2 != 0) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_scratch_addr[id2] = p;
+  }
+  *out = p;
   return ASTRO_MOE_OK;
 }
 

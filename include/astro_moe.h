@@ -114,8 +114,10 @@ int astro_moe_sort_expert_assignments(const uint32_t* selected_indices, int64_t 
  * ASTRO_MOE_ERR_UNSUPPORTED before any work is queued.  Nothing in the array
  * must start at zero.  All calls on a device share the array: calls whose
  * kernels overlap on the GPU race, so order them on one stream.  The first call
- * on each device (with that device current) looks up the array's device address
- * once; make that first call before any stream capture.  device_status is an
+ * in each CUDA context (normally a device's primary context, with that device
+ * current) looks up the array's device address and keeps it for that context
+ * only (so it is looked up again after a cudaDeviceReset or in another
+ * context); make that first call before any stream capture.  device_status is an
  * optional caller-owned device word that receives ASTRO_MOE_DEVICE_BAD_EXPERT_ID
  * (OR'ed in) for ids >= experts; NULL records nothing.  Such ids are skipped. */
 #define ASTRO_MOE_NO_ALLOC_SCRATCH_BYTES 262144
@@ -463,6 +465,8 @@ typedef struct {
   double copy_ms;           /* device time of those copies (copy-stream events) */
   int64_t resident_pages;
   int64_t capacity_pages;
+  int64_t calls;            /* paged block calls */
+  int64_t split_calls;      /* ... that copied pages in, so ran the copied experts' second launch */
 } astro_moe_pager_stats;
 /* Synchronises the pager's copy stream; reset != 0 clears the counters. */
 int astro_moe_pager_read_stats(astro_moe_pager* pager, astro_moe_pager_stats* out, int32_t reset);

@@ -39,6 +39,17 @@ def test_paged_stack_equals_resident_blocks_and_counts_pages():
     if len(seen) > 40:
         assert s["evictions"] > 0
     assert s["copy_ms"] > 0
+    # a call that copied pages ran the copied experts' second launch; every call
+    # after the first of a layer that found all its pages resident did not
+    assert s["calls"] == 3 * 3 * L
+    assert 0 < s["split_calls"] <= s["calls"] and s["split_calls"] <= s["misses"]
+    x = bf16_tensor(synthetic.make_hidden_states(1, 2048, seed=301, zipf=True))
+    stack.forward(0, x)
+    before = stack.stats()
+    stack.forward(0, x)  # same token, same layer: every page it needs is resident
+    after = stack.stats()
+    assert after["misses"] == before["misses"] and after["split_calls"] == before["split_calls"]
+    assert after["calls"] == before["calls"] + 1
     assert moe.device_status(0, reset=True) == 0
     stack.close()
     for b in resident:

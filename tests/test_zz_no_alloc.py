@@ -82,6 +82,50 @@ def test_no_alloc_sort_without_offsets_and_bad_ids():
     assert int(status.item()) & ASTRO_MOE_DEVICE_BAD_EXPERT_ID
 
 
+@pytest.mark.gpu
+def test_no_alloc_sort_without_offsets_on_many_tiles_after_a_larger_call():
+    # without an offsets output the offsets live in the array right after the
+    # per-tile histograms; a multi-tile call (777 x 8 = 3 tiles) right after a
+    # larger one must not see what that call left there
+    big = _ids(4096, 8, 256, 5)
+    _sort("astro_moe_sort_expert_assignments_no_alloc", big, 256)
+    ids = _ids(777, 8, 256, 6)
+    want = _sort("astro_moe_sort_expert_assignments", ids, 256, with_offsets=False)
+    got = _sort("astro_moe_sort_expert_assignments_no_alloc", ids, 256, with_offsets=False)
+    for w, g in zip(want, got):
+        assert np.array_equal(w, g)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("with_offsets", [True, False])
+def test_no_alloc_sort_at_the_largest_accepted_size(with_offsets):
+    # 256 tiles x 256 experts x 4 B = 262,144 B exactly with an offsets output;
+    # 254 tiles when the offsets (4 x 257 B) share the array
+    E = 256
+    n = (256 if with_offsets else 254) * 2048
+    ids = _ids(n // 8, 8, E, 7)
+    want = _sort("astro_moe_sort_expert_assignments", ids, E, with_offsets=with_offsets)
+    got = _sort("astro_moe_sort_expert_assignments_no_alloc", ids, E, with_offsets=with_offsets)
+    for w, g in zip(want, got):
+        assert np.array_equal(w, g)
+
+
+@pytest.mark.parametrize("with_offsets", [True, False])
+def test_no_alloc_sort_rejects_one_tile_past_the_limit(with_offsets):
+    # host-side check, before any CUDA call: the smallest size over the limit
+    lib = _lib.lib()
+    E = 256
+    n = (256 if with_offsets else 254) * 2048 + 1
+    need = 4 * E * -(-n // 2048) + (0 if with_offsets else 4 * (E + 1))
+    assert need > SCRATCH_BYTES
+    assert need - 4 * E <= SCRATCH_BYTES  # one tile fewer fits
+    fake = ctypes.c_void_p(256)  # never dereferenced: the call fails first
+    rc = lib.astro_moe_sort_expert_assignments_no_alloc(fake, n, 1, E, fake, fake, fake, fake,
+                                                        fake if with_offsets else None, None, None)
+    assert rc == ASTRO_MOE_ERR_UNSUPPORTED
+    assert "static array" in lib.astro_moe_last_error().decode()
+
+
 def test_no_alloc_sort_rejects_sizes_beyond_the_array():
     # host-side check, before any CUDA call: 4 * 256 * ceil(n / 2048) bytes of
     # histograms exceed 256 KiB past 522,240 assignments
