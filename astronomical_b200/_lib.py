@@ -51,7 +51,11 @@ class LayerWeights(ctypes.Structure):
         ("router_weight", ctypes.c_void_p), ("gate", Affine), ("up", Affine), ("down", Affine),
         ("shared_gate", Affine), ("shared_up", Affine), ("shared_down", Affine),
         ("shared_expert_gate", ctypes.c_void_p), ("router_affine", Affine),
-        ("shared_expert_gate_affine", Affine)]
+        ("shared_expert_gate_affine", Affine), ("router_kind", ctypes.c_int32),
+        ("router_logit_softcap", ctypes.c_float), ("routed_scaling_factor", ctypes.c_float),
+        ("router_correction_bias", ctypes.c_void_p)]
+
+ROUTER_SOFTMAX, ROUTER_SIGMOID = 0, 1
 
 
 class BlockTaps(ctypes.Structure):
@@ -104,6 +108,8 @@ SIGNATURES = {
     "astro_moe_tensor_core_probe": ([_I32, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _P],
                                     ctypes.c_int),
     "astro_moe_route_experts": ([_P, _I32, _I64, _I32, _I32, _I32, _P, _P, _P], ctypes.c_int),
+    "astro_moe_route_laguna_experts": ([_P, _I32, _I64, _I32, _I32, _P, ctypes.c_double, _I32,
+                                        _P, _P, _P], ctypes.c_int),
     "astro_moe_sort_expert_assignments": ([_P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P],
                                           ctypes.c_int),
     "astro_moe_sort_expert_assignments_no_alloc": (

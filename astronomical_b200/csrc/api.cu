@@ -11,6 +11,7 @@
 // switch (routing.rs:13, assignment count >= 64) still selects the weighted-sum
 // arithmetic, exactly as in the reference.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdarg>
@@ -250,7 +251,7 @@ size_t plan_workspace(const astro_moe_layer_weights& w, int64_t T, BlockWorkspac
   b.barrier = (uint32_t*)take(kFusedSyncBytes);
   b.logits = (uint16_t*)take(sizeof(uint16_t) * T * E);
   b.ids = (uint32_t*)take(sizeof(uint32_t) * N);
-  b.scores = (uint16_t*)take(sizeof(uint16_t) * N);
+  b.scores = (uint16_t*)take(sizeof(float) * N);  // bf16 scores, or fp32 for a Laguna router
   b.gate_logit = (uint16_t*)take(sizeof(uint16_t) * T);
   b.order = (uint32_t*)take(sizeof(uint32_t) * N);
   b.inverse = (uint32_t*)take(sizeof(uint32_t) * N);
@@ -358,7 +359,7 @@ void fill_projections(const astro_moe_layer_weights& w, astro::AffineRef (&gate)
 
 // Copies the requested intermediate arrays of a block call to the caller's taps.
 int copy_taps(astro_moe_ctx* ctx, const BlockWorkspace& b, int64_t T, int E, int K,
-              bool has_shared, const astro_moe_block_taps* taps) {
+              bool has_shared, const astro_moe_block_taps* taps, size_t score_bytes = 2) {
   if (!taps) return ASTRO_MOE_OK;
   cudaStream_t st = ctx->stream;
   const int64_t N = T * K;
@@ -370,7 +371,7 @@ int copy_taps(astro_moe_ctx* ctx, const BlockWorkspace& b, int64_t T, int E, int
       CK(cudaMemcpyAsync(taps->selected_indices, b.ids, sizeof(uint32_t) * N,
                          cudaMemcpyDeviceToDevice, st), "taps");
     if (taps->selected_scores)
-      CK(cudaMemcpyAsync(taps->selected_scores, b.scores, sizeof(uint16_t) * N,
+      CK(cudaMemcpyAsync(taps->selected_scores, b.scores, score_bytes * N,
                          cudaMemcpyDeviceToDevice, st), "taps");
     if (taps->expert_offsets)
       CK(cudaMemcpyAsync(taps->expert_offsets, b.offsets,
@@ -426,7 +427,10 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   const bool use_tc = !use_decode && astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores) &&
                       x_aligned;
   const bool router_gemv = T <= kRouterGemvTokens && x_aligned && L.router_gemv_ok;
-  const bool try_fused = use_decode && fused_shape;
+  const bool laguna = w.router_kind == ASTRO_MOE_ROUTER_SIGMOID;
+  const bool gated_shared = has_shared && !laguna;
+  const size_t score_bytes = laguna ? sizeof(float) : sizeof(uint16_t);
+  const bool try_fused = use_decode && fused_shape && !laguna;
   if (try_fused) {
     astro::DecodeFusedArgs a;
     a.x = x;
@@ -481,7 +485,7 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
                           : (use_decode ? ASTRO_MOE_KERNEL_DECODE_GEMV : ASTRO_MOE_KERNEL_GROUPED_GEMV);
     ctx->last_path.router = router_gemv ? ASTRO_MOE_KERNEL_ROUTER_GEMV
                                         : (use_tc ? ASTRO_MOE_KERNEL_TCGEN05_GEMM : ASTRO_MOE_KERNEL_SIMT_GEMM);
-    ctx->last_path.gate_logit = has_shared ? ASTRO_MOE_KERNEL_ROUTE : ASTRO_MOE_KERNEL_NONE;
+    ctx->last_path.gate_logit = gated_shared ? ASTRO_MOE_KERNEL_ROUTE : ASTRO_MOE_KERNEL_NONE;
     ctx->last_path.experts = ek;
     ctx->last_path.shared_expert =
         has_shared ? (L.shared_separate ? ASTRO_MOE_KERNEL_GROUPED_GEMV : ek) : ASTRO_MOE_KERNEL_NONE;
@@ -496,11 +500,18 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
     CK(astro::launch_dense_nt_simt(x, w.router_weight, T, E, H, b.logits, E, st), "router projection");
   }
   marks.mark();
-  // a2: route (+ shared-expert gate logit)
-  CK(astro::launch_route_experts(b.logits, ASTRO_MOE_DTYPE_BF16, T, E, K, w.normalize_top_k,
-                                 b.ids, b.scores, x, has_shared ? w.shared_expert_gate : nullptr, H,
-                                 has_shared ? b.gate_logit : nullptr, st),
-     "route experts");
+  // a2: route (+ shared-expert gate logit); Laguna: sigmoid routing, fp32 scores
+  if (laguna) {
+    CK(astro::launch_route_laguna(b.logits, ASTRO_MOE_DTYPE_BF16, T, E, K, w.router_logit_softcap,
+                                  w.router_correction_bias, w.normalize_top_k, b.ids,
+                                  reinterpret_cast<float*>(b.scores), st),
+       "route Laguna experts");
+  } else {
+    CK(astro::launch_route_experts(b.logits, ASTRO_MOE_DTYPE_BF16, T, E, K, w.normalize_top_k,
+                                   b.ids, b.scores, x, has_shared ? w.shared_expert_gate : nullptr,
+                                   H, has_shared ? b.gate_logit : nullptr, st),
+       "route experts");
+  }
   // a3: sort (+ shared segment E)
   CK(astro::launch_sort_assignments(b.ids, T, K, E, has_shared ? T : 0, b.order, b.inverse,
                                     b.sids, b.stok, b.offsets, ctx->status, b.sort_scratch, st),
@@ -617,13 +628,22 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
   }
   marks.mark();
   // a7 + a8: weighted sum fused with the shared expert and its gate
-  CK(astro::launch_block_combine(b.yrows, b.inverse, b.scores, has_shared ? b.gate_logit : nullptr,
-                                 N, T, K, H, sorted_semantics ? 1 : 0, out, st),
-     "weighted combine");
+  if (laguna) {
+    const float f = w.routed_scaling_factor > 0.0f ? w.routed_scaling_factor : 1.0f;
+    CK(astro::launch_block_combine(b.yrows, b.inverse, nullptr, nullptr, N, T, K, H,
+                                   sorted_semantics ? 1 : 0, out, st,
+                                   reinterpret_cast<const float*>(b.scores), has_shared ? 1 : 0,
+                                   __bfloat162float(__float2bfloat16_rn(f))),
+       "weighted combine");
+  } else {
+    CK(astro::launch_block_combine(b.yrows, b.inverse, b.scores, has_shared ? b.gate_logit : nullptr,
+                                   N, T, K, H, sorted_semantics ? 1 : 0, out, st),
+       "weighted combine");
+  }
   marks.mark();
   marks.commit();
   if (ctx->attribution) ctx->acc.calls += 1;
-  return copy_taps(ctx, b, T, E, K, has_shared, taps);
+  return copy_taps(ctx, b, T, E, K, has_shared, taps, score_bytes);
 }
 
 // geometry and pointer checks of one layer's weights (register_layer and the
@@ -681,6 +701,13 @@ int validate_layer(const char* op, const astro_moe_layer_weights* w, bool routed
   if (w->shared_intermediate != 0 && w->shared_intermediate != w->intermediate)
     return fail(ASTRO_MOE_ERR_UNSUPPORTED,
                 "%s: the shared expert must have the routed intermediate width (or be absent)", op);
+  if (w->router_kind != ASTRO_MOE_ROUTER_SOFTMAX && w->router_kind != ASTRO_MOE_ROUTER_SIGMOID)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: unknown router kind %d", op, (int)w->router_kind);
+  if (w->router_kind == ASTRO_MOE_ROUTER_SIGMOID &&
+      (w->router_logit_softcap != w->router_logit_softcap || w->router_logit_softcap < 0.0f ||
+       w->routed_scaling_factor != w->routed_scaling_factor || w->routed_scaling_factor < 0.0f))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "%s: the Laguna softcap and routed scaling factor must be >= 0", op);
   if (!w->router_weight) {
     if (!w->router_affine.packed)
       return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null router weight (bf16 or affine)", op);
@@ -699,7 +726,7 @@ int validate_layer(const char* op, const astro_moe_layer_weights* w, bool routed
     if (int rc = validate_affine_tensor("shared gate", w->shared_gate)) return rc;
     if (int rc = validate_affine_tensor("shared up", w->shared_up)) return rc;
     if (int rc = validate_affine_tensor("shared down", w->shared_down)) return rc;
-    if (!w->shared_expert_gate) {
+    if (!w->shared_expert_gate && w->router_kind == ASTRO_MOE_ROUTER_SOFTMAX) {
       if (!w->shared_expert_gate_affine.packed)
         return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null shared expert gate (bf16 or affine)", op);
       if (int rc = validate_affine_tensor("affine shared expert gate", w->shared_expert_gate_affine))
@@ -739,7 +766,7 @@ int resolve_layer(astro_moe_ctx* ctx, const astro_moe_layer_weights* in, int rou
     L.w.router_weight = L.router_dense;
     sync = true;
   }
-  if (has_shared && !in->shared_expert_gate) {
+  if (has_shared && !in->shared_expert_gate && in->router_kind == ASTRO_MOE_ROUTER_SOFTMAX) {
     int gb, gg;
     eff_quant(in->shared_expert_gate_affine, *in, &gb, &gg);
     CK(cudaMalloc(&L.sgate_dense, sizeof(uint16_t) * (size_t)in->hidden),
@@ -1074,6 +1101,28 @@ int astro_moe_route_experts(const void* logits, int32_t dtype, int64_t tokens, i
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
   CK(astro::launch_route_experts(logits, dtype, tokens, experts, top_k, normalize, ids, scores,
                                  nullptr, nullptr, 0, nullptr, S(stream)),
+     op);
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_route_laguna_experts(const void* logits, int32_t dtype, int64_t tokens,
+                                   int32_t experts, int32_t top_k, const float* correction_bias,
+                                   double router_logit_softcap, int32_t normalize, uint32_t* ids,
+                                   float* scores, void* stream) {
+  const char* op = "route Laguna experts";
+  if (!valid_dtype(dtype))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: router logits must use float16, bfloat16, or float32", op);
+  // validate_router_geometry, laguna/moe/router_selection.rs:127-150
+  if (tokens < 0 || experts <= 0 || top_k <= 0 || top_k > experts ||
+      router_logit_softcap != router_logit_softcap || router_logit_softcap < 0.0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT,
+                "%s: Laguna router logits, top-K, and softcap must describe a valid selection", op);
+  if (top_k > 32 || experts > 1024)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: top_k <= 32 and experts <= 1024 are supported", op);
+  if (tokens > 0 && (!logits || !ids || !scores))
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
+  CK(astro::launch_route_laguna(logits, dtype, tokens, experts, top_k, (float)router_logit_softcap,
+                                correction_bias, normalize, ids, scores, S(stream)),
      op);
   return ASTRO_MOE_OK;
 }
@@ -1504,6 +1553,8 @@ int astro_moe_ep_register_layer(astro_moe_ctx* ctx, int32_t layer, const astro_m
   if (L.shared_separate)
     return fail(ASTRO_MOE_ERR_UNSUPPORTED,
                 "%s: the shared expert must share the routed experts' quantisation here", op);
+  if (w->router_kind != ASTRO_MOE_ROUTER_SOFTMAX)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: expert parallelism takes the softmax router", op);
   L.w.experts = expert_count;
   L.ep = true;
   L.ep_first = expert_first;
@@ -1836,6 +1887,8 @@ int astro_moe_register_paged_layer(astro_moe_ctx* ctx, int32_t layer, const astr
       w->group_size != pg->group || w->bits != pg->bits)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: layer geometry differs from the pager's pages", op);
   if (int rc = validate_layer(op, w, /*routed_stacks=*/false)) return rc;
+  if (w->router_kind != ASTRO_MOE_ROUTER_SOFTMAX)
+    return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: paged layers take the softmax router", op);
   DeviceGuard g(ctx->device);
   LayerState& L = ctx->layers[layer];
   release_layer(L);

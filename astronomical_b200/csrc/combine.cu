@@ -26,34 +26,40 @@ __global__ void __launch_bounds__(256) block_combine_kernel(
     const uint4* __restrict__ rows, const uint4* __restrict__ shared_rows,
     const uint32_t* __restrict__ inverse, const __nv_bfloat16* __restrict__ scores,
     const __nv_bfloat16* __restrict__ gate_logit, int64_t shared_base, int64_t tokens, int K,
-    int H, int sorted, uint4* __restrict__ out) {
+    int H, int sorted, uint4* __restrict__ out, const float* __restrict__ scores_f32,
+    int has_shared, float factor) {
   __shared__ uint32_t s_row[32];
   __shared__ float s_score[32];
   const int chunks = H >> 3;
+  const bool laguna = scores_f32 != nullptr;
   for (int64_t t = blockIdx.x; t < tokens; t += gridDim.x) {
     if (threadIdx.x < K) {
       s_row[threadIdx.x] = __ldg(inverse + t * K + threadIdx.x);
-      s_score[threadIdx.x] = __bfloat162float(scores[t * K + threadIdx.x]);
+      s_score[threadIdx.x] = laguna ? scores_f32[t * K + threadIdx.x]
+                                    : __bfloat162float(scores[t * K + threadIdx.x]);
     }
     float sg = 0.f;
     if (gate_logit) sg = round_bf16(sigmoid_mlx(__bfloat162float(gate_logit[t])));
     __syncthreads();
     for (int c = threadIdx.x; c < chunks; c += blockDim.x)
       out[t * chunks + c] = combine_chunk(rows, shared_rows, chunks, c, s_row, s_score, K,
-                                          sorted != 0, gate_logit ? shared_base + t : -1, sg);
+                                          sorted != 0, has_shared ? shared_base + t : -1, sg,
+                                          laguna, factor);
     __syncthreads();  // s_row / s_score are rewritten for the next token
   }
 }
 
 cudaError_t launch_block_combine(const void* rows, const uint32_t* inverse, const void* scores,
                                  const void* gate_logit, int64_t shared_base, int64_t tokens,
-                                 int K, int H, int sorted, void* out, cudaStream_t st) {
+                                 int K, int H, int sorted, void* out, cudaStream_t st,
+                                 const float* scores_f32, int has_shared, float factor) {
   if (tokens == 0) return cudaSuccess;
   int64_t blocks = tokens < 148 * 64 ? tokens : 148 * 64;
   const int threads = (H / 8) < 256 ? ((H / 8 + 31) / 32) * 32 : 256;
   block_combine_kernel<<<(unsigned)blocks, threads, 0, st>>>(
       (const uint4*)rows, (const uint4*)rows, inverse, (const __nv_bfloat16*)scores,
-      (const __nv_bfloat16*)gate_logit, shared_base, tokens, K, H, sorted, (uint4*)out);
+      (const __nv_bfloat16*)gate_logit, shared_base, tokens, K, H, sorted, (uint4*)out,
+      scores_f32, has_shared < 0 ? (gate_logit != nullptr) : has_shared, factor);
   return cudaGetLastError();
 }
 
@@ -66,7 +72,8 @@ cudaError_t launch_block_combine_split(const void* rows, const void* shared_rows
   const int threads = (H / 8) < 256 ? ((H / 8 + 31) / 32) * 32 : 256;
   block_combine_kernel<<<(unsigned)blocks, threads, 0, st>>>(
       (const uint4*)rows, (const uint4*)shared_rows, inverse, (const __nv_bfloat16*)scores,
-      (const __nv_bfloat16*)gate_logit, 0, tokens, K, H, sorted, (uint4*)out);
+      (const __nv_bfloat16*)gate_logit, 0, tokens, K, H, sorted, (uint4*)out, nullptr,
+      gate_logit != nullptr, 1.0f);
   return cudaGetLastError();
 }
 

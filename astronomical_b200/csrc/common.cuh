@@ -82,6 +82,20 @@ ASTRO_DEVINL float expf_cw(float x) {
 // MLX sigmoid form: y = 1/(1+e^-|x|); x < 0 gives 1 - y.  The correctly rounded
 // reciprocal equals the correctly rounded quotient 1/d, so this matches an IEEE
 // division bit for bit.
+// 1 / (1 + e^-x) in fp32 (the Laguna router's CPU formula,
+// laguna/moe/router_selection.rs sigmoid); same steps as ao_sigmoid_plainf.
+ASTRO_DEVINL float sigmoid_plain(float x) {
+  return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf_cw(-x)));
+}
+
+// tanh(x) = s * (1 - 2 / (e^(2|x|) + 1)), s = sign(x), with the exp above (defined
+// here; same steps as ao_tanhf).
+ASTRO_DEVINL float tanh_cw(float x) {
+  const float a = fabsf(x);
+  const float t = __fsub_rn(1.0f, __fdiv_rn(2.0f, __fadd_rn(expf_cw(__fmul_rn(2.0f, a)), 1.0f)));
+  return x < 0.0f ? -t : t;
+}
+
 ASTRO_DEVINL float sigmoid_mlx(float x) {
   const float y = __frcp_rn(__fadd_rn(1.0f, expf_cw(-fabsf(x))));
   return (x < 0.0f) ? __fsub_rn(1.0f, y) : y;

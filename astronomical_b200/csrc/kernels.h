@@ -27,9 +27,14 @@ cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, 
 cudaError_t launch_take_rows(const void* src, int64_t src_rows, const uint32_t* rows, int64_t n,
                              int hidden, void* out, uint32_t* status, cudaStream_t st);
 
+// scores_f32 != nullptr: the Laguna combination (fp32 scores, routed sum times
+// `factor` -- already bf16-rounded -- and an ungated shared expert when has_shared);
+// has_shared < 0: a shared expert iff gate_logit is given (the Qwen combination).
 cudaError_t launch_block_combine(const void* rows, const uint32_t* inverse, const void* scores,
                                  const void* gate_logit, int64_t shared_base, int64_t tokens,
-                                 int K, int H, int sorted, void* out, cudaStream_t st);
+                                 int K, int H, int sorted, void* out, cudaStream_t st,
+                                 const float* scores_f32 = nullptr, int has_shared = -1,
+                                 float factor = 1.0f);
 
 // Same with the shared expert's rows in their own array: shared_rows[t] (row t
 // of the token), routed rows through `inverse` into `rows`.
@@ -141,6 +146,9 @@ cudaError_t launch_decode_fused(const DecodeFusedArgs& a, cudaStream_t st);
 
 cudaError_t launch_offsets_from_sorted(const uint32_t* ids, int64_t n, int E, uint32_t* offsets,
                                        uint32_t* status, cudaStream_t st);
+cudaError_t launch_route_laguna(const void* logits, int dtype, int64_t tokens, int E, int K,
+                                float softcap, const float* bias, int normalize, uint32_t* ids,
+                                float* scores, cudaStream_t st);
 cudaError_t launch_dequantize_affine(const uint32_t* packed, const void* scales,
                                      const void* biases, int64_t rows, int in_features, int group,
                                      int bits, void* out, cudaStream_t st);

@@ -88,6 +88,51 @@ cudaError_t launch_route_experts(const void* logits, int dtype, int64_t tokens, 
   }
 }
 
+// Laguna routing, one warp per token (route_token_laguna).
+template <typename T, int CMAX>
+__global__ void __launch_bounds__(256) route_laguna_kernel(
+    const T* __restrict__ logits, int64_t tokens, int E, int K, float softcap,
+    const float* __restrict__ bias, int normalize, uint32_t* __restrict__ out_ids,
+    float* __restrict__ out_scores) {
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t >= tokens) return;
+  route_token_laguna<T, CMAX>(logits + t * E, E, K, softcap, bias, normalize, out_ids + t * K,
+                              out_scores + t * K);
+}
+
+template <typename T>
+static cudaError_t launch_laguna_t(const void* logits, int64_t tokens, int E, int K, float softcap,
+                                   const float* bias, int normalize, uint32_t* ids, float* scores,
+                                   cudaStream_t st) {
+  if (tokens == 0) return cudaSuccess;
+  const int warps = 8;
+  const dim3 grid((unsigned)((tokens + warps - 1) / warps)), block(warps * 32);
+  const int C = (E + 31) / 32;
+  auto run = [&](auto kern) {
+    kern<<<grid, block, 0, st>>>((const T*)logits, tokens, E, K, softcap, bias, normalize, ids,
+                                 scores);
+  };
+  if (C <= 4) run(route_laguna_kernel<T, 4>);
+  else if (C <= 8) run(route_laguna_kernel<T, 8>);
+  else if (C <= 16) run(route_laguna_kernel<T, 16>);
+  else run(route_laguna_kernel<T, 32>);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_route_laguna(const void* logits, int dtype, int64_t tokens, int E, int K,
+                                float softcap, const float* bias, int normalize, uint32_t* ids,
+                                float* scores, cudaStream_t st) {
+  switch (dtype) {
+    case kBF16:
+      return launch_laguna_t<__nv_bfloat16>(logits, tokens, E, K, softcap, bias, normalize, ids,
+                                            scores, st);
+    case kF16:
+      return launch_laguna_t<__half>(logits, tokens, E, K, softcap, bias, normalize, ids, scores, st);
+    default:
+      return launch_laguna_t<float>(logits, tokens, E, K, softcap, bias, normalize, ids, scores, st);
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Dense bf16 projection out[r, c] = bf16(sum_k x[r,k] w[c,k]) for the router
 // when the tensor-core path is not used (portable SIMT tile kernel: 64x64

@@ -124,4 +124,69 @@ ASTRO_DEVINL void route_token(const T* row, int E, int K, int normalize, uint32_
 }
 
 
+// fp32 -> uint32 whose unsigned order is the IEEE total order (total_cmp)
+ASTRO_DEVINL uint32_t ordered_bits(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Laguna routing of one token with the calling warp (route_laguna_experts,
+// laguna/moe/router.rs:11-60; CPU owner laguna/moe/router_selection.rs:47-107):
+// score = sigmoid(softcap > 0 ? softcap * tanh(logit / softcap) : logit) in fp32,
+// selection = score + bias[e] (bias may be null), the K largest selections by
+// (value desc, id asc; IEEE total order), each winner's original score, and with
+// `normalize` the scores divided by their sum (in slot order) when it is > 0.
+// Lane k < K writes winner k to ids[k] / scores[k].
+template <typename T, int CMAX>
+ASTRO_DEVINL void route_token_laguna(const T* row, int E, int K, float softcap, const float* bias,
+                                     int normalize, uint32_t* ids, float* scores) {
+  const int lane = threadIdx.x & 31;
+  const int C = (E + 31) >> 5;
+  const int i0 = lane * C;
+  float orig[CMAX];
+  uint64_t key[CMAX];
+#pragma unroll
+  for (int c = 0; c < CMAX; ++c) {
+    const int i = i0 + c;
+    const bool valid = c < C && i < E;
+    float l = valid ? Num<T>::load(row, i) : 0.0f;
+    if (softcap > 0.0f) l = __fmul_rn(tanh_cw(__fdiv_rn(l, softcap)), softcap);
+    const float sc = sigmoid_plain(l);
+    const float sel = bias ? __fadd_rn(sc, bias[valid ? i : 0]) : sc;
+    orig[c] = sc;
+    key[c] = valid ? (((uint64_t)ordered_bits(sel) << 32) | (uint64_t)(0xffffffffu - (uint32_t)i)) : 0ull;
+  }
+  float sel_score = 0.0f;
+  uint32_t sel_id = 0;
+  float sum = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    uint64_t best = 0;
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c) best = key[c] > best ? key[c] : best;
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) {
+      const uint64_t o = __shfl_xor_sync(0xffffffffu, best, m);
+      best = o > best ? o : best;
+    }
+    const uint32_t wid = 0xffffffffu - (uint32_t)(best & 0xffffffffu);
+    float mine = 0.0f;
+#pragma unroll
+    for (int c = 0; c < CMAX; ++c)
+      if (key[c] == best) {
+        mine = orig[c];
+        key[c] = 0ull;
+      }
+    const float w = __shfl_sync(0xffffffffu, mine, (int)(wid / (uint32_t)C));
+    if (lane == k) {
+      sel_score = w;
+      sel_id = wid;
+    }
+    sum = __fadd_rn(sum, w);
+  }
+  if (lane < K) {
+    ids[lane] = sel_id;
+    scores[lane] = (normalize && sum > 0.0f) ? __fdiv_rn(sel_score, sum) : sel_score;
+  }
+}
+
 }  // namespace astro

@@ -136,6 +136,33 @@ def qwen3_5_moe_route_experts(router_logits: torch.Tensor, expert_count_per_toke
     return ids, scores
 
 
+def route_laguna_experts(router_logits: torch.Tensor, experts_per_token: int,
+                         correction_bias: Optional[torch.Tensor] = None,
+                         router_logit_softcap: float = 0.0, normalize: bool = True):
+    """Laguna routing (laguna/moe/router.rs:11-60): sigmoid scores (optionally
+    softcapped), correction bias for the ranking only, original fp32 scores of
+    the K winners (optionally renormalised)."""
+    shape = list(router_logits.shape)
+    if len(shape) < 2:
+        raise AstroMoeError(_lib.ERR_INVALID_ARGUMENT,
+                            "router logits must include token and expert dimensions")
+    E = shape[-1]
+    T = int(np.prod(shape[:-1]))
+    logits = router_logits.contiguous()
+    bias = None if correction_bias is None else correction_bias.to(torch.float32).contiguous()
+    if bias is not None and bias.numel() != E:
+        raise AstroMoeError(_lib.ERR_INVALID_ARGUMENT,
+                            "Laguna correction bias must have one value per expert")
+    ids = torch.empty(shape[:-1] + [experts_per_token], dtype=torch.int32, device=logits.device)
+    scores = torch.empty(shape[:-1] + [experts_per_token], dtype=torch.float32,
+                         device=logits.device)
+    check(_lib.lib().astro_moe_route_laguna_experts(
+        _ptr(logits), _dtype(logits), T, E, experts_per_token,
+        _ptr(bias) if bias is not None else None, float(router_logit_softcap), int(normalize),
+        _ptr(ids), _ptr(scores), _stream(logits)))
+    return ids, scores
+
+
 def sort_expert_assignments(expanded_states: torch.Tensor, selected_indices: torch.Tensor,
                             experts: Optional[int] = None) -> SortedExpertAssignments:
     """Stable sort by expert id; gathers the token rows (take) like the reference."""
@@ -316,6 +343,14 @@ def layer_weights_struct(t: dict, cfg: dict, experts: int, fuse_gate_up: bool = 
     lw.shared_gate, lw.shared_up, lw.shared_down = aff("sgate"), aff("sup"), aff("sdown")
     lw.shared_expert_gate = t["shared_gate_w"].data_ptr() if "shared_gate_w" in t else None
     lw.shared_expert_gate_affine = aff("shared_gate")
+    # Laguna router family (laguna/moe/router.rs): sigmoid scores, selection-only
+    # correction bias, optional logit softcap, routed scaling, ungated shared expert
+    if cfg.get("router") == "laguna":
+        lw.router_kind = _lib.ROUTER_SIGMOID
+        lw.router_logit_softcap = float(cfg.get("router_logit_softcap", 0.0))
+        lw.routed_scaling_factor = float(cfg.get("routed_scaling_factor", 1.0))
+        lw.router_correction_bias = (t["router_correction_bias"].data_ptr()
+                                     if "router_correction_bias" in t else None)
     return lw
 
 
@@ -403,7 +438,8 @@ class Qwen3_5MoEBlock:
         tp = {
             "router_logits": torch.empty((T, E), dtype=torch.bfloat16, device=x.device),
             "selected_indices": torch.empty((T, K), dtype=torch.int32, device=x.device),
-            "selected_scores": torch.empty((T, K), dtype=torch.bfloat16, device=x.device),
+            "selected_scores": torch.empty((T, K), dtype=torch.float32 if self.cfg.get("router") ==
+                                           "laguna" else torch.bfloat16, device=x.device),
             "expert_offsets": torch.empty(E + 2, dtype=torch.int32, device=x.device),
         }
         ct = _lib.BlockTaps(*(tp[k].data_ptr() for k in ("router_logits", "selected_indices",

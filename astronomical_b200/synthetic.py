@@ -33,6 +33,14 @@ CONFIGS = {
 }
 
 
+# Laguna-shaped variant of config 1 (laguna/moe: 256 experts, sigmoid router with
+# a selection-only correction bias, routed_scaling_factor 2.5, an ungated shared
+# expert of the routed width); the same block kernels, another router family
+LAGUNA = dict(tokens=512, hidden=2048, experts=256, top_k=8, intermediate=512,
+              shared_intermediate=512, group=64, bits=4, normalize=True, zipf=None,
+              router="laguna", router_logit_softcap=0.0, routed_scaling_factor=2.5)
+
+
 def f32_to_bf16(a) -> np.ndarray:
     """Round-to-nearest-even float32 -> bf16 bit patterns."""
     u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32).astype(np.uint64)
@@ -145,6 +153,11 @@ def make_block_weights(cfg: dict, seed: int = 0, quant: dict | None = None) -> d
         w["sup_q"], w["sup_s"], w["sup_b"] = _affine(rng, (Is,), H, G, B)
         w["sdown_q"], w["sdown_s"], w["sdown_b"] = _affine(rng, (H,), Is, G, B)
         w["shared_gate_w"] = f32_to_bf16(rng.normal(0.0, 0.02, size=(1, H)))
+    if cfg.get("router") == "laguna":
+        # a per-expert correction bias of the size sigmoid scores move by
+        brng = np.random.default_rng([seed, 99])
+        w["router_correction_bias"] = brng.normal(0.0, 0.05, size=E).astype(np.float32)
+        w.pop("shared_gate_w", None)  # the Laguna shared expert is ungated
     for name, (bits, group) in (quant or {}).items():
         if name not in QUANT_NAMES:
             raise ValueError(f"unknown projection {name}")

@@ -93,6 +93,20 @@ int astro_moe_route_experts(const void* router_logits, int32_t dtype, int64_t to
                             int32_t experts, int32_t top_k, int32_t normalize,
                             uint32_t* selected_indices, void* selected_scores, void* stream);
 
+/* route_laguna_experts, crates/model-serving/src/laguna/moe/router.rs:11-60 (CPU
+ * owner laguna/moe/router_selection.rs:47-107): per token, score = sigmoid(l) in
+ * fp32 with l = softcap * tanh(logit / softcap) when router_logit_softcap > 0
+ * (else the logit); selection = score + correction_bias[e] (fp32 [experts], may
+ * be NULL) ranks the experts, the K largest by (selection desc, expert id asc)
+ * are selected, and their original scores are gathered, divided by their sum
+ * (slot order) when normalize != 0 and that sum is > 0.  selected_scores fp32
+ * [tokens, top_k].  top_k <= 32, experts <= 1024. */
+int astro_moe_route_laguna_experts(const void* router_logits, int32_t dtype, int64_t tokens,
+                                   int32_t experts, int32_t top_k, const float* correction_bias,
+                                   double router_logit_softcap, int32_t normalize,
+                                   uint32_t* selected_indices, float* selected_scores,
+                                   void* stream);
+
 /* sort_expert_assignments, crates/model-serving/src/sparse_experts/assignment_sort.rs:36-97
  * (argsort_axis mlx_operations.rs:377 twice, floor_divide :178).  Stable.  Any
  * output pointer may be NULL.  expert_offsets has experts+1 entries (the
@@ -254,13 +268,24 @@ typedef struct {
   const void* shared_expert_gate;  /* bf16 [1, H] */
   astro_moe_affine router_affine;            /* [E, H*bits/32] when router_weight is NULL */
   astro_moe_affine shared_expert_gate_affine; /* [1, H*bits/32] when shared_expert_gate is NULL */
+  /* Router family.  ASTRO_MOE_ROUTER_SOFTMAX: Qwen3.5/3.6 (softmax top-K, bf16
+   * scores, sigmoid-gated shared expert).  ASTRO_MOE_ROUTER_SIGMOID: Laguna
+   * (laguna/moe/resident.rs:60-100): astro_moe_route_laguna_experts with the
+   * fields below, fp32 scores, the routed sum times routed_scaling_factor
+   * (0 = 1), and an ungated shared expert (shared_expert_gate unused). */
+  int32_t router_kind;
+  float router_logit_softcap;          /* Laguna: > 0 applies softcap * tanh(logit / softcap) */
+  float routed_scaling_factor;         /* Laguna */
+  const float* router_correction_bias; /* Laguna: fp32 [E] or NULL */
 } astro_moe_layer_weights;
+
+enum { ASTRO_MOE_ROUTER_SOFTMAX = 0, ASTRO_MOE_ROUTER_SIGMOID = 1 };
 
 /* Optional device outputs of one block call, for parity checks. */
 typedef struct {
   void* router_logits;        /* bf16 [tokens, E] */
   uint32_t* selected_indices; /* [tokens, K] */
-  void* selected_scores;      /* bf16 [tokens, K] */
+  void* selected_scores;      /* bf16 [tokens, K] (fp32 for a Laguna router) */
   uint32_t* expert_offsets;   /* [E + 2] (segment E = shared expert rows) */
 } astro_moe_block_taps;
 

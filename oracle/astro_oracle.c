@@ -411,6 +411,63 @@ int ao_route_experts(const void* logits, int dtype, int64_t tokens, int experts,
 }
 
 /* ------------------------------------------------------------------------ */
+/* f4: Laguna router                                                         */
+/* ------------------------------------------------------------------------ */
+
+float ao_sigmoid_plainf(float x) { return 1.0f / (1.0f + ao_expf(-x)); }
+
+float ao_tanhf(float x) {
+  const float a = fabsf(x);
+  const float t = 1.0f - 2.0f / (ao_expf(2.0f * a) + 1.0f);
+  return x < 0.0f ? -t : t;
+}
+
+/* IEEE total order of fp32 as an unsigned key (Rust's f32::total_cmp) */
+static inline uint32_t ordered_bits(float v) {
+  const uint32_t u = f2u(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+int ao_route_laguna_experts(const void* logits, int dtype, int64_t tokens, int experts, int top_k,
+                            const float* bias, float softcap, int normalize, uint32_t* out_ids,
+                            float* out_scores) {
+  /* validate_router_geometry, router_selection.rs:127-150 */
+  if (tokens < 0 || experts <= 0 || top_k <= 0 || top_k > experts || softcap != softcap ||
+      softcap < 0.0f)
+    return AO_ERR_INVALID_ARGUMENT;
+  if (dtype != AO_BF16 && dtype != AO_F16 && dtype != AO_F32) return AO_ERR_INVALID_ARGUMENT;
+#pragma omp parallel
+  {
+    float* sc = (float*)malloc(sizeof(float) * (size_t)experts);
+    uint64_t* key = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)experts);
+#pragma omp for schedule(static)
+    for (int64_t t = 0; t < tokens; ++t) {
+      for (int e = 0; e < experts; ++e) {
+        float l = load_dt(logits, dtype, t * experts + e);
+        if (softcap > 0.0f) l = ao_tanhf(l / softcap) * softcap;
+        sc[e] = ao_sigmoid_plainf(l);
+        const float sel = bias ? sc[e] + bias[e] : sc[e];
+        key[e] = ((uint64_t)ordered_bits(sel) << 32) | (uint64_t)(0xffffffffu - (uint32_t)e);
+      }
+      float sum = 0.0f;
+      for (int k = 0; k < top_k; ++k) {
+        int best = 0;
+        for (int e = 1; e < experts; ++e) best = key[e] > key[best] ? e : best;
+        out_ids[t * top_k + k] = (uint32_t)best;
+        out_scores[t * top_k + k] = sc[best];
+        sum = sum + sc[best];
+        key[best] = 0;
+      }
+      if (normalize && sum > 0.0f)
+        for (int k = 0; k < top_k; ++k) out_scores[t * top_k + k] = out_scores[t * top_k + k] / sum;
+    }
+    free(key);
+    free(sc);
+  }
+  return AO_OK;
+}
+
+/* ------------------------------------------------------------------------ */
 /* a3: stable sort of assignments by expert                                  */
 /* ------------------------------------------------------------------------ */
 
@@ -722,10 +779,23 @@ static uint16_t* dense_or_affine(const uint16_t* dense, const uint32_t* q, const
   return out;
 }
 
+/* Laguna combination (laguna/moe/resident.rs:89-100): routed = multiply_scalar(
+ * sparse, factor) with the scalar cast to bf16 first (mlx_operations.rs:234-242),
+ * rounded to bf16; out = bf16(routed + shared) (shared NULL: routed). */
+static void laguna_finish(const uint16_t* sparse, const uint16_t* shared, int64_t nt, int H,
+                          float factor, uint16_t* out) {
+  const float f = rnd_bf16(factor > 0.0f ? factor : 1.0f);
+  for (int64_t i = 0; i < nt * H; ++i) {
+    float y = rnd_bf16(ao_bf16_to_f32(sparse[i]) * f);
+    if (shared) y = y + ao_bf16_to_f32(shared[i]);
+    out[i] = ao_f32_to_bf16(y);
+  }
+}
+
 int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t tokens,
                          const int64_t* token_subset, int64_t n_subset,
                          const uint16_t* logits_override, uint16_t* out,
-                         uint32_t* out_ids, uint16_t* out_scores, int num_threads) {
+                         uint32_t* out_ids, void* out_scores, int num_threads) {
   return ao_moe_block_forward_terms(w, x, tokens, token_subset, n_subset, logits_override, out,
                                     out_ids, out_scores, NULL, NULL, num_threads);
 }
@@ -733,7 +803,7 @@ int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t t
 int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int64_t tokens,
                                const int64_t* token_subset, int64_t n_subset,
                                const uint16_t* logits_override, uint16_t* out,
-                               uint32_t* out_ids, uint16_t* out_scores, uint16_t* out_sparse,
+                               uint32_t* out_ids, void* out_scores, uint16_t* out_sparse,
                                uint16_t* out_shared_gated, int num_threads) {
   const int H = w->hidden, E = w->experts, K = w->top_k, I = w->intermediate;
   const int Is = w->shared_intermediate;
@@ -777,10 +847,16 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
     ao_matmul_bf16_nt_mode(xs, wr, nt, E, H, m_router, logits);
     free(wr);
   }
-  /* a2: route (routing.rs:16-49) */
+  /* a2: route (routing.rs:16-49), or the Laguna router (f4) with fp32 scores */
+  const int laguna = w->router_kind == 1;
   uint32_t* ids = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(nt > 0 ? nt : 1) * K);
   uint16_t* scores = (uint16_t*)malloc(sizeof(uint16_t) * (size_t)(nt > 0 ? nt : 1) * K);
-  ao_route_experts(logits, AO_BF16, nt, E, K, w->normalize, ids, scores);
+  float* fscores = (float*)malloc(sizeof(float) * (size_t)(nt > 0 ? nt : 1) * K);
+  if (laguna)
+    ao_route_laguna_experts(logits, AO_BF16, nt, E, K, w->router_correction_bias,
+                            w->router_logit_softcap, w->normalize, ids, fscores);
+  else
+    ao_route_experts(logits, AO_BF16, nt, E, K, w->normalize, ids, scores);
   /* a3: sort (assignment_sort.rs:79-91) */
   const int64_t n = nt * K;
   uint32_t* order = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)(n > 0 ? n : 1));
@@ -821,8 +897,9 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
       float acc = 0.0f;
       for (int k = 0; k < K; ++k) {
         const float yv = ao_bf16_to_f32(yrows[(int64_t)inv[t * K + k] * H + d]);
-        const float sv = ao_bf16_to_f32(scores[t * K + k]);
+        const float sv = laguna ? fscores[t * K + k] : ao_bf16_to_f32(scores[t * K + k]);
         if (sorted) acc = fmaf(yv, sv, acc);
+        else if (laguna) acc = acc + yv * sv; /* bf16 x f32 promotes to f32 */
         else acc = acc + rnd_bf16(yv * sv);
       }
       sparse[t * H + d] = ao_f32_to_bf16(acc);
@@ -851,12 +928,17 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
       ao_swiglu(sg + t0 * Is, su + t0 * Is, m * Is, sa + t0 * Is);
       expert_rows(&P[5], 0, H, Is, ar, m, m_sdown, so + t0 * H, H);
     }
+    if (laguna) {
+      laguna_finish(sparse, so, nt, H, w->routed_scaling_factor, out);
+      if (out_shared_gated) memcpy(out_shared_gated, so, sizeof(uint16_t) * (size_t)nt * H);
+    } else {
     uint16_t* wg = dense_or_affine(w->shared_gate_w, w->shared_gate_q, w->shared_gate_s,
                                    w->shared_gate_b, w->shared_gate_bits, w->shared_gate_group, 1, H);
     ao_matmul_bf16_nt_mode(xs, wg, nt, 1, H, m_glogit, gl);
     free(wg);
     ao_combine_sparse_and_shared(sparse, so, gl, AO_BF16, nt, H, out);
-    if (out_shared_gated) {
+    }
+    if (out_shared_gated && !laguna) {
       for (int64_t t = 0; t < nt; ++t) {
         const float g = rnd_bf16(ao_sigmoidf(ao_bf16_to_f32(gl[t])));
         for (int d = 0; d < H; ++d)
@@ -865,13 +947,17 @@ int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int
     }
     free(gl); free(so); free(sa); free(su); free(sg);
   } else {
-    memcpy(out, sparse, sizeof(uint16_t) * (size_t)nt * H);
+    if (laguna) laguna_finish(sparse, NULL, nt, H, w->routed_scaling_factor, out);
+    else memcpy(out, sparse, sizeof(uint16_t) * (size_t)nt * H);
     if (out_shared_gated) memset(out_shared_gated, 0, sizeof(uint16_t) * (size_t)nt * H);
   }
   if (out_sparse) memcpy(out_sparse, sparse, sizeof(uint16_t) * (size_t)nt * H);
   if (out_ids) memcpy(out_ids, ids, sizeof(uint32_t) * (size_t)n);
-  if (out_scores) memcpy(out_scores, scores, sizeof(uint16_t) * (size_t)n);
+  if (out_scores) {
+    if (laguna) memcpy(out_scores, fscores, sizeof(float) * (size_t)n);
+    else memcpy(out_scores, scores, sizeof(uint16_t) * (size_t)n);
+  }
   free(sparse); free(yrows); free(offs); free(stok); free(sids); free(inv); free(order);
-  free(scores); free(ids); free(logits); free(xs);
+  free(fscores); free(scores); free(ids); free(logits); free(xs);
   return AO_OK;
 }

@@ -111,6 +111,19 @@ void ao_matmul_bf16_nt_mode(const uint16_t* x, const uint16_t* w, int64_t rows, 
 int ao_route_experts(const void* logits, int dtype, int64_t tokens, int experts, int top_k,
                      int normalize, uint32_t* out_ids, void* out_scores);
 
+/* f4: Laguna router, laguna/moe/router_selection.rs:47-107 (the authoritative CPU
+ * formula of laguna/moe/router.rs:11-60): score = sigmoid(l), l = softcap *
+ * tanh(logit / softcap) when softcap > 0; selection = score + bias[e] (bias may
+ * be NULL); top-K by (selection desc, id asc; IEEE total order); the winners'
+ * original scores, divided by their slot-order sum when normalize and sum > 0.
+ * exp, sigmoid and tanh are ao_expf, ao_sigmoid_plainf and ao_tanhf (defined
+ * here; the kernel evaluates the same steps).  scores fp32 [tokens, K]. */
+float ao_sigmoid_plainf(float x);         /* 1 / (1 + e^-x) */
+float ao_tanhf(float x);                  /* sign(x) * (1 - 2 / (e^(2|x|) + 1)) */
+int ao_route_laguna_experts(const void* logits, int dtype, int64_t tokens, int experts, int top_k,
+                            const float* bias, float softcap, int normalize, uint32_t* out_ids,
+                            float* out_scores);
+
 /* a3: sort_expert_assignments, sparse_experts/assignment_sort.rs:36-97.
  * expert_offsets has experts+1 entries (exclusive scan of the histogram). */
 int ao_sort_expert_assignments(const uint32_t* ids, int64_t tokens, int top_k, int experts,
@@ -180,6 +193,15 @@ typedef struct {
   /* Accumulation modes (AO_DOT_*): router, shared-gate logit, routed gate/up,
    * routed down, shared gate/up, shared down. */
   int arith[6];
+  /* Router family: 0 Qwen (softmax, bf16 scores, sigmoid-gated shared expert);
+   * 1 Laguna (laguna/moe/resident.rs:60-100): ao_route_laguna_experts with the
+   * fields below, fp32 scores, the routed sum times bf16(routed_scaling_factor)
+   * (<= 0: 1) rounded to bf16, plus the ungated shared expert.  out_scores of
+   * the block functions are bf16 for 0 and fp32 for 1. */
+  int router_kind;
+  float router_logit_softcap;
+  float routed_scaling_factor;
+  const float* router_correction_bias;
 } ao_block_weights;
 
 /* Runs the block for the tokens listed in token_subset (NULL = all tokens).  The
@@ -190,7 +212,7 @@ typedef struct {
 int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t tokens,
                          const int64_t* token_subset, int64_t n_subset,
                          const uint16_t* logits_override, uint16_t* out,
-                         uint32_t* out_ids, uint16_t* out_scores, int num_threads);
+                         uint32_t* out_ids, void* out_scores, int num_threads);
 
 /* Same, also returning the two bf16 terms of the final addition (the routed
  * weighted sum and the gated shared-expert output; zero without a shared
@@ -198,7 +220,7 @@ int ao_moe_block_forward(const ao_block_weights* w, const uint16_t* x, int64_t t
 int ao_moe_block_forward_terms(const ao_block_weights* w, const uint16_t* x, int64_t tokens,
                                const int64_t* token_subset, int64_t n_subset,
                                const uint16_t* logits_override, uint16_t* out,
-                               uint32_t* out_ids, uint16_t* out_scores, uint16_t* out_sparse,
+                               uint32_t* out_ids, void* out_scores, uint16_t* out_sparse,
                                uint16_t* out_shared_gated, int num_threads);
 
 #ifdef __cplusplus

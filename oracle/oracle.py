@@ -72,6 +72,10 @@ def _declare(l: ctypes.CDLL) -> None:
     l.ao_moe_block_forward_terms.argtypes = [P, P, I64, P, I64, P, P, P, P, P, P, I]
     l.ao_moe_block_forward_terms.restype = I
     l.ao_tc_step.argtypes, l.ao_tc_step.restype = [ctypes.c_float, P, P], ctypes.c_float
+    l.ao_route_laguna_experts.argtypes = [P, I, I64, I, I, P, ctypes.c_float, I, P, P]
+    l.ao_route_laguna_experts.restype = I
+    l.ao_sigmoid_plainf.argtypes, l.ao_sigmoid_plainf.restype = [ctypes.c_float], ctypes.c_float
+    l.ao_tanhf.argtypes, l.ao_tanhf.restype = [ctypes.c_float], ctypes.c_float
     l.ao_dot.argtypes, l.ao_dot.restype = [P, P, I64, I], ctypes.c_float
     l.ao_tc_chain_batch.argtypes, l.ao_tc_chain_batch.restype = [P, P, P, I64, I64, P], None
     l.ao_matmul_bf16_nt_mode.argtypes = [P, P, I64, I64, I64, I, P]
@@ -91,7 +95,9 @@ class BlockWeights(ctypes.Structure):
         ("router_bits", ctypes.c_int), ("router_group", ctypes.c_int),
         ("shared_gate_q", ctypes.c_void_p), ("shared_gate_s", ctypes.c_void_p),
         ("shared_gate_b", ctypes.c_void_p), ("shared_gate_bits", ctypes.c_int),
-        ("shared_gate_group", ctypes.c_int), ("arith", ctypes.c_int * 6)]
+        ("shared_gate_group", ctypes.c_int), ("arith", ctypes.c_int * 6),
+        ("router_kind", ctypes.c_int), ("router_logit_softcap", ctypes.c_float),
+        ("routed_scaling_factor", ctypes.c_float), ("router_correction_bias", ctypes.c_void_p)]
 
 
 # accumulation modes of a dot product (AO_DOT_* in astro_oracle.h)
@@ -221,6 +227,23 @@ def route_experts(logits, top_k: int, normalize: bool = True, bf16: bool = True)
     st = lib().ao_route_experts(_p(logits), code, T, E, top_k, int(normalize), _p(ids), _p(scores))
     if st != OK:
         raise ValueError(f"route_experts status {st}")
+    return ids, scores
+
+
+def route_laguna_experts(logits, top_k: int, correction_bias=None, softcap: float = 0.0,
+                         normalize: bool = True, bf16: bool = True):
+    """Laguna router (laguna/moe/router_selection.rs:47-107): logits [T, E] ->
+    (ids u32 [T, K], fp32 original scores [T, K])."""
+    logits = np.ascontiguousarray(logits)
+    code = dtype_code(logits, bf16)
+    T, E = logits.shape
+    ids = np.empty((T, top_k), np.uint32)
+    scores = np.empty((T, top_k), np.float32)
+    b = None if correction_bias is None else _c(correction_bias, np.float32)
+    st = lib().ao_route_laguna_experts(_p(logits), code, T, E, top_k, _p(b), float(softcap),
+                                       int(normalize), _p(ids), _p(scores))
+    if st != OK:
+        raise ValueError(f"route_laguna_experts status {st}")
     return ids, scores
 
 
@@ -366,13 +389,17 @@ def moe_block_forward(weights: dict, x, token_subset=None, logits_override=None,
         shared_gate_b=arr("shared_gate_b", np.uint16),
         shared_gate_bits=int(weights.get("shared_gate_bits", 0)),
         shared_gate_group=int(weights.get("shared_gate_group", 0)),
-        arith=(ctypes.c_int * 6)(*arith_codes(arith)))
+        arith=(ctypes.c_int * 6)(*arith_codes(arith)),
+        router_kind=1 if cfg.get("router") == "laguna" else 0,
+        router_logit_softcap=float(cfg.get("router_logit_softcap", 0.0)),
+        routed_scaling_factor=float(cfg.get("routed_scaling_factor", 1.0)),
+        router_correction_bias=arr("router_correction_bias", np.float32))
     sub = None if token_subset is None else _c(token_subset, np.int64)
     n = T if sub is None else sub.size
     K = cfg["top_k"]
     y = np.empty((n, H), np.uint16)
     ids = np.empty((n, K), np.uint32)
-    sc = np.empty((n, K), np.uint16)
+    sc = np.empty((n, K), np.float32 if cfg.get("router") == "laguna" else np.uint16)
     lo = None if logits_override is None else _c(logits_override, np.uint16)
     sp = np.empty((n, H), np.uint16) if terms else None
     sg = np.empty((n, H), np.uint16) if terms else None

@@ -45,7 +45,8 @@ def compare_block(w, x, y, taps, kernels, subset=None, case="block", canonical=T
     T = x.shape[0] if T is None else T
     logits = to_np_bf16(taps["router_logits"])
     ids = to_np_u32(taps["selected_indices"])
-    scores = to_np_bf16(taps["selected_scores"])
+    scores = (taps["selected_scores"].cpu().numpy() if cfg.get("router") == "laguna"
+              else to_np_bf16(taps["selected_scores"]))
     offs = to_np_u32(taps["expert_offsets"])
     got = to_np_bf16(y)
     arith = oracle_arith(kernels)
@@ -248,3 +249,19 @@ def test_gate_and_up_must_share_their_quantisation():
     w = synthetic.make_block_weights(cfg, seed=3, quant={"gate": (8, 64)})
     with pytest.raises(moe.AstroMoeError, match="gate and up"):
         moe.Qwen3_5MoEBlock(w, max_tokens=8)
+
+
+# The Laguna router family (laguna/moe/router.rs, resident.rs:60-100) on the same
+# sort, GEMMs and combine: sigmoid scores with a selection-only correction bias,
+# fp32 scores, routed sum scaled by 2.5, ungated shared expert.
+@pytest.mark.parametrize("path", [PATHS[0], PATHS[1], PATHS[2]])
+@pytest.mark.parametrize("T", [1, 7, 64, 512])
+def test_block_laguna_router(T, path):
+    cfg = dict(synthetic.LAGUNA)
+    f = run_and_compare(cfg, T, seed=500 + T, path=path, case="laguna")
+    assert f["kernels"]["gate_logit"] == "none"
+
+
+def test_block_laguna_softcap_and_no_shared_expert():
+    cfg = dict(synthetic.LAGUNA, router_logit_softcap=1.5, shared_intermediate=0)
+    run_and_compare(cfg, 96, seed=7, case="laguna_softcap")

@@ -62,6 +62,38 @@ def test_route_known_answer():
     assert abs(got[0] - 3 / 7) <= 1e-6 and abs(got[1] - 4 / 7) <= 1e-6
 
 
+@pytest.mark.parametrize("T,E,K", [(4096, 256, 8), (77, 160, 10), (5, 4, 2), (64, 1024, 32)])
+@pytest.mark.parametrize("kind", ["normal", "ties", "router"])
+@pytest.mark.parametrize("bias,softcap,normalize", [(False, 0.0, True), (True, 0.0, True),
+                                                    (True, 2.5, False), (False, 1.0, True)])
+def test_route_laguna_bit_exact(T, E, K, kind, bias, softcap, normalize):
+    # laguna/moe/router.rs:11-60 against the oracle's restatement of the CPU owner
+    lg = f32_to_bf16(_logits(T, E, T * 11 + E, kind))
+    b = np.random.default_rng(E).normal(0, 0.05, E).astype(np.float32) if bias else None
+    ids_o, sc_o = O.route_laguna_experts(lg, K, b, softcap, normalize)
+    ids, sc = moe.route_laguna_experts(bf16_tensor(lg), K,
+                                       None if b is None else torch.from_numpy(b).cuda(),
+                                       softcap, normalize)
+    torch.cuda.synchronize()
+    assert np.array_equal(to_np_u32(ids), ids_o)
+    assert np.array_equal(sc.cpu().numpy().view(np.uint32), sc_o.view(np.uint32))
+
+
+def test_route_laguna_known_answers():
+    # laguna_hermetic/routing.rs:9-56
+    lg = torch.tensor([[0.0, 2.0, -2.0, 0.5]], device="cuda")
+    ids, sc = moe.route_laguna_experts(lg, 2, torch.tensor([2.0, 0, 0, 0], device="cuda"),
+                                       normalize=False)
+    assert ids.cpu().tolist() == [[0, 1]]
+    assert abs(sc[0, 0].item() - 0.5) < 1e-6 and abs(sc[0, 1].item() - 1 / (1 + math.exp(-2))) < 1e-6
+    ids, _ = moe.route_laguna_experts(torch.tensor([[0.0, 0.0, -4.0]], device="cuda"), 1)
+    assert ids.cpu().tolist() == [[0]]
+    _, nrm = moe.route_laguna_experts(torch.tensor([[1.0, 0.0, -1.0]], device="cuda"), 2)
+    assert abs(nrm.sum().item() - 1.0) < 1e-6
+    with pytest.raises(AstroMoeError):
+        moe.route_laguna_experts(torch.zeros((1, 2), device="cuda"), 3)
+
+
 def test_route_rejects_bad_arguments():
     lg = torch.zeros((2, 4), device="cuda")
     with pytest.raises(AstroMoeError):
