@@ -56,6 +56,7 @@ class LayerWeights(ctypes.Structure):
         ("router_correction_bias", ctypes.c_void_p)]
 
 ROUTER_SOFTMAX, ROUTER_SIGMOID = 0, 1
+PAGER_LRU, PAGER_DEMAND = 0, 1
 
 
 class BlockTaps(ctypes.Structure):
@@ -81,7 +82,7 @@ class PagerStats(ctypes.Structure):
                 ("evictions", ctypes.c_int64), ("bytes_h2d", ctypes.c_int64),
                 ("copy_ms", ctypes.c_double), ("resident_pages", ctypes.c_int64),
                 ("capacity_pages", ctypes.c_int64), ("calls", ctypes.c_int64),
-                ("split_calls", ctypes.c_int64)]
+                ("split_calls", ctypes.c_int64), ("copy_failures", ctypes.c_int64)]
 
     def as_dict(self):
         return {n: getattr(self, n) for n, _ in self._fields_}
@@ -107,6 +108,7 @@ SIGNATURES = {
     "astro_moe_device_status": ([_I32, _P, _I32], ctypes.c_int),
     "astro_moe_tensor_core_probe": ([_I32, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _P],
                                     ctypes.c_int),
+    "astro_moe_wait_probe": ([_I32, _P, ctypes.c_uint32, _I64, _P, _P, _P], ctypes.c_int),
     "astro_moe_route_experts": ([_P, _I32, _I64, _I32, _I32, _I32, _P, _P, _P], ctypes.c_int),
     "astro_moe_route_laguna_experts": ([_P, _I32, _I64, _I32, _I32, _P, ctypes.c_double, _I32,
                                         _P, _P, _P], ctypes.c_int),
@@ -162,6 +164,8 @@ SIGNATURES = {
     "astro_moe_pager_create": ([_P, _I32, _I32, _I32, _I32, _I32, _I32, _P, _I64,
                                 ctypes.POINTER(ctypes.c_void_p)], ctypes.c_int),
     "astro_moe_pager_destroy": ([_P], ctypes.c_int),
+    "astro_moe_pager_set_policy": ([_P, _I32], ctypes.c_int),
+    "astro_moe_pager_inject_copy_failures": ([_P, _I64], ctypes.c_int),
     "astro_moe_pager_read_stats": ([_P, ctypes.POINTER(PagerStats), _I32], ctypes.c_int),
     "astro_moe_register_paged_layer": ([_P, _I32, ctypes.POINTER(LayerWeights), _P], ctypes.c_int),
     "astro_moe_paged_block_forward": ([_P, _I32, _P, _I64, _P], ctypes.c_int),

@@ -204,6 +204,15 @@ struct astro_moe_pager {
   std::vector<uint8_t> missed;    // [E] this call copied the expert's page
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> pending, spare;
   astro_moe_pager_stats st{};
+  // retention policy (ASTRO_MOE_PAGER_*) and, for the demand policy, the routed
+  // assignments each page has received (expert_paging/retained_expert_layer_cache.rs
+  // record_expert_demand): the eviction victim is the slot whose page has the
+  // least demand (ties: least recently used) among those the call does not need
+  int policy = ASTRO_MOE_PAGER_LRU;
+  std::vector<uint64_t> demand;   // [layers * E]
+  // host-side fault injection: the next n page copies report a failure instead
+  // of being issued (the failure tests' simulated H2D copy error)
+  int64_t inject_copy_failures = 0;
 };
 
 namespace {
@@ -896,9 +905,37 @@ astro::AffineRef pool_ref(const astro_moe_pager* pg, int m, int64_t code_row_byt
 
 // LRU admission of the experts one block call routes to; returns the number of
 // page copies issued on the pager's copy stream.
-int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs) {
+// Victim slot for a miss once the cache is full, by the pager's policy; never a
+// slot the current call has touched (its experts run from it).
+int64_t pick_victim(astro_moe_pager* pg) {
+  if (pg->policy == ASTRO_MOE_PAGER_DEMAND) {
+    // least demand, then least recently used: walk the LRU list from its tail
+    int64_t best = -1;
+    uint64_t best_d = 0;
+    for (auto it = pg->lru.rbegin(); it != pg->lru.rend(); ++it) {
+      const int64_t sl = *it;
+      if (pg->last_call[sl] == pg->call) continue;
+      if (pg->page_of_slot[sl] < 0) return sl;  // holds no page (a failed copy)
+      const uint64_t d = pg->demand[pg->page_of_slot[sl]];
+      if (best < 0 || d < best_d) {
+        best = sl;
+        best_d = d;
+        if (d == 0) break;
+      }
+    }
+    if (best >= 0) return best;
+  }
+  auto it = pg->lru.end();
+  do {
+    --it;
+  } while (pg->last_call[*it] == pg->call && it != pg->lru.begin());
+  return *it;
+}
+
+int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs, int* failed) {
   pg->call += 1;
   int64_t copies = 0;
+  *failed = 0;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   for (int e = 0; e < pg->E; ++e) {
     pg->h_table[e] = 0;
@@ -906,6 +943,7 @@ int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs) {
     if (offs[e + 1] <= offs[e]) continue;
     const int64_t page = (int64_t)layer * pg->E + e;
     pg->st.lookups += 1;
+    pg->demand[page] += offs[e + 1] - offs[e];
     int64_t slot = pg->slot_of_page[page];
     if (slot >= 0) {
       pg->st.hits += 1;
@@ -917,15 +955,13 @@ int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs) {
         pg->lru.push_front(slot);
         pg->lru_pos[slot] = pg->lru.begin();
       } else {
-        // least recently used slot that this call does not need
-        auto it = pg->lru.end();
-        do {
-          --it;
-        } while (pg->last_call[*it] == pg->call && it != pg->lru.begin());
-        slot = *it;
-        pg->slot_of_page[pg->page_of_slot[slot]] = -1;
-        pg->st.evictions += 1;
-        pg->lru.splice(pg->lru.begin(), pg->lru, it);
+        slot = pick_victim(pg);
+        if (pg->page_of_slot[slot] >= 0) {
+          pg->slot_of_page[pg->page_of_slot[slot]] = -1;
+          pg->st.evictions += 1;
+        }
+        pg->page_of_slot[slot] = -1;
+        pg->lru.splice(pg->lru.begin(), pg->lru, pg->lru_pos[slot]);
       }
       pg->slot_of_page[page] = (int32_t)slot;
       pg->page_of_slot[slot] = page;
@@ -940,9 +976,22 @@ int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs) {
         }
         cudaEventRecord(e0, pg->copy);
       }
-      cudaMemcpyAsync(pg->pool + slot * pg->page_bytes, pg->host + page * pg->page_bytes,
-                      (size_t)pg->page_bytes, cudaMemcpyHostToDevice, pg->copy);
-      pg->st.bytes_h2d += pg->page_bytes;
+      cudaError_t ce = cudaErrorInvalidValue;
+      if (pg->inject_copy_failures > 0) {
+        pg->inject_copy_failures -= 1;
+      } else {
+        ce = cudaMemcpyAsync(pg->pool + slot * pg->page_bytes, pg->host + page * pg->page_bytes,
+                             (size_t)pg->page_bytes, cudaMemcpyHostToDevice, pg->copy);
+      }
+      if (ce != cudaSuccess) {
+        // the page never arrived: the slot holds no page, the call fails
+        pg->slot_of_page[page] = -1;
+        pg->page_of_slot[slot] = -1;
+        pg->st.copy_failures += 1;
+        *failed = 1;
+      } else {
+        pg->st.bytes_h2d += pg->page_bytes;
+      }
       copies += 1;
       pg->missed[e] = 1;
     }
@@ -999,7 +1048,15 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
   CK(cudaMemcpyAsync(pg->h_offsets, b.offsets, sizeof(uint32_t) * (E + 2), cudaMemcpyDeviceToHost, st),
      "read back expert offsets");
   CK(cudaStreamSynchronize(st), "cudaStreamSynchronize");
-  const int64_t copies = admit_pages(pg, layer, pg->h_offsets);
+  int copy_failed = 0;
+  const int64_t copies = admit_pages(pg, layer, pg->h_offsets, &copy_failed);
+  if (copy_failed) {
+    // a routed expert's page did not reach HBM: nothing reads the cache this
+    // call (the issued copies finish on the copy stream and stay valid)
+    pg->st.calls += 1;
+    return fail(ASTRO_MOE_ERR_CUDA,
+                "%s: an expert page copy to HBM failed (layer %d); no output was written", op, layer);
+  }
   // the slot tables travel on the compute stream (the next layer's read-back
   // sync covers them before the host rewrites the pinned copy); the experts whose
   // pages are resident are computed while the missing pages copy
@@ -1777,7 +1834,10 @@ int astro_moe_pager_create(astro_moe_ctx* ctx, int32_t layers, int32_t experts, 
   if (page % rq_h || page % rs_h || page % rq_i || page % rs_i || page % 16)
     return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: page size does not tile the expert rows", op);
   const int64_t slots = cache_bytes / page;
-  if (slots < 1) return fail(ASTRO_MOE_ERR_MEMORY_LIMIT, "%s: the cache ceiling holds no page", op);
+  if (slots < 1)
+    return fail(ASTRO_MOE_ERR_MEMORY_LIMIT,
+                "%s: the cache ceiling of %lld bytes holds no %lld-byte expert page", op,
+                (long long)cache_bytes, (long long)page);
   DeviceGuard g(ctx->device);
   cudaPointerAttributes attr{};
   CK(cudaPointerGetAttributes(&attr, host_pages), "cudaPointerGetAttributes");
@@ -1806,6 +1866,7 @@ int astro_moe_pager_create(astro_moe_ctx* ctx, int32_t layers, int32_t experts, 
   pg->host = static_cast<const char*>(host_pages);
   pg->slots = slots;
   pg->slot_of_page.assign((size_t)layers * experts, -1);
+  pg->demand.assign((size_t)layers * experts, 0);
   pg->page_of_slot.assign((size_t)slots, -1);
   pg->last_call.assign((size_t)slots, -1);
   pg->missed.assign((size_t)experts, 0);
@@ -1831,6 +1892,21 @@ int astro_moe_pager_create(astro_moe_ctx* ctx, int32_t layers, int32_t experts, 
   if ((e = cudaEventCreateWithFlags(&pg->ready, cudaEventDisableTiming)) != cudaSuccess) return cleanup(e, "cudaEventCreate");
   if ((e = cudaStreamCreateWithFlags(&pg->copy, cudaStreamNonBlocking)) != cudaSuccess) return cleanup(e, "cudaStreamCreate");
   *out = pg;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_pager_set_policy(astro_moe_pager* pg, int32_t policy) {
+  if (!pg) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "pager set policy: null pager");
+  if (policy != ASTRO_MOE_PAGER_LRU && policy != ASTRO_MOE_PAGER_DEMAND)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "pager set policy: unknown policy %d", (int)policy);
+  pg->policy = policy;
+  return ASTRO_MOE_OK;
+}
+
+int astro_moe_pager_inject_copy_failures(astro_moe_pager* pg, int64_t count) {
+  if (!pg || count < 0)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "pager inject copy failures: invalid argument");
+  pg->inject_copy_failures = count;
   return ASTRO_MOE_OK;
 }
 

@@ -113,6 +113,30 @@ ASTRO_DEVINL void record_status(uint32_t* status, uint32_t bits) {
   if (status) atomicOr(status, bits);
 }
 
+// Waits (acquire loads, polled) until *c >= target for at most limit_ns of
+// %globaltimer time; on timeout records kDevWaitTimeout and returns 0.  The
+// fused decode kernel's per-segment completion wait; astro_moe_wait_probe runs
+// it alone so a test can make it run out.
+ASTRO_DEVINL int wait_count_geq(const uint32_t* c, uint32_t target, uint32_t* status,
+                                uint64_t limit_ns = 2000000000ull) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  uint32_t spins = 0;
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
+    if (v >= target) return 1;
+    if ((++spins & 255u) == 0) {
+      uint64_t t1;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
+      if (t1 - t0 > limit_ns) {
+        record_status(status, kDevWaitTimeout);
+        return 0;
+      }
+    }
+  }
+}
+
 ASTRO_DEVINL uint32_t lanemask_lt() {
   uint32_t m;
   asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));

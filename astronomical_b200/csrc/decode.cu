@@ -736,27 +736,6 @@ ASTRO_DEVINL void grid_exit(uint32_t* bar) {
   }
 }
 
-// Waits (acquire, bounded at 2 s) until *c >= target; on timeout records
-// kDevWaitTimeout and returns 0.
-ASTRO_DEVINL int wait_count(const uint32_t* c, uint32_t target, uint32_t* status) {
-  uint64_t t0;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
-  uint32_t spins = 0;
-  while (true) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(c) : "memory");
-    if (v >= target) return 1;
-    if ((++spins & 255u) == 0) {
-      uint64_t t1;
-      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t1));
-      if (t1 - t0 > 2000000000ull) {
-        record_status(status, kDevWaitTimeout);
-        return 0;
-      }
-    }
-  }
-}
-
 // one bulk prefetch of [p, p + bytes) into L2 (p 16-byte aligned, bytes a
 // multiple of 16; callers keep pieces at or below 32 KB)
 ASTRO_DEVINL void prefetch_l2_bulk(const void* p, uint32_t bytes) {
@@ -1162,7 +1141,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) decode_fused_kernel(FusedDeco
         const int n = (int)(p1 - pb < (uint32_t)kStageRows ? p1 - pb : (uint32_t)kStageRows);
         const bool restage = seg != staged_seg || pb != staged_p;
         if (restage && seg != ready_seg && threadIdx.x == 0)
-          s_ready = wait_count(P.seg_done + seg, (uint32_t)per_gu, P.status);
+          s_ready = wait_count_geq(P.seg_done + seg, (uint32_t)per_gu, P.status);
         __syncthreads();  // the previous epilogue is done with red (and ap); the segment is ready
         if (restage && seg != ready_seg) {
           if (!s_ready) return;

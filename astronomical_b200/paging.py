@@ -65,7 +65,7 @@ class PagedMoEStack:
     most ``cache_bytes``."""
 
     def __init__(self, layers: Sequence[dict], store: torch.Tensor, cache_bytes: int,
-                 device: int = 0):
+                 device: int = 0, policy: str = "lru"):
         cfg = layers[0]["config"]
         self.cfg = dict(cfg)
         self.device = torch.device("cuda", device)
@@ -83,6 +83,7 @@ class PagedMoEStack:
             self.ctx, len(layers), cfg["experts"], cfg["hidden"], cfg["intermediate"], cfg["group"],
             cfg["bits"], ctypes.c_void_p(store.data_ptr()), int(cache_bytes), ctypes.byref(pg)))
         self.pager = pg
+        self.set_policy(policy)
         self._keep = []
         for li, w in enumerate(layers):
             t = moe.device_weights(w, self.device, keys=[k for k in w if not k.startswith(
@@ -91,6 +92,18 @@ class PagedMoEStack:
             lw = moe.layer_weights_struct(t, cfg, cfg["experts"], routed=False)
             check(_lib.lib().astro_moe_register_paged_layer(self.ctx, li, ctypes.byref(lw),
                                                             self.pager))
+
+    def set_policy(self, policy: str) -> None:
+        """Page retention: "lru" or "demand" (least-routed page evicted first)."""
+        codes = {"lru": _lib.PAGER_LRU, "demand": _lib.PAGER_DEMAND}
+        if policy not in codes:
+            raise ValueError(f"unknown pager policy {policy!r}")
+        check(_lib.lib().astro_moe_pager_set_policy(self.pager, codes[policy]))
+        self.policy = policy
+
+    def inject_copy_failures(self, count: int) -> None:
+        """Failure testing: the next `count` page copies fail on the host."""
+        check(_lib.lib().astro_moe_pager_inject_copy_failures(self.pager, int(count)))
 
     def forward(self, layer: int, x: torch.Tensor) -> torch.Tensor:
         out = torch.empty_like(x)

@@ -70,6 +70,17 @@ int astro_moe_tensor_core_probe(int32_t instruction, const void* a, const void* 
                                 float* d, int64_t problems, int32_t n, int32_t k16,
                                 int32_t accumulate, uint32_t* device_status, void* stream);
 
+/* No counterpart in the reference.  Runs one of the library's bounded device
+ * waits alone, for failure tests that make a wait run out without faulting or
+ * hanging the GPU: kind 0 polls *flag >= target (the fused decode kernel's
+ * completion-counter wait), kind 1 waits on an mbarrier that expects two
+ * arrivals and receives min(target, 2) (the tcgen05 GEMMs' pipeline wait).  A
+ * wait that does not complete within limit_ns (<= 2 s) records
+ * ASTRO_MOE_DEVICE_WAIT_TIMEOUT in the caller's device_status word and gives
+ * up; *result (device) is 1 when the wait completed, 0 when it ran out. */
+int astro_moe_wait_probe(int32_t kind, const uint32_t* flag, uint32_t target, int64_t limit_ns,
+                         uint32_t* device_status, uint32_t* result, void* stream);
+
 /* Thread-local message of the last failed call; replaces the handler installed
  * by crates/runtime-integration/src/mlx_runtime/error_handling.rs:10-44. */
 const char* astro_moe_last_error(void);
@@ -492,7 +503,25 @@ typedef struct {
   int64_t capacity_pages;
   int64_t calls;            /* paged block calls */
   int64_t split_calls;      /* ... that copied pages in, so ran the copied experts' second launch */
+  int64_t copy_failures;    /* page copies that failed (the call returned an error) */
 } astro_moe_pager_stats;
+
+/* Retention policy of the page cache.  LRU (default): a miss evicts the least
+ * recently used page.  DEMAND: the pager counts the routed assignments every
+ * (layer, expert) page has received (the reference's demand evidence,
+ * expert_paging/retained_expert_layer_cache.rs:35-64, :277-311) and a miss evicts
+ * the page with the least demand (ties: least recently used), so pages routed
+ * often stay resident while a cyclic pass over the layers would make LRU evict
+ * exactly the pages the next layers need.  Neither policy copies a page a call
+ * does not route to, nor evicts one the current call needs. */
+enum { ASTRO_MOE_PAGER_LRU = 0, ASTRO_MOE_PAGER_DEMAND = 1 };
+int astro_moe_pager_set_policy(astro_moe_pager* pager, int32_t policy);
+
+/* Host-side fault injection for failure tests: the next `count` page copies are
+ * not issued and report a failure as a failed cudaMemcpyAsync would, so the
+ * paged call returns ASTRO_MOE_ERR_CUDA without writing its output and the
+ * cache holds no page for the failed experts (a later call copies them again). */
+int astro_moe_pager_inject_copy_failures(astro_moe_pager* pager, int64_t count);
 /* Synchronises the pager's copy stream; reset != 0 clears the counters. */
 int astro_moe_pager_read_stats(astro_moe_pager* pager, astro_moe_pager_stats* out, int32_t reset);
 
