@@ -35,7 +35,109 @@ from . import _lib, moe
 from .moe import _ptr, check
 
 __all__ = ["expert_range", "local_expert_weights", "CudaExpertShard", "ExpertParallelBlock",
-           "ExpertParallelStack"]
+           "ExpertParallelStack", "PeerFailure", "PeerWatchdog"]
+
+
+class PeerFailure(RuntimeError):
+    """A peer rank stopped heart-beating or left; ``ranks`` lists them."""
+
+    def __init__(self, ranks, reason):
+        super().__init__(f"expert-parallel peer rank(s) {sorted(ranks)} {reason}")
+        self.ranks = sorted(ranks)
+        self.reason = reason
+
+
+class PeerWatchdog:
+    """Host-side liveness of the expert-parallel ranks, so a rank learns that a
+    peer died or left before it launches the next layer's collectives (which
+    would otherwise wait until the process group's timeout).
+
+    A background thread bumps this rank's heartbeat counter in the process
+    group's store every ``interval`` seconds and reads the peers' counters and
+    departure notices; ``check()`` (called by ExpertParallelBlock before each
+    layer) raises PeerFailure when a peer announced its departure with
+    ``leave()`` or its counter has not moved for ``timeout`` seconds.  A peer
+    that dies in the middle of a layer is caught by the process group's own
+    (short) timeout instead.  ``abort()`` tears the process group down without
+    waiting on the peers; since check() runs between layers, no collective is
+    in flight then.  The thread touches only the store, never a GPU."""
+
+    def __init__(self, store, rank: int, world: int, interval: float = 0.05,
+                 timeout: float = 2.0, prefix: str = "astro_moe_ep"):
+        import threading
+        import time
+
+        self.store, self.rank, self.world = store, rank, world
+        self.interval, self.timeout, self.prefix = interval, timeout, prefix
+        self._time = time.monotonic
+        self._lock = threading.Lock()
+        self._stop = threading.Event()
+        now = self._time()
+        self._seen = {r: (-1, now) for r in range(world) if r != rank}  # (count, last change)
+        self._left = set()
+        self._beat()
+        self._poll()
+        self._thread = threading.Thread(target=self._run, name="astro-moe-heartbeat", daemon=True)
+        self._thread.start()
+
+    def _key(self, what, r):
+        return f"{self.prefix}/{what}/{r}"
+
+    def _beat(self):
+        self.store.add(self._key("hb", self.rank), 1)
+
+    def _poll(self):
+        now = self._time()
+        for r in list(self._seen):
+            left = self.store.add(self._key("left", r), 0) > 0
+            count = self.store.add(self._key("hb", r), 0)
+            with self._lock:
+                if left:
+                    self._left.add(r)
+                if count != self._seen[r][0]:
+                    self._seen[r] = (count, now)
+
+    def _run(self):
+        while not self._stop.wait(self.interval):
+            try:
+                self._beat()
+                self._poll()
+            except Exception:  # the store went away: nothing left to report to
+                return
+
+    def check(self) -> None:
+        now = self._time()
+        with self._lock:
+            left = sorted(self._left)
+            dead = [r for r, (_, since) in self._seen.items()
+                    if r not in self._left and now - since > self.timeout]
+        if left:
+            raise PeerFailure(left, "left")
+        if dead:
+            raise PeerFailure(dead, f"sent no heartbeat for {self.timeout:.1f} s")
+
+    def stop(self) -> None:
+        """Stops this rank's heartbeat (its peers will see it go silent)."""
+        self._stop.set()
+        self._thread.join(timeout=1.0)
+
+    def leave(self) -> None:
+        """Announces that this rank leaves between layers, then stops beating."""
+        self.store.add(self._key("left", self.rank), 1)
+        self.stop()
+
+    @staticmethod
+    def abort(group=None) -> None:
+        """Destroys the process group without a final collective (NCCL's
+        communicators are aborted by the backend on destruction)."""
+        if dist.is_initialized():
+            pg = group or dist.group.WORLD
+            abort = getattr(pg, "abort", None)
+            try:
+                if callable(abort):
+                    abort()
+            finally:
+                dist.destroy_process_group(group)
 
 
 def expert_range(rank: int, world: int, experts: int) -> Tuple[int, int]:
@@ -210,7 +312,7 @@ class ExpertParallelBlock:
     process group of the `world` ranks (default: the world group)."""
 
     def __init__(self, shard, rank: int, world: int, experts: int, group=None,
-                 exchange: str = "nccl"):
+                 exchange: str = "nccl", watchdog: Optional[PeerWatchdog] = None):
         """exchange: "nccl" (all-to-all-v of rows through torch.distributed),
         "peer" (rows stored into the peers' buffers by the dispatch and expert
         kernels, placements computed on the device from count mailboxes: no host
@@ -223,6 +325,7 @@ class ExpertParallelBlock:
         self.exchange = exchange if world > 1 else "nccl"
         self.last_splits: Optional[Tuple[List[int], List[int]]] = None
         self._flag = None
+        self.watchdog = watchdog
 
     def plan(self, offsets: torch.Tensor):
         """Per-expert counts out, per-source counts in; returns host splits and the
@@ -301,6 +404,8 @@ class ExpertParallelBlock:
         """``marks``: optional callable recording a named point (stage timing)."""
         T = x.shape[0]
         mark = marks or (lambda name: None)
+        if self.watchdog is not None:
+            self.watchdog.check()  # raises PeerFailure before any collective of this layer
         if self.exchange == "peer":
             return self._forward_peer_dev(layer, x, mark)
         if self.exchange == "peer_host":

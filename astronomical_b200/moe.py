@@ -359,6 +359,8 @@ def _to_dev(a, device, bf16=False):
         t = a.to(device)
     else:
         arr = np.ascontiguousarray(a)
+        if not arr.flags.writeable:  # a read-only checkpoint memmap: torch wants its own copy
+            arr = np.array(arr)
         if arr.dtype == np.uint32:
             arr = arr.view(np.int32)
         t = torch.from_numpy(arr).to(device)
