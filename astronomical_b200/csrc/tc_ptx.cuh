@@ -40,8 +40,24 @@ ASTRO_DEVINL void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
                : "memory");
 }
 
+// A waiting thread may be suspended in hardware until the phase completes or
+// ASTRO_MBAR_SUSPEND_NS nanoseconds pass (the try_wait suspend-time hint), so
+// waiting warps do not take issue slots from the working ones; 0 leaves the
+// limit to the system.
+#ifndef ASTRO_MBAR_SUSPEND_NS
+#define ASTRO_MBAR_SUSPEND_NS 0
+#endif
 ASTRO_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
+#if ASTRO_MBAR_SUSPEND_NS > 0
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(ASTRO_MBAR_SUSPEND_NS)
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
@@ -49,6 +65,7 @@ ASTRO_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 
