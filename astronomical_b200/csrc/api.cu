@@ -528,7 +528,9 @@ int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void*
 
   if (use_tc) {
     // a4-a6 on tcgen05: gather rows, gate/up + SwiGLU, down
-    CK(astro::launch_take_rows(x, T, b.stok, rows, H, b.states, ctx->status, st), "take rows");
+    // token rows in the grouped GEMMs' K order (perm8_bf16)
+    CK(astro::launch_take_rows(x, T, b.stok, rows, H, b.states, ctx->status, st, true),
+       "take rows");
     marks.mark();
     CK(astro::moe_gemm_gate_up(L.gemm, b.states, rows, b.offsets, b.act, b.gemm_scratch,
                                ctx->status, st),
@@ -1705,11 +1707,14 @@ static int ep_experts_compute(astro_moe_ctx* ctx, int32_t layer, const char* op,
   CK(astro::launch_ep_permutation(recv_counts, world, El, (int)shared_rows, e.src_start, e.exp_start,
                                   e.offsets, e.dest, e.src_of, st),
      "expert-major permutation");
-  CK(astro::launch_take_rows(recv_rows, recv_total, e.src_of, recv_total, H, e.states, ctx->status, st),
+  // the tcgen05 GEMMs take their token rows in K order perm8_bf16
+  const bool perm8 = astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores);
+  CK(astro::launch_take_rows(recv_rows, recv_total, e.src_of, recv_total, H, e.states, ctx->status,
+                             st, perm8),
      "expert-major rows");
   if (shared_rows > 0)
-    CK(cudaMemcpyAsync(e.states + recv_total * H, x, sizeof(uint16_t) * shared_rows * H,
-                       cudaMemcpyDeviceToDevice, st),
+    CK(astro::launch_take_rows(x, shared_rows, nullptr, shared_rows, H, e.states + recv_total * H,
+                               ctx->status, st, perm8),
        "shared-expert rows");
   ctx->launches += 3;
   if (rows > 0) {
@@ -2240,7 +2245,8 @@ int astro_moe_ep_experts_dev(astro_moe_ctx* ctx, int32_t layer, const void* x, i
                                           e.src_start, e.exp_start, e.offsets, e.dest, e.src_of, st),
      "expert-major permutation");
   CK(astro::launch_ep_gather_states(ctx->xr_recv, e.src_of, x, shared_rows, W, ctx->xr_rank, H,
-                                    mailbox_matrix(ctx), n_cap, e.states, ctx->status, st),
+                                    mailbox_matrix(ctx), n_cap, e.states, ctx->status, st,
+                                    astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores)),
      "expert-major rows");
   if (astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores)) {
     CK(astro::moe_gemm_gate_up(L.gemm, e.states, rows_cap, e.offsets, e.act, e.gemm_scratch,

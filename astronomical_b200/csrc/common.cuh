@@ -109,6 +109,68 @@ ASTRO_DEVINL float swiglu_bf16(float g, float u) {
   return round_bf16(__fmul_rn(a, u));
 }
 
+// K order of the tcgen05 grouped GEMMs' operands inside every 8-element chunk:
+// position p holds element 0,4,1,5,2,6,3,7 -- the order in which the int4 codes of
+// one packed word leave the bf16 conversion, so the dequantisers need no byte
+// permutes.  Token rows (B of gate/up) and activations (B of down) are stored in
+// this order; a K step of 16 covers two whole chunks, and a tensor-core step sums
+// its 16 products exactly before rounding, so the results are unchanged.
+// perm8_bf16 reorders 8 bf16 held in a uint4 (v.x = elements 0,1 ... v.w = 6,7).
+ASTRO_DEVINL uint4 perm8_bf16(uint4 v) {
+  uint4 o;
+  o.x = __byte_perm(v.x, v.z, 0x5410);  // (e0, e4)
+  o.y = __byte_perm(v.x, v.z, 0x7632);  // (e1, e5)
+  o.z = __byte_perm(v.y, v.w, 0x5410);  // (e2, e6)
+  o.w = __byte_perm(v.y, v.w, 0x7632);  // (e3, e7)
+  return o;
+}
+// position of element e (0..7) of a chunk in that order
+ASTRO_DEVINL int perm8_pos(int e) { return 2 * (e & 3) + (e >> 2); }
+
+// expf_cw for x <= 0 (and NaN) without its branches: the same steps, the
+// underflow case selected at the end (the overflow and 2^128 cases cannot occur).
+ASTRO_DEVINL float expf_cw_nonpos(float x) {
+  const float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+  float r = __fmaf_rn(-n, 0.693115234375f, x);
+  r = __fmaf_rn(-n, __uint_as_float(0x3805fdf4u), r);
+  float p = __uint_as_float(0x39500d01u);
+  p = __fmaf_rn(p, r, __uint_as_float(0x3ab60b61u));
+  p = __fmaf_rn(p, r, __uint_as_float(0x3c088889u));
+  p = __fmaf_rn(p, r, __uint_as_float(0x3d2aaaabu));
+  p = __fmaf_rn(p, r, __uint_as_float(0x3e2aaaabu));
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  const float v = __fmul_rn(p, __uint_as_float((uint32_t)((int)n + 127) << 23));
+  return (x < -87.0f) ? 0.0f : v;
+}
+
+// Correctly rounded 1/d for d in [1, 2]: one Newton step from the hardware
+// approximation with an exact FMA residual (Markstein, IBM J. Res. Dev. 34(1),
+// 1990).  Checked against __frcp_rn for every fp32 in [1, 2] on the B200.
+ASTRO_DEVINL float rcp_1to2(float d) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(d));
+  const float e = __fmaf_rn(-d, y, 1.0f);
+  return __fmaf_rn(e, y, y);
+}
+
+// swiglu_bf16 of two (gate, up) pairs given as fp32 accumulators, packed: the
+// bf16 roundings of the inputs and of sigmoid as one cvt.rn.bf16x2 each, and the
+// two products as mul.rn.bf16x2 (a product of two bf16 values is exact in fp32,
+// so its bf16 rounding is the fp32 path's).  Bit-identical to swiglu_bf16 for
+// all 2^32 (gate, up) bf16 pairs (checked on the B200).  Returns (first, second)
+// in the low / high half.
+ASTRO_DEVINL __nv_bfloat162 swiglu_bf16x2(__nv_bfloat162 G, __nv_bfloat162 U) {
+  const uint32_t gb = *reinterpret_cast<const uint32_t*>(&G);
+  const float g0 = __uint_as_float(gb << 16), g1 = __uint_as_float(gb & 0xffff0000u);
+  const float y0 = rcp_1to2(__fadd_rn(1.0f, expf_cw_nonpos(-fabsf(g0))));
+  const float y1 = rcp_1to2(__fadd_rn(1.0f, expf_cw_nonpos(-fabsf(g1))));
+  const float s0 = g0 < 0.0f ? __fsub_rn(1.0f, y0) : y0;
+  const float s1 = g1 < 0.0f ? __fsub_rn(1.0f, y1) : y1;
+  return __hmul2(__hmul2(G, __floats2bfloat162_rn(s0, s1)), U);
+}
+
 ASTRO_DEVINL void record_status(uint32_t* status, uint32_t bits) {
   if (status) atomicOr(status, bits);
 }

@@ -346,6 +346,7 @@ __global__ void ep_push_rows_dev_kernel(const uint4* __restrict__ x, const uint3
 
 // received rows -> expert-major states (src_of), then this rank's own tokens
 // appended as the shared expert's rows after the routed ones
+template <bool PERM8>
 __global__ void ep_gather_states_kernel(const uint4* __restrict__ recv,
                                         const uint32_t* __restrict__ src_of,
                                         const uint4* __restrict__ x, int64_t T, int world, int me,
@@ -370,9 +371,11 @@ __global__ void ep_gather_states_kernel(const uint4* __restrict__ recv,
         record_status(status, kDevBadShape);
         continue;
       }
-      states[q * chunks + c] = recv[(int64_t)s * chunks + c];
+      const uint4 v = recv[(int64_t)s * chunks + c];
+      states[q * chunks + c] = PERM8 ? perm8_bf16(v) : v;
     } else {
-      states[q * chunks + c] = x[(q - n) * chunks + c];
+      const uint4 v = x[(q - n) * chunks + c];
+      states[q * chunks + c] = PERM8 ? perm8_bf16(v) : v;
     }
   }
 }
@@ -437,11 +440,16 @@ cudaError_t launch_ep_push_rows_dev(const void* x, int64_t x_rows, const uint32_
 cudaError_t launch_ep_gather_states(const void* recv, const uint32_t* src_of, const void* x,
                                     int64_t T, int world, int me, int H, const uint32_t* M,
                                     int64_t cap_rows, void* states, uint32_t* status,
-                                    cudaStream_t st) {
+                                    cudaStream_t st, bool perm8) {
   if (world < 1 || world > kMaxPeers || H % 8) return cudaErrorInvalidValue;
-  ep_gather_states_kernel<<<148 * 8, 256, 0, st>>>(
-      reinterpret_cast<const uint4*>(recv), src_of, reinterpret_cast<const uint4*>(x), T, world,
-      me, H / 8, M, cap_rows, reinterpret_cast<uint4*>(states), status);
+  if (perm8)
+    ep_gather_states_kernel<true><<<148 * 8, 256, 0, st>>>(
+        reinterpret_cast<const uint4*>(recv), src_of, reinterpret_cast<const uint4*>(x), T, world,
+        me, H / 8, M, cap_rows, reinterpret_cast<uint4*>(states), status);
+  else
+    ep_gather_states_kernel<false><<<148 * 8, 256, 0, st>>>(
+        reinterpret_cast<const uint4*>(recv), src_of, reinterpret_cast<const uint4*>(x), T, world,
+        me, H / 8, M, cap_rows, reinterpret_cast<uint4*>(states), status);
   return cudaGetLastError();
 }
 

@@ -24,8 +24,11 @@ cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, 
                                     uint32_t* sorted_tokens, uint32_t* offsets, uint32_t* status,
                                     void* scratch, cudaStream_t st);
 
+// rows == nullptr: row p; perm8: rows stored in the tcgen05 grouped GEMMs' K
+// order (perm8_bf16 in common.cuh)
 cudaError_t launch_take_rows(const void* src, int64_t src_rows, const uint32_t* rows, int64_t n,
-                             int hidden, void* out, uint32_t* status, cudaStream_t st);
+                             int hidden, void* out, uint32_t* status, cudaStream_t st,
+                             bool perm8 = false);
 
 // scores_f32 != nullptr: the Laguna combination (fp32 scores, routed sum times
 // `factor` -- already bf16-rounded -- and an ungated shared expert when has_shared);
@@ -194,7 +197,7 @@ cudaError_t launch_ep_push_rows_dev(const void* x, int64_t x_rows, const uint32_
 cudaError_t launch_ep_gather_states(const void* recv, const uint32_t* src_of, const void* x,
                                     int64_t T, int world, int me, int H, const uint32_t* M,
                                     int64_t cap_rows, void* states, uint32_t* status,
-                                    cudaStream_t st);
+                                    cudaStream_t st, bool perm8 = false);
 cudaError_t launch_ep_return_rows_dev(const void* yrows, int64_t y_rows, const uint32_t* dest,
                                       int world, int me, int H, const uint32_t* M,
                                       void* const* peer_ret, int64_t cap_rows, uint32_t* status,

@@ -88,6 +88,9 @@ ASTRO_DEVINL int epi_half(int w) {
 }
 // dequant: group * 4 + warp-in-group, or -1 (warp-in-group == warp % 4)
 ASTRO_DEVINL int dq_slot(int w) { return w >= kDqFirst ? w - kDqFirst : -1; }
+constexpr int kIssueGroup = 2;        // K blocks per MMA issue round (see the MMA issuer)
+constexpr int kIssueGroupNarrow = 4;  // ... for tiles of at most 64 token rows
+static_assert(kIssueGroupNarrow <= kOpStages, "an issue round waits for that many operand slots");
 constexpr int kAccs = 2;                                    // TMEM accumulators in flight
 constexpr int kAColsPerStage = kBK / 2;                     // 64 bf16 per row = 32 columns
 constexpr int kACol0 = kAccs * kMaxN;                       // first TMEM column of the A ring
@@ -152,8 +155,10 @@ ASTRO_DEVINL bool decode_unit(const SmemCtl& c, const GemmParams& p, int u, Unit
 }
 
 // 8 int4 codes (MLX order: code j at bits 4j) -> 8 bf16 = scale*q + bias, as
-// four 32-bit words in K order.  128+q is formed exactly by OR-ing the code into
-// the mantissa of bf16 128.0; subtracting 128 is exact; one bf16x2 FMA per pair.
+// four 32-bit words (q0,q4) (q1,q5) (q2,q6) (q3,q7): the GEMMs' K order
+// (perm8_bf16), so no byte permutes are needed.  128+q is formed exactly by
+// OR-ing the code into the mantissa of bf16 128.0; subtracting 128 is exact; one
+// bf16x2 FMA per pair.
 ASTRO_DEVINL uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
   const __nv_bfloat162 k128 = __floats2bfloat162_rn(128.0f, 128.0f);
   uint32_t t[4];
@@ -168,12 +173,7 @@ ASTRO_DEVINL uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 b2) {
     __nv_bfloat162 r = __hfma2(q, s2, b2);
     v[i] = *reinterpret_cast<uint32_t*>(&r);
   }
-  uint4 o;
-  o.x = __byte_perm(v[0], v[1], 0x5410);  // (d0, d1)
-  o.y = __byte_perm(v[2], v[3], 0x5410);  // (d2, d3)
-  o.z = __byte_perm(v[0], v[1], 0x7632);  // (d4, d5)
-  o.w = __byte_perm(v[2], v[3], 0x7632);  // (d6, d7)
-  return o;
+  return make_uint4(v[0], v[1], v[2], v[3]);
 }
 
 // ring bookkeeping for item k in a ring of S slots
@@ -371,20 +371,44 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         if (!tc::mbar_wait(&ctl.tempty[acc], acc_phase ^ 1u, abort, p.status)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kMaxN);
-        for (int kb = 0; kb < KB; ++kb) {
-          if (!tc::mbar_wait(&ctl.op_full[os], oph, abort, p.status)) goto mma_done;
-          tc::tc_fence_after();
-          const uint32_t b_lo = b_lo0 + (uint32_t)os * kSlotStep;
-          if constexpr (MODE == kRouter) {
-            tc::mma4_bf16_ss(d_tmem, a_lo0 + (uint32_t)os * kSlotStep, a_hi, b_lo, b_hi, idesc,
-                             (uint32_t)kb);
-          } else {
-            // K = 16 bf16 = 8 TMEM columns of A per MMA, 32 bytes of B
-            tc::mma4_bf16_ts(d_tmem, a_tmem0 + (uint32_t)(os * kAColsPerStage), b_lo, b_hi, idesc,
-                             (uint32_t)kb);
+        // Items are issued in groups: every branch between MMA issues (a wait's
+        // test) stalls this thread until the tensor pipe has taken the MMAs
+        // already issued, about 450 cycles a round on B200, so a round must carry
+        // more MMA work than that -- two 64-wide K blocks (576 cycles at N = 144),
+        // four when the tile is narrow.
+        const int G = n <= 64 ? kIssueGroupNarrow : kIssueGroup;
+        for (int kb = 0; kb < KB; kb += G) {
+          const int g = KB - kb < G ? KB - kb : G;
+          int ws = os;
+          uint32_t wph = oph;
+          for (int i = 0; i < g; ++i) {
+            if (!tc::mbar_wait(&ctl.op_full[ws], wph, abort, p.status)) goto mma_done;
+            if (++ws == kOpStages) { ws = 0; wph ^= 1u; }
           }
-          tc::mma_commit(&ctl.op_empty[os]);
-          if (++os == kOpStages) { os = 0; oph ^= 1u; }
+          tc::tc_fence_after();
+          // straight-line issue (no branch between the group's MMAs)
+          auto issue = [&](int k) {
+            const uint32_t b_lo = b_lo0 + (uint32_t)os * kSlotStep;
+            if constexpr (MODE == kRouter) {
+              tc::mma4_bf16_ss(d_tmem, a_lo0 + (uint32_t)os * kSlotStep, a_hi, b_lo, b_hi, idesc,
+                               (uint32_t)k);
+            } else {
+              // K = 16 bf16 = 8 TMEM columns of A per MMA, 32 bytes of B
+              tc::mma4_bf16_ts(d_tmem, a_tmem0 + (uint32_t)(os * kAColsPerStage), b_lo, b_hi,
+                               idesc, (uint32_t)k);
+            }
+            tc::mma_commit(&ctl.op_empty[os]);
+            const bool wrap = (os + 1 == kOpStages);
+            os = wrap ? 0 : os + 1;
+            oph ^= wrap ? 1u : 0u;
+          };
+          if (g == 4) {
+            issue(kb); issue(kb + 1); issue(kb + 2); issue(kb + 3);
+          } else if (g == 2) {
+            issue(kb); issue(kb + 1);
+          } else {
+            for (int i = 0; i < g; ++i) issue(kb + i);
+          }
         }
         tc::mma_commit(&ctl.tfull[acc]);
         if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
@@ -406,19 +430,40 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     auto process = [&](const uint32_t (&v)[16], const Unit& U, int cb) {
       const int rbase = U.row0 + cb * 16;
       if constexpr (MODE == kGateUp) {
-        // lane l < 16: gate row f; lane l + 16: up row f (f = 16*sub + l%16)
-        const int col = U.fb * 64 + sub * 16 + (lane & 15);
+        // Lane l < 16 holds gate feature f = 16*sub + l for the chunk's 16 token
+        // rows, lane l + 16 the up feature f.  Each lane packs its values in
+        // bf16 pairs of rows (2i, 2i+1); lanes l and l+16 trade pairs so that
+        // lane l finishes rows 0..7 and lane l + 16 rows 8..15 of feature f.
+        const bool lo_half = lane < 16;
+        // feature f goes to its position in the K order of the down GEMM's B
+        const int f = U.fb * 64 + sub * 16 + (lane & 15);
+        const int col = (f & ~7) | perm8_pos(f & 7);
+        const int r0 = lo_half ? 0 : 8;  // first chunk row of this lane
+        uint32_t pk[8];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const uint32_t send = (lane < 16) ? v[2 * m + 1] : v[2 * m];
-          const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 16);
-          const float g = __uint_as_float(lane < 16 ? v[2 * m] : recv);
-          const float up = __uint_as_float(lane < 16 ? recv : v[2 * m + 1]);
-          const int j = 2 * m + (lane >> 4);
-          const int row = rbase + j;
-          if (j + cb * 16 < U.nrows && row < p.out_rows && col < p.out_cols) {
-            const float a = swiglu_bf16(round_bf16(g), round_bf16(up));
-            p.out[(int64_t)row * p.ldo + col] = f32_to_bf16(a);
+        for (int i = 0; i < 8; ++i) {
+          const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(v[2 * i]),
+                                                         __uint_as_float(v[2 * i + 1]));
+          pk[i] = *reinterpret_cast<const uint32_t*>(&b);
+        }
+        const bool full = cb * 16 + 16 <= U.nrows && rbase + 16 <= p.out_rows;
+        uint16_t* dst = p.out + (int64_t)(rbase + r0) * p.ldo + col;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t recv = __shfl_xor_sync(0xffffffffu, lo_half ? pk[4 + i] : pk[i], 16);
+          const uint32_t g2 = lo_half ? pk[i] : recv, u2 = lo_half ? recv : pk[4 + i];
+          const __nv_bfloat162 o = swiglu_bf16x2(*reinterpret_cast<const __nv_bfloat162*>(&g2),
+                                                 *reinterpret_cast<const __nv_bfloat162*>(&u2));
+          const uint32_t ob = *reinterpret_cast<const uint32_t*>(&o);
+          const int j = r0 + 2 * i;  // chunk row of the low half
+          if (full) {
+            dst[(int64_t)(2 * i) * p.ldo] = (uint16_t)ob;
+            dst[(int64_t)(2 * i + 1) * p.ldo] = (uint16_t)(ob >> 16);
+          } else if (col < p.out_cols) {
+            if (cb * 16 + j < U.nrows && rbase + j < p.out_rows)
+              dst[(int64_t)(2 * i) * p.ldo] = (uint16_t)ob;
+            if (cb * 16 + j + 1 < U.nrows && rbase + j + 1 < p.out_rows)
+              dst[(int64_t)(2 * i + 1) * p.ldo] = (uint16_t)(ob >> 16);
           }
         }
       } else {
@@ -426,6 +471,10 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         // adjacent features: even lanes token 2m, odd lanes token 2m+1
         const int colbase = U.fb * kFeat + 32 * sub + (lane & ~1);
         const bool odd = lane & 1;
+        const bool full = cb * 16 + 16 <= U.nrows && rbase + 16 <= p.out_rows &&
+                          colbase + 1 < p.out_cols;
+        __nv_bfloat162* dst2 =
+            reinterpret_cast<__nv_bfloat162*>(p.out + (int64_t)(rbase + (odd ? 1 : 0)) * p.ldo + colbase);
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
           const uint32_t send = odd ? v[2 * m] : v[2 * m + 1];
@@ -434,7 +483,12 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
           const float hi = __uint_as_float(odd ? v[2 * m + 1] : recv);
           const int j = 2 * m + (odd ? 1 : 0);
           const int row = rbase + j;
-          if (j + cb * 16 < U.nrows && row < p.out_rows && colbase < p.out_cols) {
+          if (full) {
+            // row rbase + j = the first row of this lane + 2m
+            *reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<uint16_t*>(dst2) +
+                                               (int64_t)(2 * m) * p.ldo) =
+                __floats2bfloat162_rn(lo, hi);
+          } else if (j + cb * 16 < U.nrows && row < p.out_rows && colbase < p.out_cols) {
             uint16_t* dst = p.out + (int64_t)row * p.ldo + colbase;
             if (colbase + 1 < p.out_cols) {
               const __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);

@@ -199,7 +199,10 @@ cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, 
   return cudaGetLastError();
 }
 
-// out[p, :] = src[rows[p], :] for bf16 rows of `hidden` elements (16-byte moves).
+// out[p, :] = src[rows[p], :] for bf16 rows of `hidden` elements (16-byte moves);
+// rows == nullptr takes row p.  PERM8: each 8-element chunk in the grouped GEMMs'
+// K order (perm8_bf16).
+template <bool PERM8>
 __global__ void take_rows_kernel(const uint4* __restrict__ src, const uint32_t* __restrict__ rows,
                                  int64_t n, int chunks_per_row, int64_t src_rows,
                                  uint4* __restrict__ out, uint32_t* __restrict__ status) {
@@ -208,25 +211,31 @@ __global__ void take_rows_kernel(const uint4* __restrict__ src, const uint32_t* 
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t p = i / chunks_per_row;
     const int c = (int)(i - p * chunks_per_row);
-    const uint32_t r = rows[p];
+    const uint32_t r = rows ? rows[p] : (uint32_t)p;
     if ((int64_t)r >= src_rows) {
       record_status(status, kDevBadShape);
       continue;
     }
-    out[i] = src[(int64_t)r * chunks_per_row + c];
+    const uint4 v = src[(int64_t)r * chunks_per_row + c];
+    out[i] = PERM8 ? perm8_bf16(v) : v;
   }
 }
 
 cudaError_t launch_take_rows(const void* src, int64_t src_rows, const uint32_t* rows, int64_t n,
-                             int hidden, void* out, uint32_t* status, cudaStream_t st) {
+                             int hidden, void* out, uint32_t* status, cudaStream_t st,
+                             bool perm8) {
   if (n == 0) return cudaSuccess;
   const int chunks = hidden / 8;
   const int64_t total = n * chunks;
   const int threads = 256;
   int64_t blocks = (total + threads - 1) / threads;
   if (blocks > 148 * 16) blocks = 148 * 16;
-  take_rows_kernel<<<(unsigned)blocks, threads, 0, st>>>((const uint4*)src, rows, n, chunks,
-                                                         src_rows, (uint4*)out, status);
+  if (perm8)
+    take_rows_kernel<true><<<(unsigned)blocks, threads, 0, st>>>(
+        (const uint4*)src, rows, n, chunks, src_rows, (uint4*)out, status);
+  else
+    take_rows_kernel<false><<<(unsigned)blocks, threads, 0, st>>>(
+        (const uint4*)src, rows, n, chunks, src_rows, (uint4*)out, status);
   return cudaGetLastError();
 }
 
