@@ -109,6 +109,7 @@ SIGNATURES = {
     "astro_moe_tensor_core_probe": ([_I32, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _P, _P],
                                     ctypes.c_int),
     "astro_moe_wait_probe": ([_I32, _P, ctypes.c_uint32, _I64, _P, _P, _P], ctypes.c_int),
+    "astro_moe_numerics_check": ([_I32, _P, _P, _P], ctypes.c_int),
     "astro_moe_route_experts": ([_P, _I32, _I64, _I32, _I32, _I32, _P, _P, _P], ctypes.c_int),
     "astro_moe_route_laguna_experts": ([_P, _I32, _I64, _I32, _I32, _P, ctypes.c_double, _I32,
                                         _P, _P, _P], ctypes.c_int),

@@ -81,6 +81,17 @@ int astro_moe_tensor_core_probe(int32_t instruction, const void* a, const void* 
 int astro_moe_wait_probe(int32_t kind, const uint32_t* flag, uint32_t target, int64_t limit_ns,
                          uint32_t* device_status, uint32_t* result, void* stream);
 
+/* No counterpart in the reference.  Exhaustive device check of the packed
+ * arithmetic the tcgen05 gate/up epilogue uses in place of the scalar steps that
+ * match the CPU restatement: which 0 = the reciprocal of [1, 2] (every fp32),
+ * 1 = exp of x <= 0 (every fp32), 2 = bf16x2 multiply against the rounded fp32
+ * product (every pair of bf16), 3 = the packed SwiGLU against the scalar one
+ * (every (gate, up) pair of bf16).  Device outputs: *mismatches (uint64) counts
+ * the inputs whose results differ bit-wise (NaN == NaN), *first_index the
+ * smallest such input index (0xffffffff when none).  Asynchronous on `stream`. */
+int astro_moe_numerics_check(int32_t which, unsigned long long* mismatches,
+                             uint32_t* first_index, void* stream);
+
 /* Thread-local message of the last failed call; replaces the handler installed
  * by crates/runtime-integration/src/mlx_runtime/error_handling.rs:10-44. */
 const char* astro_moe_last_error(void);
