@@ -73,6 +73,14 @@ constexpr int kMaxSeg = 1025;
 // and the epilogue warps, which read accumulator rows the same way, each cover
 // all four sub-partitions.
 constexpr int kRawWarp = 0, kMmaWarp = 1, kBWarp = 2;
+// Warp 3 (scale-table mode, VEC == 0): copies a unit's scales and biases from
+// global memory into shared memory, transposed to [group][A row], one unit ahead
+// of the dequantisers (two buffers).  The mode needs K / 64 groups to be a
+// multiple of 8 between 8 and kMaxScaleGroups (K = 512 ... 4096).
+constexpr int kScaleWarp = 3;
+constexpr int kScaleBufs = 2;
+constexpr int kMaxScaleGroups = 64;
+__host__ __device__ constexpr int scale_buf_bytes(int groups) { return 2 * groups * 128 * 2; }  // scales + biases
 constexpr int kEpiFirst = 4;       // warps 4..11: epilogue, two per TMEM sub-partition
 constexpr int kEpiWarps = 8;
 constexpr int kDqFirst = kEpiFirst + kEpiWarps;  // warps 12..27: dequantisers
@@ -108,7 +116,7 @@ struct GemmParams {
   int64_t a_row_base[2][2];   // first tensor row of expert 0 (the up half of a fused tensor: I)
   int64_t a_expert_rows[2];   // tensor rows per expert (I, 2I when fused, H for down)
   int groups_per_row;         // scales per weight row = K / 64
-  int scale_vec;              // groups fetched per vector load: 8, 4 or 1
+  int scale_vec;              // 0: shared-memory scale table; else groups per vector load (8, 4, 1)
   const uint32_t* seg_offsets;  // [nseg + 1]; nullptr: one segment [0, total_rows)
   int nseg;
   int shared_seg;
@@ -132,6 +140,7 @@ struct SmemCtl {
   uint64_t op_full[kOpStages], op_empty[kOpStages];
   uint64_t tfull[kAccs], tempty[kAccs];
   uint64_t mma_done;
+  uint64_t sc_full[kScaleBufs], sc_empty[kScaleBufs];
   uint32_t tmem_base;
   int abort;
   int total_units;
@@ -194,6 +203,11 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
   auto a_at = [&](int s) { return ring_op + s * kOpBytes; };           // router only
   auto b_at = [&](int s) { return ring_op + s * kOpBytes + (kOpBytes - kBBytes); };
   auto raw_at = [&](int s) { return ring_raw + s * kRawBytes; };
+  // scale-table mode: kScaleBufs x ([groups][128] scales, then [groups][128] biases)
+  uint8_t* ring_sc = ring_raw + kRawStages * kRawBytes;
+  auto sc_at = [&](int b) {
+    return reinterpret_cast<uint16_t*>(ring_sc + b * scale_buf_bytes(p.groups_per_row));
+  };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int* abort = &ctl.abort;
@@ -242,6 +256,10 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         tc::mbar_init(&ctl.tempty[a], kEpiWarps);
       }
       tc::mbar_init(&ctl.mma_done, 1);
+      for (int b = 0; b < kScaleBufs; ++b) {
+        tc::mbar_init(&ctl.sc_full[b], 1);
+        tc::mbar_init(&ctl.sc_empty[b], kDequantWarps);
+      }
       tc::fence_mbar_init();
       for (int b = 0; b < kBoxKinds; ++b) tc::prefetch_tmap(&p.tm_b[b]);
       tc::prefetch_tmap(&p.tm_a[0][0]);
@@ -346,6 +364,61 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         for (int k2 = (last_k - kOpStages + 1 > 0 ? last_k - kOpStages + 1 : 0); k2 <= last_k; ++k2)
           tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages)], full_parity(k2, kOpStages),
                         (volatile int*)&dummy, nullptr, 50000000ull);
+      }
+    }
+  } else if (warp == kScaleWarp) {
+    // ================= scale-table loader (VEC == 0) =================
+    if constexpr (VEC == 0 && MODE != kRouter) {
+      const int G = p.groups_per_row;
+      int ui = 0;
+      for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x, ++ui) {
+        Unit U;
+        if (!decode_unit(ctl, p, u, U)) break;
+        const int buf = ui & 1;
+        if (!tc::mbar_wait(&ctl.sc_empty[buf], ((uint32_t)(ui >> 1) & 1u) ^ 1u, abort, p.status))
+          break;
+        const bool shared = (U.seg == p.shared_seg);
+        const int wsel = shared ? 1 : 0;
+        const int64_t e = shared ? 0 : U.seg;
+        uint16_t* ssm = sc_at(buf);
+        uint16_t* bsm = ssm + G * kBM;
+        // this lane copies A rows r = lane + 32 q (the rows the dequantisers'
+        // thread r converts), eight groups per 16-byte load
+        const uint4* sp[4];
+        const uint4* bp[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          int j = 0, f_local = lane + 32 * q;
+          if constexpr (MODE == kGateUp) {
+            j = lane < 16 ? 0 : 1;
+            f_local = q * 16 + (lane & 15);
+          }
+          const int64_t grow =
+              p.a_row_base[wsel][j] + e * p.a_expert_rows[wsel] + (int64_t)U.fb * kFeat + f_local;
+          sp[q] = reinterpret_cast<const uint4*>(p.scales[wsel][j] + grow * G);
+          bp[q] = reinterpret_cast<const uint4*>(p.biases[wsel][j] + grow * G);
+        }
+        for (int v = 0; v < G / 8; ++v) {
+          uint4 sv[4], bv[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            sv[q] = __ldg(sp[q] + v);
+            bv[q] = __ldg(bp[q] + v);
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t ws[4] = {sv[q].x, sv[q].y, sv[q].z, sv[q].w};
+            const uint32_t wb[4] = {bv[q].x, bv[q].y, bv[q].z, bv[q].w};
+            const int r = lane + 32 * q;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              ssm[(8 * v + i) * kBM + r] = (uint16_t)(ws[i >> 1] >> (16 * (i & 1)));
+              bsm[(8 * v + i) * kBM + r] = (uint16_t)(wb[i >> 1] >> (16 * (i & 1)));
+            }
+          }
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ctl.sc_full[buf]);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -529,9 +602,10 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
   } else if constexpr (MODE != kRouter) {
     if (dq_slot(warp) >= 0) {
     // ================= dequantisers =================
-    // Group g takes items k = g, g + 2, ...  Thread r converts weight row r of the
-    // A tile (64 elements = 8 packed words) per item.  The row's scales/biases
-    // come VEC groups per vector load, one vector ahead of use.
+    // Group g takes items k = g, g + kDqGroups, ...  Thread r converts weight row r
+    // of the A tile (64 elements = 8 packed words) per item.  The row's scales and
+    // biases come from the shared-memory table (VEC == 0) or VEC groups per
+    // vector load, one vector ahead of use.
     const int grp = dq_slot(warp) / kDqGroupWarps;
     const int r = (warp & 3) * 32 + lane;  // A tile row = TMEM lane this thread may write
     const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
@@ -578,6 +652,57 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       const uint32_t w = (q < 4) ? ((q < 2) ? v.x : v.y) : ((q < 6) ? v.z : v.w);
       return (uint16_t)((q & 1) ? (w >> 16) : (w & 0xffffu));
     };
+    if constexpr (VEC == 0) {
+      // scale-table mode: the unit's scales and biases are in shared memory,
+      // [group][A row]; KB >= 8, so every group has items in every unit and a
+      // unit ends at most once per item
+      int ui = 0, kb = grp;
+      int rs = grp, os = grp;
+      uint32_t rph = 0, oph = 0;
+      int waited = -1;
+      while (!*abort) {
+        if (blockIdx.x + ui * gridDim.x >= total_units) break;
+        if (ui != waited) {
+          if (!tc::mbar_wait(&ctl.sc_full[ui & 1], (uint32_t)(ui >> 1) & 1u, abort, p.status))
+            break;
+          waited = ui;
+        }
+        const uint16_t* ssm = sc_at(ui & 1);
+        const uint16_t s16 = ssm[kb * kBM + r];
+        const uint16_t b16 = ssm[(p.groups_per_row + kb) * kBM + r];
+        if (!tc::mbar_wait(&ctl.raw_full[rs], rph, abort, p.status)) break;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(raw_at(rs) + raw_row * 32);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(raw_at(rs) + raw_row * 32 + 16);
+        const __nv_bfloat162 s2 = __bfloat162bfloat162(__ushort_as_bfloat16(s16));
+        const __nv_bfloat162 b2 = __bfloat162bfloat162(__ushort_as_bfloat16(b16));
+        uint32_t o[32];
+        const uint32_t ws[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 d = dequant8(ws[i], s2, b2);
+          o[4 * i] = d.x; o[4 * i + 1] = d.y; o[4 * i + 2] = d.z; o[4 * i + 3] = d.w;
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ctl.raw_empty[rs]);
+        if (!tc::mbar_wait(&ctl.op_empty[os], oph ^ 1u, abort, p.status)) break;
+        tc::tc_fence_after();
+        tc::tmem_st32(tmem_base + lane_addr + (uint32_t)(kACol0 + os * kAColsPerStage), o);
+        tc::tmem_st_wait();
+        tc::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(&ctl.op_full[os]);
+        kb += kDqGroups;
+        if (kb >= KB) {  // this warp is done with the unit's scale table
+          kb -= KB;
+          if (lane == 0) tc::mbar_arrive(&ctl.sc_empty[ui & 1]);
+          ++ui;
+        }
+        rs += kDqGroups;
+        if (rs >= kRawStages) { rs -= kRawStages; rph ^= 1u; }
+        os += kDqGroups;
+        if (os >= kOpStages) { os -= kOpStages; oph ^= 1u; }
+      }
+    } else {
     int ui = 0, kb = grp;
     while (kb >= KB) { kb -= KB; ++ui; }
     int rs = grp, os = grp;       // ring slots of item k = grp, grp + kDqGroups, ...
@@ -642,6 +767,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       os += kDqGroups;
       if (os >= kOpStages) { os -= kOpStages; oph ^= 1u; }
     }
+    }  // VEC != 0
     }
   }
 
@@ -693,8 +819,14 @@ struct PlanData {
   int sms = 148;
 };
 
-// widest scale vector (8 or 4 groups) that every scale/bias row allows
+// How the dequantisers get scales: 0 = the shared-memory table loaded by warp 3
+// (groups a multiple of 8 in [8, kMaxScaleGroups], 16-byte aligned tensors), else
+// the widest per-thread vector (8 or 4 groups) every scale/bias row allows, or 1.
 int vec_for(int groups, std::initializer_list<const void*> ptrs) {
+  bool table = groups % 8 == 0 && groups >= 8 && groups <= kMaxScaleGroups;
+  for (const void* ptr : ptrs)
+    if (ptr && (reinterpret_cast<uintptr_t>(ptr) & 15)) table = false;
+  if (table) return 0;
   for (int v : {8, 4}) {
     if (groups % v) continue;
     bool ok = true;
@@ -715,8 +847,12 @@ int sm_count() {
 template <int MODE, int VEC>
 cudaError_t launch_vec(const GemmParams& p, int max_units, cudaStream_t st) {
   const int threads = MODE == kRouter ? kThreadsR : kThreadsQ;
-  constexpr int kSmem = smem_bytes<MODE>();
+  // the scale-table mode adds its buffers (sized for the largest table)
+  constexpr int kSmem =
+      smem_bytes<MODE>() + (VEC == 0 ? kScaleBufs * 2 * kMaxScaleGroups * 128 * 2 : 0);
   static_assert(kSmem + sizeof(SmemCtl) <= 227 * 1024, "shared memory budget");
+  const int smem = VEC == 0 ? smem_bytes<MODE>() + kScaleBufs * scale_buf_bytes(p.groups_per_row)
+                            : kSmem;
   static uint64_t configured = 0;  // per-device bit
   int dev = 0;
   cudaGetDevice(&dev);
@@ -730,16 +866,20 @@ cudaError_t launch_vec(const GemmParams& p, int max_units, cudaStream_t st) {
   int grid = sm_count();
   if (max_units < grid) grid = max_units;
   if (grid <= 0) return cudaSuccess;
-  moe_gemm_kernel<MODE, VEC><<<grid, threads, kSmem, st>>>(p);
+  moe_gemm_kernel<MODE, VEC><<<grid, threads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
 template <int MODE>
 cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
-  if constexpr (MODE == kRouter) return launch_vec<MODE, 1>(p, max_units, st);
-  if (p.scale_vec == 8) return launch_vec<MODE, 8>(p, max_units, st);
-  if (p.scale_vec == 4) return launch_vec<MODE, 4>(p, max_units, st);
-  return launch_vec<MODE, 1>(p, max_units, st);
+  if constexpr (MODE == kRouter) {
+    return launch_vec<MODE, 1>(p, max_units, st);
+  } else {
+    if (p.scale_vec == 0) return launch_vec<MODE, 0>(p, max_units, st);
+    if (p.scale_vec == 8) return launch_vec<MODE, 8>(p, max_units, st);
+    if (p.scale_vec == 4) return launch_vec<MODE, 4>(p, max_units, st);
+    return launch_vec<MODE, 1>(p, max_units, st);
+  }
 }
 
 }  // namespace
