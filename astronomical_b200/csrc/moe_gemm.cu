@@ -96,9 +96,7 @@ ASTRO_DEVINL int epi_half(int w) {
 }
 // dequant: group * 4 + warp-in-group, or -1 (warp-in-group == warp % 4)
 ASTRO_DEVINL int dq_slot(int w) { return w >= kDqFirst ? w - kDqFirst : -1; }
-constexpr int kIssueGroup = 2;        // K blocks per MMA issue round (see the MMA issuer)
-constexpr int kIssueGroupNarrow = 4;  // ... for tiles of at most 64 token rows
-static_assert(kIssueGroupNarrow <= kOpStages, "an issue round waits for that many operand slots");
+static_assert(kOpStages % 2 == 0, "operand slots complete in pairs");
 constexpr int kAccs = 2;                                    // TMEM accumulators in flight
 constexpr int kAColsPerStage = kBK / 2;                     // 64 bf16 per row = 32 columns
 constexpr int kACol0 = kAccs * kMaxN;                       // first TMEM column of the A ring
@@ -137,7 +135,9 @@ struct Unit {
 
 struct SmemCtl {
   uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-  uint64_t op_full[kOpStages], op_empty[kOpStages];
+  // operand slots fill in pairs: op_full[s / 2] completes when both items of the
+  // pair (slots 2i, 2i+1 of one ring round) are in; op_empty is per slot
+  uint64_t op_full[kOpStages / 2], op_empty[kOpStages];
   uint64_t tfull[kAccs], tempty[kAccs];
   uint64_t mma_done;
   uint64_t sc_full[kScaleBufs], sc_empty[kScaleBufs];
@@ -248,7 +248,8 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       // (+ its bytes) and the A tile: 4 dequant warps, or the weight producer's
       // expect-tx arrival for the router's TMA-loaded bf16 A
       for (int s = 0; s < kOpStages; ++s) {
-        tc::mbar_init(&ctl.op_full[s], 1 + (MODE == kRouter ? 1 : kDqGroupWarps));
+        if ((s & 1) == 0)
+          tc::mbar_init(&ctl.op_full[s >> 1], 2 * (1 + (MODE == kRouter ? 1 : kDqGroupWarps)));
         tc::mbar_init(&ctl.op_empty[s], 1);
       }
       for (int a = 0; a < kAccs; ++a) {
@@ -290,8 +291,8 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
             const int s = slot_of(k, kOpStages);
             if (!tc::mbar_wait(&ctl.op_empty[s], empty_parity(k, kOpStages), abort, p.status))
               goto raw_done;
-            tc::mbar_arrive_expect_tx(&ctl.op_full[s], (uint32_t)kABytes);
-            tc::tma_load_2d(a_at(s), &p.tm_a[0][0], kb * kBK, U.fb * kBM, &ctl.op_full[s]);
+            tc::mbar_arrive_expect_tx(&ctl.op_full[s >> 1], (uint32_t)kABytes);
+            tc::tma_load_2d(a_at(s), &p.tm_a[0][0], kb * kBK, U.fb * kBM, &ctl.op_full[s >> 1]);
           } else {
             const int s = slot_of(k, kRawStages);
             if (!tc::mbar_wait(&ctl.raw_empty[s], empty_parity(k, kRawStages), abort, p.status))
@@ -320,7 +321,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         const int ring = (MODE == kRouter) ? kOpStages : kRawStages;
         for (int k2 = (last_k - ring + 1 > 0 ? last_k - ring + 1 : 0); k2 <= last_k; ++k2) {
           if (MODE == kRouter)
-            tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages)], full_parity(k2, kOpStages),
+            tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages) >> 1], full_parity(k2, kOpStages),
                           (volatile int*)&dummy, nullptr, 50000000ull);
           else
             tc::mbar_wait(&ctl.raw_full[slot_of(k2, kRawStages)], full_parity(k2, kRawStages),
@@ -344,14 +345,14 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
           const int s = slot_of(k, kOpStages);
           if (!tc::mbar_wait(&ctl.op_empty[s], empty_parity(k, kOpStages), abort, p.status))
             goto b_done;
-          tc::mbar_arrive_expect_tx(&ctl.op_full[s], bytes);
+          tc::mbar_arrive_expect_tx(&ctl.op_full[s >> 1], bytes);
           int off = 0;
 #pragma unroll
           for (int b = 0; b < kBoxKinds; ++b) {
             const int box = 128 >> b;
             while (rows16 - off >= box) {
               tc::tma_load_2d(b_at(s) + off * 128, &p.tm_b[b], kb * kBK, U.row0 + off,
-                              &ctl.op_full[s]);
+                              &ctl.op_full[s >> 1]);
               off += box;
             }
           }
@@ -362,7 +363,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       if (*abort) {
         int dummy = 0;
         for (int k2 = (last_k - kOpStages + 1 > 0 ? last_k - kOpStages + 1 : 0); k2 <= last_k; ++k2)
-          tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages)], full_parity(k2, kOpStages),
+          tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages) >> 1], full_parity(k2, kOpStages),
                         (volatile int*)&dummy, nullptr, 50000000ull);
       }
     }
@@ -423,7 +424,12 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     }
   } else if (warp == kMmaWarp) {
     // ================= MMA issuer =================
-    if (lane == 0) {
+    // The whole warp runs the loop, so its bookkeeping is warp-uniform; one
+    // elected lane (always lane 0 with all lanes active) issues the MMAs and
+    // commits.  A loop run by lane 0 alone measured 1.6x slower per K block on
+    // B200 when the warps sharing its scheduler keep the ALU pipe busy, as the
+    // dequantisers do.
+    {
       int os = 0;          // operand slot of the next item
       uint32_t oph = 0;    // its round parity
       int acc = 0;
@@ -444,53 +450,52 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         if (!tc::mbar_wait(&ctl.tempty[acc], acc_phase ^ 1u, abort, p.status)) break;
         tc::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * kMaxN);
-        // Items are issued in groups: every branch between MMA issues (a wait's
-        // test) stalls this thread until the tensor pipe has taken the MMAs
-        // already issued, about 450 cycles a round on B200, so a round must carry
-        // more MMA work than that -- two 64-wide K blocks (576 cycles at N = 144),
-        // four when the tile is narrow.
-        const int G = n <= 64 ? kIssueGroupNarrow : kIssueGroup;
-        for (int kb = 0; kb < KB; kb += G) {
-          const int g = KB - kb < G ? KB - kb : G;
-          int ws = os;
-          uint32_t wph = oph;
-          for (int i = 0; i < g; ++i) {
-            if (!tc::mbar_wait(&ctl.op_full[ws], wph, abort, p.status)) goto mma_done;
-            if (++ws == kOpStages) { ws = 0; wph ^= 1u; }
-          }
-          tc::tc_fence_after();
-          // straight-line issue (no branch between the group's MMAs)
-          auto issue = [&](int k) {
-            const uint32_t b_lo = b_lo0 + (uint32_t)os * kSlotStep;
-            if constexpr (MODE == kRouter) {
-              tc::mma4_bf16_ss(d_tmem, a_lo0 + (uint32_t)os * kSlotStep, a_hi, b_lo, b_hi, idesc,
-                               (uint32_t)k);
-            } else {
-              // K = 16 bf16 = 8 TMEM columns of A per MMA, 32 bytes of B
-              tc::mma4_bf16_ts(d_tmem, a_tmem0 + (uint32_t)(os * kAColsPerStage), b_lo, b_hi,
-                               idesc, (uint32_t)k);
-            }
-            tc::mma_commit(&ctl.op_empty[os]);
-            const bool wrap = (os + 1 == kOpStages);
-            os = wrap ? 0 : os + 1;
-            oph ^= wrap ? 1u : 0u;
-          };
-          if (g == 4) {
-            issue(kb); issue(kb + 1); issue(kb + 2); issue(kb + 3);
-          } else if (g == 2) {
-            issue(kb); issue(kb + 1);
+        // Items are issued in pairs: every barrier wait between MMA issues stalls
+        // the issue until the tensor pipe has worked off the MMAs already issued
+        // (about 450 cycles a round on B200), so one wait covers two 64-wide K
+        // blocks (576 cycles of MMA at N = 144).  A unit with an odd number of
+        // K blocks leaves a pair split across units: its first item waits, the
+        // second one is covered.
+        auto issue = [&](int k, int s) {
+          const uint32_t b_lo = b_lo0 + (uint32_t)s * kSlotStep;
+          if constexpr (MODE == kRouter) {
+            tc::mma4_bf16_ss(d_tmem, a_lo0 + (uint32_t)s * kSlotStep, a_hi, b_lo, b_hi, idesc,
+                             (uint32_t)k);
           } else {
-            for (int i = 0; i < g; ++i) issue(kb + i);
+            // K = 16 bf16 = 8 TMEM columns of A per MMA, 32 bytes of B
+            tc::mma4_bf16_ts(d_tmem, a_tmem0 + (uint32_t)(s * kAColsPerStage), b_lo, b_hi, idesc,
+                             (uint32_t)k);
           }
+          tc::mma_commit(&ctl.op_empty[s]);
+        };
+        for (int kb = 0; kb < KB;) {
+          const bool pair = (os & 1) == 0 && kb + 1 < KB;
+          if ((os & 1) == 0) {
+            if (!tc::mbar_wait(&ctl.op_full[os >> 1], oph, abort, p.status)) goto mma_done;
+            tc::tc_fence_after();
+          }
+          if (tc::elect_one()) {
+            issue(kb, os);
+            if (pair) issue(kb + 1, os + 1);
+          }
+          __syncwarp();
+          const int step = pair ? 2 : 1;
+          kb += step;
+          os += step;
+          if (os == kOpStages) { os = 0; oph ^= 1u; }
         }
-        tc::mma_commit(&ctl.tfull[acc]);
+        if (tc::elect_one()) tc::mma_commit(&ctl.tfull[acc]);
+        __syncwarp();
         if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
       }
     mma_done:
-      // every MMA issued by this thread completes before TMEM is released
-      tc::mma_commit(&ctl.mma_done);
-      int dummy = 0;
-      tc::mbar_wait(&ctl.mma_done, 0, (volatile int*)&dummy, p.status, 200000000ull);
+      // every MMA issued by this warp's lane 0 completes before TMEM is released
+      if (tc::elect_one()) {
+        tc::mma_commit(&ctl.mma_done);
+        int dummy = 0;
+        tc::mbar_wait(&ctl.mma_done, 0, (volatile int*)&dummy, p.status, 200000000ull);
+      }
+      __syncwarp();
     }
   } else if (epi_half(warp) >= 0) {
     // ================= epilogue (TMEM -> registers -> global) =================
@@ -690,7 +695,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         tc::tmem_st_wait();
         tc::tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(&ctl.op_full[os]);
+        if (lane == 0) tc::mbar_arrive(&ctl.op_full[os >> 1]);
         kb += kDqGroups;
         if (kb >= KB) {  // this warp is done with the unit's scale table
           kb -= KB;
@@ -759,7 +764,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       tc::tmem_st_wait();
       tc::tc_fence_before();
       __syncwarp();
-      if (lane == 0) tc::mbar_arrive(&ctl.op_full[os]);
+      if (lane == 0) tc::mbar_arrive(&ctl.op_full[os >> 1]);
       kb += kDqGroups;
       while (kb >= KB) { kb -= KB; ++ui; }
       rs += kDqGroups;
@@ -894,7 +899,9 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int route
   const int H = w.hidden, E = w.experts, I = w.intermediate, Is = w.shared_intermediate;
   // eligible profile: 4-bit, group 64, shapes that tile exactly
   if (w.bits != 4 || w.group_size != 64) return 0;
-  if (H % 128 != 0 || I % 64 != 0 || (Is != 0 && Is != I)) return 0;
+  // (an even number of 64-wide K blocks on both projections: operand slots
+  // complete in pairs)
+  if (H % 128 != 0 || I % 128 != 0 || (Is != 0 && Is != I)) return 0;
   if (E > 1024 || !encode_fn()) return 0;
   auto* d = new PlanData();
   d->sms = sm_count();

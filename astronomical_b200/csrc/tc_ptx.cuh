@@ -89,6 +89,17 @@ ASTRO_DEVINL bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
   }
 }
 
+// One lane of the (converged, full) warp is elected: true in exactly one lane.
+ASTRO_DEVINL bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "elect.sync _|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // 2D TMA tile load global -> shared, completion counted on `bar` (no multicast).
 ASTRO_DEVINL void tma_load_2d(void* dst, const CUtensorMap* map, int32_t x, int32_t y,
                               uint64_t* bar) {
