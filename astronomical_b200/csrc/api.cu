@@ -402,6 +402,8 @@ constexpr int64_t kDefaultFusedTokens = 32;
 constexpr int64_t kDefaultDecodeTokens = 8;
 // batches up to this many tokens compute router logits with the router GEMV
 constexpr int64_t kRouterGemvTokens = 64;
+// a paged call of more tokens brings in all its pages first (prefill)
+constexpr int64_t kPagedDecodeTokens = 64;
 
 int run_block(astro_moe_ctx* ctx, LayerState& L, const void* x, int64_t T, void* out,
               const astro_moe_block_taps* taps) {
@@ -935,9 +937,17 @@ int64_t pick_victim(astro_moe_pager* pg) {
 }
 
 int64_t admit_pages(astro_moe_pager* pg, int layer, const uint32_t* offs, int* failed) {
+  *failed = 0;
+  // one call's pages must all fit: a page this call routes to is never evicted
+  // by it
+  int64_t needed = 0;
+  for (int e = 0; e < pg->E; ++e) needed += offs[e + 1] > offs[e] ? 1 : 0;
+  if (needed > pg->slots) {
+    *failed = 2;
+    return needed;
+  }
   pg->call += 1;
   int64_t copies = 0;
-  *failed = 0;
   cudaEvent_t e0 = nullptr, e1 = nullptr;
   for (int e = 0; e < pg->E; ++e) {
     pg->h_table[e] = 0;
@@ -1030,12 +1040,22 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
   const int64_t N = T * K;
   const int64_t rows = N + (has_shared ? T : 0);
   const int threshold = ctx->opt.sorted_threshold > 0 ? ctx->opt.sorted_threshold : 64;
-  ctx->last_path.router = L.router_gemv_ok ? ASTRO_MOE_KERNEL_ROUTER_GEMV : ASTRO_MOE_KERNEL_SIMT_GEMM;
+  // more than kPagedDecodeTokens tokens (prefill): the whole call's pages are
+  // brought in, then the tcgen05 grouped GEMMs read them through the slot table,
+  // exactly as the resident block computes (its router included)
+  const bool prefill = T > kPagedDecodeTokens &&
+                       astro::moe_gemm_enabled(L.gemm, ctx->opt.use_tensor_cores);
+  const bool router_gemv = !prefill && L.router_gemv_ok;
+  ctx->last_path.router = router_gemv ? ASTRO_MOE_KERNEL_ROUTER_GEMV
+                                      : (prefill ? ASTRO_MOE_KERNEL_TCGEN05_GEMM : ASTRO_MOE_KERNEL_SIMT_GEMM);
   ctx->last_path.gate_logit = has_shared ? ASTRO_MOE_KERNEL_ROUTE : ASTRO_MOE_KERNEL_NONE;
-  ctx->last_path.experts = ASTRO_MOE_KERNEL_DECODE_GEMV;
-  ctx->last_path.shared_expert = has_shared ? ASTRO_MOE_KERNEL_DECODE_GEMV : ASTRO_MOE_KERNEL_NONE;
-  if (L.router_gemv_ok) {
+  ctx->last_path.experts = prefill ? ASTRO_MOE_KERNEL_TCGEN05_GEMM : ASTRO_MOE_KERNEL_DECODE_GEMV;
+  ctx->last_path.shared_expert = has_shared ? ctx->last_path.experts : ASTRO_MOE_KERNEL_NONE;
+  if (router_gemv) {
     CK(astro::launch_router_gemv(x, T, w.router_weight, E, H, b.logits, st), "router projection");
+  } else if (prefill) {
+    CK(astro::moe_gemm_router(L.gemm, x, T, b.logits, b.gemm_scratch, ctx->status, st),
+       "router projection");
   } else {
     CK(astro::launch_dense_nt_simt(x, w.router_weight, T, E, H, b.logits, E, st), "router projection");
   }
@@ -1052,12 +1072,42 @@ int run_paged_block(astro_moe_ctx* ctx, LayerState& L, int layer, const void* x,
   CK(cudaStreamSynchronize(st), "cudaStreamSynchronize");
   int copy_failed = 0;
   const int64_t copies = admit_pages(pg, layer, pg->h_offsets, &copy_failed);
+  if (copy_failed == 2)
+    return fail(ASTRO_MOE_ERR_MEMORY_LIMIT,
+                "%s: the cache of %lld pages cannot hold the %lld expert pages this call routes to "
+                "(layer %d)",
+                op, (long long)pg->slots, (long long)copies, layer);
   if (copy_failed) {
     // a routed expert's page did not reach HBM: nothing reads the cache this
     // call (the issued copies finish on the copy stream and stay valid)
     pg->st.calls += 1;
     return fail(ASTRO_MOE_ERR_CUDA,
                 "%s: an expert page copy to HBM failed (layer %d); no output was written", op, layer);
+  }
+  if (prefill) {
+    // one table, every routed expert's slot; the GEMMs start once the copies
+    // have landed
+    for (int e = 0; e < E; ++e)
+      if (pg->h_table[e] == astro::kSlotElsewhere) pg->h_table[e] = pg->h_table[E + e];
+    CK(cudaMemcpyAsync(pg->d_table, pg->h_table, sizeof(uint32_t) * E, cudaMemcpyHostToDevice, st),
+       "slot table");
+    if (copies) {
+      CK(cudaEventRecord(pg->ready, pg->copy), op);
+      CK(cudaStreamWaitEvent(st, pg->ready, 0), op);
+    }
+    CK(astro::launch_take_rows(x, T, b.stok, rows, H, b.states, ctx->status, st, true), "take rows");
+    CK(astro::moe_gemm_gate_up(L.gemm, b.states, rows, b.offsets, b.act, b.gemm_scratch, ctx->status,
+                               st, pg->d_table),
+       "gate/up projection");
+    CK(astro::moe_gemm_down(L.gemm, b.act, rows, b.offsets, b.yrows, b.gemm_scratch, ctx->status,
+                            st, pg->d_table),
+       "down projection");
+    CK(astro::launch_block_combine(b.yrows, b.inverse, b.scores, has_shared ? b.gate_logit : nullptr,
+                                   N, T, K, H, N >= threshold ? 1 : 0, out, st),
+       "weighted combine");
+    ctx->launches += 8 + astro::sort_launch_count(N);
+    pg->st.calls += 1;
+    return ASTRO_MOE_OK;
   }
   // the slot tables travel on the compute stream (the next layer's read-back
   // sync covers them before the host rewrites the pinned copy); the experts whose
@@ -1986,6 +2036,18 @@ int astro_moe_register_paged_layer(astro_moe_ctx* ctx, int32_t layer, const astr
   L.pager = pg;
   L.router_gemv_ok = (reinterpret_cast<uintptr_t>(L.w.router_weight) & 15u) == 0 &&
                      astro::router_gemv_supported(w->hidden);
+  // prefill: the tcgen05 grouped GEMMs over the page pool (the routed experts'
+  // tensors are located inside each page); not eligible -> the decode kernels
+  astro::PagedStacks ps;
+  ps.pool = pg->pool;
+  ps.slots = pg->slots;
+  ps.page_bytes = pg->page_bytes;
+  for (int m = 0; m < 3; ++m) {
+    ps.off_q[m] = pg->off_q[m];
+    ps.off_s[m] = pg->off_s[m];
+    ps.off_b[m] = pg->off_b[m];
+  }
+  astro::moe_gemm_plan(L.w, &L.gemm, 0, &ps);
   return ASTRO_MOE_OK;
 }
 
@@ -1996,7 +2058,9 @@ int astro_moe_paged_block_forward(astro_moe_ctx* ctx, int32_t layer, const void*
   auto it = ctx->layers.find(layer);
   if (it == ctx->layers.end() || !it->second.registered || !it->second.pager)
     return fail(ASTRO_MOE_ERR_NOT_REGISTERED, "%s: layer %d is not a registered paged layer", op, layer);
-  if (T < 0 || T > 64) return fail(ASTRO_MOE_ERR_UNSUPPORTED, "%s: 0 <= tokens <= 64", op);
+  if (T < 0) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: negative token count", op);
+  if (T * (int64_t)it->second.w.top_k + T > 0x7fffffffLL)
+    return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: too many tokens", op);
   if (T > 0 && (!x || !out)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: null array", op);
   if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0)
     return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: hidden states must be 16-byte aligned", op);

@@ -113,6 +113,8 @@ struct GemmParams {
   const uint16_t* biases[2][2];
   int64_t a_row_base[2][2];   // first tensor row of expert 0 (the up half of a fused tensor: I)
   int64_t a_expert_rows[2];   // tensor rows per expert (I, 2I when fused, H for down)
+  int64_t a_sb_expert_rows[2];  // scale/bias rows per expert (differs for pages)
+  const uint32_t* slot_of;    // routed segment -> expert index in the stacks (pages); null: itself
   int groups_per_row;         // scales per weight row = K / 64
   int scale_vec;              // 0: shared-memory scale table; else groups per vector load (8, 4, 1)
   const uint32_t* seg_offsets;  // [nseg + 1]; nullptr: one segment [0, total_rows)
@@ -147,6 +149,11 @@ struct SmemCtl {
   int prefix[kMaxSeg + 1];
   int offs[kMaxSeg + 1];
 };
+
+// expert index of a routed segment in the stacked tensors (a slot for pages)
+ASTRO_DEVINL int64_t expert_of(const GemmParams& p, int seg) {
+  return p.slot_of ? (int64_t)p.slot_of[seg] : (int64_t)seg;
+}
 
 ASTRO_DEVINL bool decode_unit(const SmemCtl& c, const GemmParams& p, int u, Unit& out) {
   const int tile = u / p.fb_count;
@@ -285,7 +292,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         if (!decode_unit(ctl, p, u, U)) continue;
         const bool shared = (U.seg == p.shared_seg);
         const int wi = shared ? 1 : 0;
-        const int64_t e = shared ? 0 : U.seg;
+        const int64_t e = shared ? 0 : expert_of(p, U.seg);
         for (int kb = 0; kb < KB; ++kb, ++k) {
           if constexpr (MODE == kRouter) {
             const int s = slot_of(k, kOpStages);
@@ -380,7 +387,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
           break;
         const bool shared = (U.seg == p.shared_seg);
         const int wsel = shared ? 1 : 0;
-        const int64_t e = shared ? 0 : U.seg;
+        const int64_t e = shared ? 0 : expert_of(p, U.seg);
         uint16_t* ssm = sc_at(buf);
         uint16_t* bsm = ssm + G * kBM;
         // this lane copies A rows r = lane + 32 q (the rows the dequantisers'
@@ -394,8 +401,8 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
             j = lane < 16 ? 0 : 1;
             f_local = q * 16 + (lane & 15);
           }
-          const int64_t grow =
-              p.a_row_base[wsel][j] + e * p.a_expert_rows[wsel] + (int64_t)U.fb * kFeat + f_local;
+          const int64_t grow = p.a_row_base[wsel][j] + e * p.a_sb_expert_rows[wsel] +
+                               (int64_t)U.fb * kFeat + f_local;
           sp[q] = reinterpret_cast<const uint4*>(p.scales[wsel][j] + grow * G);
           bp[q] = reinterpret_cast<const uint4*>(p.biases[wsel][j] + grow * G);
         }
@@ -632,8 +639,8 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       if (!decode_unit(ctl, p, u, U)) return false;
       const bool shared = (U.seg == p.shared_seg);
       wsel = shared ? 1 : 0;
-      const int64_t e = shared ? 0 : U.seg;
-      grow = p.a_row_base[wsel][j] + e * p.a_expert_rows[wsel] + (int64_t)U.fb * kFeat + f_local;
+      const int64_t e = shared ? 0 : expert_of(p, U.seg);
+      grow = p.a_row_base[wsel][j] + e * p.a_sb_expert_rows[wsel] + (int64_t)U.fb * kFeat + f_local;
       return true;
     };
     auto load_vec = [&](int wsel, int64_t grow, int vid, uint4& vs, uint4& vb) {
@@ -889,7 +896,8 @@ cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
 
 }  // namespace
 
-int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int router_rows) {
+int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int router_rows,
+                  const PagedStacks* paged) {
   plan->ok = false;
   plan->w = w;
   if (plan->dev) {
@@ -908,9 +916,34 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int route
   const CUtensorMapDataType U32 = CU_TENSOR_MAP_DATA_TYPE_UINT32;
   const uint64_t wh = (uint64_t)H / 8, wi = (uint64_t)I / 8;
   bool ok = true;
+  // paged experts: per projection, a map over the pool from the tensor's offset
+  // in the first page to the pool's end, rows of `pitch` bytes; a slot is
+  // page_bytes / pitch rows further on
+  const int64_t rq_h = (int64_t)H / 2, rq_i = (int64_t)I / 2;            // code row bytes
+  const int64_t rs_h = (int64_t)(H / 64) * 2, rs_i = (int64_t)(I / 64) * 2;  // scale row bytes
+  auto pool_map = [&](CUtensorMap* m, int proj, int64_t pitch, uint32_t box_rows) {
+    const int64_t total = paged->slots * paged->page_bytes;
+    return make_map(m, paged->pool + paged->off_q[proj], U32, 4, (uint64_t)(pitch / 4),
+                    (uint64_t)((total - paged->off_q[proj]) / pitch), 8, box_rows,
+                    CU_TENSOR_MAP_SWIZZLE_NONE);
+  };
+  auto pool_ptr = [&](const int64_t* off, int proj) {
+    return reinterpret_cast<const uint16_t*>(paged->pool + off[proj]);
+  };
   // gate/up
   GemmParams& g = d->gate_up;
   const int64_t gate_rows = w.gate_up_fused ? 2LL * I : (int64_t)I;
+  if (paged) {
+    ok &= pool_map(&g.tm_a[0][0], 0, rq_h, 64);
+    ok &= pool_map(&g.tm_a[0][1], 1, rq_h, 64);
+    g.a_row_base[0][0] = g.a_row_base[0][1] = 0;
+    g.scales[0][0] = pool_ptr(paged->off_s, 0);
+    g.biases[0][0] = pool_ptr(paged->off_b, 0);
+    g.scales[0][1] = pool_ptr(paged->off_s, 1);
+    g.biases[0][1] = pool_ptr(paged->off_b, 1);
+    g.a_expert_rows[0] = paged->page_bytes / rq_h;
+    g.a_sb_expert_rows[0] = paged->page_bytes / rs_h;
+  } else {
   ok &= make_map(&g.tm_a[0][0], w.gate.packed, U32, 4, wh, (uint64_t)E * gate_rows, 8, 64,
                  CU_TENSOR_MAP_SWIZZLE_NONE);
   if (w.gate_up_fused) {
@@ -929,6 +962,8 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int route
   g.scales[0][0] = (const uint16_t*)w.gate.scales;
   g.biases[0][0] = (const uint16_t*)w.gate.biases;
   g.a_expert_rows[0] = gate_rows;
+  g.a_sb_expert_rows[0] = gate_rows;
+  }  // stacked experts
   if (Is > 0) {
     ok &= make_map(&g.tm_a[1][0], w.shared_gate.packed, U32, 4, wh, (uint64_t)Is, 8, 64,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
@@ -938,10 +973,10 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int route
     g.biases[1][0] = (const uint16_t*)w.shared_gate.biases;
     g.scales[1][1] = (const uint16_t*)w.shared_up.scales;
     g.biases[1][1] = (const uint16_t*)w.shared_up.biases;
-    g.a_expert_rows[1] = Is;
+    g.a_expert_rows[1] = g.a_sb_expert_rows[1] = Is;
   }
   g.groups_per_row = H / 64;
-  g.scale_vec = vec_for(H / 64, {w.gate.scales, w.gate.biases, w.up.scales, w.up.biases,
+  g.scale_vec = vec_for(H / 64, {g.scales[0][0], g.biases[0][0], g.scales[0][1], g.biases[0][1],
                                  w.shared_gate.scales, w.shared_gate.biases, w.shared_up.scales,
                                  w.shared_up.biases});
   g.kblocks = H / 64;
@@ -951,20 +986,28 @@ int moe_gemm_plan(const astro_moe_layer_weights& w, MoeGemmPlan* plan, int route
   g.ldo = I;
   // down
   GemmParams& dn = d->down;
-  ok &= make_map(&dn.tm_a[0][0], w.down.packed, U32, 4, wi, (uint64_t)E * H, 8, 128,
-                 CU_TENSOR_MAP_SWIZZLE_NONE);
-  dn.scales[0][0] = (const uint16_t*)w.down.scales;
-  dn.biases[0][0] = (const uint16_t*)w.down.biases;
-  dn.a_expert_rows[0] = H;
+  if (paged) {
+    ok &= pool_map(&dn.tm_a[0][0], 2, rq_i, 128);
+    dn.scales[0][0] = pool_ptr(paged->off_s, 2);
+    dn.biases[0][0] = pool_ptr(paged->off_b, 2);
+    dn.a_expert_rows[0] = paged->page_bytes / rq_i;
+    dn.a_sb_expert_rows[0] = paged->page_bytes / rs_i;
+  } else {
+    ok &= make_map(&dn.tm_a[0][0], w.down.packed, U32, 4, wi, (uint64_t)E * H, 8, 128,
+                   CU_TENSOR_MAP_SWIZZLE_NONE);
+    dn.scales[0][0] = (const uint16_t*)w.down.scales;
+    dn.biases[0][0] = (const uint16_t*)w.down.biases;
+    dn.a_expert_rows[0] = dn.a_sb_expert_rows[0] = H;
+  }
   if (Is > 0) {
     ok &= make_map(&dn.tm_a[1][0], w.shared_down.packed, U32, 4, wi, (uint64_t)H, 8, 128,
                    CU_TENSOR_MAP_SWIZZLE_NONE);
     dn.scales[1][0] = (const uint16_t*)w.shared_down.scales;
     dn.biases[1][0] = (const uint16_t*)w.shared_down.biases;
-    dn.a_expert_rows[1] = H;
+    dn.a_expert_rows[1] = dn.a_sb_expert_rows[1] = H;
   }
   dn.groups_per_row = I / 64;
-  dn.scale_vec = vec_for(I / 64, {w.down.scales, w.down.biases, w.shared_down.scales,
+  dn.scale_vec = vec_for(I / 64, {dn.scales[0][0], dn.biases[0][0], w.shared_down.scales,
                                   w.shared_down.biases});
   dn.kblocks = I / 64;
   dn.fb_count = H / 128;
@@ -1031,7 +1074,7 @@ cudaError_t moe_gemm_router(const MoeGemmPlan& plan, const void* x, int64_t toke
 
 cudaError_t moe_gemm_gate_up(const MoeGemmPlan& plan, const void* states, int64_t rows,
                              const uint32_t* offsets, void* act, void* scratch, uint32_t* status,
-                             cudaStream_t st) {
+                             cudaStream_t st, const uint32_t* slot_of) {
   (void)scratch;
   auto* d = reinterpret_cast<PlanData*>(plan.dev);
   if (!d) return cudaErrorNotSupported;
@@ -1045,13 +1088,14 @@ cudaError_t moe_gemm_gate_up(const MoeGemmPlan& plan, const void* states, int64_
   p.out = (uint16_t*)act;
   p.out_rows = (int)rows;
   p.status = status;
+  p.slot_of = slot_of;
   const int max_units = (int)((rows + kMaxN - 1) / kMaxN + p.nseg) * p.fb_count;
   return launch<kGateUp>(p, max_units, st);
 }
 
 cudaError_t moe_gemm_down(const MoeGemmPlan& plan, const void* act, int64_t rows,
                           const uint32_t* offsets, void* yrows, void* scratch, uint32_t* status,
-                          cudaStream_t st) {
+                          cudaStream_t st, const uint32_t* slot_of) {
   (void)scratch;
   auto* d = reinterpret_cast<PlanData*>(plan.dev);
   if (!d) return cudaErrorNotSupported;
@@ -1065,6 +1109,7 @@ cudaError_t moe_gemm_down(const MoeGemmPlan& plan, const void* act, int64_t rows
   p.out = (uint16_t*)yrows;
   p.out_rows = (int)rows;
   p.status = status;
+  p.slot_of = slot_of;
   const int max_units = (int)((rows + kMaxN - 1) / kMaxN + p.nseg) * p.fb_count;
   return launch<kDown>(p, max_units, st);
 }

@@ -33,6 +33,10 @@ def page_bytes(cfg: dict) -> int:
 
 
 def _bytes_per_expert(a) -> torch.Tensor:
+    if not isinstance(a, torch.Tensor):
+        a = np.asarray(a)
+        if not a.flags.writeable:  # memory-mapped checkpoint tensors: torch wants writable
+            a = a.copy()
     t = torch.as_tensor(a) if not isinstance(a, torch.Tensor) else a
     t = t.detach().contiguous()
     return t.view(torch.uint8).reshape(t.shape[0], -1)
@@ -62,16 +66,19 @@ def pack_expert_pages(layers: Sequence[dict], pin: bool = True) -> torch.Tensor:
 class PagedMoEStack:
     """Paged MoE layers on one GPU: routers, shared experts and their gates are
     resident; routed experts come from ``store`` through an HBM page cache of at
-    most ``cache_bytes``."""
+    most ``cache_bytes``.  Calls of up to 64 tokens (decode) compute the resident
+    experts while the missing pages copy; longer calls (prefill) bring in every
+    page they route to and run the tensor-core grouped GEMMs over the cache, so a
+    call's pages must fit in it."""
 
     def __init__(self, layers: Sequence[dict], store: torch.Tensor, cache_bytes: int,
-                 device: int = 0, policy: str = "lru"):
+                 device: int = 0, policy: str = "lru", max_tokens: int = 64):
         cfg = layers[0]["config"]
         self.cfg = dict(cfg)
         self.device = torch.device("cuda", device)
         self.store = store  # must stay alive: the pager reads it
         opts = _lib.Options()
-        opts.max_tokens = 64
+        opts.max_tokens = int(max_tokens)
         ctx = ctypes.c_void_p()
         with torch.cuda.device(self.device):
             check(_lib.lib().astro_moe_ctx_create(device, ctypes.c_void_p(
@@ -112,6 +119,12 @@ class PagedMoEStack:
         check(_lib.lib().astro_moe_paged_block_forward(self.ctx, layer, _ptr(x), x.shape[0],
                                                        _ptr(out)))
         return out
+
+    def last_path(self) -> dict:
+        """Kernels the last paged call ran, per stage, by name."""
+        p = _lib.BlockPath()
+        check(_lib.lib().astro_moe_ctx_last_block_path(self.ctx, ctypes.byref(p)))
+        return p.as_dict()
 
     def stats(self, reset: bool = False) -> dict:
         s = _lib.PagerStats()
