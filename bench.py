@@ -586,12 +586,44 @@ def measure_paging(args, dev):
                 "copy_ms_per_step": st["copy_ms"] / steps, "cache_pages": st["capacity_pages"]}
 
     by_policy = {p: run(p) for p in ("lru", "demand")}
+
+    def run_prefill(tokens=4096, layers=4):
+        # paged prefill: every call brings in the pages it routes to (nearly all
+        # 256 of the layer at 4096 tokens) and runs the tcgen05 grouped GEMMs over
+        # the cache; layers cycled so each call finds the layer's pages evicted
+        stack = paging.PagedMoEStack(resident, store, cache_bytes=cache, device=dev.index,
+                                     max_tokens=tokens)
+        g = torch.Generator(device=dev)
+        g.manual_seed(77)
+        x = torch.randn((tokens, 2048), generator=g, device=dev).to(torch.bfloat16)
+        span = min(L, max(layers, 1))
+        for l in range(L):  # fill the cache; the last layers' pages evict the first ones'
+            stack.forward(l, x[:64])
+        torch.cuda.synchronize()
+        stack.stats(reset=True)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for l in range(span):
+            stack.forward(l, x)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / span
+        st = stack.stats(reset=True)
+        stack.close()
+        pcie = st["bytes_h2d"] / max(st["copy_ms"], 1e-9) / 1e6
+        return {"tokens": tokens, "layers_timed": span, "ms_per_layer": ms,
+                "tokens_per_s_per_layer": tokens / (ms / 1e3),
+                "pages_copied_per_layer": st["misses"] / span, "pcie_gbs": pcie,
+                "pcie_frac": pcie / peak_gbs if peak_gbs else None,
+                "path": "all routed pages in, then tcgen05 grouped GEMMs over the cache"}
+
+    prefill = run_prefill()
     del store
     out = {"workload": "config4_paged_decode_zipf1.1", "layers": L, "tokens_per_step": T,
            "pages_total": L * E, "page_bytes": P, "cache_bytes": cache,
            "pinned_h2d_peak_gbs": peak_gbs,
            "pinned_h2d_peak_how": "1 GiB pinned host -> device copy, best of 5, CUDA events",
-           "policies": by_policy}
+           "policies": by_policy, "prefill": prefill}
     # top-level figures: the better policy of this run (both are listed)
     best = max(by_policy.values(), key=lambda r: r["tokens_per_s"])
     out.update(best)
