@@ -396,9 +396,10 @@ constexpr int kMailboxExperts = 1024;
 // batches up to this many tokens take the decode path unless the options say
 // otherwise: the fused decode kernel where its shapes apply (it takes up to 64
 // tokens when asked; above 16 it restages and re-dequantises per 16 token rows
-// of a segment: ahead of the grouped GEMMs at 32 tokens, 88 against 96 us per
-// layer, behind them at 64, 130 against 110), else the separate decode GEMVs
-constexpr int64_t kDefaultFusedTokens = 32;
+// of a segment: level with the grouped GEMMs at 32 tokens, 88 us per layer,
+// ahead at 48, 97 against 109, behind at 64, 125 against 108), else the
+// separate decode GEMVs
+constexpr int64_t kDefaultFusedTokens = 48;
 constexpr int64_t kDefaultDecodeTokens = 8;
 // batches up to this many tokens compute router logits with the router GEMV
 constexpr int64_t kRouterGemvTokens = 64;

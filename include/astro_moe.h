@@ -242,7 +242,7 @@ typedef struct {
   int32_t sorted_threshold;  /* 0 = 64, MINIMUM_SORTED_EXPERT_ASSIGNMENTS (routing.rs:13) */
   int32_t use_tensor_cores;  /* 0 = auto (tcgen05 path for 4-bit g64), -1 = never */
   int64_t decode_max_tokens; /* batches of at most this many tokens take the decode
-                                path (4-bit g64 layers); 0 = 32 where the fused
+                                path (4-bit g64 layers); 0 = 48 where the fused
                                 decode kernel applies, else 8; -1 = never */
   int64_t decode_fused;      /* decode batches of <= 64 tokens run as one cooperative
                                 kernel; 0 = auto, -1 = never (separate kernels) */
