@@ -2289,7 +2289,7 @@ int astro_moe_ep_experts_dev(astro_moe_ctx* ctx, int32_t layer, const void* x, i
   if (int rc = ep_dev_check(ctx, layer, op, &Lp)) return rc;
   LayerState& L = *Lp;
   const astro_moe_layer_weights& w = L.w;
-  const int H = w.hidden, El = w.experts, I = w.intermediate, K = w.top_k, W = ctx->xr_world;
+  const int H = w.hidden, El = w.experts, I = w.intermediate, W = ctx->xr_world;
   const bool has_shared = w.shared_intermediate > 0;
   if (T < 0 || (T > 0 && !x)) return fail(ASTRO_MOE_ERR_INVALID_ARGUMENT, "%s: invalid tokens", op);
   const int64_t n_cap = ctx->xr_recv_rows;  // every row this rank can receive
