@@ -21,19 +21,25 @@
 //   B    smem (kOpStages x 20 KB)  token rows, bf16, 128-byte swizzle, TMA <- warp 2
 //   A    TMEM (kOpStages x 32 col) dequantised weights, written with one
 //                                  tcgen05.st per row per item <- warps 12-27
+//   scale table smem (2 units)     the unit's scales/biases, [group][A row] <- warp 3
 // The MMA reads A from tensor memory, so shared memory only carries the raw
-// codes and the token rows; per operand slot one full barrier (token bytes + 4
-// dequant warps) and one empty barrier (one MMA commit).
-// The token-row stream is the critical one, so it gets the deepest ring; a tile
-// is covered by the fewest 128/64/32/16-row boxes (each TMA issue has a fixed
-// cost) and only rows the MMA reads are fetched.  Four groups of 4 dequant warps take
-// items round robin (nibbles -> bf16 with bf16x2 FMAs, w = s*q + b); each thread
-// converts one 64-element weight row per item.  Warp 1 (one thread) issues
-// tcgen05.mma (M=128, N<=160, K=16) into one of two TMEM accumulators and
-// commits; eight epilogue warps (two per TMEM sub-partition) drain the others:
-// tcgen05.ld -> SwiGLU / bf16 -> global.  For gate/up the 128 A rows hold 64
-// gate and 64 up rows, interleaved in 16-row groups so each gate row and its up
-// row land in lanes l and l+16 of the same epilogue warp (one shuffle pairs them).
+// codes, the token rows and the scale table; operand slots complete in pairs
+// (one full barrier per two slots: their token bytes and dequant warps) and each
+// slot has one empty barrier (one MMA commit).
+// A tile of token rows is covered by the fewest 128/64/32/16-row boxes (each TMA
+// issue has a fixed cost) and only rows the MMA reads are fetched; the rows are
+// stored in the dequantisers' K order (perm8_bf16), so the conversion needs no
+// byte permutes.  Four groups of 4 dequant warps take items round robin (nibbles
+// -> bf16 with bf16x2 FMAs, w = s*q + b); each thread converts one 64-element
+// weight row per item.  Warp 1 runs the MMA loop as a whole warp and one elected
+// lane issues tcgen05.mma (M=128, N<=160, K=16), two K blocks per wait, into one
+// of two TMEM accumulators and commits; eight epilogue warps (two per TMEM
+// sub-partition) drain the others: tcgen05.ld -> SwiGLU (bf16 pairs) / bf16 ->
+// global.  For gate/up the 128 A rows hold 64 gate and 64 up rows, interleaved
+// in 16-row groups so each gate row and its up row land in lanes l and l+16 of
+// the same epilogue warp (one shuffle pairs them).
+// The routed experts may be stacked tensors or the pages of a page pool
+// (slot_of maps a segment to its slot; codes and scales get their own strides).
 //
 // Every mbarrier wait is bounded (2 s); on timeout the kernel records
 // kDevWaitTimeout, waits (bounded) for its own copies and MMAs, frees TMEM and
