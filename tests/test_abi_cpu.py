@@ -101,6 +101,16 @@ def test_invert_assignment_order_on_host():
         _lib.ERR_OUT_OF_RANGE_SLOT
 
 
+def test_numerics_check_rejects_bad_arguments_on_the_host():
+    L = _lib.lib()
+    fake = ctypes.c_void_p(16)  # never dereferenced: the host checks come first
+    for which in (-1, 4, 99):
+        assert L.astro_moe_numerics_check(which, fake, fake, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.astro_moe_numerics_check(0, None, fake, None) == _lib.ERR_INVALID_ARGUMENT
+    assert L.astro_moe_numerics_check(3, fake, None, None) == _lib.ERR_INVALID_ARGUMENT
+    assert b"numerics_check" in L.astro_moe_last_error()
+
+
 def test_tensor_core_probe_rejects_bad_shapes_on_the_host():
     L = _lib.lib()
     fake = ctypes.c_void_p(256)  # never dereferenced: rejected before any CUDA call
