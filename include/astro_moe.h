@@ -545,8 +545,13 @@ int astro_moe_register_paged_layer(astro_moe_ctx* ctx, int32_t layer,
 
 /* forward_qwen3_5_moe for a paged layer: routes, reads the routed experts back
  * to the host (one stream synchronisation, as the reference's pager does),
- * admits the missing pages, and runs the experts from the cache.  tokens <= 64
- * (decode batches). */
+ * admits the missing pages, and runs the experts from the cache.  Up to 64
+ * tokens (decode, forward.rs:229-312) the resident experts are computed while
+ * the missing pages copy; more tokens (prefill, the reference's layer streaming,
+ * expert_pager/rust_layer_streaming.rs:8-11) bring in every routed page first
+ * and run the tcgen05 grouped GEMMs over the cache.  A call that routes to more
+ * pages than the cache holds returns ASTRO_MOE_ERR_MEMORY_LIMIT (a call never
+ * evicts its own pages). */
 int astro_moe_paged_block_forward(astro_moe_ctx* ctx, int32_t layer, const void* hidden_states,
                                   int64_t tokens, void* out);
 
