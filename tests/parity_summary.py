@@ -1,8 +1,8 @@
 """Summarises the parity log the GPU block tests write ($ASTRO_PARITY_LOG, one JSON
 line per compared block call) as the markdown table kept in profiles/.
 
-    ASTRO_PARITY_LOG=gpurun_out/parity.jsonl python -m pytest tests/test_gpu_block.py -m gpu
-    python tests/parity_summary.py gpurun_out/parity.jsonl
+    ASTRO_PARITY_LOG=parity.jsonl python -m pytest tests/test_gpu_block.py -m gpu
+    python tests/parity_summary.py parity.jsonl
 """
 from __future__ import annotations
 
