@@ -71,13 +71,45 @@ ASTRO_DEVINL void route_token(const T* row, int E, int K, int normalize, uint32_
     }
   }
 
+  // Up to 8 keys a lane (E <= 256): the lane's keys are sorted once, descending
+  // (bitonic network), so a selection round is one warp max over the lanes'
+  // first keys and a shift in the winning lane; keys are unique (they carry the
+  // expert id), so the winners and their order are those of a max over all keys.
+  constexpr bool kSortedKeys = sizeof(T) == 2 && CMAX <= 8;
+  if constexpr (kSortedKeys) {
+#pragma unroll
+    for (int kk = 2; kk <= CMAX; kk <<= 1) {
+#pragma unroll
+      for (int j = kk >> 1; j >= 1; j >>= 1) {
+#pragma unroll
+        for (int i = 0; i < CMAX; ++i) {
+          const int l = i ^ j;
+          if (l > i) {
+            const uint32_t a = key[i], b = key[l];
+            const bool desc = (i & kk) == 0;
+            key[i] = desc ? (a > b ? a : b) : (a < b ? a : b);
+            key[l] = desc ? (a > b ? b : a) : (a < b ? b : a);
+          }
+        }
+      }
+    }
+  }
+
   float sel_val = 0.0f;  // lane k keeps winner k
   uint32_t sel_id = 0;
   float sum_sel = 0.0f;
   for (int k = 0; k < K; ++k) {
     uint32_t wid;
     float wval;
-    if constexpr (sizeof(T) == 2) {
+    if constexpr (kSortedKeys) {
+      const uint32_t best = __reduce_max_sync(0xffffffffu, key[0]);
+      wid = 0xffffu - (best & 0xffffu);
+      wval = RouteKey<T>::value(best >> 16);
+      const bool won = key[0] == best;
+#pragma unroll
+      for (int c = 0; c + 1 < CMAX; ++c) key[c] = won ? key[c + 1] : key[c];
+      if (won) key[CMAX - 1] = 0u;
+    } else if constexpr (sizeof(T) == 2) {
       uint32_t best = 0;
 #pragma unroll
       for (int c = 0; c < CMAX; ++c) best = (key[c] > best) ? key[c] : best;
