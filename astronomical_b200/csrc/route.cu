@@ -21,7 +21,7 @@
 namespace astro {
 
 template <typename T, int CMAX>
-__global__ void __launch_bounds__(256) route_experts_kernel(
+__global__ void __launch_bounds__(256, CMAX <= 16 ? 4 : 1) route_experts_kernel(
     const T* __restrict__ logits, int64_t tokens, int E, int K, int normalize,
     uint32_t* __restrict__ out_ids, T* __restrict__ out_scores,
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ wg, int H,
@@ -29,21 +29,42 @@ __global__ void __launch_bounds__(256) route_experts_kernel(
   const int lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= tokens) return;
+  // bf16(x[t] . wg): 16-byte chunks c = lane, lane + 32, ... in one fp32 fma chain
+  // per lane, then a butterfly.  The token's first kGateBatch chunks per lane are
+  // loaded before the routing so that their latency overlaps it (the 4 KB of
+  // gate weights are shared by every warp and stay in L1).
+  constexpr int kGateBatch = CMAX <= 8 ? 8 : 4;
+  const int nch = gate_logit != nullptr ? H / 8 : 0;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + t * (int64_t)H);
+  const uint4* wr = reinterpret_cast<const uint4*>(wg);
+  uint4 xa[kGateBatch];
+  auto load_batch = [&](int base) {
+#pragma unroll
+    for (int j = 0; j < kGateBatch; ++j) {
+      const int c = base + j * 32 + lane;
+      if (c < nch) xa[j] = xr[c];
+    }
+  };
+  load_batch(0);
   route_token<T, CMAX>(logits + t * E, E, K, normalize, out_ids + t * K, out_scores + t * K);
 
   if (gate_logit != nullptr) {
-    // bf16(x[t] . wg): 16-byte chunks strided over the warp, fp32 fma, butterfly.
-    const uint4* xr = reinterpret_cast<const uint4*>(x + t * (int64_t)H);
-    const uint4* wr = reinterpret_cast<const uint4*>(wg);
     float acc = 0.0f;
-    for (int c = lane; c < H / 8; c += 32) {
-      const uint4 a = xr[c], b = __ldg(wr + c);
-      const uint32_t av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+    for (int base = 0; base < nch; base += 32 * kGateBatch) {
+      if (base > 0) load_batch(base);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        acc = __fmaf_rn(__uint_as_float(av[j] << 16), __uint_as_float(bv[j] << 16), acc);
-        acc = __fmaf_rn(__uint_as_float(av[j] & 0xffff0000u), __uint_as_float(bv[j] & 0xffff0000u),
-                        acc);
+      for (int j = 0; j < kGateBatch; ++j) {
+        const int c = base + j * 32 + lane;
+        if (c >= nch) break;
+        const uint4 w = __ldg(wr + c);
+        const uint32_t av[4] = {xa[j].x, xa[j].y, xa[j].z, xa[j].w};
+        const uint32_t bv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          acc = __fmaf_rn(__uint_as_float(av[i] << 16), __uint_as_float(bv[i] << 16), acc);
+          acc = __fmaf_rn(__uint_as_float(av[i] & 0xffff0000u),
+                          __uint_as_float(bv[i] & 0xffff0000u), acc);
+        }
       }
     }
 #pragma unroll

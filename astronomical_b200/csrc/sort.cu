@@ -201,23 +201,38 @@ cudaError_t launch_sort_assignments(const uint32_t* ids, int64_t tokens, int K, 
 
 // out[p, :] = src[rows[p], :] for bf16 rows of `hidden` elements (16-byte moves);
 // rows == nullptr takes row p.  PERM8: each 8-element chunk in the grouped GEMMs'
-// K order (perm8_bf16).
+// K order (perm8_bf16).  One warp per output row: the row index is read once and
+// each lane keeps kTakeBatch loads in flight before it stores them.
+constexpr int kTakeBatch = 8;
+constexpr int kTakeWarps = 8;  // warps per block
+
 template <bool PERM8>
-__global__ void take_rows_kernel(const uint4* __restrict__ src, const uint32_t* __restrict__ rows,
-                                 int64_t n, int chunks_per_row, int64_t src_rows,
-                                 uint4* __restrict__ out, uint32_t* __restrict__ status) {
-  const int64_t total = n * chunks_per_row;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t p = i / chunks_per_row;
-    const int c = (int)(i - p * chunks_per_row);
-    const uint32_t r = rows ? rows[p] : (uint32_t)p;
+__global__ void __launch_bounds__(kTakeWarps * 32) take_rows_kernel(
+    const uint4* __restrict__ src, const uint32_t* __restrict__ rows, int64_t n,
+    int chunks_per_row, int64_t src_rows, uint4* __restrict__ out, uint32_t* __restrict__ status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t stride = (int64_t)gridDim.x * kTakeWarps;
+  for (int64_t p = (int64_t)blockIdx.x * kTakeWarps + (threadIdx.x >> 5); p < n; p += stride) {
+    const uint32_t r = rows ? __ldg(rows + p) : (uint32_t)p;
     if ((int64_t)r >= src_rows) {
-      record_status(status, kDevBadShape);
+      if (lane == 0) record_status(status, kDevBadShape);
       continue;
     }
-    const uint4 v = src[(int64_t)r * chunks_per_row + c];
-    out[i] = PERM8 ? perm8_bf16(v) : v;
+    const uint4* s = src + (int64_t)r * chunks_per_row;
+    uint4* o = out + p * chunks_per_row;
+    for (int c0 = 0; c0 < chunks_per_row; c0 += 32 * kTakeBatch) {
+      uint4 v[kTakeBatch];
+#pragma unroll
+      for (int j = 0; j < kTakeBatch; ++j) {
+        const int c = c0 + j * 32 + lane;
+        if (c < chunks_per_row) v[j] = s[c];
+      }
+#pragma unroll
+      for (int j = 0; j < kTakeBatch; ++j) {
+        const int c = c0 + j * 32 + lane;
+        if (c < chunks_per_row) o[c] = PERM8 ? perm8_bf16(v[j]) : v[j];
+      }
+    }
   }
 }
 
@@ -226,15 +241,13 @@ cudaError_t launch_take_rows(const void* src, int64_t src_rows, const uint32_t* 
                              bool perm8) {
   if (n == 0) return cudaSuccess;
   const int chunks = hidden / 8;
-  const int64_t total = n * chunks;
-  const int threads = 256;
-  int64_t blocks = (total + threads - 1) / threads;
-  if (blocks > 148 * 16) blocks = 148 * 16;
+  int64_t blocks = (n + kTakeWarps - 1) / kTakeWarps;
+  if (blocks > 148 * 8) blocks = 148 * 8;  // one resident wave, rows strided over it
   if (perm8)
-    take_rows_kernel<true><<<(unsigned)blocks, threads, 0, st>>>(
+    take_rows_kernel<true><<<(unsigned)blocks, kTakeWarps * 32, 0, st>>>(
         (const uint4*)src, rows, n, chunks, src_rows, (uint4*)out, status);
   else
-    take_rows_kernel<false><<<(unsigned)blocks, threads, 0, st>>>(
+    take_rows_kernel<false><<<(unsigned)blocks, kTakeWarps * 32, 0, st>>>(
         (const uint4*)src, rows, n, chunks, src_rows, (uint4*)out, status);
   return cudaGetLastError();
 }
