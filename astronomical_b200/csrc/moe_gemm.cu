@@ -38,6 +38,9 @@
 // global.  For gate/up the 128 A rows hold 64 gate and 64 up rows, interleaved
 // in 16-row groups so each gate row and its up row land in lanes l and l+16 of
 // the same epilogue warp (one shuffle pairs them).
+// With full token tiles (prefill), a gate/up unit of the scale-table mode covers
+// two weight-row blocks (FB = 2): one token-row slot per K block feeds the MMAs
+// of both blocks, which accumulate into the two TMEM accumulators.
 // The routed experts may be stacked tensors or the pages of a page pool
 // (slot_of maps a segment to its slot; codes and scales get their own strides).
 //
@@ -70,8 +73,15 @@ constexpr int kOpStages = 6;              // operand slots: B tile in smem (+ A 
 // Dequantised weights go to TMEM (A from tensor memory), so an operand slot of the
 // quantised modes is just the B tile; the router's bf16 A comes by TMA into smem.
 template <int MODE> constexpr int op_bytes() { return MODE == 2 ? kABytes + kBBytes : kBBytes; }
-template <int MODE> constexpr int smem_bytes() {
-  return kOpStages * op_bytes<MODE>() + (MODE == 2 ? 0 : kRawStages * kRawBytes) + 1024;
+// Gate/up units of the scale-table mode cover FB = 2 weight-row blocks that
+// share every token-row tile: one B slot per 64-wide K block feeds the MMAs of
+// both blocks (their A tiles are two TMEM slots, their accumulators the two TMEM
+// accumulators), so the token rows cross L2 -> SM once per two blocks.  The
+// accumulators then hold one unit, so its epilogue does not overlap the next
+// unit's MMAs; the operand rings keep filling meanwhile.
+template <int FB> constexpr int b_slots() { return kOpStages / FB; }
+template <int MODE, int FB = 1> constexpr int smem_bytes() {
+  return b_slots<FB>() * op_bytes<MODE>() + (MODE == 2 ? 0 : kRawStages * kRawBytes) + 1024;
 }
 constexpr int kMaxSeg = 1025;
 // Warp roles.  A warp can only reach the TMEM lanes of its own SM sub-partition
@@ -86,6 +96,7 @@ constexpr int kRawWarp = 0, kMmaWarp = 1, kBWarp = 2;
 constexpr int kScaleWarp = 3;
 constexpr int kScaleBufs = 2;
 constexpr int kMaxScaleGroups = 64;
+constexpr int kMaxScaleGroupsFB2 = 48;  // two blocks' tables, double-buffered, fit shared memory
 __host__ __device__ constexpr int scale_buf_bytes(int groups) { return 2 * groups * 128 * 2; }  // scales + biases
 constexpr int kEpiFirst = 4;       // warps 4..11: epilogue, two per TMEM sub-partition
 constexpr int kEpiWarps = 8;
@@ -161,9 +172,12 @@ ASTRO_DEVINL int64_t expert_of(const GemmParams& p, int seg) {
   return p.slot_of ? (int64_t)p.slot_of[seg] : (int64_t)seg;
 }
 
+// unit u -> (segment, rows, first weight-row block); a tile has fb_count / FB units
+template <int FB>
 ASTRO_DEVINL bool decode_unit(const SmemCtl& c, const GemmParams& p, int u, Unit& out) {
-  const int tile = u / p.fb_count;
-  out.fb = u - tile * p.fb_count;
+  const int per_tile = p.fb_count / FB;
+  const int tile = u / per_tile;
+  out.fb = (u - tile * per_tile) * FB;
   int lo = 0, hi = p.nseg - 1;
   while (lo < hi) {  // last segment whose first tile <= tile
     const int mid = (lo + hi + 1) >> 1;
@@ -203,23 +217,26 @@ ASTRO_DEVINL int slot_of(int k, int S) { return k % S; }
 ASTRO_DEVINL uint32_t full_parity(int k, int S) { return (uint32_t)(k / S) & 1u; }
 ASTRO_DEVINL uint32_t empty_parity(int k, int S) { return ((uint32_t)(k / S) & 1u) ^ 1u; }
 
-template <int MODE, int VEC>
+template <int MODE, int VEC, int FB>
 __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     moe_gemm_kernel(const __grid_constant__ GemmParams p) {
+  static_assert(FB == 1 || (FB == 2 && MODE == kGateUp && VEC == 0),
+                "two weight-row blocks per unit: gate/up with the scale table only");
+  constexpr int kBS = b_slots<FB>();  // token-row (B) slots
   extern __shared__ uint8_t smem_raw[];
   __shared__ SmemCtl ctl;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   constexpr int kOpBytes = op_bytes<MODE>();
-  uint8_t* ring_op = smem;                                 // kOpStages x ([A tile,] B tile)
-  uint8_t* ring_raw = ring_op + kOpStages * kOpBytes;      // kRawStages x kRawBytes
+  uint8_t* ring_op = smem;                                 // kBS x ([A tile,] B tile)
+  uint8_t* ring_raw = ring_op + kBS * kOpBytes;            // kRawStages x kRawBytes
   auto a_at = [&](int s) { return ring_op + s * kOpBytes; };           // router only
   auto b_at = [&](int s) { return ring_op + s * kOpBytes + (kOpBytes - kBBytes); };
   auto raw_at = [&](int s) { return ring_raw + s * kRawBytes; };
-  // scale-table mode: kScaleBufs x ([groups][128] scales, then [groups][128] biases)
+  // scale-table mode: kScaleBufs x FB x ([groups][128] scales, then [groups][128] biases)
   uint8_t* ring_sc = ring_raw + kRawStages * kRawBytes;
   auto sc_at = [&](int b) {
-    return reinterpret_cast<uint16_t*>(ring_sc + b * scale_buf_bytes(p.groups_per_row));
+    return reinterpret_cast<uint16_t*>(ring_sc + b * FB * scale_buf_bytes(p.groups_per_row));
   };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -251,7 +268,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     }
     if (lane == 0) {
       ctl.prefix[p.nseg] = carry;
-      ctl.total_units = carry * p.fb_count;
+      ctl.total_units = carry * (p.fb_count / FB);
       ctl.abort = 0;
       for (int s = 0; s < kRawStages; ++s) {
         tc::mbar_init(&ctl.raw_full[s], 1);
@@ -261,9 +278,17 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       // (+ its bytes) and the A tile: 4 dequant warps, or the weight producer's
       // expect-tx arrival for the router's TMA-loaded bf16 A
       for (int s = 0; s < kOpStages; ++s) {
-        if ((s & 1) == 0)
-          tc::mbar_init(&ctl.op_full[s >> 1], 2 * (1 + (MODE == kRouter ? 1 : kDqGroupWarps)));
-        tc::mbar_init(&ctl.op_empty[s], 1);
+        if constexpr (FB == 2) {
+          // one slot per K block: the token producer's arrival and both A tiles
+          if (s < kBS) {
+            tc::mbar_init(&ctl.op_full[s], 1 + FB * kDqGroupWarps);
+            tc::mbar_init(&ctl.op_empty[s], 1);
+          }
+        } else {
+          if ((s & 1) == 0)
+            tc::mbar_init(&ctl.op_full[s >> 1], 2 * (1 + (MODE == kRouter ? 1 : kDqGroupWarps)));
+          tc::mbar_init(&ctl.op_empty[s], 1);
+        }
       }
       for (int a = 0; a < kAccs; ++a) {
         tc::mbar_init(&ctl.tfull[a], 1);
@@ -295,11 +320,12 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       int last_k = -1;
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
         Unit U;
-        if (!decode_unit(ctl, p, u, U)) continue;
+        if (!decode_unit<FB>(ctl, p, u, U)) continue;
         const bool shared = (U.seg == p.shared_seg);
         const int wi = shared ? 1 : 0;
         const int64_t e = shared ? 0 : expert_of(p, U.seg);
-        for (int kb = 0; kb < KB; ++kb, ++k) {
+        for (int kb = 0; kb < KB; ++kb) {
+          for (int h = 0; h < FB; ++h, ++k) {  // weight-row block U.fb + h of the unit
           if constexpr (MODE == kRouter) {
             const int s = slot_of(k, kOpStages);
             if (!tc::mbar_wait(&ctl.op_empty[s], empty_parity(k, kOpStages), abort, p.status))
@@ -312,18 +338,19 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
               goto raw_done;
             tc::mbar_arrive_expect_tx(&ctl.raw_full[s], (uint32_t)kRawBytes);
             if constexpr (MODE == kGateUp) {
-              const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * 64;
+              const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)(U.fb + h) * 64;
               tc::tma_load_2d(raw_at(s), &p.tm_a[wi][0], kb * 8,
                               (int32_t)(p.a_row_base[wi][0] + r0), &ctl.raw_full[s]);
               tc::tma_load_2d(raw_at(s) + 2048, &p.tm_a[wi][1], kb * 8,
                               (int32_t)(p.a_row_base[wi][1] + r0), &ctl.raw_full[s]);
             } else {
-              const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)U.fb * kBM;
+              const int64_t r0 = e * p.a_expert_rows[wi] + (int64_t)(U.fb + h) * kBM;
               tc::tma_load_2d(raw_at(s), &p.tm_a[wi][0], kb * 8,
                               (int32_t)(p.a_row_base[wi][0] + r0), &ctl.raw_full[s]);
             }
           }
           last_k = k;
+          }
         }
       }
     raw_done:
@@ -349,23 +376,23 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       int last_k = -1;
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
         Unit U;
-        if (!decode_unit(ctl, p, u, U)) continue;
+        if (!decode_unit<FB>(ctl, p, u, U)) continue;
         // cover the rows the MMA reads with the fewest boxes (each TMA issue has a
         // fixed cost): 144 rows -> one 128-row box and one 16-row box
         const int rows16 = (U.nrows + kBoxRows - 1) / kBoxRows * kBoxRows;
         const uint32_t bytes = (uint32_t)rows16 * 128;
         for (int kb = 0; kb < KB; ++kb, ++k) {
-          const int s = slot_of(k, kOpStages);
-          if (!tc::mbar_wait(&ctl.op_empty[s], empty_parity(k, kOpStages), abort, p.status))
+          const int s = slot_of(k, kBS);
+          if (!tc::mbar_wait(&ctl.op_empty[s], empty_parity(k, kBS), abort, p.status))
             goto b_done;
-          tc::mbar_arrive_expect_tx(&ctl.op_full[s >> 1], bytes);
+          uint64_t* full = &ctl.op_full[FB == 2 ? s : s >> 1];
+          tc::mbar_arrive_expect_tx(full, bytes);
           int off = 0;
 #pragma unroll
           for (int b = 0; b < kBoxKinds; ++b) {
             const int box = 128 >> b;
             while (rows16 - off >= box) {
-              tc::tma_load_2d(b_at(s) + off * 128, &p.tm_b[b], kb * kBK, U.row0 + off,
-                              &ctl.op_full[s >> 1]);
+              tc::tma_load_2d(b_at(s) + off * 128, &p.tm_b[b], kb * kBK, U.row0 + off, full);
               off += box;
             }
           }
@@ -375,9 +402,9 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     b_done:
       if (*abort) {
         int dummy = 0;
-        for (int k2 = (last_k - kOpStages + 1 > 0 ? last_k - kOpStages + 1 : 0); k2 <= last_k; ++k2)
-          tc::mbar_wait(&ctl.op_full[slot_of(k2, kOpStages) >> 1], full_parity(k2, kOpStages),
-                        (volatile int*)&dummy, nullptr, 50000000ull);
+        for (int k2 = (last_k - kBS + 1 > 0 ? last_k - kBS + 1 : 0); k2 <= last_k; ++k2)
+          tc::mbar_wait(&ctl.op_full[FB == 2 ? slot_of(k2, kBS) : slot_of(k2, kBS) >> 1],
+                        full_parity(k2, kBS), (volatile int*)&dummy, nullptr, 50000000ull);
       }
     }
   } else if (warp == kScaleWarp) {
@@ -387,14 +414,15 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       int ui = 0;
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x, ++ui) {
         Unit U;
-        if (!decode_unit(ctl, p, u, U)) break;
+        if (!decode_unit<FB>(ctl, p, u, U)) break;
         const int buf = ui & 1;
         if (!tc::mbar_wait(&ctl.sc_empty[buf], ((uint32_t)(ui >> 1) & 1u) ^ 1u, abort, p.status))
           break;
         const bool shared = (U.seg == p.shared_seg);
         const int wsel = shared ? 1 : 0;
         const int64_t e = shared ? 0 : expert_of(p, U.seg);
-        uint16_t* ssm = sc_at(buf);
+        for (int h = 0; h < FB; ++h) {  // table of weight-row block U.fb + h
+        uint16_t* ssm = sc_at(buf) + h * 2 * G * kBM;
         uint16_t* bsm = ssm + G * kBM;
         // this lane copies A rows r = lane + 32 q (the rows the dequantisers'
         // thread r converts), eight groups per 16-byte load
@@ -408,7 +436,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
             f_local = q * 16 + (lane & 15);
           }
           const int64_t grow = p.a_row_base[wsel][j] + e * p.a_sb_expert_rows[wsel] +
-                               (int64_t)U.fb * kFeat + f_local;
+                               (int64_t)(U.fb + h) * kFeat + f_local;
           sp[q] = reinterpret_cast<const uint4*>(p.scales[wsel][j] + grow * G);
           bp[q] = reinterpret_cast<const uint4*>(p.biases[wsel][j] + grow * G);
         }
@@ -430,6 +458,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
               bsm[(8 * v + i) * kBM + r] = (uint16_t)(wb[i >> 1] >> (16 * (i & 1)));
             }
           }
+        }
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ctl.sc_full[buf]);
@@ -455,9 +484,42 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       const uint32_t a_lo0 = (uint32_t)ad0, a_hi = (uint32_t)(ad0 >> 32);
       constexpr uint32_t kSlotStep = (uint32_t)(kOpBytes >> 4);
       const uint32_t a_tmem0 = tmem_base + (uint32_t)kACol0;
+      if constexpr (FB == 2) {
+        // K block kb of a unit: slot ks holds its token rows (B) and the A tiles
+        // of both weight-row blocks (TMEM slots 2 ks, 2 ks + 1); block h
+        // accumulates into TMEM columns h * kMaxN.  One wait covers 8 MMAs.
+        int ks = 0;
+        uint32_t kph = 0;
+        for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
+          Unit U;
+          if (!decode_unit<FB>(ctl, p, u, U)) continue;
+          const int n = (U.nrows + 15) & ~15;
+          const uint32_t idesc = tc::idesc_bf16(kBM, n);
+          if (!tc::mbar_wait(&ctl.tempty[0], acc_phase ^ 1u, abort, p.status)) break;
+          tc::tc_fence_after();
+          for (int kb = 0; kb < KB; ++kb) {
+            if (!tc::mbar_wait(&ctl.op_full[ks], kph, abort, p.status)) goto mma_done;
+            tc::tc_fence_after();
+            if (tc::elect_one()) {
+              const uint32_t b_lo = b_lo0 + (uint32_t)ks * kSlotStep;
+#pragma unroll
+              for (int h = 0; h < FB; ++h)
+                tc::mma4_bf16_ts(tmem_base + (uint32_t)(h * kMaxN),
+                                 a_tmem0 + (uint32_t)((FB * ks + h) * kAColsPerStage), b_lo, b_hi,
+                                 idesc, (uint32_t)kb);
+              tc::mma_commit(&ctl.op_empty[ks]);
+            }
+            __syncwarp();
+            if (++ks == kBS) { ks = 0; kph ^= 1u; }
+          }
+          if (tc::elect_one()) tc::mma_commit(&ctl.tfull[0]);
+          __syncwarp();
+          acc_phase ^= 1u;
+        }
+      } else {
       for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
         Unit U;
-        if (!decode_unit(ctl, p, u, U)) continue;
+        if (!decode_unit<FB>(ctl, p, u, U)) continue;
         const int n = (U.nrows + 15) & ~15;
         const uint32_t idesc = tc::idesc_bf16(kBM, n);
         if (!tc::mbar_wait(&ctl.tempty[acc], acc_phase ^ 1u, abort, p.status)) break;
@@ -501,6 +563,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         __syncwarp();
         if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
       }
+      }  // FB == 1
     mma_done:
       // every MMA issued by this warp's lane 0 completes before TMEM is released
       if (tc::elect_one()) {
@@ -518,7 +581,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     const int half = epi_half(warp);             // which alternate chunks
     int acc = 0;
     uint32_t acc_phase = 0;
-    auto process = [&](const uint32_t (&v)[16], const Unit& U, int cb) {
+    auto process = [&](const uint32_t (&v)[16], const Unit& U, int fb, int cb) {
       const int rbase = U.row0 + cb * 16;
       if constexpr (MODE == kGateUp) {
         // Lane l < 16 holds gate feature f = 16*sub + l for the chunk's 16 token
@@ -527,7 +590,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         // lane l finishes rows 0..7 and lane l + 16 rows 8..15 of feature f.
         const bool lo_half = lane < 16;
         // feature f goes to its position in the K order of the down GEMM's B
-        const int f = U.fb * 64 + sub * 16 + (lane & 15);
+        const int f = fb * 64 + sub * 16 + (lane & 15);
         const int col = (f & ~7) | perm8_pos(f & 7);
         const int r0 = lo_half ? 0 : 8;  // first chunk row of this lane
         uint32_t pk[8];
@@ -560,7 +623,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       } else {
         // lanes l and l^1 trade one value so each stores a bf16 pair of
         // adjacent features: even lanes token 2m, odd lanes token 2m+1
-        const int colbase = U.fb * kFeat + 32 * sub + (lane & ~1);
+        const int colbase = fb * kFeat + 32 * sub + (lane & ~1);
         const bool odd = lane & 1;
         const bool full = cb * 16 + 16 <= U.nrows && rbase + 16 <= p.out_rows &&
                           colbase + 1 < p.out_cols;
@@ -593,29 +656,40 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     };
     for (int u = blockIdx.x; u < total_units && !*abort; u += gridDim.x) {
       Unit U;
-      if (!decode_unit(ctl, p, u, U)) continue;
+      if (!decode_unit<FB>(ctl, p, u, U)) continue;
       if (!tc::mbar_wait(&ctl.tfull[acc], acc_phase, abort, p.status)) break;
       tc::tc_fence_after();
       const int nch = ((U.nrows + 15) & ~15) / 16;
-      const uint32_t t0 = tmem_base + ((uint32_t)(32 * sub) << 16) + (uint32_t)(acc * kMaxN);
+      // chunks q of the unit: FB == 2 runs over both accumulators (weight-row
+      // blocks U.fb, U.fb + 1: chunks nch of each), else over accumulator acc
+      const uint32_t tb = tmem_base + ((uint32_t)(32 * sub) << 16) +
+                          (uint32_t)((FB == 2 ? 0 : acc) * kMaxN);
+      const int nq = FB * nch;
+      auto blk = [&](int q) { return (FB == 2 && q >= nch) ? 1 : 0; };
+      auto tcol = [&](int q) { return (uint32_t)(blk(q) * (kMaxN - 16 * nch) + q * 16); };
       uint32_t va[16], vb[16];
-      int cb = half;
-      if (cb < nch) tc::tmem_ld16(t0 + (uint32_t)(cb * 16), va);
-      while (cb < nch) {
+      int q = half;
+      if (q < nq) tc::tmem_ld16(tb + tcol(q), va);
+      while (q < nq) {
         tc::tmem_ld_wait16(va);
-        if (cb + 2 < nch) tc::tmem_ld16(t0 + (uint32_t)((cb + 2) * 16), vb);
-        process(va, U, cb);
-        cb += 2;
-        if (cb >= nch) break;
+        if (q + 2 < nq) tc::tmem_ld16(tb + tcol(q + 2), vb);
+        process(va, U, U.fb + blk(q), q - blk(q) * nch);
+        q += 2;
+        if (q >= nq) break;
         tc::tmem_ld_wait16(vb);
-        if (cb + 2 < nch) tc::tmem_ld16(t0 + (uint32_t)((cb + 2) * 16), va);
-        process(vb, U, cb);
-        cb += 2;
+        if (q + 2 < nq) tc::tmem_ld16(tb + tcol(q + 2), va);
+        process(vb, U, U.fb + blk(q), q - blk(q) * nch);
+        q += 2;
       }
       tc::tc_fence_before();
       __syncwarp();
       if (lane == 0) tc::mbar_arrive(&ctl.tempty[acc]);
-      if (++acc == kAccs) { acc = 0; acc_phase ^= 1u; }
+      if (FB == 2) {
+        acc_phase ^= 1u;
+      } else if (++acc == kAccs) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
     }
   } else if constexpr (MODE != kRouter) {
     if (dq_slot(warp) >= 0) {
@@ -642,7 +716,7 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
       const int u = blockIdx.x + ui * gridDim.x;
       if (u >= total_units) return false;
       Unit U;
-      if (!decode_unit(ctl, p, u, U)) return false;
+      if (!decode_unit<FB>(ctl, p, u, U)) return false;
       const bool shared = (U.seg == p.shared_seg);
       wsel = shared ? 1 : 0;
       const int64_t e = shared ? 0 : expert_of(p, U.seg);
@@ -672,9 +746,10 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
     };
     if constexpr (VEC == 0) {
       // scale-table mode: the unit's scales and biases are in shared memory,
-      // [group][A row]; KB >= 8, so every group has items in every unit and a
-      // unit ends at most once per item
-      int ui = 0, kb = grp;
+      // [block][group][A row]; KB >= 8, so every group has items in every unit and
+      // a unit ends at most once per item.  Item it of a unit is K block it / FB of
+      // weight-row block it % FB (with FB == 2 a group keeps one block).
+      int ui = 0, it = grp;
       int rs = grp, os = grp;
       uint32_t rph = 0, oph = 0;
       int waited = -1;
@@ -685,7 +760,8 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
             break;
           waited = ui;
         }
-        const uint16_t* ssm = sc_at(ui & 1);
+        const int kb = it / FB;
+        const uint16_t* ssm = sc_at(ui & 1) + (it - kb * FB) * 2 * p.groups_per_row * kBM;
         const uint16_t s16 = ssm[kb * kBM + r];
         const uint16_t b16 = ssm[(p.groups_per_row + kb) * kBM + r];
         if (!tc::mbar_wait(&ctl.raw_full[rs], rph, abort, p.status)) break;
@@ -702,16 +778,18 @@ __global__ void __launch_bounds__(MODE == kRouter ? kThreadsR : kThreadsQ, 1)
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ctl.raw_empty[rs]);
-        if (!tc::mbar_wait(&ctl.op_empty[os], oph ^ 1u, abort, p.status)) break;
+        // the slot's previous MMAs are done (FB == 2: one barrier per K-block slot)
+        if (!tc::mbar_wait(&ctl.op_empty[FB == 2 ? os >> 1 : os], oph ^ 1u, abort, p.status))
+          break;
         tc::tc_fence_after();
         tc::tmem_st32(tmem_base + lane_addr + (uint32_t)(kACol0 + os * kAColsPerStage), o);
         tc::tmem_st_wait();
         tc::tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(&ctl.op_full[os >> 1]);
-        kb += kDqGroups;
-        if (kb >= KB) {  // this warp is done with the unit's scale table
-          kb -= KB;
+        it += kDqGroups;
+        if (it >= FB * KB) {  // this warp is done with the unit's scale table
+          it -= FB * KB;
           if (lane == 0) tc::mbar_arrive(&ctl.sc_empty[ui & 1]);
           ++ui;
         }
@@ -862,21 +940,25 @@ int sm_count() {
   return n;
 }
 
-template <int MODE, int VEC>
+template <int MODE, int VEC, int FB = 1>
 cudaError_t launch_vec(const GemmParams& p, int max_units, cudaStream_t st) {
   const int threads = MODE == kRouter ? kThreadsR : kThreadsQ;
   // the scale-table mode adds its buffers (sized for the largest table)
   constexpr int kSmem =
-      smem_bytes<MODE>() + (VEC == 0 ? kScaleBufs * 2 * kMaxScaleGroups * 128 * 2 : 0);
+      smem_bytes<MODE, FB>() +
+      (VEC == 0 ? kScaleBufs * FB * scale_buf_bytes(FB == 2 ? kMaxScaleGroupsFB2 : kMaxScaleGroups)
+                : 0);
   static_assert(kSmem + sizeof(SmemCtl) <= 227 * 1024, "shared memory budget");
-  const int smem = VEC == 0 ? smem_bytes<MODE>() + kScaleBufs * scale_buf_bytes(p.groups_per_row)
+  const int smem = VEC == 0 ? smem_bytes<MODE, FB>() +
+                                  kScaleBufs * FB * scale_buf_bytes(p.groups_per_row)
                             : kSmem;
+  max_units = (max_units + FB - 1) / FB;
   static uint64_t configured = 0;  // per-device bit
   int dev = 0;
   cudaGetDevice(&dev);
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured & bit)) {
-    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<MODE, VEC>,
+    cudaError_t e = cudaFuncSetAttribute(moe_gemm_kernel<MODE, VEC, FB>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
     if (e != cudaSuccess) return e;
     configured |= bit;
@@ -884,16 +966,22 @@ cudaError_t launch_vec(const GemmParams& p, int max_units, cudaStream_t st) {
   int grid = sm_count();
   if (max_units < grid) grid = max_units;
   if (grid <= 0) return cudaSuccess;
-  moe_gemm_kernel<MODE, VEC><<<grid, threads, smem, st>>>(p);
+  moe_gemm_kernel<MODE, VEC, FB><<<grid, threads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
+// pair: gate/up units may cover two weight-row blocks (FB = 2)
 template <int MODE>
-cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st) {
+cudaError_t launch(const GemmParams& p, int max_units, cudaStream_t st, bool pair = false) {
   if constexpr (MODE == kRouter) {
     return launch_vec<MODE, 1>(p, max_units, st);
   } else {
-    if (p.scale_vec == 0) return launch_vec<MODE, 0>(p, max_units, st);
+    if (p.scale_vec == 0) {
+      if constexpr (MODE == kGateUp)
+        if (pair && p.groups_per_row <= kMaxScaleGroupsFB2 && p.fb_count % 2 == 0)
+          return launch_vec<MODE, 0, 2>(p, max_units, st);
+      return launch_vec<MODE, 0>(p, max_units, st);
+    }
     if (p.scale_vec == 8) return launch_vec<MODE, 8>(p, max_units, st);
     if (p.scale_vec == 4) return launch_vec<MODE, 4>(p, max_units, st);
     return launch_vec<MODE, 1>(p, max_units, st);
@@ -1096,7 +1184,13 @@ cudaError_t moe_gemm_gate_up(const MoeGemmPlan& plan, const void* states, int64_
   p.status = status;
   p.slot_of = slot_of;
   const int max_units = (int)((rows + kMaxN - 1) / kMaxN + p.nseg) * p.fb_count;
-  return launch<kGateUp>(p, max_units, st);
+  // Two weight-row blocks per unit pay off for full token tiles (prefill: gate/up
+  // 229 us against 235 us at T = 4096 on B200); with a few rows per segment
+  // (decode) the epilogue no longer overlaps the next unit and the grid has half
+  // the units (115 us against 107 us per layer at T = 64), so the pairing starts
+  // at 64 rows per segment on average.
+  const bool pair = rows >= 64 * (int64_t)p.nseg;
+  return launch<kGateUp>(p, max_units, st, pair);
 }
 
 cudaError_t moe_gemm_down(const MoeGemmPlan& plan, const void* act, int64_t rows,
