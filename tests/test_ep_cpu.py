@@ -1,4 +1,4 @@
-"""Expert-parallel exchange logic on CPU: two gloo ranks run
+"""Expert-parallel exchange logic on CPU: 2, 4 or 8 gloo ranks run
 astronomical_b200.ep.ExpertParallelBlock with the oracle's expert arithmetic, and
 every token's output must equal the single-process oracle block bit for bit
 (routing, sort, dispatch splits, the expert-major permutation on the receiving
@@ -44,7 +44,10 @@ def _rank_main(rank, world, port, T, layers, outdir, skew):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("T,skew,world", [(40, None, 2), (3, None, 2), (24, 1.1, 2), (16, 1.1, 4)])
+# world 8 is the scaling run's size: one expert per rank; with 2 tokens per rank
+# most ranks receive no rows from most others
+@pytest.mark.parametrize("T,skew,world", [(40, None, 2), (3, None, 2), (24, 1.1, 2), (16, 1.1, 4),
+                                          (12, 1.1, 8), (2, None, 8)])
 def test_expert_parallel_exchange_matches_single_process_oracle(T, skew, world):
     from oracle import oracle as O
 
