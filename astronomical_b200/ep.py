@@ -356,9 +356,9 @@ class ExpertParallelBlock:
         recv_counts = torch.empty(W * self.El, dtype=torch.int32, device=x.device)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
         per_dest = counts.view(W, self.El).sum(1).to(torch.int32)
-        M = torch.empty((W, W), dtype=torch.int32, device=x.device)
+        M = torch.empty(W * W, dtype=torch.int32, device=x.device)  # flat: NCCL and gloo
         dist.all_gather_into_tensor(M, per_dest, group=self.group)
-        Mh = M.cpu().tolist()  # Mh[s][d]: rows rank s sends to rank d
+        Mh = M.view(W, W).cpu().tolist()  # Mh[s][d]: rows rank s sends to rank d
         send_starts = [sum(Mh[me][:d]) for d in range(W)]
         dest_offsets = [sum(Mh[s][d] for s in range(me)) for d in range(W)]
         recv_starts = [sum(Mh[s][me] for s in range(q)) for q in range(W)]

@@ -75,3 +75,62 @@ class OracleExpertShard:
         if "shared" in st:
             sparse = O.combine_sparse_and_shared(sparse, st["shared"], st["gate_logit"])
         return _t(sparse)
+
+
+class PeerOracleShard(OracleExpertShard):
+    """The peer exchange of ExpertParallelBlock(exchange="peer_host") with the
+    oracle's arithmetic.  Each rank's receive and return buffers are files mapped
+    by every rank (np.memmap), standing in for the CUDA IPC mappings of
+    astro_moe_ep_exchange_connect; push and experts_push store rows at the
+    placements the block computes, as astro_moe_ep_push (the rows for rank d go
+    to d's receive buffer at dest_offsets[d]) and astro_moe_ep_experts_push (the
+    rows received from rank s return to s's return buffer at return_offsets[s])
+    do.  The block's collectives order the stores, as on the GPUs."""
+
+    def connect_exchange(self, max_tokens, directory, group=None):
+        import torch.distributed as dist
+
+        H, K = self.cfg["hidden"], self.cfg["top_k"]
+        self.recv_rows, self.ret_rows = self.world * max_tokens * K, max_tokens * K
+
+        def path(kind, r):
+            return f"{directory}/{kind}_{r}.bin"
+
+        np.memmap(path("recv", self.rank), np.uint16, "w+", shape=(self.recv_rows, H)).flush()
+        np.memmap(path("ret", self.rank), np.uint16, "w+", shape=(self.ret_rows, H)).flush()
+        dist.barrier(group=group)
+        self.recv = [np.memmap(path("recv", r), np.uint16, "r+", shape=(self.recv_rows, H))
+                     for r in range(self.world)]
+        self.ret = [np.memmap(path("ret", r), np.uint16, "r+", shape=(self.ret_rows, H))
+                    for r in range(self.world)]
+
+    def route(self, layer, x):
+        send, offsets = self.dispatch(layer, x)
+        self.state[layer]["send"] = _np(send)
+        return offsets
+
+    def push(self, layer, x, send_starts, dest_offsets):
+        st = self.state[layer]
+        offs = st["srt"]["expert_offsets"].astype(np.int64)
+        for d in range(self.world):
+            n = int(offs[(d + 1) * self.El] - offs[d * self.El])
+            a, b = int(send_starts[d]), int(dest_offsets[d])
+            assert b + n <= self.recv_rows
+            self.recv[d][b:b + n] = st["send"][a:a + n]
+            self.recv[d].flush()
+
+    def experts_push(self, layer, recv_counts, recv_total, x, recv_starts, return_offsets):
+        assert recv_total <= self.recv_rows
+        rows = np.array(self.recv[self.rank][:recv_total])
+        out = _np(self.experts(layer, _t(rows), recv_counts, recv_total, x))
+        per_source = recv_counts.numpy().reshape(self.world, self.El).sum(1)
+        for s in range(self.world):
+            n, a, b = int(per_source[s]), int(recv_starts[s]), int(return_offsets[s])
+            assert b + n <= self.ret_rows
+            self.ret[s][b:b + n] = out[a:a + n]
+            self.ret[s].flush()
+
+    def combine(self, layer, returned, T):
+        if returned is None:  # the peers stored this rank's rows in its return buffer
+            returned = _t(np.array(self.ret[self.rank][:T * self.K]))
+        return super().combine(layer, returned, T)
