@@ -150,6 +150,15 @@ def test_block_decode_gemv_1024_all_rows():
     run_and_compare(small_cfg(), 1024, seed=13, path=(0, 1024, -1), case="config1_decode_1024")
 
 
+# The gate/up GEMM takes units of two weight-row blocks from 64 rows per segment
+# on average: segments that fill a tile partly (T = 1900, about 66 rows each) and
+# skewed routing with segments of several tiles beside nearly empty ones (T =
+# 2048, Zipf hidden states), all rows.
+@pytest.mark.parametrize("T,zipf", [(1900, None), (2048, 1.1)])
+def test_block_paired_gate_up_units_all_rows(T, zipf):
+    run_and_compare(small_cfg(zipf=zipf), T, seed=17, path=(1, -1, -1), case="config1_paired")
+
+
 @pytest.mark.parametrize("path", PATHS)
 def test_block_paths_agree_within_tolerance(path):
     """The two GPU paths compute the same block (different accumulation order)."""
