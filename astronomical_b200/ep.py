@@ -400,6 +400,20 @@ class ExpertParallelBlock:
                     [M[s][self.rank] for s in range(self.world)])
         return self.last_splits
 
+    def forward_host(self, layer: int, hx: torch.Tensor, hy: Optional[torch.Tensor] = None,
+                     device=None) -> torch.Tensor:
+        """The layer on host buffers: ``hx`` (this rank's tokens, pinned for an
+        asynchronous upload) is copied to ``device``, the layer runs there and
+        its output is copied into ``hy`` (pinned, same shape as ``hx``; a new host
+        tensor when omitted).  The copies are queued on the current stream; with
+        ``hy`` given the call does not wait for them."""
+        x = hx.to(device if device is not None else hx.device, non_blocking=True)
+        y = self.forward(layer, x)
+        if hy is None:
+            return y.cpu()
+        hy.copy_(y, non_blocking=True)
+        return hy
+
     def forward(self, layer: int, x: torch.Tensor, marks=None) -> torch.Tensor:
         """``marks``: optional callable recording a named point (stage timing)."""
         T = x.shape[0]

@@ -41,6 +41,10 @@ def _rank_main(rank, world, port, T, layers, outdir, skew):
         y = block.forward(l, x)
         np.save(os.path.join(outdir, f"y_{rank}_{l}.npy"), y.numpy().view(np.uint16))
     np.save(os.path.join(outdir, f"splits_{rank}.npy"), np.array(block.last_splits))
+    # the host-buffer entry: the same layer into a caller's output buffer
+    hy = torch.empty_like(x)
+    block.forward_host(layers - 1, x.clone(), hy)
+    np.save(os.path.join(outdir, f"yh_{rank}.npy"), hy.numpy().view(np.uint16))
     dist.destroy_process_group()
 
 
@@ -72,6 +76,9 @@ def test_expert_parallel_exchange_matches_single_process_oracle(T, skew, world):
             want = np.concatenate([O.moe_block_forward(w, x_all[r * T:(r + 1) * T])[0]
                                    for r in range(world)])
             assert np.array_equal(got, want)
+        for r in range(world):
+            assert np.array_equal(np.load(os.path.join(d, f"yh_{r}.npy")),
+                                  np.load(os.path.join(d, f"y_{r}_{layers - 1}.npy")))
         # rows sent by rank a to rank b are the rows rank b received from rank a
         sp = [np.load(os.path.join(d, f"splits_{r}.npy")) for r in range(world)]
         for a in range(world):
